@@ -1,0 +1,534 @@
+#!/usr/bin/env python
+"""Headline benchmark of the B200 Q4 quantized-matmul path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl thq4|reference]
+
+Workload (the configuration the GEMV GB/s metric is
+scaled on): one decode token through the projection set of a hidden-5120
+transformer layer -- q/k/v/o (5120x5120, 1024x5120 x2, 5120x5120) and the MLP
+gate/up/down (intermediate 17408) -- Q4 affine group-64 weights with f16
+scale/bias, batch 1, bf16 activations.  A step runs `--layers` (24) distinct
+layers back to back, so the 4.46 GB of weights exceed the 126 MB L2 many
+times over and no flush is needed.  Per layer: the fused qkv GEMV, o, the
+fused gate/up GEMV with the SwiGLU epilogue, and down; each layer starts from
+the same input activation (no norms or attention exist on this path, and
+chaining raw projections would overflow bf16), while every projection still
+consumes the previous one's output.  With N GPUs every projection is
+column-sharded (rows split in multiples of 16) and its output is
+all-gathered over NVLink with NCCL before the next projection reads it.
+
+One JSON line on rank 0: `value` is algorithmic weight bytes of the whole job
+per step / max-over-ranks step time (GB/s), the step captured in a CUDA graph
+and timed with CUDA events; `e2e` is the same metric with the input copied
+from pinned host memory and the result read back inside the timed region;
+`roofline` times the dominant kernel (the fused gate/up GEMV) alone;
+`cpu_baseline` times the CPU restatement of the reference's CPU path on a
+bounded sample (N=1 only); `prefill` reports the prefill GEMM (BASELINE
+configs[2], M=512) in TFLOP/s.
+
+`--impl reference` times the reference's CPU semantics (the oracle port, all
+host threads) on the same workload and metric; under torchrun only rank 0
+runs.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime as _dt
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "token-horizon_b200"))
+
+HIDDEN, INTER, KV = 5120, 17408, 1024
+Q4_BYTES_PER_WEIGHT = 0.5625
+LAYER_WEIGHTS = 2 * HIDDEN * HIDDEN + 2 * KV * HIDDEN + 3 * INTER * HIDDEN
+LAYER_BYTES = int(LAYER_WEIGHTS * Q4_BYTES_PER_WEIGHT)  # 185,794,560
+METRIC = "Q4 GEMV achieved HBM GB/s (% of peak); prefill GEMM TFLOP/s; at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="thq4", choices=["thq4", "reference"])
+    p.add_argument("--layers", type=int, default=24)
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--skip-prefill", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.rows = []
+        self.proc = None
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
+        if gpu_ids:
+            cmd += ["-i", ",".join(gpu_ids)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                self.rows.append((ts, int(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0: _dt.datetime, t1: _dt.datetime):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        inwin = [r for r in self.rows if t0 <= r[0] <= t1]
+        note = None
+        if not inwin:  # region shorter than the sampling period: nearest samples
+            inwin = sorted(self.rows, key=lambda r: abs((r[0] - t0).total_seconds()))[:4]
+            note = "timed region shorter than 100 ms sampling: nearest samples"
+        reasons = sorted({self.REASONS[i] for r in inwin for i, v in enumerate(r[4]) if v.lower() == "active"})
+        out = {"sm_mhz": statistics.median(r[2] for r in inwin), "sm_max_mhz": max(r[3] for r in inwin),
+               "reasons": reasons, "samples": len(inwin)}
+        if note:
+            out["note"] = note
+        return out
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def shard_rows(total: int, world: int, rank: int):
+    per = total // world
+    assert per * world == total and per % 16 == 0, f"{total} rows do not split into {world} x 16k"
+    return rank * per, per
+
+
+# ---------------------------------------------------------------------------
+# the thq4 arm
+# ---------------------------------------------------------------------------
+def run_thq4(args):
+    import torch
+    import torch.distributed as dist
+    import thq4
+    from thq4 import synth
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=_dt.timedelta(seconds=300))
+    L = args.layers
+    hbm_peak, tc_peak, tc_sust, peak_kind = peaks()
+
+    # -- weights: each rank quantises the full layer on its GPU, keeps its rows
+    def packed(out_rows, inp, seed, begin, rows):
+        wq, sb = synth.normal_weight(out_rows, inp, seed, dev)
+        p = thq4.PackedWeight.repack(thq4.SRC_MLX, wq, sb, out_rows, inp, thq4.F16, begin, rows)
+        del wq, sb
+        return p
+
+    q0, qn = shard_rows(HIDDEN, world, rank)
+    k0, kn = shard_rows(KV, world, rank)
+    i0, inn = shard_rows(INTER, world, rank)
+    layers = []
+    for l in range(L):
+        s = 1000 * (l + 1)
+        # fused qkv shard = [q rows | k rows | v rows] of this rank, repacked as three weights then joined
+        wq_q, sb_q = synth.normal_weight(HIDDEN, HIDDEN, s + 1, dev)
+        wq_k, sb_k = synth.normal_weight(KV, HIDDEN, s + 2, dev)
+        wq_v, sb_v = synth.normal_weight(KV, HIDDEN, s + 3, dev)
+        wq_qkv = torch.cat([wq_q[q0:q0 + qn], wq_k[k0:k0 + kn], wq_v[k0:k0 + kn]], 0).contiguous()
+        sb_qkv = torch.cat([sb_q[q0:q0 + qn], sb_k[k0:k0 + kn], sb_v[k0:k0 + kn]], 0).contiguous()
+        del wq_q, wq_k, wq_v, sb_q, sb_k, sb_v
+        qkv = thq4.PackedWeight.repack(thq4.SRC_MLX, wq_qkv, sb_qkv, qn + 2 * kn, HIDDEN, thq4.F16)
+        del wq_qkv, sb_qkv
+        o = packed(HIDDEN, HIDDEN, s + 4, q0, qn)
+        gate = packed(INTER, HIDDEN, s + 5, i0, inn)
+        up = packed(INTER, HIDDEN, s + 6, i0, inn)
+        down = packed(HIDDEN, INTER, s + 7, q0, qn)
+        layers.append((qkv, o, gate, up, down))
+    torch.cuda.synchronize()
+    rank_bytes = sum(p.nbytes for lay in layers for p in lay)
+
+    lib = thq4.lib()
+    BF = thq4.BF16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    x_in = (torch.randn((1, HIDDEN), generator=gen, device=dev)).to(torch.bfloat16)
+    t_qkv = torch.empty((1, qn + 2 * kn), dtype=torch.bfloat16, device=dev)
+    t_o = torch.empty((1, qn), dtype=torch.bfloat16, device=dev)
+    t_h = torch.empty((1, inn), dtype=torch.bfloat16, device=dev)
+    t_d = torch.empty((1, qn), dtype=torch.bfloat16, device=dev)
+    full_q = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    full_o = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=dev) if world > 1 else t_o
+    full_h = torch.empty((1, INTER), dtype=torch.bfloat16, device=dev) if world > 1 else t_h
+    y_out = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=dev) if world > 1 else t_d
+
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def stream():
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def step():
+        s = stream()
+        for (qkv, o, gate, up, down) in layers:
+            thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, None, 0, s))
+            if world > 1:
+                dist.all_gather_into_tensor(full_q, t_qkv[:, :qn])
+                src_o = full_q
+            else:
+                src_o = t_qkv  # the first 5120 outputs are q; o reads in = 5120 of them
+            thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(src_o), BF, 1, P(t_o), BF, None, 0, s))
+            if world > 1:
+                dist.all_gather_into_tensor(full_o, t_o)
+            thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h),
+                                        BF, None, 0, s))
+            if world > 1:
+                dist.all_gather_into_tensor(full_h, t_h)
+            thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(full_h), BF, 1, P(t_d), BF, None, 0, s))
+            if world > 1:
+                dist.all_gather_into_tensor(y_out, t_d)
+
+    launches_per_step = 4 * L
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # warm up eagerly (sets kernel attributes), then capture the step
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+
+    gpu_ids = []
+    if rank == 0:
+        try:
+            gpu_ids = ["GPU-" + str(torch.cuda.get_device_properties(i).uuid) for i in range(torch.cuda.device_count())][:max(world, 1)]
+        except Exception:
+            gpu_ids = []
+    sampler = ClockSampler(gpu_ids) if rank == 0 else None
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier()
+
+    def timed(body, reps):
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            body()
+        b.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    w0 = _dt.datetime.now()
+    ms = timed(run, args.steps)
+    w1 = _dt.datetime.now()
+    ms_step = ms / args.steps
+    total_bytes = LAYER_BYTES * L
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+
+    # e2e: pinned host input -> device, step, result -> pinned host
+    x_host = torch.empty((1, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(x_in.cpu())
+    y_host = torch.empty((1, HIDDEN), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_body():
+        x_in.copy_(x_host, non_blocking=True)
+        run()
+        y_host.copy_(y_out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_body()
+    ms_e2e = timed(e2e_body, args.steps) / args.steps
+    e2e_value = total_bytes / (ms_e2e * 1e-3) / 1e9
+
+    # roofline: the fused gate/up GEMV (dominant kernel) alone, one launch per layer
+    g2 = None
+
+    def gu_only():
+        s = stream()
+        for (_, _, gate, up, _) in layers:
+            thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h), BF,
+                                        None, 0, s))
+
+    gu_only()
+    if not args.no_graph:
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            gu_only()
+    run_gu = g2.replay if g2 is not None else gu_only
+    for _ in range(3):
+        run_gu()
+    reps = max(5, min(200, args.steps))
+    ms_gu = timed(run_gu, reps) / (reps * L)
+    gu_bytes = 2 * inn * HIDDEN * Q4_BYTES_PER_WEIGHT
+    achieved = gu_bytes / (ms_gu * 1e-3) / 1e9
+    if sampler:
+        sampler.stop()
+    clocks = sampler.summary(w0, w1) if sampler else None
+
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            tr = json.load(f).get("gate_up_gemv_bytes_per_weight")
+        if tr:
+            traffic = tr * 2 * inn * HIDDEN
+    except Exception:
+        pass
+
+    prefill = None
+    if rank == 0 and not args.skip_prefill:
+        prefill = bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind)
+
+    # free graphs holding NCCL work before the process group goes away
+    graph = g2 = None
+    torch.cuda.synchronize()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: x ~ N(0,1) bf16; W ~ N(0,0.02) quantised Q4 affine group-64, f16 scale/bias",
+            "config": {
+                "workload": "decode-layer projection set, hidden 5120 (q/k/v/o 5120x5120, 1024x5120 x2, "
+                            "5120x5120; MLP gate/up/down intermediate 17408), batch 1",
+                "layers_per_step": L, "bytes_per_step": total_bytes, "batch": 1, "hidden": HIDDEN,
+                "intermediate": INTER, "group": 64, "scale_dtype": "f16",
+                "l2": f"inputs larger than L2: {total_bytes / 1e9:.2f} GB of weights per step "
+                      f"({rank_bytes / 1e9:.2f} GB per GPU), no flush",
+                "parallelism": f"column-shard x{world}" + (" + NCCL all-gather per projection" if world > 1 else ""),
+                "cuda_graph": graph is not None or not args.no_graph,
+            },
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue)",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "bytes_per_launch": int(gu_bytes), "us_per_launch": round(ms_gu * 1e3, 3),
+                         "step_frac": round(value / world / hbm_peak, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * HIDDEN * world,
+                    "d2h_bytes_per_step": 2 * HIDDEN * world, "ms_per_step": round(ms_e2e, 5)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "prefill": prefill,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
+    """x [512 x 4096] bf16, W [12288 x 4096] Q4 -> TFLOP/s."""
+    M, N, K = 512, 12288, 4096
+    wq, sb = synth.normal_weight(N, K, 99, dev)
+    w = thq4.PackedWeight.repack(thq4.SRC_MLX, wq, sb, N, K, thq4.F16)
+    x = torch.randn((M, K), device=dev).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    lib = thq4.lib()
+
+    def call():
+        thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, M,
+                                   ctypes.c_void_p(y.data_ptr()), thq4.BF16, None, 0,
+                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    a.record()
+    for _ in range(reps):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    return {"config": "x 512x4096 bf16, W 12288x4096 Q4 (f16 scale/bias)", "tflops": round(tflops, 2),
+            "ms": round(ms, 4), "peak_tflops": tc_peak, "frac": round(tflops / tc_peak, 4), "peak_kind": peak_kind,
+            "kernel": "verify-kernel token passes (no tcgen05 prefill kernel yet)"}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference CPU semantics)
+# ---------------------------------------------------------------------------
+def _cpu_layer(seed: int):
+    """One layer's MLX weights made on the CPU (same quantiser), as numpy."""
+    import numpy as np
+    import torch
+    from thq4 import synth
+    out = []
+    for i, (rows, inp) in enumerate([(HIDDEN + 2 * KV, HIDDEN), (HIDDEN, HIDDEN), (2 * INTER, HIDDEN), (HIDDEN, INTER)]):
+        wq, sb = synth.normal_weight(rows, inp, seed + i, "cpu")
+        out.append((wq.numpy().view(np.uint32), sb.view(torch.int16).numpy().view(np.uint16), rows, inp))
+    return out
+
+
+def _cpu_step(O, layer, xs):
+    for (wq, sb, rows, inp) in layer:
+        O.cpu_linear(wq, sb, O.SB_F16, xs[inp])
+
+
+def cpu_baseline(seconds: float):
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import q4oracle as O
+    layer = _cpu_layer(5)
+    rng = np.random.default_rng(0)
+    xs = {HIDDEN: rng.standard_normal((1, HIDDEN)).astype(np.float32),
+          INTER: rng.standard_normal((1, INTER)).astype(np.float32)}
+    _cpu_step(O, layer, xs)
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        _cpu_step(O, layer, xs)
+        n += 1
+    dt = time.perf_counter() - t0
+    threads = O.threads()
+    return {"value": round(LAYER_BYTES * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} passes over one decode layer's projections ({LAYER_BYTES / 1e6:.1f} MB Q4, MLX layout), "
+                      f"dequantise-to-bf16 + f32 accumulate, {threads} threads, {dt:.1f} s"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import q4oracle as O
+    layer = _cpu_layer(5)
+    rng = np.random.default_rng(0)
+    xs = {HIDDEN: rng.standard_normal((1, HIDDEN)).astype(np.float32),
+          INTER: rng.standard_normal((1, INTER)).astype(np.float32)}
+    t0 = time.perf_counter()
+    _cpu_step(O, layer, xs)
+    t_one = time.perf_counter() - t0
+    # bound the run to ~2 minutes: sample fewer projections per step if needed
+    sample = layer
+    label = "one decode layer's projections"
+    if t_one * (args.steps + args.warmup) > 120:
+        sample = [layer[1]]
+        label = "the o projection (5120x5120) of one decode layer"
+    sample_bytes = sum(int(r * i * Q4_BYTES_PER_WEIGHT) for (_, _, r, i) in sample)
+    for _ in range(args.warmup):
+        _cpu_step(O, sample, xs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_step(O, sample, xs)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample_bytes / dt / 1e9
+    threads = O.threads()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1); W ~ N(0,0.02) quantised Q4 affine group-64, f16 scale/bias",
+        "config": {"workload": "decode-layer projection set, hidden 5120, batch 1 (CPU sample: " + label + ")",
+                   "hidden": HIDDEN, "intermediate": INTER, "group": 64, "scale_dtype": "f16"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{label}, {sample_bytes / 1e6:.1f} MB Q4 per step, reference CPU semantics "
+                                   f"(dequantise to bf16, f32 accumulate), {threads} threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_thq4(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,169 @@
+/*
+ * thq4.h -- C ABI of the B200 (sm_100a) Q4 affine quantized-matmul path.
+ *
+ * This is the drop-in boundary for th-engine's quant-linear operator.  The
+ * reference reaches its kernels through candle custom ops on (wq: U32,
+ * sb: BF16, x: BF16) behind QLin (engine/src/qwen35.rs:398 linear_ps, :711
+ * gate_up_act_ps, :918 lin_apply_ps; ops engine/src/quant_kernel.rs:2686-2766,
+ * 3040-3135, 3514-3735, 4860-5084) and, for MoE, through Splash's
+ * MoE::add (docs/splash/runtime/ops/MoE.cpp:119-231).  Each entry point below
+ * names the reference interface it replaces.
+ *
+ * Conventions
+ *   - Every data pointer is a DEVICE pointer unless stated otherwise; `stream`
+ *     is a cudaStream_t passed as void* (NULL = the legacy default stream).
+ *   - Every call validates its arguments on the host before launching anything
+ *     and returns a thq4_status; on failure nothing was launched and
+ *     thq4_last_error() holds a message (per host thread).  This mirrors the
+ *     reference's bail!-before-encode checks (quant_kernel.rs:2671-2684,
+ *     qwen35.rs:405-411) and MoE::add's throw-before-encode
+ *     (MoE.cpp:119-144).
+ *   - Inputs are read-only; outputs never alias inputs; weights are immutable
+ *     after repack.  No entry point allocates device memory: scratch comes
+ *     from the caller's workspace.  Calls on distinct streams are thread-safe.
+ *   - Launches are asynchronous; a kernel-side status (bad expert id, etc.) is
+ *     reported by thq4_device_status().
+ */
+#ifndef THQ4_H
+#define THQ4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define THQ4_ABI_VERSION 1
+
+typedef enum thq4_status {
+  THQ4_OK = 0,
+  THQ4_ERR_INVALID_ARGUMENT = 1, /* shape/dtype/pointer/alignment mismatch */
+  THQ4_ERR_UNSUPPORTED = 2,      /* valid request this build does not serve */
+  THQ4_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  THQ4_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+  THQ4_ERR_NCCL = 5              /* a collective failed */
+} thq4_status;
+
+typedef enum thq4_dtype {
+  THQ4_BF16 = 0,
+  THQ4_F16 = 1,
+  THQ4_F32 = 2
+} thq4_dtype;
+
+/* Source layouts thq4_repack accepts (the reference's formats, plus ours). */
+typedef enum thq4_src_layout {
+  /* MLX affine: w u32 [out][in/8] nibbles LSB first, sb [out][2*ng] = a row's
+   * ng scales then its ng biases (qwen35.rs:249-300, quant_kernel.rs:14-15). */
+  THQ4_SRC_MLX = 0,
+  /* QLin::tiled (qwen35.rs:629-697): words [tile][group][col][8] over rows
+   * padded to 256; sb planar, scales then biases at + padded*ng. */
+  THQ4_SRC_TILED = 1,
+  /* Splash expert slab (moe_expert_slab.h:15-28): [weights][scales][biases]
+   * in StorageN=256 order, out % 256 == 0; `sb` is ignored. */
+  THQ4_SRC_SLAB = 2,
+  /* This library's frag16 layout (a device copy of an already packed weight). */
+  THQ4_SRC_FRAG16 = 3
+} thq4_src_layout;
+
+/* One packed projection in the frag16 layout (documented in
+ * token-horizon_b200/csrc/thq4_common.cuh): rows pad to 16, one 512-byte
+ * nibble chunk and one 64-byte scale/bias chunk per (16-row tile, group).
+ * Replaces QLin {wq, sb, out, inp, gs, tiled} (qwen35.rs:303-325). */
+typedef struct thq4_weight {
+  int32_t out;      /* logical output rows */
+  int32_t in;       /* input size K, a multiple of 64 */
+  int32_t gs;       /* quant group size; 64 */
+  int32_t sb_dtype; /* THQ4_BF16 (reference format) or THQ4_F16 */
+  const void *qw;   /* nibbles, 16-byte aligned, thq4_weight_bytes() long */
+  const void *sb;   /* scale/bias quads, 16-byte aligned */
+} thq4_weight;
+
+/* A set of experts with identical shape, packed back to back in frag16
+ * (replaces Splash ExpertQ4Projection, docs/splash/runtime/ops/Linear.hpp:
+ * 37-43).  Expert e's nibbles start at qw + e*qw_stride bytes, its scales at
+ * sb + e*sb_stride bytes. */
+typedef struct thq4_experts {
+  int32_t experts;
+  int32_t out;
+  int32_t in;
+  int32_t gs;
+  int32_t sb_dtype;
+  int32_t reserved;
+  const void *qw;
+  const void *sb;
+  uint64_t qw_stride;
+  uint64_t sb_stride;
+} thq4_experts;
+
+/* ---- library ------------------------------------------------------------ */
+
+/* "thq4 <semver> sm_100a" -- a static string. */
+const char *thq4_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * `cap`); returns its full length. */
+size_t thq4_last_error(char *buf, size_t cap);
+/* Reads and clears the device-side status word of the current device (bad
+ * expert ids and similar conditions a kernel skipped instead of faulting).
+ * Synchronises `stream`.  *status_out = 0 when clean. */
+thq4_status thq4_device_status(uint32_t *status_out, void *stream);
+
+/* ---- weights (replaces Weights::get_lin + QLin::tiled, qwen35.rs:249-300,
+ * 629-697, and the Splash package loader's slab view) -------------------- */
+
+/* Bytes of the frag16 buffers for `rows` x `in` (either pointer may be NULL).
+ * Returns the total. */
+size_t thq4_weight_bytes(int rows, int in, int gs, size_t *qw_bytes,
+                         size_t *sb_bytes);
+/* Repacks rows [row_begin, row_begin + rows) of a `src_out` x `in` weight in
+ * `src_layout` into frag16.  All pointers are device pointers.  Row ranges
+ * let one call cut a column shard or the gate/up halves of a fused
+ * [gate | up] weight (fuse_lins, qwen35.rs:1581-1610). */
+thq4_status thq4_repack(int src_layout, const void *src_w, const void *src_sb,
+                        int src_out, int in, int gs, int sb_dtype,
+                        int row_begin, int rows, void *dst_qw,
+                        size_t dst_qw_bytes, void *dst_sb, size_t dst_sb_bytes,
+                        void *stream);
+/* Fills a thq4_weight after checking alignment and shape. */
+thq4_status thq4_weight_init(thq4_weight *w, int out, int in, int gs,
+                             int sb_dtype, const void *qw, const void *sb);
+
+/* ---- projections ---------------------------------------------------------
+ * x [m][in] (x_dtype THQ4_BF16 or THQ4_F32), y [m][out] (y_dtype THQ4_BF16
+ * or THQ4_F32).  m = 1 runs the decode GEMV, 2..8 the verify kernel, larger
+ * m the prefill GEMM: the row-count routing of QLin::linear_ps
+ * (qwen35.rs:398-617).  Output element (t, n) = sum over groups of
+ * s * sum(q*x) + b * sum(x), accumulated in f32 (decode/verify), or the
+ * bf16-dequantised weight times x accumulated in f32 (prefill). */
+
+/* Replaces QLin::linear_ps / AffineQmvT / AffineQmpp / AffineQsg / AffineQmm
+ * / AffineQpf / AffineQmppPrefill (qwen35.rs:398-617). */
+thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
+                        void *y, int y_dtype, void *workspace,
+                        size_t workspace_bytes, void *stream);
+/* Replaces QLin::gate_up_act_ps (qwen35.rs:711-884): y [m][gate.out] =
+ * bf16(silu(bf16 g) * bf16 u) with g = gate x, u = up x.  gate and up are
+ * the two halves of the fused weight (same out, in, sb_dtype). */
+thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
+                         const void *x, int x_dtype, int m, void *y,
+                         int y_dtype, void *workspace, size_t workspace_bytes,
+                         void *stream);
+/* Workspace bytes thq4_linear / thq4_gate_up need for this shape (0 today for
+ * every routed kernel; callers should still ask). */
+size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
+/* Replaces AffineDequant (quant_kernel.rs:1743-1782, 5836-5899): y bf16
+ * [out][in] = bf16(q * s + b). */
+thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);
+
+/* ---- testing hooks -------------------------------------------------------
+ * Forces the decode/verify kernel's split (K slices per 16-row tile, warps per
+ * CTA) for every later call in this process; ks = 0 restores the policy.  The
+ * reference's tests run every instantiated tile config the same way
+ * (qwen35.rs:6963-6989).  Returns THQ4_ERR_INVALID_ARGUMENT for ks not in
+ * {0,1,2,4,8,16} or warps not in {0,4,8,16}. */
+thq4_status thq4_debug_set_gemv(int ks, int warps);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* THQ4_H */

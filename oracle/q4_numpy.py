@@ -1,0 +1,135 @@
+"""Independent numpy restatement of the oracle's arithmetic, used only to
+cross-check oracle/q4_oracle.c.  TEST INFRASTRUCTURE ONLY.
+
+Every function restates the same reference lines as its C counterpart
+(q4_oracle.h) but is written array-at-a-time, so the two share no code.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def bf16_to_f32(a: np.ndarray) -> np.ndarray:
+    return (np.asarray(a, dtype=np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(a: np.ndarray) -> np.ndarray:
+    """Round to nearest even (LinearNumerics.hpp:19-23)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = u + 0x7FFF + ((u >> 16) & 1)
+    return ((u >> 16) & 0xFFFF).astype(np.uint16)
+
+
+def sb_values(sb: np.ndarray, sb_dtype: int) -> np.ndarray:
+    sb = np.ascontiguousarray(sb, dtype=np.uint16)
+    return sb.view(np.float16).astype(np.float64) if sb_dtype == 1 else bf16_to_f32(sb).astype(np.float64)
+
+
+def unpack_mlx(wq: np.ndarray) -> np.ndarray:
+    """u32 [out][in/8] -> nibbles [out][in], element 8w+e = bits 4e.. of word w
+    (qwen35.rs:126-128)."""
+    shifts = (np.arange(8, dtype=np.uint32) * 4)[None, None, :]
+    q = (np.asarray(wq, dtype=np.uint32)[:, :, None] >> shifts) & 0xF
+    return q.reshape(wq.shape[0], -1).astype(np.uint8)
+
+
+def pack_mlx(q: np.ndarray) -> np.ndarray:
+    out, inp = q.shape
+    q = q.reshape(out, inp // 8, 8).astype(np.uint32)
+    return np.bitwise_or.reduce(q << (np.arange(8, dtype=np.uint32) * 4), axis=2).astype(np.uint32)
+
+
+def linear_group(wq, sb, sb_dtype: int, x: np.ndarray) -> np.ndarray:
+    """acc += s * sum(q*x) + b * sum(x) per group (quant_kernel.rs:1994-2001)."""
+    x = np.atleast_2d(np.asarray(x, dtype=np.float64))
+    q = unpack_mlx(wq).astype(np.float64)
+    out, inp = q.shape
+    ng = inp // 64
+    s = sb_values(sb, sb_dtype)
+    sc, bi = s[:, :ng], s[:, ng:]
+    dots = np.einsum("ngk,mgk->mng", q.reshape(out, ng, 64), x.reshape(-1, ng, 64))
+    sums = x.reshape(-1, ng, 64).sum(axis=2)  # [m][ng]
+    return (dots * sc[None]).sum(axis=2) + sums @ bi.T
+
+
+def frag16_from_mlx(wq, sb, out: int, inp: int):
+    """The frag16 layout (thq4_layout.cuh), built with index arithmetic."""
+    q = unpack_mlx(wq)
+    rt_n, ng = (out + 15) // 16, inp // 64
+    qp = np.zeros((rt_n * 16, inp), dtype=np.uint32)
+    qp[:out] = q
+    lane = np.arange(32)
+    r, c = lane // 4, lane % 4
+    fq = np.zeros((rt_n, ng, 32, 4), dtype=np.uint32)
+    for j in range(4):
+        word = np.zeros((rt_n, ng, 32), dtype=np.uint32)
+        for i in range(4):
+            for h in range(2):
+                rows = r + 8 * (i & 1)  # [32]
+                ks = 16 * j + 2 * c + 8 * (i >> 1) + h  # [32]
+                tile_rows = (np.arange(rt_n)[:, None] * 16 + rows[None, :])  # [rt][32]
+                kk = np.arange(ng)[:, None] * 64 + ks[None, :]  # [g][32]
+                vals = qp[tile_rows[:, None, :], kk[None, :, :]]  # [rt][g][32]
+                word |= vals << np.uint32(16 * h + 4 * i)
+        fq[:, :, :, j] = word
+    sbp = np.zeros((rt_n * 16, 2 * ng), dtype=np.uint16)
+    sbp[:out] = sb
+    fsb = np.zeros((rt_n, ng, 8, 4), dtype=np.uint16)
+    for rr in range(8):
+        for half in range(2):
+            rows = np.arange(rt_n) * 16 + rr + 8 * half
+            fsb[:, :, rr, 2 * half] = sbp[rows, :ng]
+            fsb[:, :, rr, 2 * half + 1] = sbp[rows, ng:]
+    return fq.reshape(-1), fsb.reshape(-1)
+
+
+def tiled_from_mlx(wq, sb, out: int, inp: int):
+    """QLin::tiled (qwen35.rs:629-697)."""
+    ng, tiles = inp // 64, (out + 255) // 256
+    padded = tiles * 256
+    w = np.zeros((padded, ng, 8), dtype=np.uint32)
+    w[:out] = np.asarray(wq).reshape(out, ng, 8)
+    tw = w.reshape(tiles, 256, ng, 8).transpose(0, 2, 1, 3).reshape(-1)
+    s = np.zeros((padded, 2 * ng), dtype=np.uint16)
+    s[:out] = sb
+    sc = s[:, :ng].reshape(tiles, 256, ng).transpose(0, 2, 1).reshape(-1)
+    bi = s[:, ng:].reshape(tiles, 256, ng).transpose(0, 2, 1).reshape(-1)
+    return tw, np.concatenate([sc, bi])
+
+
+def moe_select(logits_bf16: np.ndarray, k: int):
+    """Stable sort on (-score, id) (moe_metal_test.mm:366-372)."""
+    s = bf16_to_f32(logits_bf16)
+    T, E = s.shape
+    ids = np.empty((T, k), dtype=np.uint32)
+    w = np.empty((T, k), dtype=np.uint16)
+    for t in range(T):
+        order = sorted(range(E), key=lambda e: (-float(s[t, e]), e))[:k]
+        ids[t] = order
+        top = s[t, order].astype(np.float32)
+        ex = np.exp((top - top[0]).astype(np.float32)).astype(np.float32)
+        den = np.float32(0)
+        for v in ex:
+            den = np.float32(den + v)
+        w[t] = f32_to_bf16((ex / den).astype(np.float32))
+    return ids, w
+
+
+def moe_group(ids: np.ndarray, E: int, tile_rows: int):
+    """Stable counting sort by expert; returns (tiles list, grouped, route_rows)."""
+    flat = np.asarray(ids, dtype=np.int64).ravel()
+    order = np.argsort(flat, kind="stable")
+    counts = np.bincount(flat, minlength=E)
+    tiles, grouped, route_rows = [], [], np.empty(flat.size, dtype=np.uint32)
+    pos = 0
+    for e in range(E):
+        routes = order[pos:pos + counts[e]]
+        pos += counts[e]
+        for t0 in range(0, counts[e], tile_rows):
+            chunk = routes[t0:t0 + tile_rows]
+            tiles.append((e, len(chunk)))
+            for i, r in enumerate(chunk):
+                route_rows[r] = len(grouped) + i
+            grouped.extend(int(r) for r in chunk)
+            grouped.extend([0xFFFFFFFF] * (tile_rows - len(chunk)))
+    return tiles, np.array(grouped, dtype=np.uint32), route_rows

@@ -1,0 +1,365 @@
+"""numpy/ctypes front end of the CPU oracle (oracle/q4_oracle.c).
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker the CUDA path is compared
+against; only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline and
+reference legs import it.  The product library never loads it.
+
+Parity status: partially pinned -- see q4_oracle.h.  ``ref_pins()`` returns the
+reference's own compiled helpers (oracle/_ref/libq4ref.so) when they were built
+here; they travel to the GPU box with the rest of the tree, but nothing on the
+box rebuilds them.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, c_double, c_float, c_int, c_size_t, c_uint16, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = os.path.join(_HERE, "libq4oracle.so")
+_REF = os.path.join(_HERE, "_ref", "libq4ref.so")
+_lib = None
+_ref = None
+
+SB_BF16 = 0
+SB_F16 = 1
+
+
+def build(force: bool = False) -> None:
+    """Compile the oracle (and the reference pins when the reference exists)."""
+    if force or not os.path.exists(_LIB):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "oracle"])
+    if os.path.isdir("/root/reference") and (force or not os.path.exists(_REF)):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "ref"])
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB):
+            build()
+        _lib = ctypes.CDLL(_LIB)
+        _declare(_lib)
+    return _lib
+
+
+def ref_pins():
+    """The reference's own helpers compiled from its sources, or None."""
+    global _ref
+    if _ref is None and os.path.exists(_REF):
+        r = ctypes.CDLL(_REF)
+        r.ref_float_to_bf16.restype = c_uint16
+        r.ref_float_to_bf16.argtypes = [c_float]
+        r.ref_bf16_to_float.restype = c_float
+        r.ref_bf16_to_float.argtypes = [c_uint16]
+        r.ref_ulp_bf16.restype = c_float
+        r.ref_ulp_bf16.argtypes = [c_float]
+        r.ref_silu.restype = c_float
+        r.ref_silu.argtypes = [c_float]
+        r.ref_reassociation_slack.restype = c_float
+        r.ref_reassociation_slack.argtypes = [c_uint32, c_float]
+        r.ref_split_tolerance.restype = c_float
+        r.ref_split_tolerance.argtypes = [c_int, c_float, c_float, c_float, c_float, c_float]
+        r.ref_moe_maximum_tiles.restype = c_uint32
+        r.ref_moe_maximum_tiles.argtypes = [c_uint32] * 6
+        r.ref_moe_tile_descriptor_bytes.restype = c_uint32
+        r.ref_moe_tile_descriptor_bytes.argtypes = []
+        _ref = r
+    return _ref
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(c_void_p)
+
+
+def _declare(L) -> None:
+    v = c_void_p
+    sig = {
+        "q4o_f32_to_bf16": (c_uint16, [c_float]),
+        "q4o_bf16_to_f32": (c_float, [c_uint16]),
+        "q4o_f32_to_f16": (c_uint16, [c_float]),
+        "q4o_f16_to_f32": (c_float, [c_uint16]),
+        "q4o_f32_to_bf16_n": (None, [v, v, c_size_t]),
+        "q4o_bf16_to_f32_n": (None, [v, v, c_size_t]),
+        "q4o_lcg": (c_uint64, [POINTER(c_uint64)]),
+        "q4o_rand_qlin": (None, [c_int, c_int, c_uint64, v, v]),
+        "q4o_rand_x": (None, [c_int, c_uint64, v]),
+        "q4o_rand_pf_case": (None, [c_int, c_int, c_int, POINTER(c_uint64), v, v, v]),
+        "q4o_quantize": (None, [v, c_int, c_int, c_int, c_int, v, v, c_int]),
+        "q4o_mlx_to_tiled": (None, [v, v, c_int, c_int, v, v]),
+        "q4o_tiled_to_mlx": (None, [v, v, c_int, c_int, v, v]),
+        "q4o_slab_bytes": (c_size_t, [c_int, c_int]),
+        "q4o_mlx_to_slab": (None, [v, v, c_int, c_int, v]),
+        "q4o_slab_to_mlx": (None, [v, c_int, c_int, v, v]),
+        "q4o_frag16_qw_bytes": (c_size_t, [c_int, c_int]),
+        "q4o_frag16_sb_bytes": (c_size_t, [c_int, c_int]),
+        "q4o_mlx_to_frag16": (None, [v, v, c_int, c_int, v, v]),
+        "q4o_frag16_to_mlx": (None, [v, v, c_int, c_int, v, v]),
+        "q4o_linear_group": (None, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
+        "q4o_linear_dequant": (None, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
+        "q4o_dequant_bf16": (None, [v, v, c_int, c_int, c_int, v]),
+        "q4o_silu_mul_bf16": (c_uint16, [c_float, c_float]),
+        "q4o_gate_up": (None, [v, v, c_int, c_int, c_int, c_int, c_int, v, c_int, v, c_int]),
+        "q4o_moe_select": (None, [v, c_int, c_int, c_int, v, v]),
+        "q4o_moe_max_tiles": (c_uint32, [c_int, c_int, c_int, c_int]),
+        "q4o_moe_group": (c_int, [v, c_int, c_int, c_int, c_int, c_int, v, v, v]),
+        "q4o_moe_forward": (None, [v, v, c_int, c_int, c_int, c_int, c_int, v, v, v, v, v, v,
+                                   c_int, v, v, v, c_int]),
+        "q4o_cpu_linear": (c_int, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+
+
+def threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+# ---- conversions --------------------------------------------------------------
+
+def f32_to_bf16(a) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    out = np.empty(a.shape, dtype=np.uint16)
+    lib().q4o_f32_to_bf16_n(_p(a), _p(out), a.size)
+    return out
+
+
+def bf16_to_f32(a) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    out = np.empty(a.shape, dtype=np.float32)
+    lib().q4o_bf16_to_f32_n(_p(a), _p(out), a.size)
+    return out
+
+
+def bf16_round(a) -> np.ndarray:
+    return bf16_to_f32(f32_to_bf16(a))
+
+
+def sb_to_f32(a, sb_dtype: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    if sb_dtype == SB_F16:
+        return a.view(np.float16).astype(np.float32)
+    return bf16_to_f32(a)
+
+
+# ---- generators -----------------------------------------------------------------
+
+def rand_qlin(out: int, inp: int, seed: int):
+    """The reference tests' random packed weight (qwen35.rs:6896-6915)."""
+    wq = np.empty((out, inp // 8), dtype=np.uint32)
+    sb = np.empty((out, 2 * (inp // 64)), dtype=np.uint16)
+    lib().q4o_rand_qlin(out, inp, seed, _p(wq), _p(sb))
+    return wq, sb
+
+
+def rand_x(inp: int, seed: int) -> np.ndarray:
+    """The reference tests' random activation as bf16 bits (qwen35.rs:6917-6923)."""
+    x = np.empty(inp, dtype=np.uint16)
+    lib().q4o_rand_x(inp, seed, _p(x))
+    return x
+
+
+class PfStream:
+    """The prefill tests' single LCG state (quant_kernel.rs:5446)."""
+
+    def __init__(self, seed: int = 0x5EED):
+        self.state = c_uint64(seed)
+
+    def case(self, total_out: int, inp: int, m: int):
+        """(tiled words, planar sb, x bf16 [m][inp]) for the next case."""
+        ng, padded = inp // 64, (total_out + 255) // 256 * 256
+        tw = np.empty(padded * ng * 8, dtype=np.uint32)
+        tsb = np.empty(2 * padded * ng, dtype=np.uint16)
+        x = np.empty((m, inp), dtype=np.uint16)
+        lib().q4o_rand_pf_case(total_out, inp, m, ctypes.byref(self.state), _p(tw), _p(tsb), _p(x))
+        return tw, tsb, x
+
+
+# (out per stream, inp, gate_up, m) of pf_vec_matches_legacy_bitwise
+PF_CASES = [(640, 512, False, 130), (720, 256, False, 257), (384, 1024, False, 64),
+            (1280, 512, False, 200), (512, 512, True, 161), (256, 1024, True, 96)]
+# (out, ng) of qmvt_plain_matches_scalar and (half, ng) of qmvt_gate_up_matches_scalar
+QMVT_PLAIN_CASES = [(520, 7), (256, 80), (1000, 17), (72, 96)]
+QMVT_GATE_UP_CASES = [(256, 7), (264, 80), (512, 17), (1000, 6)]
+
+
+def quantize(w: np.ndarray, sb_dtype: int = SB_F16, gs: int = 64):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out, inp = w.shape
+    wq = np.empty((out, inp // 8), dtype=np.uint32)
+    sb = np.empty((out, 2 * (inp // gs)), dtype=np.uint16)
+    lib().q4o_quantize(_p(w), out, inp, gs, sb_dtype, _p(wq), _p(sb), threads())
+    return wq, sb
+
+
+def synthetic_weight(out: int, inp: int, seed: int, sb_dtype: int = SB_F16, std: float = 0.02):
+    """W ~ N(0, std) quantised by this repository's min/max group-64 quantiser."""
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((out, inp), dtype=np.float32) * np.float32(std)
+    return quantize(w, sb_dtype)
+
+
+# ---- layouts --------------------------------------------------------------------
+
+def mlx_to_tiled(wq, sb):
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    ng, tiles = inp // 64, (out + 255) // 256
+    tw = np.empty(tiles * ng * 2048, dtype=np.uint32)
+    tsb = np.empty(2 * tiles * 256 * ng, dtype=np.uint16)
+    lib().q4o_mlx_to_tiled(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), out, inp, _p(tw), _p(tsb))
+    return tw, tsb
+
+
+def tiled_to_mlx(tw, tsb, out: int, inp: int):
+    wq = np.empty((out, inp // 8), dtype=np.uint32)
+    sb = np.empty((out, 2 * (inp // 64)), dtype=np.uint16)
+    lib().q4o_tiled_to_mlx(_p(tw), _p(tsb), out, inp, _p(wq), _p(sb))
+    return wq, sb
+
+
+def mlx_to_slab(wq, sb) -> np.ndarray:
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    slab = np.empty(lib().q4o_slab_bytes(out, inp), dtype=np.uint8)
+    lib().q4o_mlx_to_slab(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), out, inp, _p(slab))
+    return slab
+
+
+def slab_to_mlx(slab, out: int, inp: int):
+    wq = np.empty((out, inp // 8), dtype=np.uint32)
+    sb = np.empty((out, 2 * (inp // 64)), dtype=np.uint16)
+    lib().q4o_slab_to_mlx(_p(slab), out, inp, _p(wq), _p(sb))
+    return wq, sb
+
+
+def mlx_to_frag16(wq, sb):
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    fq = np.empty(lib().q4o_frag16_qw_bytes(out, inp) // 4, dtype=np.uint32)
+    fsb = np.empty(lib().q4o_frag16_sb_bytes(out, inp) // 2, dtype=np.uint16)
+    lib().q4o_mlx_to_frag16(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), out, inp, _p(fq), _p(fsb))
+    return fq, fsb
+
+
+def frag16_to_mlx(fq, fsb, out: int, inp: int):
+    wq = np.empty((out, inp // 8), dtype=np.uint32)
+    sb = np.empty((out, 2 * (inp // 64)), dtype=np.uint16)
+    lib().q4o_frag16_to_mlx(_p(fq), _p(fsb), out, inp, _p(wq), _p(sb))
+    return wq, sb
+
+
+# ---- products -------------------------------------------------------------------
+
+def _x2d(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return x.reshape(1, -1) if x.ndim == 1 else x
+
+
+def linear_group(wq, sb, sb_dtype: int, x) -> np.ndarray:
+    """Per-group kernel semantics in fp64: y [m][out] (unrounded)."""
+    x = _x2d(x)
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    y = np.empty((x.shape[0], out), dtype=np.float64)
+    lib().q4o_linear_group(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), sb_dtype, out, inp,
+                           _p(x), x.shape[0], _p(y), threads())
+    return y
+
+
+def linear_dequant(wq, sb, sb_dtype: int, x) -> np.ndarray:
+    """Reference CPU path: bf16-dequantised weight, fp64 dot: y [m][out]."""
+    x = _x2d(x)
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    y = np.empty((x.shape[0], out), dtype=np.float64)
+    lib().q4o_linear_dequant(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), sb_dtype, out, inp,
+                             _p(x), x.shape[0], _p(y), threads())
+    return y
+
+
+def dequant_bf16(wq, sb, sb_dtype: int) -> np.ndarray:
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    w = np.empty((out, inp), dtype=np.uint16)
+    lib().q4o_dequant_bf16(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), sb_dtype, out, inp, _p(w))
+    return w
+
+
+def silu_mul_bf16(gate, up) -> np.ndarray:
+    gate = np.asarray(gate, dtype=np.float32).ravel()
+    up = np.asarray(up, dtype=np.float32).ravel()
+    f = lib().q4o_silu_mul_bf16
+    return np.array([f(float(g), float(u)) for g, u in zip(gate, up)], dtype=np.uint16)
+
+
+def gate_up(wq, sb, sb_dtype: int, up_row: int, half: int, x) -> np.ndarray:
+    """Fused [gate | up] projection with the SwiGLU epilogue -> bf16 [m][half]."""
+    x = _x2d(x)
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    y = np.empty((x.shape[0], half), dtype=np.uint16)
+    lib().q4o_gate_up(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), sb_dtype, out, inp,
+                      up_row, half, _p(x), x.shape[0], _p(y), threads())
+    return y
+
+
+# ---- MoE ------------------------------------------------------------------------
+
+def moe_select(logits_bf16, k: int):
+    logits_bf16 = np.ascontiguousarray(logits_bf16, dtype=np.uint16)
+    T, E = logits_bf16.shape
+    ids = np.empty((T, k), dtype=np.uint32)
+    w = np.empty((T, k), dtype=np.uint16)
+    lib().q4o_moe_select(_p(logits_bf16), T, E, k, _p(ids), _p(w))
+    return ids, w
+
+
+def moe_max_tiles(T: int, E: int, k: int, tile_rows: int) -> int:
+    return int(lib().q4o_moe_max_tiles(T, E, k, tile_rows))
+
+
+def moe_group(ids, E: int, tile_rows: int, max_tiles: int | None = None):
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    T, k = ids.shape
+    if max_tiles is None:
+        max_tiles = moe_max_tiles(T, E, k, tile_rows)
+    tiles = np.empty((max_tiles, 2), dtype=np.uint32)
+    grouped = np.empty(max_tiles * tile_rows, dtype=np.uint32)
+    route_rows = np.empty(T * k, dtype=np.uint32)
+    n = lib().q4o_moe_group(_p(ids), T, k, E, tile_rows, max_tiles, _p(tiles), _p(grouped), _p(route_rows))
+    if n < 0:
+        raise ValueError("max_tiles too small")
+    return tiles, n, grouped, route_rows
+
+
+def moe_forward(x_bf16, residual_bf16, ids, weights_bf16, gu_wq, gu_sb, dn_wq, dn_sb, sb_dtype: int,
+                I: int, want_h: bool = False):
+    """One MoE layer on MLX row-major experts; returns (y, h, d) as bf16."""
+    x_bf16 = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T, H = x_bf16.shape
+    k = ids.shape[1]
+    E = gu_wq.shape[0]
+    y = np.empty((T, H), dtype=np.uint16)
+    d = np.empty((T * k, H), dtype=np.uint16)
+    h = np.empty((T * k, I), dtype=np.uint16) if want_h else None
+    res = None if residual_bf16 is None else np.ascontiguousarray(residual_bf16, dtype=np.uint16)
+    lib().q4o_moe_forward(_p(x_bf16), None if res is None else _p(res), T, H, I, E, k,
+                          _p(np.ascontiguousarray(ids, dtype=np.uint32)),
+                          _p(np.ascontiguousarray(weights_bf16, dtype=np.uint16)),
+                          _p(np.ascontiguousarray(gu_wq)), _p(np.ascontiguousarray(gu_sb)),
+                          _p(np.ascontiguousarray(dn_wq)), _p(np.ascontiguousarray(dn_sb)), sb_dtype,
+                          None if h is None else _p(h), _p(d), _p(y), threads())
+    return y, h, d
+
+
+# ---- CPU baseline ---------------------------------------------------------------
+
+def cpu_linear(wq, sb, sb_dtype: int, x, nthreads: int | None = None):
+    """The timed CPU baseline (f32 accumulate, threaded).  Returns (y, threads)."""
+    x = _x2d(x)
+    out, inp = wq.shape[0], wq.shape[1] * 8
+    y = np.empty((x.shape[0], out), dtype=np.float32)
+    n = lib().q4o_cpu_linear(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), sb_dtype, out, inp,
+                             _p(x), x.shape[0], _p(y), nthreads or threads())
+    if n < 0:
+        raise ValueError("unsupported shape for the CPU baseline")
+    return y, n

@@ -1,0 +1,73 @@
+"""Builds libthq4.so (the C-ABI library) in-tree for sm_100a with nvcc.
+
+    python token-horizon_b200/build.py [--verbose]
+
+Every .cu under csrc/ is compiled with
+``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into
+token-horizon_b200/thq4/libthq4.so next to the Python host mirror.  The .so
+is git-ignored but travels to the GPU box with the source tree.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import glob
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+OUT = os.path.join(HERE, "thq4", "libthq4.so")
+BUILD = os.path.join(HERE, "_build")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+         "-Xcompiler", "-Wall", "-diag-suppress", "177"]
+
+
+def sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def _stale(out: str, deps: list[str]) -> bool:
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    headers = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
+        glob.glob(os.path.join(HERE, "..", "include", "*.h"))
+    objs, jobs = [], []
+    for src in sources():
+        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        objs.append(obj)
+        if force or _stale(obj, [src] + headers):
+            cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
+            if verbose:
+                cmd += ["-Xptxas", "-v"]
+            jobs.append(cmd)
+
+    def run(cmd):
+        p = subprocess.run(cmd, capture_output=True, text=True)
+        return cmd, p
+
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
+        for cmd, p in ex.map(run, jobs):
+            if verbose or p.returncode != 0:
+                sys.stderr.write(p.stdout + p.stderr)
+            if p.returncode != 0:
+                raise RuntimeError("nvcc failed: " + " ".join(cmd))
+    if force or jobs or _stale(OUT, objs):
+        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs, "-lcuda"]
+        p = subprocess.run(cmd, capture_output=True, text=True)
+        if p.returncode != 0:
+            sys.stderr.write(p.stdout + p.stderr)
+            raise RuntimeError("link failed")
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(verbose="--verbose" in sys.argv, force="--force" in sys.argv))

@@ -1,0 +1,268 @@
+// thq4_api.cu -- the C ABI: argument validation, routing and error reporting.
+//
+// Host-side mirror of the reference's operator layer: QLin::linear_ps's
+// row-count routing (engine/src/qwen35.rs:398-617), gate_up_act_ps
+// (:711-884) and the candle op checks that bail before anything is encoded
+// (check3, quant_kernel.rs:2671-2684; presum length check :3642-3657).
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "thq4_common.cuh"
+#include "thq4_internal.h"
+
+namespace thq4 {
+
+__device__ uint32_t g_status = 0;
+
+uint32_t *status_word() {
+  static DeviceOnce once;
+  static uint32_t *addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  once.run([&] { return cudaGetSymbolAddress(reinterpret_cast<void **>(&addr[dev]), g_status); });
+  return addr[dev];
+}
+
+namespace {
+thread_local std::string t_last_error;
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+}  // namespace
+
+thq4_status set_error(thq4_status s, const std::string &msg) {
+  t_last_error = msg;
+  return s;
+}
+
+thq4_status cuda_error(cudaError_t e, const char *what) {
+  return set_error(THQ4_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                                      cudaGetErrorString(e) + ")");
+}
+
+int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+namespace {
+std::atomic<int> g_force_ks{-1}, g_force_warps{0};
+}  // namespace
+
+GemvCfg gemv_cfg_override() {
+  const int fk = g_force_ks.load(std::memory_order_relaxed);
+  if (fk >= 0) {
+    GemvCfg c;
+    c.ks = fk;
+    c.warps = g_force_warps.load(std::memory_order_relaxed);
+    return c;
+  }
+  static const GemvCfg cfg = [] {
+    GemvCfg c;
+    const char *e = std::getenv("THQ4_GEMV");
+    if (e && *e) {
+      int ks = 0, warps = 0;
+      if (std::sscanf(e, "%d,%d", &ks, &warps) >= 1) {
+        if (ks == 1 || ks == 2 || ks == 4 || ks == 8 || ks == 16) c.ks = ks;
+        if (warps == 4 || warps == 8 || warps == 16) c.warps = warps;
+      }
+    }
+    return c;
+  }();
+  return cfg;
+}
+
+namespace {
+
+thq4_status check_weight(const thq4_weight *w, const char *who) {
+  if (!w) return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": weight is NULL");
+  if (w->out <= 0 || w->in <= 0)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": weight has out " +
+                                                    std::to_string(w->out) + ", in " + std::to_string(w->in));
+  if (w->gs != kGroup)
+    return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": group size " + std::to_string(w->gs) +
+                                               " (only 64 is packed)");
+  if (w->in % kGroup != 0)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": in " + std::to_string(w->in) +
+                                                    " is not a multiple of 64");
+  if (w->sb_dtype != THQ4_BF16 && w->sb_dtype != THQ4_F16)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": scale dtype must be bf16 or f16");
+  if (!w->qw || !w->sb || !aligned(w->qw, 16) || !aligned(w->sb, 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": weight buffers must be non-NULL and "
+                                                                   "16-byte aligned");
+  return THQ4_OK;
+}
+
+thq4_status check_io(const void *x, int x_dtype, int m, const void *y, int y_dtype, const char *who) {
+  if (m < 1) return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": m must be >= 1");
+  if (x_dtype != THQ4_BF16 && x_dtype != THQ4_F32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": x dtype must be bf16 or f32");
+  if (y_dtype != THQ4_BF16 && y_dtype != THQ4_F32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": y dtype must be bf16 or f32");
+  if (!x || !y) return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": x and y must be non-NULL");
+  // the kernels read x as 16-byte vectors (the reference rejects a
+  // misaligned x the same way, qwen35.rs:366, 7034-7037)
+  if (!aligned(x, 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": x must be 16-byte aligned");
+  if (!aligned(y, y_dtype == THQ4_F32 ? 4 : 2))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": y is misaligned");
+  return THQ4_OK;
+}
+
+}  // namespace
+}  // namespace thq4
+
+using namespace thq4;
+
+extern "C" {
+
+const char *thq4_version(void) { return "thq4 " THQ4_SEMVER " sm_100a"; }
+
+size_t thq4_last_error(char *buf, size_t cap) {
+  const std::string &s = t_last_error;
+  if (buf && cap) {
+    const size_t n = s.size() < cap - 1 ? s.size() : cap - 1;
+    std::memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+  }
+  return s.size();
+}
+
+thq4_status thq4_device_status(uint32_t *status_out, void *stream) {
+  if (!status_out) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_device_status: status_out is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(status_out, g_status, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(uint32_t), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_error(e, "thq4_device_status");
+  return THQ4_OK;
+}
+
+size_t thq4_weight_bytes(int rows, int in, int gs, size_t *qw_bytes, size_t *sb_bytes) {
+  size_t q = 0, s = 0;
+  if (rows > 0 && in > 0 && gs == kGroup && in % kGroup == 0) {
+    const size_t chunks = (size_t)row_tiles(rows) * (size_t)(in / kGroup);
+    q = chunks * kChunkBytes;
+    s = chunks * kQuadBytes;
+  }
+  if (qw_bytes) *qw_bytes = q;
+  if (sb_bytes) *sb_bytes = s;
+  return q + s;
+}
+
+thq4_status thq4_repack(int src_layout, const void *src_w, const void *src_sb, int src_out, int in, int gs,
+                        int sb_dtype, int row_begin, int rows, void *dst_qw, size_t dst_qw_bytes, void *dst_sb,
+                        size_t dst_sb_bytes, void *stream) {
+  const char *who = "thq4_repack";
+  if (src_layout < THQ4_SRC_MLX || src_layout > THQ4_SRC_FRAG16)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: unknown source layout");
+  if (gs != kGroup) return set_error(THQ4_ERR_UNSUPPORTED, "thq4_repack: only group size 64 is packed");
+  if (sb_dtype != THQ4_BF16 && sb_dtype != THQ4_F16)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: scale dtype must be bf16 or f16");
+  if (src_out <= 0 || in <= 0 || in % kGroup != 0)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": bad shape " + std::to_string(src_out) +
+                                                    " x " + std::to_string(in));
+  if (rows <= 0 || row_begin < 0 || row_begin + rows > src_out)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": row range [" + std::to_string(row_begin) +
+                                                    ", " + std::to_string(row_begin + rows) + ") outside " +
+                                                    std::to_string(src_out) + " rows");
+  if (src_layout == THQ4_SRC_SLAB && src_out % 256 != 0)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: a slab needs out % 256 == 0 (StorageN=256)");
+  if (src_layout == THQ4_SRC_FRAG16 && (row_begin != 0 || rows != src_out))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: a frag16 source is copied whole");
+  if (!src_w || (src_layout != THQ4_SRC_SLAB && !src_sb))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: source pointers must be non-NULL");
+  if (!aligned(src_w, 16) || (src_sb && !aligned(src_sb, 2)) ||
+      (src_layout == THQ4_SRC_FRAG16 && !aligned(src_sb, 16)))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: source weights must be 16-byte aligned");
+  size_t need_q = 0, need_s = 0;
+  thq4_weight_bytes(rows, in, gs, &need_q, &need_s);
+  if (!dst_qw || !dst_sb || !aligned(dst_qw, 16) || !aligned(dst_sb, 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: destination buffers must be 16-byte aligned");
+  if (dst_qw_bytes < need_q || dst_sb_bytes < need_s)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     std::string(who) + ": destination too small (need " + std::to_string(need_q) + " + " +
+                         std::to_string(need_s) + " bytes)");
+  cudaError_t e = repack_launch(src_layout, src_w, src_sb, src_out, in, row_begin, rows, dst_qw, dst_sb,
+                                static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+thq4_status thq4_weight_init(thq4_weight *w, int out, int in, int gs, int sb_dtype, const void *qw,
+                             const void *sb) {
+  if (!w) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_weight_init: w is NULL");
+  thq4_weight t{out, in, gs, sb_dtype, qw, sb};
+  thq4_status s = check_weight(&t, "thq4_weight_init");
+  if (s != THQ4_OK) return s;
+  *w = t;
+  return THQ4_OK;
+}
+
+size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m) {
+  (void)w;
+  (void)m;
+  return 0;
+}
+
+thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
+                        void *workspace, size_t workspace_bytes, void *stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  thq4_status s = check_weight(w, "thq4_linear");
+  if (s != THQ4_OK) return s;
+  s = check_io(x, x_dtype, m, y, y_dtype, "thq4_linear");
+  if (s != THQ4_OK) return s;
+  cudaError_t e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32,
+                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "thq4_linear");
+  return THQ4_OK;
+}
+
+thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const void *x, int x_dtype, int m,
+                         void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  thq4_status s = check_weight(gate, "thq4_gate_up");
+  if (s != THQ4_OK) return s;
+  s = check_weight(up, "thq4_gate_up");
+  if (s != THQ4_OK) return s;
+  if (gate->out != up->out || gate->in != up->in || gate->sb_dtype != up->sb_dtype)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_gate_up: gate and up halves differ in shape or dtype");
+  s = check_io(x, x_dtype, m, y, y_dtype, "thq4_gate_up");
+  if (s != THQ4_OK) return s;
+  cudaError_t e = gemv_launch(*gate, up, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32,
+                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "thq4_gate_up");
+  return THQ4_OK;
+}
+
+thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream) {
+  thq4_status s = check_weight(w, "thq4_dequant");
+  if (s != THQ4_OK) return s;
+  if (!y || !aligned(y, 16)) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_dequant: y must be 16-byte aligned");
+  cudaError_t e = dequant_launch(*w, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "thq4_dequant");
+  return THQ4_OK;
+}
+
+thq4_status thq4_debug_set_gemv(int ks, int warps) {
+  if (!(ks == 0 || ks == 1 || ks == 2 || ks == 4 || ks == 8 || ks == 16) ||
+      !(warps == 0 || warps == 4 || warps == 8 || warps == 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_debug_set_gemv: ks must be 0/1/2/4/8/16, warps 0/4/8/16");
+  g_force_warps.store(warps, std::memory_order_relaxed);
+  g_force_ks.store(ks == 0 ? -1 : ks, std::memory_order_relaxed);
+  return THQ4_OK;
+}
+
+}  // extern "C"

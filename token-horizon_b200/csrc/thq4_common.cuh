@@ -1,0 +1,130 @@
+// thq4_common.cuh -- shared device/host helpers of the thq4 library (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/thq4.h"
+
+#define THQ4_SEMVER "0.1.0"
+
+// ---------------------------------------------------------------------------
+// frag16 weight layout
+// ---------------------------------------------------------------------------
+// Rows pad to a multiple of 16 (a "row tile", the M of one mma.m16n8k16).
+// K splits into quant groups of 64.  For tile rt and group g:
+//
+//   nibbles: 512 bytes at byte offset (rt * ng + g) * 512.  Lane l of a warp
+//            owns bytes [16 l, 16 l + 16): four u32 words, word j = k-step j
+//            (k 16 j .. 16 j + 15 of the group).  With r = l / 4, c = l % 4,
+//            nibble slot i = 0..3 of word half h (h = 0: bits 4i..4i+3,
+//            h = 1: bits 16+4i..16+4i+3) holds
+//                row  = 16 rt + r + 8 (i & 1)
+//                k    = 64 g + 16 j + 2 c + 8 (i >> 1) + h.
+//            So (w >> 4i) & 0x000F000F is the A-fragment register i of
+//            mma.m16n8k16 (rows r / r+8, k pairs 2c / 2c+8) as two nibbles in
+//            the low bits of each 16-bit half, and OR-ing 0x43004300 turns it
+//            into the bf16 pair (128 + q_lo, 128 + q_hi) exactly.
+//   scales:  64 bytes at byte offset (rt * ng + g) * 64: eight quads
+//            {s_r, b_r, s_r+8, b_r+8} (16-bit, bf16 or f16), quad r at + 8 r.
+//
+// Padding rows have zero nibbles, scales and biases.  Per weight the layout
+// stores exactly 0.5 + 4/64 = 0.5625 bytes, the same as the reference's
+// formats; only the order differs.
+namespace thq4 {
+
+constexpr int kGroup = 64;
+constexpr int kTileRows = 16;
+constexpr int kChunkBytes = 512;  // nibbles per (tile, group)
+constexpr int kQuadBytes = 64;    // scale/bias per (tile, group)
+
+__host__ __device__ inline int row_tiles(int rows) { return (rows + 15) / 16; }
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+
+// Streaming 16-byte load: read-only path, no L1 allocation, evict-first in L2
+// (each weight byte is used exactly once per call).
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p, uint64_t policy) {
+  uint4 v;
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;\n"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(policy));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const void *p, uint64_t policy) {
+  uint2 v;
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;\n"
+      : "=r"(v.x), "=r"(v.y)
+      : "l"(p), "l"(policy));
+  return v;
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
+// (w >> shift) & 0x000F000F | 0x43004300 as one LOP3 after the shift:
+// bf16x2 (128 + q_lo, 128 + q_hi).
+__device__ __forceinline__ uint32_t nib_bf16x2(uint32_t w, int shift) {
+  uint32_t v = w >> shift, r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(v), "r"(0x000F000Fu), "r"(0x43004300u));
+  return r;
+}
+
+// D = A * B + D, bf16 inputs, f32 accumulate, m16n8k16.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t lo16) {
+  return __uint_as_float(lo16 << 16);
+}
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t lo16) {
+  return __half2float(__ushort_as_half((unsigned short)lo16));
+}
+template <bool F16>
+__device__ __forceinline__ float sb_to_f32(uint32_t lo16) {
+  if constexpr (F16)
+    return f16_bits_to_f32(lo16);
+  else
+    return bf16_bits_to_f32(lo16);
+}
+__device__ __forceinline__ float round_bf16(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// silu(bf16 g) * bf16 u in f32, the reference's gate/up epilogue
+// (quant_kernel.rs:2039-2046): gate / (1 + exp(-gate)) * up.
+__device__ __forceinline__ float silu_mul(float gate, float up) {
+  const float g = round_bf16(gate), u = round_bf16(up);
+  return g / (1.0f + expf(-g)) * u;
+}
+
+// Kernels record conditions they skip instead of faulting (bad ids, bounds)
+// by OR-ing these bits into the device status word whose address the host
+// passes in; thq4_device_status reads and clears it.
+enum : uint32_t {
+  kStatusBadExpert = 1u << 0,
+  kStatusBounds = 1u << 1,
+};
+__device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bit) {
+  if (status) atomicOr(status, bit);
+}
+
+}  // namespace thq4

@@ -1,0 +1,73 @@
+// thq4_internal.h -- declarations shared by the thq4 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "../../include/thq4.h"
+
+namespace thq4 {
+
+// Dynamic shared memory the GEMV may use per CTA (B200: 227 KB opt-in).
+constexpr int kGemvMaxSmem = 200 * 1024;
+
+// Runs `fn` once per device (e.g. a cudaFuncSetAttribute), remembering
+// success; a failure is returned and retried on the next call.
+class DeviceOnce {
+ public:
+  template <class Fn>
+  cudaError_t run(Fn &&fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << dev;
+    if (done_.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+    e = fn();
+    if (e == cudaSuccess) done_.fetch_or(bit, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+  std::mutex mu_;
+};
+
+int device_sm_count();
+// Device address of the status word on the current device (nullptr on error).
+uint32_t *status_word();
+
+// ---- GEMV / verify ---------------------------------------------------------
+struct GemvCfg {
+  int ks = 0;     // forced K slices (0 = policy)
+  int warps = 0;  // forced warps per CTA (0 = policy)
+};
+// THQ4_GEMV="ks,warps" read once per process (the reference reads its
+// TH_QMVT / TH_Q4_POLICY switches once the same way, quant_kernel.rs:41-78,
+// 367-432).
+GemvCfg gemv_cfg_override();
+
+struct GemvPlan {
+  bool ok;
+  int ks, rt_per_cta, threads, gps, grid, tokens_per_pass;
+  size_t smem;
+};
+GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
+cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
+                        int m, void *y, bool y_f32, cudaStream_t stream);
+
+// ---- repack / dequant ------------------------------------------------------
+cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,
+                          int row_begin, int rows, void *dst_qw, void *dst_sb, cudaStream_t stream);
+cudaError_t dequant_launch(const thq4_weight &w, void *y, cudaStream_t stream);
+
+// ---- errors ----------------------------------------------------------------
+thq4_status set_error(thq4_status s, const std::string &msg);
+thq4_status cuda_error(cudaError_t e, const char *what);
+
+}  // namespace thq4

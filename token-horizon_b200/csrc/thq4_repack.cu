@@ -1,0 +1,185 @@
+// thq4_repack.cu -- load-time repack of the reference's Q4 formats into the
+// frag16 layout, and the dequantise-to-bf16 kernel.
+//
+// Replaces QLin::tiled's host-thread repack (engine/src/qwen35.rs:629-697)
+// with a device kernel, and reads every layout the reference stores:
+//   MLX row-major    wq [out][in/8] + sb [out][2 ng]   (qwen35.rs:249-300)
+//   QLin::tiled      [tile][group][col][8] + planar sb  (qwen35.rs:629-697,
+//                    addressing quant_kernel.rs:1085-1101)
+//   Splash slab      [weights][scales][biases]          (moe_expert_slab.h:15-28)
+// AffineDequant (quant_kernel.rs:1765-1781) becomes dequant_kernel below.
+#include "thq4_common.cuh"
+#include "thq4_internal.h"
+
+namespace thq4 {
+namespace {
+
+struct RepackArgs {
+  int layout;
+  const uint32_t *w;   // source words (MLX / tiled) or slab bytes
+  const uint16_t *sb;  // source scale/bias (MLX / tiled)
+  int src_out, in, ng, row_begin, rows, rtiles;
+  uint32_t *dq;        // frag16 nibbles
+  uint16_t *dsb;       // frag16 quads
+};
+
+// The 8 words of source row `row`, group g (zeros for rows past `rows`).
+__device__ inline void load_row_group(const RepackArgs &a, int local_row, int g, uint32_t (&wv)[8],
+                                      uint16_t &s, uint16_t &b) {
+  if (local_row >= a.rows) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wv[i] = 0;
+    s = b = 0;
+    return;
+  }
+  const int row = a.row_begin + local_row;
+  if (a.layout == THQ4_SRC_MLX) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(a.w + (size_t)row * a.ng * 8 + (size_t)g * 8);
+    const uint4 lo = p[0], hi = p[1];
+    wv[0] = lo.x, wv[1] = lo.y, wv[2] = lo.z, wv[3] = lo.w;
+    wv[4] = hi.x, wv[5] = hi.y, wv[6] = hi.z, wv[7] = hi.w;
+    s = a.sb[(size_t)row * 2 * a.ng + g];
+    b = a.sb[(size_t)row * 2 * a.ng + a.ng + g];
+    return;
+  }
+  // tiled and slab share the word order [tile][group][col][8]
+  const size_t t = (size_t)row / 256, col = (size_t)row % 256;
+  const uint4 *p = reinterpret_cast<const uint4 *>(a.w + t * a.ng * 2048 + (size_t)g * 2048 + col * 8);
+  const uint4 lo = p[0], hi = p[1];
+  wv[0] = lo.x, wv[1] = lo.y, wv[2] = lo.z, wv[3] = lo.w;
+  wv[4] = hi.x, wv[5] = hi.y, wv[6] = hi.z, wv[7] = hi.w;
+  const size_t prm = (t * a.ng + g) * 256 + col;
+  if (a.layout == THQ4_SRC_TILED) {
+    const size_t tiles = ((size_t)a.src_out + 255) / 256;
+    s = a.sb[prm];
+    b = a.sb[prm + tiles * a.ng * 256];
+  } else {  // slab: scales at elements/2 bytes, biases elements/32 bytes later
+    const size_t elements = (size_t)a.src_out * a.in;
+    const uint16_t *sc = reinterpret_cast<const uint16_t *>(reinterpret_cast<const char *>(a.w) + elements / 2);
+    const uint16_t *bi = reinterpret_cast<const uint16_t *>(reinterpret_cast<const char *>(a.w) + elements / 2 + elements / 32);
+    s = sc[prm];
+    b = bi[prm];
+  }
+}
+
+// One thread per (row tile, group, lane): four output words and, for c == 0,
+// the quad of rows r and r+8.
+__global__ void repack_kernel(const RepackArgs a) {
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t total = (size_t)a.rtiles * a.ng * 32;
+  if (tid >= total) return;
+  const int lane = (int)(tid % 32);
+  const size_t chunk = tid / 32;
+  const int g = (int)(chunk % a.ng), rt = (int)(chunk / a.ng);
+  const int r = lane >> 2, c = lane & 3;
+  uint32_t w0[8], w1[8];
+  uint16_t s0, b0, s1, b1;
+  load_row_group(a, rt * 16 + r, g, w0, s0, b0);
+  load_row_group(a, rt * 16 + r + 8, g, w1, s1, b1);
+  auto nib = [&](int which, int k) -> uint32_t {  // k within the group
+    const uint32_t word = which ? w1[k >> 3] : w0[k >> 3];
+    return (word >> (4 * (k & 7))) & 0xFu;
+  };
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = 16 * j + 2 * c + 8 * (i >> 1) + h;
+        word |= nib(i & 1, k) << (16 * h + 4 * i);
+      }
+    out[j] = word;
+  }
+  reinterpret_cast<uint4 *>(a.dq)[tid] = make_uint4(out[0], out[1], out[2], out[3]);
+  if (c == 0) {
+    uint2 q;
+    q.x = (uint32_t)s0 | ((uint32_t)b0 << 16);
+    q.y = (uint32_t)s1 | ((uint32_t)b1 << 16);
+    reinterpret_cast<uint2 *>(a.dsb)[chunk * 8 + r] = q;
+  }
+}
+
+// Copies an already packed frag16 weight (rows must cover whole tiles).
+__global__ void copy_kernel(const uint4 *src, uint4 *dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+// y[n][k] = bf16(q * s + b), one thread per 8 consecutive k of a row.
+template <bool SF16>
+__global__ void dequant_kernel(const uint32_t *qw, const uint16_t *sb, int out, int in, uint4 *y) {
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int kb8 = in / 8, ng = in / 64;
+  if (tid >= (size_t)out * kb8) return;
+  const int n = (int)(tid / kb8), k0 = (int)(tid % kb8) * 8;
+  const int rt = n / 16, rr = n % 16, r = rr % 8, irow = rr / 8;
+  const int g = k0 / 64, kk = k0 % 64, j = kk / 16, ik = (kk % 16) / 8;
+  const size_t chunk = (size_t)rt * ng + g;
+  const uint2 quad = reinterpret_cast<const uint2 *>(sb)[chunk * 8 + r];
+  const uint32_t qd = irow ? quad.y : quad.x;
+  const float s = sb_to_f32<SF16>(qd & 0xffffu), b = sb_to_f32<SF16>(qd >> 16);
+  const int i = irow + 2 * ik;
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    float v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = e / 2;  // (k % 16 within the half-step) / 2
+      const uint32_t word = qw[(chunk * 32 + 4 * r + c) * 4 + j];
+      const uint32_t q = (word >> (16 * h + 4 * i)) & 0xFu;
+      v[h] = fmaf((float)q, s, b);
+    }
+    o[e / 2] = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+  }
+  y[tid] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+}  // namespace
+
+cudaError_t repack_launch(int layout, const void *src_w, const void *src_sb, int src_out, int in,
+                          int row_begin, int rows, void *dst_qw, void *dst_sb, cudaStream_t stream) {
+  const int ng = in / kGroup, rtiles = row_tiles(rows);
+  if (layout == THQ4_SRC_FRAG16) {
+    // a frag16 source is copied as is (row_begin must be 0 and rows whole)
+    const size_t nq = (size_t)rtiles * ng * kChunkBytes / 16, ns = (size_t)rtiles * ng * kQuadBytes / 16;
+    copy_kernel<<<1024, 256, 0, stream>>>(static_cast<const uint4 *>(src_w), static_cast<uint4 *>(dst_qw), nq);
+    copy_kernel<<<256, 256, 0, stream>>>(static_cast<const uint4 *>(src_sb), static_cast<uint4 *>(dst_sb), ns);
+    return cudaGetLastError();
+  }
+  RepackArgs a{};
+  a.layout = layout;
+  a.w = static_cast<const uint32_t *>(src_w);
+  a.sb = static_cast<const uint16_t *>(src_sb);
+  a.src_out = src_out;
+  a.in = in;
+  a.ng = ng;
+  a.row_begin = row_begin;
+  a.rows = rows;
+  a.rtiles = rtiles;
+  a.dq = static_cast<uint32_t *>(dst_qw);
+  a.dsb = static_cast<uint16_t *>(dst_sb);
+  const size_t total = (size_t)rtiles * ng * 32;
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+  repack_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t dequant_launch(const thq4_weight &w, void *y, cudaStream_t stream) {
+  const size_t total = (size_t)w.out * (w.in / 8);
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+  if (w.sb_dtype == THQ4_F16)
+    dequant_kernel<true><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w.qw),
+                                                     static_cast<const uint16_t *>(w.sb), w.out, w.in,
+                                                     static_cast<uint4 *>(y));
+  else
+    dequant_kernel<false><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w.qw),
+                                                      static_cast<const uint16_t *>(w.sb), w.out, w.in,
+                                                      static_cast<uint4 *>(y));
+  return cudaGetLastError();
+}
+
+}  // namespace thq4

@@ -1,0 +1,108 @@
+"""ctypes binding of libthq4.so, the C ABI declared in include/thq4.h.
+
+The library is built in-tree by token-horizon_b200/build.py.  Loading fails
+loudly when it is missing: there is no CPU fallback for any operator.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_int, c_size_t, c_uint32, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libthq4.so")
+
+# thq4_status
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_WORKSPACE = 3
+ERR_CUDA = 4
+ERR_NCCL = 5
+
+# thq4_dtype
+BF16 = 0
+F16 = 1
+F32 = 2
+
+# thq4_src_layout
+SRC_MLX = 0
+SRC_TILED = 1
+SRC_SLAB = 2
+SRC_FRAG16 = 3
+
+
+class Thq4Error(RuntimeError):
+    """A thq4 call returned a non-OK status; `status` holds the code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class thq4_weight(ctypes.Structure):
+    _fields_ = [("out", ctypes.c_int32), ("in_", ctypes.c_int32), ("gs", ctypes.c_int32),
+                ("sb_dtype", ctypes.c_int32), ("qw", c_void_p), ("sb", c_void_p)]
+
+
+class thq4_experts(ctypes.Structure):
+    _fields_ = [("experts", ctypes.c_int32), ("out", ctypes.c_int32), ("in_", ctypes.c_int32),
+                ("gs", ctypes.c_int32), ("sb_dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("qw", c_void_p), ("sb", c_void_p), ("qw_stride", ctypes.c_uint64),
+                ("sb_stride", ctypes.c_uint64)]
+
+
+_lib = None
+
+# name -> (restype, argtypes); every symbol include/thq4.h declares
+SIGNATURES = {
+    "thq4_version": (c_char_p, []),
+    "thq4_last_error": (c_size_t, [c_void_p, c_size_t]),
+    "thq4_device_status": (c_int, [POINTER(c_uint32), c_void_p]),
+    "thq4_weight_bytes": (c_size_t, [c_int, c_int, c_int, POINTER(c_size_t), POINTER(c_size_t)]),
+    "thq4_repack": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                            c_void_p, c_size_t, c_void_p, c_size_t, c_void_p]),
+    "thq4_weight_init": (c_int, [POINTER(thq4_weight), c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "thq4_linear": (c_int, [POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
+                            c_size_t, c_void_p]),
+    "thq4_gate_up": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
+                             c_int, c_void_p, c_size_t, c_void_p]),
+    "thq4_linear_workspace_bytes": (c_size_t, [POINTER(thq4_weight), c_int]),
+    "thq4_dequant": (c_int, [POINTER(thq4_weight), c_void_p, c_void_p]),
+    "thq4_debug_set_gemv": (c_int, [c_int, c_int]),
+}
+
+
+def lib():
+    """The loaded library; raises if libthq4.so was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise Thq4Error(ERR_UNSUPPORTED,
+                            f"{LIB_PATH} is missing: build it with `python token-horizon_b200/build.py`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name, None)
+            if f is None:
+                continue
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    L = lib()
+    n = L.thq4_last_error(None, 0)
+    buf = ctypes.create_string_buffer(n + 1)
+    L.thq4_last_error(buf, n + 1)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise Thq4Error(status, last_error())
+
+
+def version() -> str:
+    return lib().thq4_version().decode()

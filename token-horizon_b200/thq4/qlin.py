@@ -1,0 +1,211 @@
+"""Host-side mirror of th-engine's quant-linear operator (QLin) over the C ABI.
+
+The reference's operator surface is ``QLin`` in engine/src/qwen35.rs:303-923:
+``QLin::new`` (:320), ``tiled`` (:629-697), ``linear`` / ``linear_ps``
+(:389-617), ``gate_up_act`` / ``gate_up_act_ps`` (:704-884), ``fuse_lins``
+(:1581-1610), ``maybe_tiled`` (:890-898) and ``lin_apply`` / ``lin_apply_ps``
+(:912-923).  This module keeps those names, argument meanings and error
+messages; the arithmetic runs in libthq4.so (include/thq4.h).  torch provides
+device memory and the current stream only.
+
+Shapes follow the reference: ``wq`` u32 [out, in/8] (MLX nibbles, LSB first)
+and ``sb`` [out, 2*ng] (a row's scales then its biases), bf16 or f16.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F16, F32, SRC_MLX, SRC_SLAB, SRC_TILED, Thq4Error, check, thq4_weight
+
+_SB_DTYPE = {torch.bfloat16: BF16, torch.float16: F16}
+_X_DTYPE = {torch.bfloat16: BF16, torch.float32: F32}
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+class PackedWeight:
+    """One frag16 weight (rows x in) resident on the device."""
+
+    def __init__(self, rows: int, inp: int, sb_dtype: int, device: torch.device):
+        qb, sbb = ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.lib().thq4_weight_bytes(rows, inp, 64, ctypes.byref(qb), ctypes.byref(sbb))
+        self.rows, self.inp, self.sb_dtype = rows, inp, sb_dtype
+        self.qw = torch.empty(qb.value, dtype=torch.uint8, device=device)
+        self.sb = torch.empty(sbb.value, dtype=torch.uint8, device=device)
+        self.desc = thq4_weight()
+        check(_lib.lib().thq4_weight_init(ctypes.byref(self.desc), rows, inp, 64, sb_dtype,
+                                          _ptr(self.qw), _ptr(self.sb)))
+
+    @property
+    def nbytes(self) -> int:
+        return self.qw.numel() + self.sb.numel()
+
+    @classmethod
+    def repack(cls, layout: int, w: torch.Tensor, sb: Optional[torch.Tensor], src_out: int, inp: int,
+               sb_dtype: int, row_begin: int = 0, rows: Optional[int] = None) -> "PackedWeight":
+        rows = src_out - row_begin if rows is None else rows
+        p = cls(rows, inp, sb_dtype, w.device)
+        check(_lib.lib().thq4_repack(layout, _ptr(w), _ptr(sb), src_out, inp, 64, sb_dtype, row_begin, rows,
+                                     _ptr(p.qw), p.qw.numel(), _ptr(p.sb), p.sb.numel(), _stream()))
+        return p
+
+
+class QLin:
+    """Packed Q4 projection; mirror of ``QLin`` (qwen35.rs:303-325).
+
+    ``tiled`` is True once the weight is packed in the kernels' layout (the
+    reference's Splash tile layout becomes this library's frag16 layout).
+    """
+
+    def __init__(self, wq: torch.Tensor, sb: torch.Tensor, out: int, inp: int, gs: int = 64):
+        # QLin::new (qwen35.rs:320-324)
+        self.wq, self.sb = wq, sb
+        self.out, self.inp, self.gs = out, inp, gs
+        self.tiled_flag = False
+        self.sb_dtype = _SB_DTYPE.get(sb.dtype)
+        if self.sb_dtype is None:
+            raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin: scale/bias dtype {sb.dtype} is not bf16 or f16")
+        self.packed: Optional[PackedWeight] = None
+        # fused [gate | up]: the two halves packed separately (see tiled)
+        self.up_row = 0
+        self.packed_gate: Optional[PackedWeight] = None
+        self.packed_up: Optional[PackedWeight] = None
+
+    new = classmethod(lambda cls, wq, sb, out, inp, gs: cls(wq, sb, out, inp, gs))
+
+    @classmethod
+    def from_layout(cls, layout: int, w: torch.Tensor, sb: Optional[torch.Tensor], out: int, inp: int,
+                    sb_dtype: int) -> "QLin":
+        """A QLin straight from a reference layout (SRC_TILED / SRC_SLAB)."""
+        q = cls.__new__(cls)
+        q.wq, q.sb, q.out, q.inp, q.gs = None, None, out, inp, 64
+        q.sb_dtype, q.up_row = sb_dtype, 0
+        q.packed = PackedWeight.repack(layout, w, sb, out, inp, sb_dtype)
+        q.packed_gate = q.packed_up = None
+        q.tiled_flag = True
+        return q
+
+    def tiled(self, up_row: int = 0) -> "QLin":
+        """Repack for the kernels (QLin::tiled, qwen35.rs:629-697).  With
+        ``up_row`` > 0 the weight is a fused [gate | up] and the halves
+        [0, up_row) and [up_row, out) are packed as separate weights so that
+        the up stream may start anywhere (the reference allows any up_row)."""
+        if self.tiled_flag and (up_row == 0 or self.packed_gate is not None):
+            return self
+        if self.gs != 64 or self.inp % 64 != 0:
+            raise Thq4Error(_lib.ERR_UNSUPPORTED, f"QLin::tiled: group size {self.gs}, inp {self.inp}")
+        wq = self.wq.contiguous()
+        sb = self.sb.contiguous()
+        self.packed = PackedWeight.repack(SRC_MLX, wq, sb, self.out, self.inp, self.sb_dtype)
+        if up_row > 0:
+            half = self.out - up_row
+            self.packed_gate = PackedWeight.repack(SRC_MLX, wq, sb, self.out, self.inp, self.sb_dtype, 0, up_row)
+            self.packed_up = PackedWeight.repack(SRC_MLX, wq, sb, self.out, self.inp, self.sb_dtype, up_row, half)
+            self.up_row = up_row
+        self.tiled_flag = True
+        return self
+
+    # -- QLin::linear_ps (qwen35.rs:398-617) -----------------------------------
+    def linear(self, x: torch.Tensor) -> torch.Tensor:
+        return self.linear_ps(x, False)
+
+    def linear_ps(self, x: torch.Tensor, presum: bool = False, out_dtype: Optional[torch.dtype] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [..., in] -> y [..., out].  ``presum`` is accepted for interface
+        parity: this library computes the per-group input sums inside the
+        kernel's prologue, so a producer's presum block is an ordinary x."""
+        del presum
+        dims = list(x.shape)
+        in_d = dims[-1]
+        rows = 1
+        for d in dims[:-1]:
+            rows *= d
+        if in_d != self.inp:
+            raise Thq4Error(_lib.ERR_INVALID_ARGUMENT,
+                            f"QLin::linear: x last dim {in_d} != weight inp {self.inp} (x {dims})")
+        if not self.tiled_flag:
+            self.tiled()
+        x_dtype = _X_DTYPE.get(x.dtype)
+        if x_dtype is None:
+            raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin::linear: x dtype {x.dtype} is not bf16 or f32")
+        xv = x.reshape(rows, in_d).contiguous()
+        ydt = out_dtype or (torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
+        y = out if out is not None else torch.empty((rows, self.out), dtype=ydt, device=x.device)
+        check(_lib.lib().thq4_linear(ctypes.byref(self.packed.desc), _ptr(xv), x_dtype, rows, _ptr(y),
+                                     F32 if y.dtype == torch.float32 else BF16, None, 0, _stream()))
+        return y.reshape(dims[:-1] + [self.out])
+
+    # -- QLin::gate_up_act_ps (qwen35.rs:711-884) -------------------------------
+    def gate_up_act(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+        r = self.gate_up_act_ps(x, False)
+        return None if r is None else r[0]
+
+    def gate_up_act_ps(self, x: torch.Tensor, presum: bool = False, up_row: Optional[int] = None,
+                       out: Optional[torch.Tensor] = None):
+        """Fused [gate | up] -> silu(bf16 g) * bf16 u, [..., half].  Returns
+        (tensor, emitted_presum) like the reference; the flag is always False
+        (no presum blocks are needed downstream)."""
+        del presum
+        if self.out % 2 != 0 and up_row is None:
+            return None
+        half = self.out // 2 if up_row is None else self.out - up_row
+        up_row = self.out - half
+        dims = list(x.shape)
+        rows = 1
+        for d in dims[:-1]:
+            rows *= d
+        if dims[-1] != self.inp:
+            raise Thq4Error(_lib.ERR_INVALID_ARGUMENT,
+                            f"QLin::gate_up_act: x last dim {dims[-1]} != weight inp {self.inp} (x {dims})")
+        if self.packed_gate is None or self.up_row != up_row:
+            if self.wq is None:
+                raise Thq4Error(_lib.ERR_UNSUPPORTED, "QLin::gate_up_act: weight was not built from MLX tensors")
+            self.tiled_flag = False
+            self.tiled(up_row)
+        x_dtype = _X_DTYPE.get(x.dtype)
+        if x_dtype is None:
+            raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin::gate_up_act: x dtype {x.dtype}")
+        xv = x.reshape(rows, dims[-1]).contiguous()
+        y = out if out is not None else torch.empty((rows, half), dtype=torch.bfloat16, device=x.device)
+        check(_lib.lib().thq4_gate_up(ctypes.byref(self.packed_gate.desc), ctypes.byref(self.packed_up.desc),
+                                      _ptr(xv), x_dtype, rows, _ptr(y),
+                                      F32 if y.dtype == torch.float32 else BF16, None, 0, _stream()))
+        return y.reshape(dims[:-1] + [half]), False
+
+    def dequant(self) -> torch.Tensor:
+        """bf16 [out, in] (AffineDequant, quant_kernel.rs:1765-1781)."""
+        if not self.tiled_flag:
+            self.tiled()
+        y = torch.empty((self.out, self.inp), dtype=torch.bfloat16, device=self.packed.qw.device)
+        check(_lib.lib().thq4_dequant(ctypes.byref(self.packed.desc), _ptr(y), _stream()))
+        return y
+
+
+def fuse_lins(lins: Sequence[QLin]) -> QLin:
+    """Concatenate packed projections along out (qwen35.rs:1581-1610)."""
+    wq = torch.cat([l.wq for l in lins], 0)
+    sb = torch.cat([l.sb for l in lins], 0)
+    return QLin(wq, sb, sum(l.out for l in lins), lins[0].inp, lins[0].gs)
+
+
+def maybe_tiled(l: QLin) -> QLin:
+    """The reference tiles by default (qwen35.rs:890-898)."""
+    return l.tiled()
+
+
+def lin_apply_ps(x: torch.Tensor, l: QLin, presum: bool = False) -> torch.Tensor:
+    return l.linear_ps(x, presum)
+
+
+def lin_apply(x: torch.Tensor, l: QLin) -> torch.Tensor:
+    return lin_apply_ps(x, l, False)
