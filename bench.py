@@ -201,6 +201,9 @@ def run_thq4(args):
 
     lib = thq4.lib()
     BF = thq4.BF16
+    # one zero-filled workspace for the chain (calls are stream-ordered)
+    ws_bytes = max(lib.thq4_linear_workspace_bytes(ctypes.byref(p.desc), 1) for lay in layers for p in lay)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(7)
     x_in = (torch.randn((1, HIDDEN), generator=gen, device=dev)).to(torch.bfloat16)
@@ -221,20 +224,20 @@ def run_thq4(args):
     def step():
         s = stream()
         for (qkv, o, gate, up, down) in layers:
-            thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, None, 0, s))
+            thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
             if world > 1:
                 dist.all_gather_into_tensor(full_q, t_qkv[:, :qn])
                 src_o = full_q
             else:
                 src_o = t_qkv  # the first 5120 outputs are q; o reads in = 5120 of them
-            thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(src_o), BF, 1, P(t_o), BF, None, 0, s))
+            thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(src_o), BF, 1, P(t_o), BF, P(ws), ws_bytes, s))
             if world > 1:
                 dist.all_gather_into_tensor(full_o, t_o)
             thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h),
-                                        BF, None, 0, s))
+                                        BF, P(ws), ws_bytes, s))
             if world > 1:
                 dist.all_gather_into_tensor(full_h, t_h)
-            thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(full_h), BF, 1, P(t_d), BF, None, 0, s))
+            thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(full_h), BF, 1, P(t_d), BF, P(ws), ws_bytes, s))
             if world > 1:
                 dist.all_gather_into_tensor(y_out, t_d)
 
@@ -316,7 +319,7 @@ def run_thq4(args):
         s = stream()
         for (_, _, gate, up, _) in layers:
             thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h), BF,
-                                        None, 0, s))
+                                        P(ws), ws_bytes, s))
 
     gu_only()
     if not args.no_graph:
@@ -405,10 +408,12 @@ def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
     x = torch.randn((M, K), device=dev).to(torch.bfloat16)
     y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     lib = thq4.lib()
+    need = lib.thq4_linear_workspace_bytes(ctypes.byref(w.desc), M)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
 
     def call():
         thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, M,
-                                   ctypes.c_void_p(y.data_ptr()), thq4.BF16, None, 0,
+                                   ctypes.c_void_p(y.data_ptr()), thq4.BF16, ctypes.c_void_p(ws.data_ptr()), need,
                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
 
     for _ in range(3):

@@ -62,13 +62,13 @@ typedef enum thq4_src_layout {
   /* Splash expert slab (moe_expert_slab.h:15-28): [weights][scales][biases]
    * in StorageN=256 order, out % 256 == 0; `sb` is ignored. */
   THQ4_SRC_SLAB = 2,
-  /* This library's frag16 layout (a device copy of an already packed weight). */
-  THQ4_SRC_FRAG16 = 3
+  /* This library's frag layout (a device copy of an already packed weight). */
+  THQ4_SRC_FRAG = 3
 } thq4_src_layout;
 
-/* One packed projection in the frag16 layout (documented in
- * token-horizon_b200/csrc/thq4_common.cuh): rows pad to 16, one 512-byte
- * nibble chunk and one 64-byte scale/bias chunk per (16-row tile, group).
+/* One packed projection in the frag layout (documented in
+ * token-horizon_b200/csrc/thq4_common.cuh): rows pad to 128, one 4096-byte
+ * nibble chunk and one 512-byte scale/bias chunk per (128-row slab, group).
  * Replaces QLin {wq, sb, out, inp, gs, tiled} (qwen35.rs:303-325). */
 typedef struct thq4_weight {
   int32_t out;      /* logical output rows */
@@ -79,7 +79,7 @@ typedef struct thq4_weight {
   const void *sb;   /* scale/bias quads, 16-byte aligned */
 } thq4_weight;
 
-/* A set of experts with identical shape, packed back to back in frag16
+/* A set of experts with identical shape, packed back to back in the frag layout
  * (replaces Splash ExpertQ4Projection, docs/splash/runtime/ops/Linear.hpp:
  * 37-43).  Expert e's nibbles start at qw + e*qw_stride bytes, its scales at
  * sb + e*sb_stride bytes. */
@@ -111,12 +111,12 @@ thq4_status thq4_device_status(uint32_t *status_out, void *stream);
 /* ---- weights (replaces Weights::get_lin + QLin::tiled, qwen35.rs:249-300,
  * 629-697, and the Splash package loader's slab view) -------------------- */
 
-/* Bytes of the frag16 buffers for `rows` x `in` (either pointer may be NULL).
+/* Bytes of the frag buffers for `rows` x `in` (either pointer may be NULL).
  * Returns the total. */
 size_t thq4_weight_bytes(int rows, int in, int gs, size_t *qw_bytes,
                          size_t *sb_bytes);
 /* Repacks rows [row_begin, row_begin + rows) of a `src_out` x `in` weight in
- * `src_layout` into frag16.  All pointers are device pointers.  Row ranges
+ * `src_layout` into the frag layout.  All pointers are device pointers.  Row ranges
  * let one call cut a column shard or the gate/up halves of a fused
  * [gate | up] weight (fuse_lins, qwen35.rs:1581-1610). */
 thq4_status thq4_repack(int src_layout, const void *src_w, const void *src_sb,
@@ -143,25 +143,32 @@ thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
                         size_t workspace_bytes, void *stream);
 /* Replaces QLin::gate_up_act_ps (qwen35.rs:711-884): y [m][gate.out] =
  * bf16(silu(bf16 g) * bf16 u) with g = gate x, u = up x.  gate and up are
- * the two halves of the fused weight (same out, in, sb_dtype). */
+ * the two halves of the fused weight (same out, in, sb_dtype).  Both calls
+ * return THQ4_ERR_WORKSPACE without a large enough workspace. */
 thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
                          const void *x, int x_dtype, int m, void *y,
                          int y_dtype, void *workspace, size_t workspace_bytes,
                          void *stream);
-/* Workspace bytes thq4_linear / thq4_gate_up need for this shape (0 today for
- * every routed kernel; callers should still ask). */
+/* Workspace bytes thq4_linear / thq4_gate_up need for this weight (for
+ * thq4_gate_up pass the gate half).  The decode/verify kernel splits tiles
+ * over warps and finishes each split tile in the warp that arrives last: the
+ * workspace holds the partial sums and one arrival counter per 16-row tile.
+ * It must be 256-byte aligned and zero-filled before its first use; every
+ * call returns it zeroed, so one allocation serves every later call.  Calls
+ * that may overlap on the GPU need separate workspaces. */
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
 /* Replaces AffineDequant (quant_kernel.rs:1743-1782, 5836-5899): y bf16
  * [out][in] = bf16(q * s + b). */
 thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);
 
 /* ---- testing hooks -------------------------------------------------------
- * Forces the decode/verify kernel's split (K slices per 16-row tile, warps per
- * CTA) for every later call in this process; ks = 0 restores the policy.  The
- * reference's tests run every instantiated tile config the same way
- * (qwen35.rs:6963-6989).  Returns THQ4_ERR_INVALID_ARGUMENT for ks not in
- * {0,1,2,4,8,16} or warps not in {0,4,8,16}. */
-thq4_status thq4_debug_set_gemv(int ks, int warps);
+ * Forces the decode/verify kernel's launch shape for every later call in this
+ * process: slab-groups per streamed stage (1, 2 or 4), stages in the
+ * shared-memory ring (2 .. 8) and CTAs in the grid (1 .. 2x SM count); 0
+ * leaves a field to the policy, all zeros restore it.  The reference's tests
+ * run every instantiated tile config the same way (qwen35.rs:6963-6989).
+ * Returns THQ4_ERR_INVALID_ARGUMENT for other values; `reserved` must be 0. */
+thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved);
 
 #ifdef __cplusplus
 }

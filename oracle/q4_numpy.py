@@ -52,34 +52,34 @@ def linear_group(wq, sb, sb_dtype: int, x: np.ndarray) -> np.ndarray:
     return (dots * sc[None]).sum(axis=2) + sums @ bi.T
 
 
-def frag16_from_mlx(wq, sb, out: int, inp: int):
-    """The frag16 layout (thq4_layout.cuh), built with index arithmetic."""
+def frag_from_mlx(wq, sb, out: int, inp: int, ts: int = 8):
+    """The frag layout (thq4_common.cuh), built with index arithmetic."""
     q = unpack_mlx(wq)
-    rt_n, ng = (out + 15) // 16, inp // 64
-    qp = np.zeros((rt_n * 16, inp), dtype=np.uint32)
+    nb, ng = (out + 16 * ts - 1) // (16 * ts), inp // 64
+    qp = np.zeros((nb * 16 * ts, inp), dtype=np.uint32)
     qp[:out] = q
     lane = np.arange(32)
     r, c = lane // 4, lane % 4
-    fq = np.zeros((rt_n, ng, 32, 4), dtype=np.uint32)
-    for j in range(4):
-        word = np.zeros((rt_n, ng, 32), dtype=np.uint32)
-        for i in range(4):
-            for h in range(2):
-                rows = r + 8 * (i & 1)  # [32]
-                ks = 16 * j + 2 * c + 8 * (i >> 1) + h  # [32]
-                tile_rows = (np.arange(rt_n)[:, None] * 16 + rows[None, :])  # [rt][32]
-                kk = np.arange(ng)[:, None] * 64 + ks[None, :]  # [g][32]
-                vals = qp[tile_rows[:, None, :], kk[None, :, :]]  # [rt][g][32]
-                word |= vals << np.uint32(16 * h + 4 * i)
-        fq[:, :, :, j] = word
-    sbp = np.zeros((rt_n * 16, 2 * ng), dtype=np.uint16)
+    fq = np.zeros((nb, ng, ts, 32, 4), dtype=np.uint32)
+    for t in range(ts):
+        for j in range(4):
+            word = np.zeros((nb, ng, 32), dtype=np.uint32)
+            for i in range(4):
+                for h in range(2):
+                    rows = (np.arange(nb)[:, None] * ts + t) * 16 + (r + 8 * (i & 1))[None, :]
+                    kk = np.arange(ng)[:, None] * 64 + (16 * j + 2 * c + 8 * (i >> 1) + h)[None, :]
+                    vals = qp[rows[:, None, :], kk[None, :, :]]
+                    word |= vals << np.uint32(16 * h + 4 * i)
+            fq[:, :, t, :, j] = word
+    sbp = np.zeros((nb * 16 * ts, 2 * ng), dtype=np.uint16)
     sbp[:out] = sb
-    fsb = np.zeros((rt_n, ng, 8, 4), dtype=np.uint16)
-    for rr in range(8):
-        for half in range(2):
-            rows = np.arange(rt_n) * 16 + rr + 8 * half
-            fsb[:, :, rr, 2 * half] = sbp[rows, :ng]
-            fsb[:, :, rr, 2 * half + 1] = sbp[rows, ng:]
+    fsb = np.zeros((nb, ng, ts, 8, 4), dtype=np.uint16)
+    for t in range(ts):
+        for rr in range(8):
+            for half in range(2):
+                rows = (np.arange(nb) * ts + t) * 16 + rr + 8 * half
+                fsb[:, :, t, rr, 2 * half] = sbp[rows, :ng]
+                fsb[:, :, t, rr, 2 * half + 1] = sbp[rows, ng:]
     return fq.reshape(-1), fsb.reshape(-1)
 
 

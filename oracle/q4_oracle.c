@@ -284,85 +284,92 @@ void q4o_slab_to_mlx(const uint8_t *slab, int out, int in, uint32_t *wq,
     }
 }
 
-/* frag16: 16-row tiles, one 512-byte chunk per (tile, group).  Lane l of a
- * warp owns bytes [16l, 16l+16) = words j = 0..3 (k-step j of the group);
- * with r = l/4, c = l%4, nibble slot i (0..3) of half h (0: bits 4i..4i+3,
- * 1: bits 16+4i..) holds row r + 8*(i&1), k = 16j + 2c + 8*(i>>1) + h.
- * Scales: per (tile, group) 8 quads {s_r, b_r, s_r+8, b_r+8}. */
-size_t q4o_frag16_qw_bytes(int out, int in) {
-  return (size_t)((out + 15) / 16) * (size_t)(in / 64) * 512;
+/* The B200 "frag" layout (token-horizon_b200/csrc/thq4_common.cuh): rows pad
+ * to slabs of 16*ts rows = ts tiles of 16 (the library uses ts = 8).  Chunk
+ * ((slab*ng + g)*ts + t) holds the 512 nibble bytes of tile t of the slab for
+ * group g; lane l owns bytes [16l, 16l+16) = words j = 0..3; with r = l/4,
+ * c = l%4, nibble slot i (0..3) of half h (0: bits 4i..4i+3, 1: bits
+ * 16+4i..) holds row 16(ts*slab + t) + r + 8(i&1), k = 64g + 16j + 2c +
+ * 8(i>>1) + h.  Scales: 64 bytes per chunk, eight quads
+ * {s_r, b_r, s_r+8, b_r+8}. */
+size_t q4o_frag_qw_bytes(int out, int in, int ts) {
+  return (size_t)((out + 16 * ts - 1) / (16 * ts)) * ts * (size_t)(in / 64) * 512;
 }
-size_t q4o_frag16_sb_bytes(int out, int in) {
-  return (size_t)((out + 15) / 16) * (size_t)(in / 64) * 64;
+size_t q4o_frag_sb_bytes(int out, int in, int ts) {
+  return (size_t)((out + 16 * ts - 1) / (16 * ts)) * ts * (size_t)(in / 64) * 64;
 }
 
 static inline uint32_t mlx_nibble(const uint32_t *wq, int in, int row, int k) {
   return (wq[(size_t)row * (in / 8) + k / 8] >> (4 * (k % 8))) & 0xFu;
 }
 
-void q4o_mlx_to_frag16(const uint32_t *wq, const uint16_t *sb, int out, int in,
-                       uint32_t *fq, uint16_t *fsb) {
-  int ng = in / 64, rtiles = (out + 15) / 16;
-  for (int rt = 0; rt < rtiles; ++rt)
-    for (int g = 0; g < ng; ++g) {
-      size_t chunk = (size_t)rt * ng + g;
-      for (int lane = 0; lane < 32; ++lane) {
-        int r = lane >> 2, c = lane & 3;
-        for (int j = 0; j < 4; ++j) {
-          uint32_t word = 0;
-          for (int i = 0; i < 4; ++i)
-            for (int h = 0; h < 2; ++h) {
-              int row = rt * 16 + r + 8 * (i & 1);
-              int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
-              uint32_t q = row < out ? mlx_nibble(wq, in, row, k) : 0;
-              word |= q << (16 * h + 4 * i);
-            }
-          fq[(chunk * 32 + lane) * 4 + j] = word;
-        }
-      }
-      for (int r = 0; r < 8; ++r)
-        for (int half = 0; half < 2; ++half) {
-          int row = rt * 16 + r + 8 * half;
-          uint16_t s = 0, b = 0;
-          if (row < out) {
-            s = sb[(size_t)row * 2 * ng + g];
-            b = sb[(size_t)row * 2 * ng + ng + g];
+void q4o_mlx_to_frag(const uint32_t *wq, const uint16_t *sb, int out, int in, int ts,
+                     uint32_t *fq, uint16_t *fsb) {
+  int ng = in / 64, slabs = (out + 16 * ts - 1) / (16 * ts);
+  for (int sl = 0; sl < slabs; ++sl)
+    for (int g = 0; g < ng; ++g)
+      for (int t = 0; t < ts; ++t) {
+        size_t chunk = ((size_t)sl * ng + g) * ts + t;
+        int row0 = (sl * ts + t) * 16;
+        for (int lane = 0; lane < 32; ++lane) {
+          int r = lane >> 2, c = lane & 3;
+          for (int j = 0; j < 4; ++j) {
+            uint32_t word = 0;
+            for (int i = 0; i < 4; ++i)
+              for (int h = 0; h < 2; ++h) {
+                int row = row0 + r + 8 * (i & 1);
+                int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
+                uint32_t q = row < out ? mlx_nibble(wq, in, row, k) : 0;
+                word |= q << (16 * h + 4 * i);
+              }
+            fq[(chunk * 32 + lane) * 4 + j] = word;
           }
-          fsb[(chunk * 8 + r) * 4 + 2 * half] = s;
-          fsb[(chunk * 8 + r) * 4 + 2 * half + 1] = b;
         }
-    }
+        for (int r = 0; r < 8; ++r)
+          for (int half = 0; half < 2; ++half) {
+            int row = row0 + r + 8 * half;
+            uint16_t s = 0, bb = 0;
+            if (row < out) {
+              s = sb[(size_t)row * 2 * ng + g];
+              bb = sb[(size_t)row * 2 * ng + ng + g];
+            }
+            fsb[(chunk * 8 + r) * 4 + 2 * half] = s;
+            fsb[(chunk * 8 + r) * 4 + 2 * half + 1] = bb;
+          }
+      }
 }
 
-void q4o_frag16_to_mlx(const uint32_t *fq, const uint16_t *fsb, int out, int in,
-                       uint32_t *wq, uint16_t *sb) {
-  int ng = in / 64, rtiles = (out + 15) / 16;
+void q4o_frag_to_mlx(const uint32_t *fq, const uint16_t *fsb, int out, int in, int ts,
+                     uint32_t *wq, uint16_t *sb) {
+  int ng = in / 64, slabs = (out + 16 * ts - 1) / (16 * ts);
   memset(wq, 0, sizeof(uint32_t) * (size_t)out * (in / 8));
-  for (int rt = 0; rt < rtiles; ++rt)
-    for (int g = 0; g < ng; ++g) {
-      size_t chunk = (size_t)rt * ng + g;
-      for (int lane = 0; lane < 32; ++lane) {
-        int r = lane >> 2, c = lane & 3;
-        for (int j = 0; j < 4; ++j) {
-          uint32_t word = fq[(chunk * 32 + lane) * 4 + j];
-          for (int i = 0; i < 4; ++i)
-            for (int h = 0; h < 2; ++h) {
-              int row = rt * 16 + r + 8 * (i & 1);
-              int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
-              if (row >= out) continue;
-              uint32_t q = (word >> (16 * h + 4 * i)) & 0xFu;
-              wq[(size_t)row * (in / 8) + k / 8] |= q << (4 * (k % 8));
-            }
+  for (int sl = 0; sl < slabs; ++sl)
+    for (int g = 0; g < ng; ++g)
+      for (int t = 0; t < ts; ++t) {
+        size_t chunk = ((size_t)sl * ng + g) * ts + t;
+        int row0 = (sl * ts + t) * 16;
+        for (int lane = 0; lane < 32; ++lane) {
+          int r = lane >> 2, c = lane & 3;
+          for (int j = 0; j < 4; ++j) {
+            uint32_t word = fq[(chunk * 32 + lane) * 4 + j];
+            for (int i = 0; i < 4; ++i)
+              for (int h = 0; h < 2; ++h) {
+                int row = row0 + r + 8 * (i & 1);
+                int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
+                if (row >= out) continue;
+                uint32_t q = (word >> (16 * h + 4 * i)) & 0xFu;
+                wq[(size_t)row * (in / 8) + k / 8] |= q << (4 * (k % 8));
+              }
+          }
         }
+        for (int r = 0; r < 8; ++r)
+          for (int half = 0; half < 2; ++half) {
+            int row = row0 + r + 8 * half;
+            if (row >= out) continue;
+            sb[(size_t)row * 2 * ng + g] = fsb[(chunk * 8 + r) * 4 + 2 * half];
+            sb[(size_t)row * 2 * ng + ng + g] = fsb[(chunk * 8 + r) * 4 + 2 * half + 1];
+          }
       }
-      for (int r = 0; r < 8; ++r)
-        for (int half = 0; half < 2; ++half) {
-          int row = rt * 16 + r + 8 * half;
-          if (row >= out) continue;
-          sb[(size_t)row * 2 * ng + g] = fsb[(chunk * 8 + r) * 4 + 2 * half];
-          sb[(size_t)row * 2 * ng + ng + g] = fsb[(chunk * 8 + r) * 4 + 2 * half + 1];
-        }
-    }
 }
 
 /* ------------------------------------------------------------------------ */

@@ -86,15 +86,16 @@ void q4o_mlx_to_slab(const uint32_t *wq, const uint16_t *sb, int out, int in,
                      uint8_t *slab);
 void q4o_slab_to_mlx(const uint8_t *slab, int out, int in, uint32_t *wq,
                      uint16_t *sb);
-/* This repository's B200 layout ("frag16"), described in full in
- * token-horizon_b200/csrc/thq4_common.cuh.  Rows pad to 16; fq holds
- * ceil(out/16)*ng*128 words and fsb ceil(out/16)*ng*32 entries. */
-size_t q4o_frag16_qw_bytes(int out, int in);
-size_t q4o_frag16_sb_bytes(int out, int in);
-void q4o_mlx_to_frag16(const uint32_t *wq, const uint16_t *sb, int out, int in,
-                       uint32_t *fq, uint16_t *fsb);
-void q4o_frag16_to_mlx(const uint32_t *fq, const uint16_t *fsb, int out, int in,
-                       uint32_t *wq, uint16_t *sb);
+/* This repository's B200 layout ("frag"), described in full in
+ * token-horizon_b200/csrc/thq4_common.cuh: rows pad to slabs of 16*ts rows
+ * (ts tiles of 16; the library uses ts = 8); fq holds slabs*ts*ng*128 words
+ * and fsb slabs*ts*ng*32 entries. */
+size_t q4o_frag_qw_bytes(int out, int in, int ts);
+size_t q4o_frag_sb_bytes(int out, int in, int ts);
+void q4o_mlx_to_frag(const uint32_t *wq, const uint16_t *sb, int out, int in, int ts,
+                     uint32_t *fq, uint16_t *fsb);
+void q4o_frag_to_mlx(const uint32_t *fq, const uint16_t *fsb, int out, int in, int ts,
+                     uint32_t *wq, uint16_t *sb);
 
 /* ---- products ----------------------------------------------------------- */
 /* Kernel semantics of every reference GPU family (qmvt quant_kernel.rs:

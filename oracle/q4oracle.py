@@ -94,10 +94,10 @@ def _declare(L) -> None:
         "q4o_slab_bytes": (c_size_t, [c_int, c_int]),
         "q4o_mlx_to_slab": (None, [v, v, c_int, c_int, v]),
         "q4o_slab_to_mlx": (None, [v, c_int, c_int, v, v]),
-        "q4o_frag16_qw_bytes": (c_size_t, [c_int, c_int]),
-        "q4o_frag16_sb_bytes": (c_size_t, [c_int, c_int]),
-        "q4o_mlx_to_frag16": (None, [v, v, c_int, c_int, v, v]),
-        "q4o_frag16_to_mlx": (None, [v, v, c_int, c_int, v, v]),
+        "q4o_frag_qw_bytes": (c_size_t, [c_int, c_int, c_int]),
+        "q4o_frag_sb_bytes": (c_size_t, [c_int, c_int, c_int]),
+        "q4o_mlx_to_frag": (None, [v, v, c_int, c_int, c_int, v, v]),
+        "q4o_frag_to_mlx": (None, [v, v, c_int, c_int, c_int, v, v]),
         "q4o_linear_group": (None, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
         "q4o_linear_dequant": (None, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
         "q4o_dequant_bf16": (None, [v, v, c_int, c_int, c_int, v]),
@@ -236,18 +236,23 @@ def slab_to_mlx(slab, out: int, inp: int):
     return wq, sb
 
 
-def mlx_to_frag16(wq, sb):
+# tiles per slab of the library's layout (thq4_common.cuh)
+SLAB_TILES = 8
+
+
+def mlx_to_frag(wq, sb, ts: int = SLAB_TILES):
+    """The B200 frag layout (nibbles as u32 words, quads as u16)."""
     out, inp = wq.shape[0], wq.shape[1] * 8
-    fq = np.empty(lib().q4o_frag16_qw_bytes(out, inp) // 4, dtype=np.uint32)
-    fsb = np.empty(lib().q4o_frag16_sb_bytes(out, inp) // 2, dtype=np.uint16)
-    lib().q4o_mlx_to_frag16(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), out, inp, _p(fq), _p(fsb))
+    fq = np.empty(lib().q4o_frag_qw_bytes(out, inp, ts) // 4, dtype=np.uint32)
+    fsb = np.empty(lib().q4o_frag_sb_bytes(out, inp, ts) // 2, dtype=np.uint16)
+    lib().q4o_mlx_to_frag(_p(np.ascontiguousarray(wq)), _p(np.ascontiguousarray(sb)), out, inp, ts, _p(fq), _p(fsb))
     return fq, fsb
 
 
-def frag16_to_mlx(fq, fsb, out: int, inp: int):
+def frag_to_mlx(fq, fsb, out: int, inp: int, ts: int = SLAB_TILES):
     wq = np.empty((out, inp // 8), dtype=np.uint32)
     sb = np.empty((out, 2 * (inp // 64)), dtype=np.uint16)
-    lib().q4o_frag16_to_mlx(_p(fq), _p(fsb), out, inp, _p(wq), _p(sb))
+    lib().q4o_frag_to_mlx(_p(fq), _p(fsb), out, inp, ts, _p(wq), _p(sb))
     return wq, sb
 
 

@@ -62,3 +62,21 @@ def assert_rms_close(tag: str, got: np.ndarray, want: np.ndarray, rel: float = 1
     err = float(np.abs(got - want).max())
     assert err <= rel * rms, f"{tag}: max|err| {err:.3e} > {rel} * RMS {rms:.3e}"
     return err / rms
+
+
+def assert_gate_up_close(tag: str, got: np.ndarray, gate: np.ndarray, up: np.ndarray, inp: int) -> None:
+    """The reference's split-K tolerance for the gate/up epilogue
+    (LinearNumerics.hpp:112-126, pinned by tests/test_oracle.py): the output
+    bf16(silu(bf16 g) * bf16 u) may move by one ulp of the output plus what one
+    ulp (plus fp32 reassociation slack) of g and of u propagates to."""
+    from helpers_tol import split_tolerance
+    got = np.asarray(got, dtype=np.float64).ravel()
+    gate = np.asarray(gate, dtype=np.float64).ravel()
+    up = np.asarray(up, dtype=np.float64).ravel()
+    import q4oracle as O
+    want = O.bf16_to_f32(O.silu_mul_bf16(gate.astype(np.float32), up.astype(np.float32))).astype(np.float64)
+    slack = (inp // 64) * 2.0 ** -24 * max(np.abs(gate).max(), np.abs(up).max())
+    for i in range(got.size):
+        tol = split_tolerance(2, want[i], 0.0, gate[i], up[i], slack)
+        assert abs(got[i] - want[i]) <= tol, (f"{tag}: element {i}: got {got[i]} want {want[i]} "
+                                              f"(g {gate[i]}, u {up[i]}, tol {tol})")

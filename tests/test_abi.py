@@ -39,7 +39,7 @@ def test_weight_bytes_match_q4_package_size():
     assert tot == 6144 * 2048 * 9 // 16 == 7077888  # 0.5625 B/weight, same as q4PackedBytes
     assert q.value == 6144 * 2048 // 2
     # ragged rows pad to the 16-row tile
-    assert thq4.lib().thq4_weight_bytes(520, 448, 64, None, None) == 528 * 448 * 9 // 16
+    assert thq4.lib().thq4_weight_bytes(520, 448, 64, None, None) == 640 * 448 * 9 // 16  # 128-row slabs
     assert thq4.lib().thq4_weight_bytes(64, 100, 64, None, None) == 0
 
 
@@ -96,9 +96,19 @@ def test_repack_validation():
     assert st == _lib.ERR_INVALID_ARGUMENT and "too small" in thq4.last_error()
 
 
+def test_linear_requires_workspace():
+    w = _w()
+    st = thq4.lib().thq4_linear(ctypes.byref(w), ctypes.c_void_p(0x3000), thq4.BF16, 1, ctypes.c_void_p(0x4000),
+                                thq4.BF16, None, 0, None)
+    assert st == _lib.ERR_WORKSPACE and "zero-filled workspace" in thq4.last_error()
+    assert thq4.lib().thq4_linear_workspace_bytes(ctypes.byref(w), 1) > 0
+
+
 def test_debug_hook_validation():
-    assert thq4.lib().thq4_debug_set_gemv(3, 0) == _lib.ERR_INVALID_ARGUMENT
-    assert thq4.lib().thq4_debug_set_gemv(0, 0) == _lib.OK
+    assert thq4.lib().thq4_debug_set_gemv(3, 0, 0, 0) == _lib.ERR_INVALID_ARGUMENT
+    assert thq4.lib().thq4_debug_set_gemv(0, 9, 0, 0) == _lib.ERR_INVALID_ARGUMENT
+    assert thq4.lib().thq4_debug_set_gemv(0, 0, 0, 1) == _lib.ERR_INVALID_ARGUMENT
+    assert thq4.lib().thq4_debug_set_gemv(0, 0, 0, 0) == _lib.OK
 
 
 def test_error_messages_are_per_thread():

@@ -11,17 +11,18 @@ import torch
 
 import q4oracle as O
 import thq4
-from helpers import assert_close_ref, assert_rms_close, dev, dev_sb, host_bits, to_f32
+from helpers import assert_close_ref, assert_gate_up_close, assert_rms_close, dev, dev_sb, host_bits, to_f32
 
 pytestmark = pytest.mark.gpu
 
-SPLITS = [(1, 8), (2, 8), (4, 8), (8, 8), (16, 16), (1, 4), (4, 16)]
+# (slab-groups per stage, ring stages, CTAs; 0 = policy)
+SPLITS = [(0, 0, 0), (1, 2, 0), (2, 6, 0), (4, 3, 7), (1, 8, 0), (2, 2, 3), (4, 4, 1), (1, 3, 296)]
 
 
 @pytest.fixture(autouse=True)
 def _reset_split():
     yield
-    thq4.lib().thq4_debug_set_gemv(0, 0)
+    thq4.lib().thq4_debug_set_gemv(0, 0, 0, 0)
 
 
 def _qlin(wq, sb, sb_dtype=O.SB_BF16):
@@ -34,11 +35,11 @@ def _x_bf16(bits):
 
 
 @pytest.mark.parametrize("case", range(4))
-def test_repack_matches_oracle_frag16(case):
+def test_repack_matches_oracle_frag(case):
     out, ng = O.QMVT_PLAIN_CASES[case]
     inp = ng * 64
     wq, sb = O.rand_qlin(out, inp, 11 + case)
-    fq, fsb = O.mlx_to_frag16(wq, sb)
+    fq, fsb = O.mlx_to_frag(wq, sb)
     q = _qlin(wq, sb)
     assert np.array_equal(host_bits(q.packed.qw).view(np.uint32), fq)
     assert np.array_equal(host_bits(q.packed.sb).view(np.uint16), fsb)
@@ -57,7 +58,7 @@ def test_repack_matches_oracle_frag16(case):
 def test_repack_row_range():
     wq, sb = O.rand_qlin(520, 448, 3)
     q = thq4.PackedWeight.repack(thq4.SRC_MLX, dev(wq), dev(sb), 520, 448, thq4.BF16, 136, 264)
-    fq, fsb = O.mlx_to_frag16(wq[136:400], sb[136:400])
+    fq, fsb = O.mlx_to_frag(wq[136:400], sb[136:400])
     assert np.array_equal(host_bits(q.qw).view(np.uint32), fq)
     assert np.array_equal(host_bits(q.sb).view(np.uint16), fsb)
 
@@ -80,12 +81,12 @@ def test_qmvt_plain_matches_oracle(case):
     want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = _qlin(wq, sb)
     x = _x_bf16(xb)
-    for ks, warps in SPLITS:
-        thq4.check(thq4.lib().thq4_debug_set_gemv(ks, warps))
+    for warps, ch, stages in SPLITS:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
         y = q.linear(x.reshape(1, 1, inp))
         assert tuple(y.shape) == (1, 1, out)
         got = to_f32(y).ravel()
-        assert_close_ref(f"plain {out}x{inp} ks{ks} w{warps}", got, want)
+        assert_close_ref(f"plain {out}x{inp} w{warps} ch{ch} r{stages}", got, want)
         again = to_f32(q.linear(x.reshape(1, 1, inp))).ravel()
         assert np.array_equal(got, again), "not deterministic"
 
@@ -96,15 +97,15 @@ def test_qmvt_gate_up_matches_oracle(case):
     inp, out = ng * 64, 2 * half
     wq, sb = O.rand_qlin(out, inp, 211 + case)
     xb = O.rand_x(inp, 307 + case)
-    want = O.bf16_to_f32(O.gate_up(wq, sb, O.SB_BF16, half, half, O.bf16_to_f32(xb)))[0]
+    gu = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = thq4.QLin(dev(wq), dev(sb), out, inp, 64)
     x = _x_bf16(xb)
-    for ks, warps in SPLITS:
-        thq4.check(thq4.lib().thq4_debug_set_gemv(ks, warps))
+    for warps, ch, stages in SPLITS:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
         y = q.gate_up_act(x.reshape(1, 1, inp))
         assert tuple(y.shape) == (1, 1, half)
         got = to_f32(y).ravel()
-        assert_close_ref(f"gate_up {half}x{inp} ks{ks}", got, want)
+        assert_gate_up_close(f"gate_up {half}x{inp} w{warps} ch{ch}", got, gu[:half], gu[half:], inp)
         again = to_f32(q.gate_up_act(x.reshape(1, 1, inp))).ravel()
         assert np.array_equal(got, again)
 
@@ -123,11 +124,11 @@ def test_verify_small_m_matches_oracle(m):
     # gate/up at the same m
     half = 264
     wq2, sb2 = O.rand_qlin(2 * half, inp, 77 + m)
-    want2 = O.bf16_to_f32(O.gate_up(wq2, sb2, O.SB_BF16, half, half, O.bf16_to_f32(xs)))
+    gu2 = O.linear_group(wq2, sb2, O.SB_BF16, O.bf16_to_f32(xs))
     q2 = thq4.QLin(dev(wq2), dev(sb2), 2 * half, inp, 64)
     got2 = to_f32(q2.gate_up_act(dev(xs)))
     for t in range(m):
-        assert_close_ref(f"gate_up m={m} t={t}", got2[t], want2[t])
+        assert_gate_up_close(f"gate_up m={m} t={t}", got2[t], gu2[t, :half], gu2[t, half:], inp)
 
 
 def test_x_f32_y_f32():
@@ -169,9 +170,14 @@ def test_routing_m1_equals_direct_call():
     q = _qlin(wq, sb)
     x = _x_bf16(O.rand_x(inp, 97))
     direct = torch.empty((1, out), dtype=torch.bfloat16, device="cuda")
+    need = thq4.lib().thq4_linear_workspace_bytes(ctypes.byref(q.packed.desc), 1)
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
     thq4.check(thq4.lib().thq4_linear(ctypes.byref(q.packed.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, 1,
-                                      ctypes.c_void_p(direct.data_ptr()), thq4.BF16, None, 0,
-                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+                                      ctypes.c_void_p(direct.data_ptr()), thq4.BF16, ctypes.c_void_p(ws.data_ptr()),
+                                      need, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    cnt = ws[need - ((q.packed.desc.out + 127) // 128 * 8 * 4 + 255) // 256 * 256:]
+    assert int(cnt.count_nonzero()) == 0, "arrival counters must return to zero"
     routed = q.linear(x.reshape(1, 1, inp))
     assert torch.equal(routed.reshape(-1), direct.reshape(-1))
 
@@ -179,21 +185,68 @@ def test_routing_m1_equals_direct_call():
 @pytest.mark.parametrize("m", [1, 2, 4, 8])
 def test_verify_config_shapes(m):
     """The spec-verify configuration: gate/up 2x9728x2560 and down
-    2560x9728 at M in {1,2,4,8}, f16 scales, x ~ N(0,1) bf16."""
+    2560x9728 at M in {1,2,4,8}, f16 scales, x ~ N(0,1) bf16.
+
+    The north-star bar (max|err| <= 1e-2 RMS against the reference CPU path,
+    fp32 accumulate) is applied to f32 outputs: a bf16 output's own rounding
+    is up to 2^-9 of the value, which alone exceeds 1e-2 RMS on the largest
+    elements.  bf16 outputs are held to the reference's per-element rules."""
     rng = np.random.default_rng(100 + m)
     gu_wq, gu_sb = O.synthetic_weight(2 * 9728, 2560, 31, O.SB_F16)
     dn_wq, dn_sb = O.synthetic_weight(2560, 9728, 32, O.SB_F16)
     x = O.f32_to_bf16(rng.standard_normal((m, 2560)).astype(np.float32))
+    xf = O.bf16_to_f32(x)
     gu = thq4.QLin(dev(gu_wq), dev_sb(gu_sb, O.SB_F16), 2 * 9728, 2560, 64)
+    # the two projections alone, f32 out, against the reference CPU path
+    gu_f32 = to_f32(gu.linear_ps(dev(x), out_dtype=torch.float32))
+    assert_rms_close("gate|up f32 vs reference CPU path", gu_f32, O.linear_dequant(gu_wq, gu_sb, O.SB_F16, xf))
+    # the fused epilogue, bf16 out
     h = gu.gate_up_act(dev(x))
-    want_h = O.bf16_to_f32(O.gate_up(gu_wq, gu_sb, O.SB_F16, 9728, 9728, O.bf16_to_f32(x)))
+    g_exact = O.linear_group(gu_wq, gu_sb, O.SB_F16, xf)
     got_h = to_f32(h)
-    assert_rms_close("gate_up", got_h, want_h, 1e-2)
     for t in range(m):
-        assert_close_ref(f"gate_up t{t}", got_h[t], want_h[t])
+        assert_gate_up_close(f"gate_up t{t}", got_h[t], g_exact[t, :9728], g_exact[t, 9728:], 2560)
     dn = _qlin(dn_wq, dn_sb, O.SB_F16)
     y = to_f32(dn.linear(h))
     want_y = O.linear_group(dn_wq, dn_sb, O.SB_F16, got_h)
     for t in range(m):
         assert_close_ref(f"down t{t}", y[t], want_y[t])
-    assert_rms_close("down vs reference CPU path", y, O.linear_dequant(dn_wq, dn_sb, O.SB_F16, got_h))
+    y32 = to_f32(dn.linear_ps(h, out_dtype=torch.float32))
+    assert_rms_close("down f32 vs reference CPU path", y32, O.linear_dequant(dn_wq, dn_sb, O.SB_F16, got_h))
+
+
+@pytest.mark.parametrize("out,inp", [(16, 64), (16, 448), (48, 128), (33 * 16 + 8, 7 * 64), (4096, 64)])
+def test_tiny_and_ragged_weights(out, inp):
+    """Weights with fewer tile-groups than warps (empty runs), one group, one
+    tile, and a ragged last tile -- every split the last-arriver scheme meets."""
+    wq, sb = O.rand_qlin(out, inp, out + inp)
+    xb = O.rand_x(inp, 3)
+    want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
+    q = _qlin(wq, sb)
+    for warps, ch, stages in [(0, 0, 0), (1, 2, 0), (4, 5, 5), (2, 2, 1)]:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
+        got = to_f32(q.linear(_x_bf16(xb).reshape(1, inp))).ravel()
+        assert_close_ref(f"{out}x{inp} w{warps} ch{ch}", got, want)
+
+
+def test_workspace_required_and_reused():
+    out, inp = 1000, 1088
+    wq, sb = O.rand_qlin(out, inp, 8)
+    q = _qlin(wq, sb)
+    x = _x_bf16(O.rand_x(inp, 9))
+    y = torch.empty((1, out), dtype=torch.bfloat16, device="cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    st = thq4.lib().thq4_linear(ctypes.byref(q.packed.desc), P(x), thq4.BF16, 1, P(y), thq4.BF16, None, 0, None)
+    assert st == thq4._lib.ERR_WORKSPACE and "workspace" in thq4.last_error()
+    need = thq4.lib().thq4_linear_workspace_bytes(ctypes.byref(q.packed.desc), 1)
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(3):  # the same workspace serves back-to-back calls
+        thq4.check(thq4.lib().thq4_linear(ctypes.byref(q.packed.desc), P(x), thq4.BF16, 1, P(y), thq4.BF16, P(ws),
+                                          need, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        outs.append(y.clone())
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    st = ctypes.c_uint32(0)
+    thq4.check(thq4.lib().thq4_device_status(ctypes.byref(st), None))
+    assert st.value == 0

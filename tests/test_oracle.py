@@ -40,11 +40,12 @@ def test_linear_group_matches_numpy(out, ng):
 @pytest.mark.parametrize("sb_dtype", [O.SB_BF16, O.SB_F16])
 def test_layouts_round_trip_and_match_numpy(sb_dtype):
     wq, sb = O.synthetic_weight(520, 448, 1, sb_dtype)
-    fq, fsb = O.mlx_to_frag16(wq, sb)
-    fq2, fsb2 = N.frag16_from_mlx(wq, sb, 520, 448)
-    assert np.array_equal(fq, fq2) and np.array_equal(fsb, fsb2)
-    w2, s2 = O.frag16_to_mlx(fq, fsb, 520, 448)
-    assert np.array_equal(w2, wq) and np.array_equal(s2, sb)
+    for ts in (1, 2, 8):
+        fq, fsb = O.mlx_to_frag(wq, sb, ts)
+        fq2, fsb2 = N.frag_from_mlx(wq, sb, 520, 448, ts)
+        assert np.array_equal(fq, fq2) and np.array_equal(fsb, fsb2)
+        w2, s2 = O.frag_to_mlx(fq, fsb, 520, 448, ts)
+        assert np.array_equal(w2, wq) and np.array_equal(s2, sb)
     tw, tsb = O.mlx_to_tiled(wq, sb)
     tw2, tsb2 = N.tiled_from_mlx(wq, sb, 520, 448)
     assert np.array_equal(tw, tw2) and np.array_equal(tsb, tsb2)

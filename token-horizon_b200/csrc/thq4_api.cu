@@ -54,30 +54,39 @@ int device_sm_count() {
 }
 
 namespace {
-std::atomic<int> g_force_ks{-1}, g_force_warps{0};
+std::atomic<int> g_force_warps{0}, g_force_depth{0}, g_force_grid{0};
 }  // namespace
 
+bool gemv_pdl_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("THQ4_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 GemvCfg gemv_cfg_override() {
-  const int fk = g_force_ks.load(std::memory_order_relaxed);
-  if (fk >= 0) {
-    GemvCfg c;
-    c.ks = fk;
-    c.warps = g_force_warps.load(std::memory_order_relaxed);
-    return c;
-  }
-  static const GemvCfg cfg = [] {
-    GemvCfg c;
-    const char *e = std::getenv("THQ4_GEMV");
-    if (e && *e) {
-      int ks = 0, warps = 0;
-      if (std::sscanf(e, "%d,%d", &ks, &warps) >= 1) {
-        if (ks == 1 || ks == 2 || ks == 4 || ks == 8 || ks == 16) c.ks = ks;
-        if (warps == 4 || warps == 8 || warps == 16) c.warps = warps;
+  GemvCfg c;
+  c.warps = g_force_warps.load(std::memory_order_relaxed);
+  c.depth = g_force_depth.load(std::memory_order_relaxed);
+  c.grid = g_force_grid.load(std::memory_order_relaxed);
+  if (c.warps || c.depth || c.grid) return c;
+  // THQ4_GEMV="chunk,stages,grid", read once (the reference reads its TH_QMVT /
+  // TH_Q4_POLICY switches once the same way, quant_kernel.rs:41-78, 367-432)
+  static const GemvCfg env = [] {
+    GemvCfg e;
+    const char *s = std::getenv("THQ4_GEMV");
+    if (s && *s) {
+      int w = 0, d = 0, g = 0;
+      if (std::sscanf(s, "%d,%d,%d", &w, &d, &g) >= 1) {
+        if (w == 1 || w == 2 || w == 4) e.warps = w;
+        if (d >= 2 && d <= 8) e.depth = d;
+        if (g > 0) e.grid = g;
       }
     }
-    return c;
+    return e;
   }();
-  return cfg;
+  return env;
 }
 
 namespace {
@@ -117,6 +126,15 @@ thq4_status check_io(const void *x, int x_dtype, int m, const void *y, int y_dty
   return THQ4_OK;
 }
 
+thq4_status check_workspace(void *ws, size_t have, size_t need, const char *who) {
+  if (need == 0) return THQ4_OK;
+  if (!ws || have < need || !aligned(ws, 256))
+    return set_error(THQ4_ERR_WORKSPACE, std::string(who) + ": needs a 256-byte aligned, zero-filled workspace of " +
+                                             std::to_string(need) + " bytes (thq4_linear_workspace_bytes), got " +
+                                             std::to_string(have));
+  return THQ4_OK;
+}
+
 }  // namespace
 }  // namespace thq4
 
@@ -151,7 +169,7 @@ thq4_status thq4_device_status(uint32_t *status_out, void *stream) {
 size_t thq4_weight_bytes(int rows, int in, int gs, size_t *qw_bytes, size_t *sb_bytes) {
   size_t q = 0, s = 0;
   if (rows > 0 && in > 0 && gs == kGroup && in % kGroup == 0) {
-    const size_t chunks = (size_t)row_tiles(rows) * (size_t)(in / kGroup);
+    const size_t chunks = (size_t)row_slabs(rows) * kSlabTiles * (size_t)(in / kGroup);
     q = chunks * kChunkBytes;
     s = chunks * kQuadBytes;
   }
@@ -164,7 +182,7 @@ thq4_status thq4_repack(int src_layout, const void *src_w, const void *src_sb, i
                         int sb_dtype, int row_begin, int rows, void *dst_qw, size_t dst_qw_bytes, void *dst_sb,
                         size_t dst_sb_bytes, void *stream) {
   const char *who = "thq4_repack";
-  if (src_layout < THQ4_SRC_MLX || src_layout > THQ4_SRC_FRAG16)
+  if (src_layout < THQ4_SRC_MLX || src_layout > THQ4_SRC_FRAG)
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: unknown source layout");
   if (gs != kGroup) return set_error(THQ4_ERR_UNSUPPORTED, "thq4_repack: only group size 64 is packed");
   if (sb_dtype != THQ4_BF16 && sb_dtype != THQ4_F16)
@@ -178,12 +196,12 @@ thq4_status thq4_repack(int src_layout, const void *src_w, const void *src_sb, i
                                                     std::to_string(src_out) + " rows");
   if (src_layout == THQ4_SRC_SLAB && src_out % 256 != 0)
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: a slab needs out % 256 == 0 (StorageN=256)");
-  if (src_layout == THQ4_SRC_FRAG16 && (row_begin != 0 || rows != src_out))
-    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: a frag16 source is copied whole");
+  if (src_layout == THQ4_SRC_FRAG && (row_begin != 0 || rows != src_out))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: a frag source is copied whole");
   if (!src_w || (src_layout != THQ4_SRC_SLAB && !src_sb))
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: source pointers must be non-NULL");
   if (!aligned(src_w, 16) || (src_sb && !aligned(src_sb, 2)) ||
-      (src_layout == THQ4_SRC_FRAG16 && !aligned(src_sb, 16)))
+      (src_layout == THQ4_SRC_FRAG && !aligned(src_sb, 16)))
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_repack: source weights must be 16-byte aligned");
   size_t need_q = 0, need_s = 0;
   thq4_weight_bytes(rows, in, gs, &need_q, &need_s);
@@ -210,20 +228,20 @@ thq4_status thq4_weight_init(thq4_weight *w, int out, int in, int gs, int sb_dty
 }
 
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m) {
-  (void)w;
   (void)m;
-  return 0;
+  if (!w || w->out <= 0) return 0;
+  return gemv_workspace_bytes(w->out);
 }
 
 thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
                         void *workspace, size_t workspace_bytes, void *stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   thq4_status s = check_weight(w, "thq4_linear");
   if (s != THQ4_OK) return s;
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_linear");
   if (s != THQ4_OK) return s;
-  cudaError_t e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32,
+  s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(w->out), "thq4_linear");
+  if (s != THQ4_OK) return s;
+  cudaError_t e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, workspace,
                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, "thq4_linear");
   return THQ4_OK;
@@ -231,8 +249,6 @@ thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
 
 thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const void *x, int x_dtype, int m,
                          void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   thq4_status s = check_weight(gate, "thq4_gate_up");
   if (s != THQ4_OK) return s;
   s = check_weight(up, "thq4_gate_up");
@@ -241,7 +257,9 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const v
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_gate_up: gate and up halves differ in shape or dtype");
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_gate_up");
   if (s != THQ4_OK) return s;
-  cudaError_t e = gemv_launch(*gate, up, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32,
+  s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(gate->out), "thq4_gate_up");
+  if (s != THQ4_OK) return s;
+  cudaError_t e = gemv_launch(*gate, up, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, workspace,
                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, "thq4_gate_up");
   return THQ4_OK;
@@ -256,12 +274,14 @@ thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream) {
   return THQ4_OK;
 }
 
-thq4_status thq4_debug_set_gemv(int ks, int warps) {
-  if (!(ks == 0 || ks == 1 || ks == 2 || ks == 4 || ks == 8 || ks == 16) ||
-      !(warps == 0 || warps == 4 || warps == 8 || warps == 16))
-    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_debug_set_gemv: ks must be 0/1/2/4/8/16, warps 0/4/8/16");
-  g_force_warps.store(warps, std::memory_order_relaxed);
-  g_force_ks.store(ks == 0 ? -1 : ks, std::memory_order_relaxed);
+thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
+  if (!(chunk == 0 || chunk == 1 || chunk == 2 || chunk == 4) || stages < 0 || stages == 1 || stages > 8 ||
+      grid < 0 || grid > 2 * device_sm_count() || reserved != 0)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_debug_set_gemv: chunk 0/1/2/4, stages 0 or 2..8, grid 0..2x SM count, reserved 0");
+  g_force_warps.store(chunk, std::memory_order_relaxed);
+  g_force_depth.store(stages, std::memory_order_relaxed);
+  g_force_grid.store(grid, std::memory_order_relaxed);
   return THQ4_OK;
 }
 

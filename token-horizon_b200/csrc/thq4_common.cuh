@@ -11,35 +11,42 @@
 #define THQ4_SEMVER "0.1.0"
 
 // ---------------------------------------------------------------------------
-// frag16 weight layout
+// frag weight layout
 // ---------------------------------------------------------------------------
-// Rows pad to a multiple of 16 (a "row tile", the M of one mma.m16n8k16).
-// K splits into quant groups of 64.  For tile rt and group g:
+// Rows pad to slabs of 128 = eight 16-row tiles (a tile is the M of one
+// mma.m16n8k16).  K splits into quant groups of 64.  Chunk
+// ch = (slab * ng + g) * 8 + t covers tile t of the slab for group g:
 //
-//   nibbles: 512 bytes at byte offset (rt * ng + g) * 512.  Lane l of a warp
-//            owns bytes [16 l, 16 l + 16): four u32 words, word j = k-step j
-//            (k 16 j .. 16 j + 15 of the group).  With r = l / 4, c = l % 4,
-//            nibble slot i = 0..3 of word half h (h = 0: bits 4i..4i+3,
-//            h = 1: bits 16+4i..16+4i+3) holds
-//                row  = 16 rt + r + 8 (i & 1)
+//   nibbles: 512 bytes at byte offset ch * 512.  Lane l of a warp owns bytes
+//            [16 l, 16 l + 16): four u32 words, word j = k-step j (k 16 j ..
+//            16 j + 15 of the group).  With r = l / 4, c = l % 4, nibble slot
+//            i = 0..3 of word half h (h = 0: bits 4i..4i+3, h = 1:
+//            bits 16+4i..16+4i+3) holds
+//                row  = 128 slab + 16 t + r + 8 (i & 1)
 //                k    = 64 g + 16 j + 2 c + 8 (i >> 1) + h.
 //            So (w >> 4i) & 0x000F000F is the A-fragment register i of
 //            mma.m16n8k16 (rows r / r+8, k pairs 2c / 2c+8) as two nibbles in
 //            the low bits of each 16-bit half, and OR-ing 0x43004300 turns it
 //            into the bf16 pair (128 + q_lo, 128 + q_hi) exactly.
-//   scales:  64 bytes at byte offset (rt * ng + g) * 64: eight quads
+//   scales:  64 bytes at byte offset ch * 64: eight quads
 //            {s_r, b_r, s_r+8, b_r+8} (16-bit, bf16 or f16), quad r at + 8 r.
 //
-// Padding rows have zero nibbles, scales and biases.  Per weight the layout
-// stores exactly 0.5 + 4/64 = 0.5625 bytes, the same as the reference's
-// formats; only the order differs.
+// One (slab, group) -- a "slab-group" (SG), the unit the kernels stream -- is
+// 4096 contiguous nibble bytes and 512 contiguous scale bytes, and slab-groups
+// follow each other slab-major, so any run of them is one contiguous byte
+// range, fetched with large bulk copies.  Padding rows have zero nibbles,
+// scales and biases.  Per weight the layout stores exactly 0.5 + 4/64 =
+// 0.5625 bytes, the same as the reference's formats; only the order differs.
 namespace thq4 {
 
 constexpr int kGroup = 64;
 constexpr int kTileRows = 16;
+constexpr int kSlabTiles = 8;
+constexpr int kSlabRows = kSlabTiles * kTileRows;
 constexpr int kChunkBytes = 512;  // nibbles per (tile, group)
 constexpr int kQuadBytes = 64;    // scale/bias per (tile, group)
 
+__host__ __device__ inline int row_slabs(int rows) { return (rows + kSlabRows - 1) / kSlabRows; }
 __host__ __device__ inline int row_tiles(int rows) { return (rows + 15) / 16; }
 
 // ---------------------------------------------------------------------------
@@ -78,6 +85,25 @@ __device__ __forceinline__ uint32_t nib_bf16x2(uint32_t w, int shift) {
   return r;
 }
 
+// (w >> shift) & 0x000F000F | 0x43004300 with the shift done as a multiply-high
+// (the FMA pipe) and the mask/or as one LOP3 (the ALU pipe).
+__device__ __forceinline__ uint32_t nib_bf16x2_mh(uint32_t w, int shift) {
+  const uint32_t v = shift ? __umulhi(w, 1u << (32 - shift)) : w;
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(v), "r"(0x000F000Fu), "r"(0x43004300u));
+  return r;
+}
+
+// D = A * B (C = 0), bf16 inputs, f32 accumulate, m16n8k16.
+__device__ __forceinline__ void mma_bf16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
 // D = A * B + D, bf16 inputs, f32 accumulate, m16n8k16.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
@@ -87,6 +113,68 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- mbarrier / bulk-copy / PDL wrappers --------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+// Makes mbarrier initialisation visible to the async proxy (the bulk copies).
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// One-dimensional bulk copy global -> shared (no multicast), completing on
+// `bar` with its byte count; evict-first in L2.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Waits for phase `parity` of `bar` for at most `limit_ns`; false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+// Programmatic dependent launch: wait for the preceding grid's results /
+// allow the next grid to start its prologue.  No-ops without the launch
+// attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t lo16) {
@@ -122,7 +210,11 @@ __device__ __forceinline__ float silu_mul(float gate, float up) {
 enum : uint32_t {
   kStatusBadExpert = 1u << 0,
   kStatusBounds = 1u << 1,
+  kStatusTimeout = 1u << 2,  // an mbarrier wait ran out of time
 };
+// Bound on any single wait for an in-flight copy (a healthy one completes in
+// microseconds).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bit) {
   if (status) atomicOr(status, bit);
 }

@@ -12,7 +12,10 @@
 namespace thq4 {
 
 // Dynamic shared memory the GEMV may use per CTA (B200: 227 KB opt-in).
-constexpr int kGemvMaxSmem = 200 * 1024;
+constexpr int kGemvMaxSmem = 227 * 1024;
+// Half of it: the decode kernel sizes its rings so two CTAs share an SM.
+constexpr int kGemvHalfSmem = 113 * 1024;
+
 
 // Runs `fn` once per device (e.g. a cudaFuncSetAttribute), remembering
 // success; a failure is returned and retried on the next call.
@@ -44,22 +47,27 @@ uint32_t *status_word();
 
 // ---- GEMV / verify ---------------------------------------------------------
 struct GemvCfg {
-  int ks = 0;     // forced K slices (0 = policy)
-  int warps = 0;  // forced warps per CTA (0 = policy)
+  int warps = 0;  // forced slab-groups per ring stage (0 = policy)
+  int depth = 0;  // forced ring stages (0 = policy)
+  int grid = 0;   // forced CTAs (0 = policy)
 };
-// THQ4_GEMV="ks,warps" read once per process (the reference reads its
-// TH_QMVT / TH_Q4_POLICY switches once the same way, quant_kernel.rs:41-78,
-// 367-432).
+// The testing hook's forced shape, else THQ4_GEMV (read once), else none.
 GemvCfg gemv_cfg_override();
 
 struct GemvPlan {
   bool ok;
-  int ks, rt_per_cta, threads, gps, grid, tokens_per_pass;
+  int threads, grid, pieces, tokens_per_pass, ch, stages;
   size_t smem;
 };
+// Workspace the decode/verify kernel needs for a weight of `rows` rows:
+// partial-sum slots for every warp plus one counter per 16-row tile.  It
+// must be zero-filled before first use; every call leaves it zeroed.
+size_t gemv_workspace_bytes(int rows);
+// Programmatic dependent launch for the GEMV (THQ4_PDL=0 disables; read once).
+bool gemv_pdl_enabled();
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
-                        int m, void *y, bool y_f32, cudaStream_t stream);
+                        int m, void *y, bool y_f32, void *workspace, cudaStream_t stream);
 
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,

@@ -1,5 +1,5 @@
 // thq4_repack.cu -- load-time repack of the reference's Q4 formats into the
-// frag16 layout, and the dequantise-to-bf16 kernel.
+// frag layout, and the dequantise-to-bf16 kernel.
 //
 // Replaces QLin::tiled's host-thread repack (engine/src/qwen35.rs:629-697)
 // with a device kernel, and reads every layout the reference stores:
@@ -18,9 +18,9 @@ struct RepackArgs {
   int layout;
   const uint32_t *w;   // source words (MLX / tiled) or slab bytes
   const uint16_t *sb;  // source scale/bias (MLX / tiled)
-  int src_out, in, ng, row_begin, rows, rtiles;
-  uint32_t *dq;        // frag16 nibbles
-  uint16_t *dsb;       // frag16 quads
+  int src_out, in, ng, row_begin, rows, slabs;
+  uint32_t *dq;        // frag nibbles
+  uint16_t *dsb;       // frag quads
 };
 
 // The 8 words of source row `row`, group g (zeros for rows past `rows`).
@@ -62,20 +62,23 @@ __device__ inline void load_row_group(const RepackArgs &a, int local_row, int g,
   }
 }
 
-// One thread per (row tile, group, lane): four output words and, for c == 0,
-// the quad of rows r and r+8.
+// One thread per (chunk, lane): four output words and, for c == 0, the quad
+// of rows r and r+8.  Chunk (slab * ng + g) * 8 + t is tile t of the slab.
 __global__ void repack_kernel(const RepackArgs a) {
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const size_t total = (size_t)a.rtiles * a.ng * 32;
+  const size_t total = (size_t)a.slabs * a.ng * kSlabTiles * 32;
   if (tid >= total) return;
   const int lane = (int)(tid % 32);
   const size_t chunk = tid / 32;
-  const int g = (int)(chunk % a.ng), rt = (int)(chunk / a.ng);
+  const int t = (int)(chunk % kSlabTiles);
+  const size_t sg = chunk / kSlabTiles;
+  const int g = (int)(sg % a.ng), slab = (int)(sg / a.ng);
   const int r = lane >> 2, c = lane & 3;
+  const int row0 = slab * kSlabRows + t * kTileRows;
   uint32_t w0[8], w1[8];
   uint16_t s0, b0, s1, b1;
-  load_row_group(a, rt * 16 + r, g, w0, s0, b0);
-  load_row_group(a, rt * 16 + r + 8, g, w1, s1, b1);
+  load_row_group(a, row0 + r, g, w0, s0, b0);
+  load_row_group(a, row0 + r + 8, g, w1, s1, b1);
   auto nib = [&](int which, int k) -> uint32_t {  // k within the group
     const uint32_t word = which ? w1[k >> 3] : w0[k >> 3];
     return (word >> (4 * (k & 7))) & 0xFu;
@@ -102,7 +105,7 @@ __global__ void repack_kernel(const RepackArgs a) {
   }
 }
 
-// Copies an already packed frag16 weight (rows must cover whole tiles).
+// Copies an already packed frag weight (rows must cover whole tiles).
 __global__ void copy_kernel(const uint4 *src, uint4 *dst, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = src[i];
@@ -115,9 +118,9 @@ __global__ void dequant_kernel(const uint32_t *qw, const uint16_t *sb, int out, 
   const int kb8 = in / 8, ng = in / 64;
   if (tid >= (size_t)out * kb8) return;
   const int n = (int)(tid / kb8), k0 = (int)(tid % kb8) * 8;
-  const int rt = n / 16, rr = n % 16, r = rr % 8, irow = rr / 8;
+  const int slab = n / kSlabRows, t = (n % kSlabRows) / kTileRows, rr = n % kTileRows, r = rr % 8, irow = rr / 8;
   const int g = k0 / 64, kk = k0 % 64, j = kk / 16, ik = (kk % 16) / 8;
-  const size_t chunk = (size_t)rt * ng + g;
+  const size_t chunk = ((size_t)slab * ng + g) * kSlabTiles + t;
   const uint2 quad = reinterpret_cast<const uint2 *>(sb)[chunk * 8 + r];
   const uint32_t qd = irow ? quad.y : quad.x;
   const float s = sb_to_f32<SF16>(qd & 0xffffu), b = sb_to_f32<SF16>(qd >> 16);
@@ -142,10 +145,11 @@ __global__ void dequant_kernel(const uint32_t *qw, const uint16_t *sb, int out, 
 
 cudaError_t repack_launch(int layout, const void *src_w, const void *src_sb, int src_out, int in,
                           int row_begin, int rows, void *dst_qw, void *dst_sb, cudaStream_t stream) {
-  const int ng = in / kGroup, rtiles = row_tiles(rows);
-  if (layout == THQ4_SRC_FRAG16) {
-    // a frag16 source is copied as is (row_begin must be 0 and rows whole)
-    const size_t nq = (size_t)rtiles * ng * kChunkBytes / 16, ns = (size_t)rtiles * ng * kQuadBytes / 16;
+  const int ng = in / kGroup, slabs = row_slabs(rows);
+  if (layout == THQ4_SRC_FRAG) {
+    // a frag source is copied as is (row_begin must be 0 and rows whole)
+    const size_t nq = (size_t)slabs * ng * kSlabTiles * kChunkBytes / 16;
+    const size_t ns = (size_t)slabs * ng * kSlabTiles * kQuadBytes / 16;
     copy_kernel<<<1024, 256, 0, stream>>>(static_cast<const uint4 *>(src_w), static_cast<uint4 *>(dst_qw), nq);
     copy_kernel<<<256, 256, 0, stream>>>(static_cast<const uint4 *>(src_sb), static_cast<uint4 *>(dst_sb), ns);
     return cudaGetLastError();
@@ -159,10 +163,10 @@ cudaError_t repack_launch(int layout, const void *src_w, const void *src_sb, int
   a.ng = ng;
   a.row_begin = row_begin;
   a.rows = rows;
-  a.rtiles = rtiles;
+  a.slabs = slabs;
   a.dq = static_cast<uint32_t *>(dst_qw);
   a.dsb = static_cast<uint16_t *>(dst_sb);
-  const size_t total = (size_t)rtiles * ng * 32;
+  const size_t total = (size_t)slabs * ng * kSlabTiles * 32;
   const unsigned blocks = (unsigned)((total + 255) / 256);
   repack_kernel<<<blocks, 256, 0, stream>>>(a);
   return cudaGetLastError();

@@ -3,10 +3,10 @@
 The operators live in libthq4.so (C ABI: include/thq4.h); this package is the
 host-side mirror of the reference's operator API on top of it.
 """
-from ._lib import (BF16, F16, F32, SRC_FRAG16, SRC_MLX, SRC_SLAB, SRC_TILED, Thq4Error, check, last_error,
+from ._lib import (BF16, F16, F32, SRC_FRAG, SRC_MLX, SRC_SLAB, SRC_TILED, Thq4Error, check, last_error,
                    lib, version)
 from .qlin import PackedWeight, QLin, fuse_lins, lin_apply, lin_apply_ps, maybe_tiled
 
-__all__ = ["BF16", "F16", "F32", "SRC_FRAG16", "SRC_MLX", "SRC_SLAB", "SRC_TILED", "Thq4Error", "check",
+__all__ = ["BF16", "F16", "F32", "SRC_FRAG", "SRC_MLX", "SRC_SLAB", "SRC_TILED", "Thq4Error", "check",
            "last_error", "lib", "version", "PackedWeight", "QLin", "fuse_lins", "lin_apply", "lin_apply_ps",
            "maybe_tiled"]

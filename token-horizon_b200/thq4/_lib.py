@@ -29,7 +29,7 @@ F32 = 2
 SRC_MLX = 0
 SRC_TILED = 1
 SRC_SLAB = 2
-SRC_FRAG16 = 3
+SRC_FRAG = 3
 
 
 class Thq4Error(RuntimeError):
@@ -69,7 +69,7 @@ SIGNATURES = {
                              c_int, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_workspace_bytes": (c_size_t, [POINTER(thq4_weight), c_int]),
     "thq4_dequant": (c_int, [POINTER(thq4_weight), c_void_p, c_void_p]),
-    "thq4_debug_set_gemv": (c_int, [c_int, c_int]),
+    "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
 }
 
 

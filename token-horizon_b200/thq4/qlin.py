@@ -33,8 +33,24 @@ def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_WORKSPACES: dict = {}
+
+
+def workspace(desc, device: torch.device) -> torch.Tensor:
+    """A zero-filled workspace big enough for `desc`, cached per device and
+    stream (the kernels return it zeroed after every call)."""
+    need = _lib.lib().thq4_linear_workspace_bytes(ctypes.byref(desc), 1)
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(device).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 class PackedWeight:
-    """One frag16 weight (rows x in) resident on the device."""
+    """One frag weight (rows x in) resident on the device."""
 
     def __init__(self, rows: int, inp: int, sb_dtype: int, device: torch.device):
         qb, sbb = ctypes.c_size_t(), ctypes.c_size_t()
@@ -64,7 +80,7 @@ class QLin:
     """Packed Q4 projection; mirror of ``QLin`` (qwen35.rs:303-325).
 
     ``tiled`` is True once the weight is packed in the kernels' layout (the
-    reference's Splash tile layout becomes this library's frag16 layout).
+    reference's Splash tile layout becomes this library's frag layout).
     """
 
     def __init__(self, wq: torch.Tensor, sb: torch.Tensor, out: int, inp: int, gs: int = 64):
@@ -141,8 +157,9 @@ class QLin:
         xv = x.reshape(rows, in_d).contiguous()
         ydt = out_dtype or (torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         y = out if out is not None else torch.empty((rows, self.out), dtype=ydt, device=x.device)
+        ws = workspace(self.packed.desc, x.device)
         check(_lib.lib().thq4_linear(ctypes.byref(self.packed.desc), _ptr(xv), x_dtype, rows, _ptr(y),
-                                     F32 if y.dtype == torch.float32 else BF16, None, 0, _stream()))
+                                     F32 if y.dtype == torch.float32 else BF16, _ptr(ws), ws.numel(), _stream()))
         return y.reshape(dims[:-1] + [self.out])
 
     # -- QLin::gate_up_act_ps (qwen35.rs:711-884) -------------------------------
@@ -177,9 +194,10 @@ class QLin:
             raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin::gate_up_act: x dtype {x.dtype}")
         xv = x.reshape(rows, dims[-1]).contiguous()
         y = out if out is not None else torch.empty((rows, half), dtype=torch.bfloat16, device=x.device)
+        ws = workspace(self.packed_gate.desc, x.device)
         check(_lib.lib().thq4_gate_up(ctypes.byref(self.packed_gate.desc), ctypes.byref(self.packed_up.desc),
                                       _ptr(xv), x_dtype, rows, _ptr(y),
-                                      F32 if y.dtype == torch.float32 else BF16, None, 0, _stream()))
+                                      F32 if y.dtype == torch.float32 else BF16, _ptr(ws), ws.numel(), _stream()))
         return y.reshape(dims[:-1] + [half]), False
 
     def dequant(self) -> torch.Tensor:
