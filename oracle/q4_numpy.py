@@ -64,12 +64,11 @@ def frag_from_mlx(wq, sb, out: int, inp: int, ts: int = 8):
     for t in range(ts):
         for j in range(4):
             word = np.zeros((nb, ng, 32), dtype=np.uint32)
-            for i in range(4):
-                for h in range(2):
-                    rows = (np.arange(nb)[:, None] * ts + t) * 16 + (r + 8 * (i & 1))[None, :]
-                    kk = np.arange(ng)[:, None] * 64 + (16 * j + 2 * c + 8 * (i >> 1) + h)[None, :]
-                    vals = qp[rows[:, None, :], kk[None, :, :]]
-                    word |= vals << np.uint32(16 * h + 4 * i)
+            for i in range(8):
+                rows = (np.arange(nb)[:, None] * ts + t) * 16 + (r + 8 * ((i >> 1) & 1))[None, :]
+                kk = np.arange(ng)[:, None] * 64 + (32 * (j >> 1) + 8 * (j & 1) + 16 * (i & 1) + 2 * c + (i >> 2))[None, :]
+                vals = qp[rows[:, None, :], kk[None, :, :]]
+                word |= vals << np.uint32(4 * i)
             fq[:, :, t, :, j] = word
     sbp = np.zeros((nb * 16 * ts, 2 * ng), dtype=np.uint16)
     sbp[:out] = sb

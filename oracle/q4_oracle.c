@@ -288,15 +288,20 @@ void q4o_slab_to_mlx(const uint8_t *slab, int out, int in, uint32_t *wq,
  * to slabs of 16*ts rows = ts tiles of 16 (the library uses ts = 8).  Chunk
  * ((slab*ng + g)*ts + t) holds the 512 nibble bytes of tile t of the slab for
  * group g; lane l owns bytes [16l, 16l+16) = words j = 0..3; with r = l/4,
- * c = l%4, nibble slot i (0..3) of half h (0: bits 4i..4i+3, 1: bits
- * 16+4i..) holds row 16(ts*slab + t) + r + 8(i&1), k = 64g + 16j + 2c +
- * 8(i>>1) + h.  Scales: 64 bytes per chunk, eight quads
- * {s_r, b_r, s_r+8, b_r+8}. */
+ * c = l%4, the nibble at bits 4i..4i+3 (i = 0..7) of word j holds
+ *   row = 16(ts*slab + t) + r + 8((i>>1)&1),
+ *   k   = 64g + 32(j>>1) + 8(j&1) + 16(i&1) + 2c + (i>>2).
+ * Scales: 64 bytes per chunk, eight quads {s_r, b_r, s_r+8, b_r+8}. */
 size_t q4o_frag_qw_bytes(int out, int in, int ts) {
   return (size_t)((out + 16 * ts - 1) / (16 * ts)) * ts * (size_t)(in / 64) * 512;
 }
 size_t q4o_frag_sb_bytes(int out, int in, int ts) {
   return (size_t)((out + 16 * ts - 1) / (16 * ts)) * ts * (size_t)(in / 64) * 64;
+}
+
+/* k of the nibble at bits 4i..4i+3 of word j for lane column c, group g */
+static inline int frag_k(int g, int j, int i, int c) {
+  return g * 64 + 32 * (j >> 1) + 8 * (j & 1) + 16 * (i & 1) + 2 * c + (i >> 2);
 }
 
 static inline uint32_t mlx_nibble(const uint32_t *wq, int in, int row, int k) {
@@ -315,13 +320,12 @@ void q4o_mlx_to_frag(const uint32_t *wq, const uint16_t *sb, int out, int in, in
           int r = lane >> 2, c = lane & 3;
           for (int j = 0; j < 4; ++j) {
             uint32_t word = 0;
-            for (int i = 0; i < 4; ++i)
-              for (int h = 0; h < 2; ++h) {
-                int row = row0 + r + 8 * (i & 1);
-                int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
-                uint32_t q = row < out ? mlx_nibble(wq, in, row, k) : 0;
-                word |= q << (16 * h + 4 * i);
-              }
+            for (int i = 0; i < 8; ++i) {
+              int row = row0 + r + 8 * ((i >> 1) & 1);
+              int k = frag_k(g, j, i, c);
+              uint32_t q = row < out ? mlx_nibble(wq, in, row, k) : 0;
+              word |= q << (4 * i);
+            }
             fq[(chunk * 32 + lane) * 4 + j] = word;
           }
         }
@@ -352,14 +356,13 @@ void q4o_frag_to_mlx(const uint32_t *fq, const uint16_t *fsb, int out, int in, i
           int r = lane >> 2, c = lane & 3;
           for (int j = 0; j < 4; ++j) {
             uint32_t word = fq[(chunk * 32 + lane) * 4 + j];
-            for (int i = 0; i < 4; ++i)
-              for (int h = 0; h < 2; ++h) {
-                int row = row0 + r + 8 * (i & 1);
-                int k = g * 64 + 16 * j + 2 * c + 8 * (i >> 1) + h;
-                if (row >= out) continue;
-                uint32_t q = (word >> (16 * h + 4 * i)) & 0xFu;
-                wq[(size_t)row * (in / 8) + k / 8] |= q << (4 * (k % 8));
-              }
+            for (int i = 0; i < 8; ++i) {
+              int row = row0 + r + 8 * ((i >> 1) & 1);
+              int k = frag_k(g, j, i, c);
+              if (row >= out) continue;
+              uint32_t q = (word >> (4 * i)) & 0xFu;
+              wq[(size_t)row * (in / 8) + k / 8] |= q << (4 * (k % 8));
+            }
           }
         }
         for (int r = 0; r < 8; ++r)

@@ -16,7 +16,7 @@ from helpers import assert_close_ref, assert_gate_up_close, assert_rms_close, de
 pytestmark = pytest.mark.gpu
 
 # (slab-groups per stage, ring stages, CTAs; 0 = policy)
-SPLITS = [(0, 0, 0), (1, 2, 0), (2, 6, 0), (4, 3, 7), (1, 8, 0), (2, 2, 3), (4, 4, 1), (1, 3, 296)]
+SPLITS = [(0, 0, 0), (2, 2, 0), (2, 6, 0), (4, 3, 7), (2, 8, 0), (4, 2, 3), (4, 4, 1), (2, 3, 296)]
 
 
 @pytest.fixture(autouse=True)
@@ -81,12 +81,12 @@ def test_qmvt_plain_matches_oracle(case):
     want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = _qlin(wq, sb)
     x = _x_bf16(xb)
-    for warps, ch, stages in SPLITS:
-        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
+    for chunk, stages, grid in SPLITS:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(chunk, stages, grid, 0))
         y = q.linear(x.reshape(1, 1, inp))
         assert tuple(y.shape) == (1, 1, out)
         got = to_f32(y).ravel()
-        assert_close_ref(f"plain {out}x{inp} w{warps} ch{ch} r{stages}", got, want)
+        assert_close_ref(f"plain {out}x{inp} cb{chunk} st{stages} grid{grid}", got, want)
         again = to_f32(q.linear(x.reshape(1, 1, inp))).ravel()
         assert np.array_equal(got, again), "not deterministic"
 
@@ -100,12 +100,12 @@ def test_qmvt_gate_up_matches_oracle(case):
     gu = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = thq4.QLin(dev(wq), dev(sb), out, inp, 64)
     x = _x_bf16(xb)
-    for warps, ch, stages in SPLITS:
-        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
+    for chunk, stages, grid in SPLITS:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(chunk, stages, grid, 0))
         y = q.gate_up_act(x.reshape(1, 1, inp))
         assert tuple(y.shape) == (1, 1, half)
         got = to_f32(y).ravel()
-        assert_gate_up_close(f"gate_up {half}x{inp} w{warps} ch{ch}", got, gu[:half], gu[half:], inp)
+        assert_gate_up_close(f"gate_up {half}x{inp} cb{chunk} st{stages} grid{grid}", got, gu[:half], gu[half:], inp)
         again = to_f32(q.gate_up_act(x.reshape(1, 1, inp))).ravel()
         assert np.array_equal(got, again)
 
@@ -223,10 +223,10 @@ def test_tiny_and_ragged_weights(out, inp):
     xb = O.rand_x(inp, 3)
     want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = _qlin(wq, sb)
-    for warps, ch, stages in [(0, 0, 0), (1, 2, 0), (4, 5, 5), (2, 2, 1)]:
-        thq4.check(thq4.lib().thq4_debug_set_gemv(warps, ch, stages, 0))
+    for chunk, stages, grid in [(0, 0, 0), (2, 2, 0), (4, 5, 5), (2, 2, 1)]:
+        thq4.check(thq4.lib().thq4_debug_set_gemv(chunk, stages, grid, 0))
         got = to_f32(q.linear(_x_bf16(xb).reshape(1, inp))).ravel()
-        assert_close_ref(f"{out}x{inp} w{warps} ch{ch}", got, want)
+        assert_close_ref(f"{out}x{inp} cb{chunk} st{stages} grid{grid}", got, want)
 
 
 def test_workspace_required_and_reused():

@@ -18,16 +18,20 @@
 // ch = (slab * ng + g) * 8 + t covers tile t of the slab for group g:
 //
 //   nibbles: 512 bytes at byte offset ch * 512.  Lane l of a warp owns bytes
-//            [16 l, 16 l + 16): four u32 words, word j = k-step j (k 16 j ..
-//            16 j + 15 of the group).  With r = l / 4, c = l % 4, nibble slot
-//            i = 0..3 of word half h (h = 0: bits 4i..4i+3, h = 1:
-//            bits 16+4i..16+4i+3) holds
-//                row  = 128 slab + 16 t + r + 8 (i & 1)
-//                k    = 64 g + 16 j + 2 c + 8 (i >> 1) + h.
-//            So (w >> 4i) & 0x000F000F is the A-fragment register i of
-//            mma.m16n8k16 (rows r / r+8, k pairs 2c / 2c+8) as two nibbles in
-//            the low bits of each 16-bit half, and OR-ing 0x43004300 turns it
-//            into the bf16 pair (128 + q_lo, 128 + q_hi) exactly.
+//            [16 l, 16 l + 16): four u32 words.  With r = l / 4, c = l % 4,
+//            the nibble at bits 4i..4i+3 (i = 0..7) of word j holds
+//                row = 128 slab + 16 t + r + 8 ((i >> 1) & 1)
+//                k   = 64 g + 32 (j >> 1) + 8 (j & 1) + 16 (i & 1) + 2 c + (i >> 2)
+//            (frag_k below).  So for word w of k-step pair p = j >> 1:
+//              w & 0x000F000F         rows r   / k-step 2p   (low nibbles)
+//              (w >> 8) & 0x000F000F  rows r+8 / k-step 2p
+//              w & 0x00F000F0         rows r   / k-step 2p+1 (nibbles x 16)
+//              (w >> 8) & 0x00F000F0  rows r+8 / k-step 2p+1
+//            each a pair of adjacent k (2c, 2c+1) in the two 16-bit halves:
+//            exactly the A-fragment registers of mma.m16n8k16 (words j = 2p
+//            and 2p+1 give the k and k+8 halves).  OR-ing 0x64006400 makes
+//            each half the fp16 number 1024 + q (low nibbles) or 1024 + 16 q
+//            (high nibbles) -- exact, five ALU operations per word.
 //   scales:  64 bytes at byte offset ch * 64: eight quads
 //            {s_r, b_r, s_r+8, b_r+8} (16-bit, bf16 or f16), quad r at + 8 r.
 //
@@ -45,6 +49,11 @@ constexpr int kSlabTiles = 8;
 constexpr int kSlabRows = kSlabTiles * kTileRows;
 constexpr int kChunkBytes = 512;  // nibbles per (tile, group)
 constexpr int kQuadBytes = 64;    // scale/bias per (tile, group)
+
+// k (within the group) of the nibble at bits 4i..4i+3 of word j, lane column c
+__host__ __device__ constexpr int frag_k(int j, int i, int c) {
+  return 32 * (j >> 1) + 8 * (j & 1) + 16 * (i & 1) + 2 * c + (i >> 2);
+}
 
 __host__ __device__ inline int row_slabs(int rows) { return (rows + kSlabRows - 1) / kSlabRows; }
 __host__ __device__ inline int row_tiles(int rows) { return (rows + 15) / 16; }
@@ -77,39 +86,21 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return p;
 }
 
-// (w >> shift) & 0x000F000F | 0x43004300 as one LOP3 after the shift:
-// bf16x2 (128 + q_lo, 128 + q_hi).
-__device__ __forceinline__ uint32_t nib_bf16x2(uint32_t w, int shift) {
-  uint32_t v = w >> shift, r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(v), "r"(0x000F000Fu), "r"(0x43004300u));
-  return r;
-}
-
-// (w >> shift) & 0x000F000F | 0x43004300 with the shift done as a multiply-high
-// (the FMA pipe) and the mask/or as one LOP3 (the ALU pipe).
-__device__ __forceinline__ uint32_t nib_bf16x2_mh(uint32_t w, int shift) {
-  const uint32_t v = shift ? __umulhi(w, 1u << (32 - shift)) : w;
+// (w & mask) | 0x64006400 as one LOP3: with mask 0x000F000F the fp16 pair
+// (1024 + q0, 1024 + q1), with mask 0x00F000F0 the pair (1024 + 16 q0,
+// 1024 + 16 q1).  Both are exact (fp16 has a unit step on [1024, 2048)).
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t nib_f16x2(uint32_t w) {
   uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(v), "r"(0x000F000Fu), "r"(0x43004300u));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(w), "n"(MASK), "n"(0x64006400));
   return r;
 }
 
-// D = A * B (C = 0), bf16 inputs, f32 accumulate, m16n8k16.
-__device__ __forceinline__ void mma_bf16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                                 uint32_t b0, uint32_t b1) {
+// D = A * B + C, fp16 inputs, f32 accumulate, m16n8k16.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
-}
-
-// D = A * B + D, bf16 inputs, f32 accumulate, m16n8k16.
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
-                                               uint32_t a2, uint32_t a3, uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

@@ -5,37 +5,43 @@
 // AffineQmpp (th_mpp_tile, :1793-2569), AffineQsg (:1149-1632) and AffineQmm
 // (:1634-1740), with one kernel.
 //
-// The path is bound by HBM bandwidth (0.5625 bytes per weight, each read once).
-// Measured on B200: a warp-per-run stream of 16-byte loads tops out near
-// 4 TB/s whatever its depth (each warp tracks only a few loads), while
-// one-dimensional bulk copies of 16 KB stream at ~5.8 TB/s from 148 CTAs.
+// The path is bound by HBM bandwidth (0.5625 bytes per weight, each read
+// once), and on B200 the instruction budget per streamed byte is tight: at
+// full bandwidth an SM has ~25 cycles for each 16x64 tile-group (576 bytes).
 // Hence:
 //   - the weight is a stream of "slab-groups" (SG): 128 rows x 64 k, 4096
 //     bytes of nibbles + 512 bytes of scale/bias, slab-major, so any run of
 //     SGs is one contiguous byte range of the frag layout.  A persistent grid
-//     (one or two CTAs per SM) gives every CTA an equal contiguous run of
-//     SGs; a run may start and end inside a slab;
+//     (one or two CTAs per SM) gives every CTA an equal run of "chunks" (CB
+//     consecutive SGs of one slab, CB-aligned); a run may start and end
+//     inside a slab;
 //   - one producer warp per CTA streams the run into a ring of shared-memory
 //     stages with bulk copies (cp.async.bulk, evict-first in L2, no
-//     multicast) of ~16 KB, completing on a "full" mbarrier per stage; the
-//     first stages are requested before the kernel waits for its input;
+//     multicast) of one chunk each, completing on a "full" mbarrier per stage;
+//     the first stages are requested before the kernel waits for its input;
 //   - eight consumer warps each own one 16-row tile of every SG, so their
 //     output rows are disjoint and no reduction crosses warps.  Per SG a warp
-//     runs four mma.m16n8k16 with the weight as the A operand (16 rows) and
-//     the m tokens as N (8 columns), bf16 with f32 accumulation.  A nibble
-//     pair becomes the bf16 pair (128 + q) by one shift and one LOP3 --
-//     exact -- and the 128 offset is removed per group in the epilogue
-//     together with the bias, the per-group form of the reference kernels
-//     (quant_kernel.rs:1994-2001, 2887-2890):
-//         y += s * sum((128+q) x) + (b - 128 s) * sum(x)
-//            = s * sum(q x) + b * sum(x),
-//     then releases the stage on an "empty" mbarrier.  Every mbarrier wait is
-//     bounded in time and reports kStatusTimeout instead of hanging;
-//   - an f32 activation is split into bf16 hi + lo parts that occupy two of
-//     the eight N columns, so an f32 GEMV keeps ~16 significant bits of x at
-//     no extra weight traffic;
-//   - the activation is staged once per CTA in shared memory in B-fragment
-//     order, with its per-group sums;
+//     runs four mma.m16n8k16 (fp16 x fp16 -> f32) with the weight as the A
+//     operand (16 rows) and activation columns as N (8).  One LOP3 per
+//     register turns a nibble pair into the fp16 pair (1024 + q) or
+//     (1024 + 16 q) (frag layout, thq4_common.cuh); the two kinds accumulate
+//     in separate chains ("lo" and "hi") and meet in the epilogue as
+//     lo + hi / 16.  The 1024 offsets are removed by seeding the lo chain
+//     with -off, off = 1024 sum(x, lo k) + 64 sum(x, hi k), computed when x
+//     is staged.  The group's value is then the reference's per-group form
+//     (quant_kernel.rs:1994-2001, 2887-2890):  s * sum(q x) + b * sum(x);
+//   - with few tokens most of the 8 columns are free, so consecutive groups
+//     share one accumulator: in a "window" of GW groups (4 when a group
+//     needs <= 2 columns), group j's activation sits in columns
+//     [8j/GW, 8(j+1)/GW) and is zero elsewhere.  After the window each lane
+//     holds the sums of exactly one group (its own columns), so the scale /
+//     bias epilogue runs once per window with every lane busy -- 4x fewer
+//     epilogue instructions for a matvec;
+//   - the activation is converted to fp16 per (group, token) with a power-of-
+//     two scale 2^e that puts the group's largest |x| in [2^14, 2^15): exact
+//     for bf16 input over 31 binades below the group maximum, no overflow at
+//     any magnitude; e is undone in the epilogue.  An f32 activation is split
+//     into fp16 hi + lo parts in two columns (22 significant bits);
 //   - a slab split between CTAs (only a CTA's first and last slab can be) is
 //     finished per tile by the warp that arrives last ("last arriver
 //     reduces", the reference's split-K scheme, quant_kernel.rs:1299-1332):
@@ -43,10 +49,13 @@
 //     (slab, tile) counter; the last one adds the partials in CTA order, so
 //     results are bitwise deterministic (qwen35.rs:6986-6988) with no
 //     waiting, and resets the counter;
-//   - CTAs stay within half an SM when the activation allows, and the kernel
-//     uses programmatic dependent launch: the next projection's CTA can become
-//     resident and request its weights while this one finishes; griddepcontrol
-//     .wait guards only the activation reads and the output writes.
+//   - the kernel uses programmatic dependent launch: the next projection's
+//     CTA can become resident and request its weights while this one
+//     finishes; griddepcontrol.wait guards only the activation reads and the
+//     output writes.  Every mbarrier wait is bounded in time and reports
+//     kStatusTimeout instead of hanging.
+#include <algorithm>
+
 #include "thq4_common.cuh"
 #include "thq4_internal.h"
 
@@ -58,186 +67,176 @@ constexpr int kConsumers = kSlabTiles;  // one consumer warp per tile of a slab
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kSgBytes = kSlabTiles * (kChunkBytes + kQuadBytes);  // 4608
 constexpr int kMaxStages = 8;
+constexpr uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u;
 
 struct GemvArgs {
   const uint8_t *qw0;  // gate (or the only) weight: frag nibbles
   const uint8_t *sb0;
   const uint8_t *qw1;  // up weight (gate/up only)
   const uint8_t *sb1;
-  const void *x;       // [m][in]
-  void *y;             // [m][out]
+  const void *x;       // [m][in], bf16 or f32
+  void *y;             // [m][out], bf16 or f32
   uint32_t *status;    // device status word
   float *part;         // workspace: partials [cta][2 sides][8 tiles][NS][32 lanes][4]
   uint32_t *count;     // workspace: arrivals per (slab, tile) (zero between calls)
-  long long sgs;       // slab-groups in the weight (slabs * ng)
-  int m;               // tokens in this launch
-  int in, ng, out;
-  int mcols;           // B columns in use: m (bf16 x) or 2m (f32 x)
+  long long chunks;    // slabs * cps: the units CTA runs are cut in
+  int cps;             // chunks per slab, ceil(ng / cb)
+  int m, in, ng, out;
+  int P;               // B columns in use: m (bf16 x) or 2m (f32 x)
+  int xf32, yf32;
   int stages;          // ring stages
-  int cb;              // slab-groups per stage
+  int xcap;            // activation groups staged per CTA
 };
 
-__host__ __device__ inline size_t xs_bytes(int ng, int mcols) { return (size_t)ng * 2 * mcols * 64; }
-__host__ __device__ inline size_t xsum_bytes(int ng) { return (size_t)ng * 8 * sizeof(float); }
+__host__ __device__ inline int colpairs(int P) { return (P + 1) / 2; }
+// fp16 B fragments [slot][P][2][4] x 16 B, a 128-byte zero block, then per
+// (slot, column pair) {xs0, xs1, f0, f1} and {off0, off1}
+__host__ __device__ inline size_t xstage_bytes(int xcap, int P) {
+  return (size_t)xcap * P * 128 + 128 + (size_t)xcap * colpairs(P) * 24;
+}
 __host__ __device__ inline size_t stage_bytes(int cb, bool gate_up) { return (size_t)(gate_up ? 2 : 1) * cb * kSgBytes; }
-__host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, int ng, int mcols) {
-  return 128 + (size_t)stages * stage_bytes(cb, gate_up) + xs_bytes(ng, mcols) + xsum_bytes(ng);
+__host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, int xcap, int P) {
+  return 128 + (size_t)stages * stage_bytes(cb, gate_up) + xstage_bytes(xcap, P);
 }
 // floats of one CTA side's partial: 8 tiles x NS x 32 lanes x 4
 __host__ __device__ inline int side_floats(bool gate_up) { return kSlabTiles * (gate_up ? 2 : 1) * 32 * 4; }
-__device__ __forceinline__ long long run_begin(long long i, long long total, long long parts) {
+__host__ __device__ inline long long run_begin(long long i, long long total, long long parts) {
   return i * total / parts;
 }
-// The run holding offset o (0 <= o < total): the largest i with
+// The run holding unit o (0 <= o < total): the largest i with
 // run_begin(i) <= o, which is never an empty run.
 __device__ __forceinline__ long long run_of(long long o, long long total, long long parts) {
   return ((o + 1) * parts + total - 1) / total - 1;
+}
+// slab-groups before chunk C
+__host__ __device__ inline long long sgs_before(long long C, int cps, int ng, int cb) {
+  const long long sl = C / cps;
+  const int cg = (int)(C - sl * cps);
+  return sl * ng + min(cg * cb, ng);
 }
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumers * 32) : "memory");
 }
 
-// ---- packed f32x2 arithmetic (sm_100) ---------------------------------------
-__device__ __forceinline__ uint64_t pk(float lo, float hi) {
-  uint64_t v;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
-  return v;
-}
-__device__ __forceinline__ void upk(uint64_t v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
-// Stage x into shared memory in B-fragment order (consumer warps only):
-// entry ((g*2 + h)*mcols + col)*4 + c (16 bytes) holds, for k-steps
-// j = 2h, 2h+1 of group g, the bf16 pairs {x[2c], x[2c+1]} and
-// {x[2c+8], x[2c+9]} (k relative to 64 g + 16 j) of B column col: token col
-// (bf16 x), or token col/2's hi (even col) or lo (odd col) part (f32 x).  One
-// thread builds one entry with one 16-byte store; the 8 threads holding
-// (g, col)'s 8 entries reduce the group sum xsum[g*8 + col] with a fixed
-// shuffle tree.  Columns >= mcols have sum 0.
-template <bool XF32>
-__device__ void stage_x(const GemvArgs &a, uint4 *xs4, float *xsum) {
+// Stage the activation groups [gs, gs + xcnt) (mod ng) of the m tokens into
+// shared memory (consumer warps only).  Fragment entry ((slot*P + q)*2 + h)*4
+// + c (16 bytes) holds, for k-steps 2h and 2h+1 of the group, the fp16 pairs
+// {x'[2c], x'[2c+1]}, {x'[2c+8], x'[2c+9]} (k relative to the k-step) of
+// column q: token q (bf16 x) or token q/2's hi (even q) or lo (odd q) part
+// (f32 x), with x' = x 2^-e.  The 8 threads of one (slot, q) reduce the
+// group's max |x| and sums with a fixed shuffle tree (deterministic).
+__device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float *mxf, float *moff) {
   const int tid = threadIdx.x, nthr = kConsumers * 32;
-  for (int i = tid; i < a.ng * 8; i += nthr)
-    if ((i & 7) >= a.mcols) xsum[i] = 0.0f;  // disjoint from the sums below
-  const int entries = a.ng * a.mcols * 8;   // (g, col, h, c)
+  const int P = a.P, CP = colpairs(P);
+  if (tid < 8) zero[tid] = make_uint4(0, 0, 0, 0);
+  if (P & 1)  // the unused column of the last pair contributes nothing
+    for (int i = tid; i < xcnt; i += nthr) {
+      const int e = i * CP + CP - 1;
+      mxf[e * 4 + 1] = 0.0f;
+      mxf[e * 4 + 3] = 0.0f;
+      moff[e * 2 + 1] = 0.0f;
+    }
+  const int entries = xcnt * P * 8;
   const int span = (entries + 31) / 32 * 32;
   for (int idx = tid; idx < span; idx += nthr) {
     const bool live = idx < entries;
     const int e = live ? idx : 0;
-    const int c = e & 3, h = (e >> 2) & 1, gc = e >> 3;
-    const int col = gc % a.mcols, g = gc / a.mcols;
-    const int t = XF32 ? col >> 1 : col, part = XF32 ? col & 1 : 0;
+    const int c = e & 3, h = (e >> 2) & 1, sq = e >> 3;
+    const int q = sq % P, slot = sq / P;
+    int g = gs + slot;
+    if (g >= a.ng) g -= a.ng;
+    const int t = a.xf32 ? q >> 1 : q, part = a.xf32 ? q & 1 : 0;
     float v[8];
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int k = g * 64 + 16 * (2 * h + jj) + 2 * c;
+    for (int vv = 0; vv < 8; ++vv) {
+      const int k = 16 * (2 * h + (vv >> 2)) + 2 * c + (vv & 1) + 8 * ((vv >> 1) & 1);
+      const size_t at = (size_t)t * a.in + (size_t)g * kGroup + k;
+      float xv = 0.0f;
+      if (live)
+        xv = a.xf32 ? static_cast<const float *>(a.x)[at]
+                    : __uint_as_float((uint32_t)static_cast<const uint16_t *>(a.x)[at] << 16);
+      v[vv] = xv;
+    }
+    float mx = 0.0f;
 #pragma unroll
-      for (int hi8 = 0; hi8 < 2; ++hi8) {
-        float p0 = 0.0f, p1 = 0.0f;
-        if (live) {
-          if constexpr (XF32) {
-            const float2 f = *reinterpret_cast<const float2 *>(static_cast<const float *>(a.x) + (size_t)t * a.in +
-                                                              k + 8 * hi8);
-            const float h0 = round_bf16(f.x), h1 = round_bf16(f.y);
-            p0 = part ? round_bf16(f.x - h0) : h0;
-            p1 = part ? round_bf16(f.y - h1) : h1;
-          } else {
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(static_cast<const uint16_t *>(a.x) +
-                                                                   (size_t)t * a.in + k + 8 * hi8);
-            p0 = __uint_as_float(w << 16);
-            p1 = __uint_as_float(w & 0xffff0000u);
-          }
-        }
-        v[jj * 4 + hi8 * 2] = p0;
-        v[jj * 4 + hi8 * 2 + 1] = p1;
-      }
+    for (int vv = 0; vv < 8; ++vv) mx = fmaxf(mx, fabsf(v[vv]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    // 2^e with the group max in [2^14, 2^15); e = 0 for an all-zero group
+    const int ex = (__float_as_int(mx) >> 23) & 0xff;
+    const int e2 = ex == 0 ? 0 : min(max(ex - 127 - 14, -110), 114);
+    const float dn = __int_as_float((127 - e2) << 23), f = __int_as_float((127 + e2) << 23);
+    uint32_t hv[4] = {0, 0, 0, 0};
+    float hf[8];
+#pragma unroll
+    for (int vv = 0; vv < 8; ++vv) {
+      const float xs = v[vv] * dn;
+      const __half hi = __float2half_rn(xs);
+      const __half val = part ? __float2half_rn(xs - __half2float(hi)) : hi;
+      hf[vv] = __half2float(val);
+      hv[vv >> 1] |= (uint32_t)__half_as_ushort(val) << (16 * (vv & 1));
     }
-    if (live) {
-      uint4 o;
-      o.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
-      o.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
-      o.z = (uint32_t)f32_to_bf16_bits(v[4]) | ((uint32_t)f32_to_bf16_bits(v[5]) << 16);
-      o.w = (uint32_t)f32_to_bf16_bits(v[6]) | ((uint32_t)f32_to_bf16_bits(v[7]) << 16);
-      xs4[((size_t)(g * 2 + h) * a.mcols + col) * 4 + c] = o;
+    if (live) xf[idx] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    // k-step 2h (lo chain) holds values 0..3, k-step 2h+1 (hi chain) 4..7
+    float slo = (hf[0] + hf[1]) + (hf[2] + hf[3]);
+    float shi = (hf[4] + hf[5]) + (hf[6] + hf[7]);
+    slo += __shfl_xor_sync(0xffffffffu, slo, 1);
+    shi += __shfl_xor_sync(0xffffffffu, shi, 1);
+    slo += __shfl_xor_sync(0xffffffffu, slo, 2);
+    shi += __shfl_xor_sync(0xffffffffu, shi, 2);
+    slo += __shfl_xor_sync(0xffffffffu, slo, 4);
+    shi += __shfl_xor_sync(0xffffffffu, shi, 4);
+    if (live && (idx & 7) == 0) {
+      const int pe = slot * CP + (q >> 1), w = q & 1;
+      mxf[pe * 4 + w] = f * (slo + shi);
+      mxf[pe * 4 + 2 + w] = f;
+      moff[pe * 2 + w] = 1024.0f * slo + 64.0f * shi;
     }
-    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    if (live && (idx & 7) == 0) xsum[g * 8 + col] = s;
   }
   consumer_sync();
 }
 
-// One tile-group's contribution: four mma.m16n8k16 (two independent chains,
-// started from a zero C) on the dequantised nibbles, then the per-group
-// scale / bias epilogue.  y[0..3] = rows (r, r, r+8, r+8) x columns (2c,
-// 2c+1, 2c, 2c+1); with ONE_COL only column 0 (m = 1, bf16 x) is kept.
-template <bool SF16, bool ONE_COL>
-__device__ __forceinline__ void gt_step(float (&y)[4], const uint4 w, const uint2 q, const uint4 xa, const uint4 xb,
-                                        const float2 xsm) {
-  float a0[4], a1[4];
-  mma_bf16_16816_z(a0, nib_bf16x2_mh(w.x, 0), nib_bf16x2_mh(w.x, 4), nib_bf16x2_mh(w.x, 8),
-                   nib_bf16x2_mh(w.x, 12), xa.x, xa.y);
-  mma_bf16_16816_z(a1, nib_bf16x2_mh(w.z, 0), nib_bf16x2_mh(w.z, 4), nib_bf16x2_mh(w.z, 8),
-                   nib_bf16x2_mh(w.z, 12), xb.x, xb.y);
-  mma_bf16_16816(a0, nib_bf16x2_mh(w.y, 0), nib_bf16x2_mh(w.y, 4), nib_bf16x2_mh(w.y, 8), nib_bf16x2_mh(w.y, 12),
-                 xa.z, xa.w);
-  mma_bf16_16816(a1, nib_bf16x2_mh(w.w, 0), nib_bf16x2_mh(w.w, 4), nib_bf16x2_mh(w.w, 8), nib_bf16x2_mh(w.w, 12),
-                 xb.z, xb.w);
-  const float sr = sb_to_f32<SF16>(q.x & 0xffffu), br = sb_to_f32<SF16>(q.x >> 16);
-  const float sr8 = sb_to_f32<SF16>(q.y & 0xffffu), br8 = sb_to_f32<SF16>(q.y >> 16);
-  const float bpr = fmaf(-128.0f, sr, br), bpr8 = fmaf(-128.0f, sr8, br8);
-  y[0] = fmaf(sr, a1[0], fmaf(sr, a0[0], fmaf(bpr, xsm.x, y[0])));
-  y[2] = fmaf(sr8, a1[2], fmaf(sr8, a0[2], fmaf(bpr8, xsm.x, y[2])));
-  if constexpr (!ONE_COL) {
-    y[1] = fmaf(sr, a1[1], fmaf(sr, a0[1], fmaf(bpr, xsm.y, y[1])));
-    y[3] = fmaf(sr8, a1[3], fmaf(sr8, a0[3], fmaf(bpr8, xsm.y, y[3])));
-  }
-}
-
-// Final values of one 16-row tile; gate/up combines streams 0 and 1.
-template <bool XF32, bool GATE_UP, bool YF32>
+// Final values of one 16-row tile from lanes holding reduced column pairs;
+// gate/up combines streams 0 and 1.
+template <int GW, bool GATE_UP>
 __device__ __forceinline__ void store_tile(const GemvArgs &a, int rt, int lane, const float *y0, const float *y1) {
+  constexpr int LPJ = 4 / GW;
   const int r = lane >> 2, c = lane & 3;
+  if (c >= LPJ) return;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int row = rt * 16 + r + 8 * half;
     if (row >= a.out) continue;
-    if constexpr (XF32) {
-      const int t = c;  // columns 2c (hi) and 2c+1 (lo) are the parts of token c
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      int t;
+      float v, u = 0.0f;
+      if (a.xf32) {  // columns 2c (hi) and 2c + 1 (lo) are the parts of token c
+        if (e) break;
+        t = c;
+        v = y0[2 * half] + y0[2 * half + 1];
+        if (GATE_UP) u = y1[2 * half] + y1[2 * half + 1];
+      } else {
+        t = 2 * c + e;
+        v = y0[2 * half + e];
+        if (GATE_UP) u = y1[2 * half + e];
+      }
       if (t >= a.m) continue;
-      float v = y0[2 * half] + y0[2 * half + 1];
-      if constexpr (GATE_UP) v = silu_mul(v, y1[2 * half] + y1[2 * half + 1]);
-      if constexpr (YF32)
+      if constexpr (GATE_UP) v = silu_mul(v, u);
+      if (a.yf32)
         static_cast<float *>(a.y)[(size_t)t * a.out + row] = v;
       else
         static_cast<uint16_t *>(a.y)[(size_t)t * a.out + row] = f32_to_bf16_bits(v);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = 2 * c + e;
-        if (t >= a.m) continue;
-        float v = y0[2 * half + e];
-        if constexpr (GATE_UP) v = silu_mul(v, y1[2 * half + e]);
-        if constexpr (YF32)
-          static_cast<float *>(a.y)[(size_t)t * a.out + row] = v;
-        else
-          static_cast<uint16_t *>(a.y)[(size_t)t * a.out + row] = f32_to_bf16_bits(v);
-      }
     }
   }
 }
 
-template <int CB, bool ONE_COL, bool XF32, bool SF16, bool GATE_UP, bool YF32>
+template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr int NS = GATE_UP ? 2 : 1;
+  constexpr int CPG = 8 / GW;  // B columns per window position
+  constexpr int LPJ = 4 / GW;  // lanes (c) per window position
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int R = a.stages;
@@ -245,13 +244,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
   unsigned char *ring = smem + 128;
-  unsigned char *tail = ring + (size_t)R * SB;
-  uint4 *xs4 = reinterpret_cast<uint4 *>(tail);
-  float *xsum = reinterpret_cast<float *>(tail + xs_bytes(a.ng, a.mcols));
+  unsigned char *xt = ring + (size_t)R * SB;
+  const int P = a.P, CP = colpairs(P);
+  uint4 *xf = reinterpret_cast<uint4 *>(xt);
+  uint4 *zero = reinterpret_cast<uint4 *>(xt + (size_t)a.xcap * P * 128);
+  float *mxf = reinterpret_cast<float *>(xt + (size_t)a.xcap * P * 128 + 128);
+  float *moff = mxf + (size_t)a.xcap * CP * 4;
 
-  // this CTA's run of slab-groups, in chunks of CB
-  const long long F0 = run_begin(blockIdx.x, a.sgs, gridDim.x), F1 = run_begin(blockIdx.x + 1, a.sgs, gridDim.x);
-  const int nch = (int)((F1 - F0 + CB - 1) / CB);
+  // this CTA's run of chunks
+  const long long C0 = run_begin(blockIdx.x, a.chunks, gridDim.x), C1 = run_begin(blockIdx.x + 1, a.chunks, gridDim.x);
+  const int nch = (int)(C1 - C0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; ++s) {
@@ -276,15 +278,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
           if (k >= 0) (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
         return;
       }
-      const long long fb = F0 + (long long)n * CB;
-      const int cnt = (int)min((long long)CB, F1 - fb);
+      const long long C = C0 + n;
+      const long long sl = C / a.cps;
+      const int g0c = (int)(C - sl * a.cps) * CB, cnt = min(CB, a.ng - g0c);
+      const long long sg = sl * a.ng + g0c;
       unsigned char *dst = ring + (size_t)s * SB;
       mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
-      bulk_g2s(dst, a.qw0 + fb * 4096, cnt * 4096, &full[s], pol);
-      bulk_g2s(dst + (size_t)NS * CB * 4096, a.sb0 + fb * 512, cnt * 512, &full[s], pol);
+      bulk_g2s(dst, a.qw0 + sg * 4096, cnt * 4096, &full[s], pol);
+      bulk_g2s(dst + (size_t)NS * CB * 4096, a.sb0 + sg * 512, cnt * 512, &full[s], pol);
       if constexpr (GATE_UP) {
-        bulk_g2s(dst + (size_t)CB * 4096, a.qw1 + fb * 4096, cnt * 4096, &full[s], pol);
-        bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, a.sb1 + fb * 512, cnt * 512, &full[s], pol);
+        bulk_g2s(dst + (size_t)CB * 4096, a.qw1 + sg * 4096, cnt * 4096, &full[s], pol);
+        bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, a.sb1 + sg * 512, cnt * 512, &full[s], pol);
       }
     }
     // the consumers wait for every chunk before they release it
@@ -292,90 +296,117 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   }
 
   // ---- consumers: warp `warp` owns tile `warp` of every slab-group ----------
-  const int r = lane >> 2, c = lane & 3;
   pdl_wait();
-  stage_x<XF32>(a, xs4, xsum);
-  const bool col_live = r < a.mcols;
-  // this lane's B-fragment entries and group sums, advanced per group
-  const int xstride = 2 * a.mcols * 4;  // uint4 entries per group
-  const uint4 *xl = xs4 + r * 4 + c;
-  const float *xsl = xsum + 2 * c;
+  const int gs = (int)(C0 % a.cps) * CB;
+  const int xcnt =
+      (int)min((long long)a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
+  stage_x(a, gs, xcnt, xf, zero, mxf, moff);
 
-  float y[NS][4], yfirst[NS][4];
-#pragma unroll
-  for (int s = 0; s < NS; ++s)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) y[s][e] = yfirst[s][e] = 0.0f;
-  int slab = (int)(F0 / a.ng), g = (int)(F0 % a.ng);
-  long long seg0 = F0;
-  bool have_first = false;
-  int first_slab = slab;
+  const int r = lane >> 2, c = lane & 3;
+  const int jr = r / CPG, qr = r % CPG;  // this lane's B column: window position jr, column qr
+  const bool bq = qr < P;
+  const int jc = c / LPJ, cp = c % LPJ;  // this lane's D columns 2c, 2c+1: position jc, pair cp
+  const bool colv = 2 * cp < P;
+  const int cpv = min(cp, CP - 1);
+  auto slot_of = [&](int g) { return g >= gs ? g - gs : g + a.ng - gs; };
 
-  auto step = [&](const unsigned char *wq_u, const unsigned char *sb_u, int gg) {
-    uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-    if (col_live) {
-      xa = xl[(size_t)gg * xstride];
-      xb = xl[(size_t)gg * xstride + a.mcols * 4];
+  float lo[NS][4], hi[NS][4], y[NS][4];
+  uint2 sc[NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    sc[s] = make_uint2(0, 0);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) lo[s][e] = hi[s][e] = y[s][e] = 0.0f;
+  }
+  int wlo = -1, whi = 0, wbase = 0;  // open window: first / last position, its group 0
+  bool seg_whole = (C0 % a.cps) == 0;  // the current slab segment began at the slab's start
+  bool finished_any = false;
+
+  auto open_window = [&](int g, int j) {
+    wbase = g - j;
+    wlo = j;
+    const int gl = wbase + jc;
+    float o0 = 0.0f, o1 = 0.0f;
+    // a lane whose group lies outside this run's staged groups keeps 0 (it
+    // is not processed here, and close_window skips it)
+    const int gsl = gl < a.ng ? slot_of(gl) : xcnt;
+    if (colv && jc >= j && gsl < xcnt) {
+      const float2 o = *reinterpret_cast<const float2 *>(moff + (size_t)(gsl * CP + cpv) * 2);
+      o0 = o.x;
+      o1 = o.y;
     }
-    const float2 xsm = *reinterpret_cast<const float2 *>(xsl + gg * 8);
 #pragma unroll
-    for (int si = 0; si < NS; ++si) {
-      const uint4 w = *reinterpret_cast<const uint4 *>(wq_u + (size_t)si * CB * 4096);
-      const uint2 q = *reinterpret_cast<const uint2 *>(sb_u + (size_t)si * CB * 512);
-      gt_step<SF16, ONE_COL>(y[si], w, q, xa, xb, xsm);
+    for (int s = 0; s < NS; ++s) {
+      lo[s][0] = -o0, lo[s][1] = -o1, lo[s][2] = -o0, lo[s][3] = -o1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hi[s][e] = 0.0f;
     }
   };
-
-  long long f = F0;
-  for (int n = 0; n < nch; ++n) {
-    const int s = n % R;
-    if (!mbar_wait_bounded(&full[s], (uint32_t)((n / R) & 1), kWaitLimitNs)) {
-      // the producer then times out on this stage's release and stops;
-      // outputs of this call are undefined and the status word says so
-      raise_status(a.status, kStatusTimeout);
-      return;
+  auto group = [&](const unsigned char *nib, const unsigned char *scl, int u, int g, int j) {
+    const uint4 *bp = (jr == j && bq) ? xf + ((size_t)slot_of(g) * P + qr) * 8 + c : zero + c;
+    const uint4 xa = bp[0], xb = bp[4];
+    if (jc == j) {
+#pragma unroll
+      for (int s = 0; s < NS; ++s)
+        sc[s] = *reinterpret_cast<const uint2 *>(scl + (size_t)(s * CB + u) * 512 + warp * 64 + r * 8);
     }
-    const unsigned char *stw = ring + (size_t)s * SB + warp * 512 + lane * 16;
-    const unsigned char *sts = ring + (size_t)s * SB + (size_t)NS * CB * 4096 + warp * 64 + r * 8;
-    const int cnt = (int)min((long long)CB, F1 - f);
-    if (cnt == CB && a.ng - g > CB) {
-      // no slab boundary in this chunk
 #pragma unroll
-      for (int u = 0; u < CB; ++u) step(stw + u * 4096, sts + u * 512, g + u);
-      g += CB;
-      f += CB;
-    } else {
-      for (int u = 0; u < cnt; ++u, ++f) {
-        step(stw + u * 4096, sts + u * 512, g);
-        if (++g == a.ng) {  // slab boundary
-          const long long s0 = (long long)slab * a.ng;
-          if (seg0 == s0) {
-            store_tile<XF32, GATE_UP, YF32>(a, slab * kSlabTiles + warp, lane, y[0], y[NS - 1]);
-          } else {  // the run's first segment, partial: kept for the hand-over
-            have_first = true;
-            first_slab = slab;
+    for (int s = 0; s < NS; ++s) {
+      const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(s * CB + u) * 4096 + warp * 512 + lane * 16);
+      const uint32_t t0 = w.x >> 8, t1 = w.y >> 8, t2 = w.z >> 8, t3 = w.w >> 8;
+      mma_f16_16816(lo[s], nib_f16x2<kLoMask>(w.x), nib_f16x2<kLoMask>(t0), nib_f16x2<kLoMask>(w.y),
+                    nib_f16x2<kLoMask>(t1), xa.x, xa.y);
+      mma_f16_16816(hi[s], nib_f16x2<kHiMask>(w.x), nib_f16x2<kHiMask>(t0), nib_f16x2<kHiMask>(w.y),
+                    nib_f16x2<kHiMask>(t1), xa.z, xa.w);
+      mma_f16_16816(lo[s], nib_f16x2<kLoMask>(w.z), nib_f16x2<kLoMask>(t2), nib_f16x2<kLoMask>(w.w),
+                    nib_f16x2<kLoMask>(t3), xb.x, xb.y);
+      mma_f16_16816(hi[s], nib_f16x2<kHiMask>(w.z), nib_f16x2<kHiMask>(t2), nib_f16x2<kHiMask>(w.w),
+                    nib_f16x2<kHiMask>(t3), xb.z, xb.w);
+    }
+    whi = j;
+  };
+  auto close_window = [&]() {
+    const int gl = wbase + jc;
+    const bool valid = colv && jc >= wlo && jc <= whi;
+    float4 xm = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (valid) xm = *reinterpret_cast<const float4 *>(mxf + (size_t)(slot_of(gl) * CP + cpv) * 4);
 #pragma unroll
-            for (int si = 0; si < NS; ++si)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) yfirst[si][e] = y[si][e];
-          }
-#pragma unroll
-          for (int si = 0; si < NS; ++si)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) y[si][e] = 0.0f;
-          g = 0;
-          ++slab;
-          seg0 = f + 1;
+    for (int s = 0; s < NS; ++s) {
+      const float sr = sb_to_f32<SF16>(sc[s].x & 0xffffu), br = sb_to_f32<SF16>(sc[s].x >> 16);
+      const float s8 = sb_to_f32<SF16>(sc[s].y & 0xffffu), b8 = sb_to_f32<SF16>(sc[s].y >> 16);
+      if (valid) {
+        y[s][0] = fmaf(sr * xm.z, fmaf(hi[s][0], 0.0625f, lo[s][0]), fmaf(br, xm.x, y[s][0]));
+        y[s][2] = fmaf(s8 * xm.z, fmaf(hi[s][2], 0.0625f, lo[s][2]), fmaf(b8, xm.x, y[s][2]));
+        if constexpr (!ONE) {
+          y[s][1] = fmaf(sr * xm.w, fmaf(hi[s][1], 0.0625f, lo[s][1]), fmaf(br, xm.y, y[s][1]));
+          y[s][3] = fmaf(s8 * xm.w, fmaf(hi[s][3], 0.0625f, lo[s][3]), fmaf(b8, xm.y, y[s][3]));
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
+    wlo = -1;
+  };
+  // lanes of one column pair but different window positions hold disjoint
+  // groups of the same outputs: add them (every such lane gets the same sum)
+  auto reduce_y = [&]() {
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = y[s][e];
+        if constexpr (GW == 4) {
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+        } else if constexpr (GW == 2) {
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+        }
+        y[s][e] = v;
+      }
+  };
 
   // The run's partial slabs: its first (if it began inside a slab) and its
-  // last (if it ended inside one).  Publish this CTA's part; the CTA that
-  // arrives last adds every part in CTA order and stores the tile.
+  // last (if it ended inside one).  Publish this CTA's part (side 0: the
+  // run's first segment, side 1: its last); the CTA that arrives last adds
+  // every part in CTA order and stores the tile.
   auto hand_over = [&](int sl, int side, float (&v)[NS][4]) {
     float *gslot = a.part + (((size_t)blockIdx.x * 2 + side) * kSlabTiles + warp) * (NS * 128) + lane * 4;
 #pragma unroll
@@ -384,11 +415,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       for (int e = 0; e < 4; ++e) gslot[si * 128 + e] = v[si][e];
     __threadfence();
     __syncwarp();
-    const long long t0 = (long long)sl * a.ng, t1 = t0 + a.ng;
-    const long long clo = run_of(t0, a.sgs, gridDim.x), chi = run_of(t1 - 1, a.sgs, gridDim.x);
+    const long long t0 = (long long)sl * a.cps, t1 = t0 + a.cps;
+    const long long clo = run_of(t0, a.chunks, gridDim.x), chi = run_of(t1 - 1, a.chunks, gridDim.x);
     uint32_t old = 0;
-    uint32_t *cnt = &a.count[(size_t)sl * kSlabTiles + warp];
-    if (lane == 0) old = atomicAdd(cnt, 1u);
+    uint32_t *cntp = &a.count[(size_t)sl * kSlabTiles + warp];
+    if (lane == 0) old = atomicAdd(cntp, 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old + 1 != (uint32_t)(chi - clo + 1)) return;
     __threadfence();
@@ -398,25 +429,86 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[si][e] = 0.0f;
     for (long long q = clo; q <= chi; ++q) {
-      const int qs = (q == clo && run_begin(q, a.sgs, gridDim.x) < t0) ? 1 : 0;
+      const int qs = (q == clo && run_begin(q, a.chunks, gridDim.x) < t0) ? 1 : 0;
       const volatile float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
 #pragma unroll
       for (int si = 0; si < NS; ++si)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[si][e] += src[si * 128 + e];
     }
-    if (lane == 0) *cnt = 0;  // ready for the next call
-    store_tile<XF32, GATE_UP, YF32>(a, sl * kSlabTiles + warp, lane, acc[0], acc[NS - 1]);
+    if (lane == 0) *cntp = 0;  // ready for the next call
+    store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, acc[0], acc[NS - 1]);
   };
-  if (have_first) hand_over(first_slab, 0, yfirst);
-  // a last segment that did not end on a slab boundary (it is also the first
-  // segment when the whole run lies inside one slab)
-  if (F1 > F0 && seg0 < F1) hand_over(slab, seg0 == F0 ? 0 : 1, y);
+  for (int n = 0; n < nch; ++n) {
+    const int s = n % R;
+    if (!mbar_wait_bounded(&full[s], (uint32_t)((n / R) & 1), kWaitLimitNs)) {
+      // the producer then times out on this stage's release and stops;
+      // outputs of this call are undefined and the status word says so
+      raise_status(a.status, kStatusTimeout);
+      return;
+    }
+    const long long C = C0 + n;
+    const int sl = (int)(C / a.cps), cg = (int)(C - (long long)sl * a.cps);
+    const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
+    const unsigned char *nib = ring + (size_t)s * SB;
+    const unsigned char *scl = nib + (size_t)NS * CB * 4096;
+    if (cnt == CB) {
+      if constexpr (CB >= GW) {
+        // chunks are window-aligned: positions are compile-time
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+          if (u % GW == 0) open_window(g0c + u, 0);
+          group(nib, scl, u, g0c + u, u % GW);
+          if (u % GW == GW - 1) close_window();
+        }
+      } else {  // two-group chunks of a four-group window
+        if ((g0c & 3) == 0) {
+          open_window(g0c, 0);
+          group(nib, scl, 0, g0c, 0);
+          group(nib, scl, 1, g0c + 1, 1);
+        } else {
+          if (wlo < 0) open_window(g0c, 2);
+          group(nib, scl, 0, g0c, 2);
+          group(nib, scl, 1, g0c + 1, 3);
+          close_window();
+        }
+      }
+    } else {
+      for (int u = 0; u < cnt; ++u) {
+        const int g = g0c + u, j = g % GW;
+        if (wlo < 0) open_window(g, j);
+        group(nib, scl, u, g, j);
+        if (j == GW - 1) close_window();
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (cg == a.cps - 1) {  // slab end
+      if (wlo >= 0) close_window();
+      reduce_y();
+      if (seg_whole)
+        store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, y[0], y[NS - 1]);
+      else  // the run's first segment, partial
+        hand_over(sl, 0, y);
+#pragma unroll
+      for (int si = 0; si < NS; ++si)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[si][e] = 0.0f;
+      seg_whole = true;
+      finished_any = true;
+    }
+  }
+
+  if (nch > 0 && C1 % a.cps != 0) {  // the run ended inside a slab
+    if (wlo >= 0) close_window();
+    reduce_y();
+    hand_over((int)((C1 - 1) / a.cps), finished_any ? 1 : 0, y);
+  }
 }
 
-template <int CB, bool ONE_COL, bool XF32, bool SF16, bool GATE_UP, bool YF32>
+template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
 cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t stream) {
-  auto *k = &gemv_kernel<CB, ONE_COL, XF32, SF16, GATE_UP, YF32>;
+  auto *k = &gemv_kernel<CB, GW, ONE, SF16, GATE_UP>;
   static DeviceOnce once;
   cudaError_t e = once.run([&] {
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
@@ -435,28 +527,24 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
   return cudaLaunchKernelEx(&cfg, k, a);
 }
 
-template <bool XF32, bool SF16>
-cudaError_t dispatch(const GemvArgs &a, bool gate_up, bool yf32, int grid, size_t smem, cudaStream_t s) {
-  // chunk of slab-groups per stage: 2 per stream for gate/up, 4 otherwise
-  // (a forced 1, 2 or 4 is honoured for the plain projection)
-  if (gate_up)
-    return yf32 ? launch_one<2, false, XF32, SF16, true, true>(a, grid, smem, s)
-                : launch_one<2, false, XF32, SF16, true, false>(a, grid, smem, s);
-  const bool one = !XF32 && a.mcols == 1;
-#define THQ4_PLAIN(CB_)                                                                         \
-  if (a.cb == CB_) {                                                                            \
-    if (one)                                                                                    \
-      return yf32 ? launch_one<CB_, true, XF32, SF16, false, true>(a, grid, smem, s)            \
-                  : launch_one<CB_, true, XF32, SF16, false, false>(a, grid, smem, s);          \
-    return yf32 ? launch_one<CB_, false, XF32, SF16, false, true>(a, grid, smem, s)             \
-                : launch_one<CB_, false, XF32, SF16, false, false>(a, grid, smem, s);           \
-  }
-  THQ4_PLAIN(4)
-  THQ4_PLAIN(2)
-  THQ4_PLAIN(1)
-#undef THQ4_PLAIN
-  return cudaErrorInvalidValue;
+template <int CB, bool SF16, bool GATE_UP>
+cudaError_t dispatch_gw(const GemvArgs &a, int gw, int grid, size_t smem, cudaStream_t s) {
+  if (gw == 4)
+    return a.P == 1 ? launch_one<CB, 4, true, SF16, GATE_UP>(a, grid, smem, s)
+                    : launch_one<CB, 4, false, SF16, GATE_UP>(a, grid, smem, s);
+  if (gw == 2) return launch_one<CB, 2, false, SF16, GATE_UP>(a, grid, smem, s);
+  return launch_one<CB, 1, false, SF16, GATE_UP>(a, grid, smem, s);
 }
+
+template <bool SF16>
+cudaError_t dispatch(const GemvArgs &a, bool gate_up, int cb, int gw, int grid, size_t smem, cudaStream_t s) {
+  if (gate_up)
+    return cb == 4 ? dispatch_gw<4, SF16, true>(a, gw, grid, smem, s) : dispatch_gw<2, SF16, true>(a, gw, grid, smem, s);
+  return cb == 4 ? dispatch_gw<4, SF16, false>(a, gw, grid, smem, s)
+                 : dispatch_gw<2, SF16, false>(a, gw, grid, smem, s);
+}
+
+int window_groups(int P) { return P <= 2 ? 4 : (P <= 4 ? 2 : 1); }
 
 }  // namespace
 
@@ -470,51 +558,49 @@ size_t gemv_workspace_bytes(int rows) {
 
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
   GemvPlan p{};
+  p.ok = false;
   const int ng = in / kGroup;
   const int sms = device_sm_count();
   const GemvCfg cfg = gemv_cfg_override();
+  const int cb = cfg.warps > 0 ? cfg.warps : (gate_up ? 2 : 4);
+  const int cps = (ng + cb - 1) / cb;
+  const long long chunks = (long long)row_slabs(out) * cps;
   int per = x_f32 ? 4 : 8;  // tokens per launch: 8 B columns, two per f32 token
   if (per > m) per = m;
-  const long long sgs = (long long)row_slabs(out) * ng;
-  // ~16 KB of nibbles per stage: 4 slab-groups, or 2 per stream for gate/up
-  const int cb = gate_up ? 2 : (cfg.warps > 0 ? cfg.warps : 4);
-  p.ok = false;
-  int per_sm = 2;
   for (;;) {
-    const int mcols = x_f32 ? 2 * per : per;
-    int st = 0;
-    if (cfg.depth > 0) {
-      if (gemv_smem(cfg.depth, cb, gate_up, ng, mcols) <= (size_t)kGemvMaxSmem) st = cfg.depth;
-      per_sm = st && gemv_smem(st, cb, gate_up, ng, mcols) <= (size_t)kGemvHalfSmem ? 2 : 1;
-    } else {
-      // two CTAs per SM with the deepest ring that fits half an SM (up to 6),
-      // else one CTA per SM
-      for (int t = 6; t >= 2 && !st; --t)
-        if (gemv_smem(t, cb, gate_up, ng, mcols) <= (size_t)kGemvHalfSmem) st = t;
-      per_sm = 2;
-      if (!st) {
-        per_sm = 1;
-        for (int t = kMaxStages; t >= 2 && !st; --t)
-          if (gemv_smem(t, cb, gate_up, ng, mcols) <= (size_t)kGemvMaxSmem) st = t;
+    const int P = x_f32 ? 2 * per : per;
+    for (int per_sm = 2; per_sm >= 1 && !p.ok; --per_sm) {
+      long long grid = cfg.grid > 0 ? cfg.grid : (long long)sms * per_sm;
+      if (grid > (long long)sms * 2) grid = (long long)sms * 2;
+      if (chunks < grid) grid = chunks;  // every CTA run holds at least one chunk
+      const long long max_run = (chunks + grid - 1) / grid;
+      const int xcap = (int)std::min<long long>(ng, max_run * cb);
+      const size_t limit = per_sm == 2 ? (size_t)kGemvHalfSmem : (size_t)kGemvMaxSmem;
+      int st = 0;
+      if (cfg.depth > 0) {
+        if (gemv_smem(cfg.depth, cb, gate_up, xcap, P) <= limit) st = cfg.depth;
+      } else {
+        for (int t = per_sm == 2 ? 6 : kMaxStages; t >= 2 && !st; --t)
+          if (gemv_smem(t, cb, gate_up, xcap, P) <= limit) st = t;
+      }
+      if (st) {
+        p.ok = true;
+        p.stages = st;
+        p.grid = (int)grid;
+        p.xcap = xcap;
+        p.smem = gemv_smem(st, cb, gate_up, xcap, P);
       }
     }
-    if (st) {
-      p.ok = true;
-      p.stages = st;
-      p.smem = gemv_smem(st, cb, gate_up, ng, mcols);
-      break;
-    }
-    if (per == 1) break;
+    if (p.ok) break;
+    if (per == 1) return p;
     per = (per + 1) / 2;
   }
-  long long grid = cfg.grid > 0 ? cfg.grid : (long long)sms * per_sm;
-  if (grid > (long long)sms * 2) grid = (long long)sms * 2;
-  if (sgs < grid) grid = sgs;  // every CTA run holds at least one slab-group
-  p.grid = (int)grid;
   p.threads = kThreads;
-  p.pieces = (int)grid;
+  p.pieces = p.grid;
   p.tokens_per_pass = per;
   p.ch = cb;
+  p.cps = cps;
+  p.chunks = chunks;
   return p;
 }
 
@@ -524,7 +610,6 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
   const GemvPlan p = gemv_plan(w0.out, w0.in, m, x_f32, gate_up);
   if (!p.ok) return cudaErrorInvalidConfiguration;
   const int xb = x_f32 ? 4 : 2, yb = y_f32 ? 4 : 2;
-  const int ng = w0.in / kGroup;
   const size_t part_bytes =
       gemv_workspace_bytes(w0.out) - ((size_t)row_slabs(w0.out) * kSlabTiles * 4 + 255) / 256 * 256;
   for (int t0 = 0; t0 < m; t0 += p.tokens_per_pass) {
@@ -539,23 +624,22 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     a.status = status_word();
     a.part = static_cast<float *>(workspace);
     a.count = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + part_bytes);
-    a.sgs = (long long)row_slabs(w0.out) * ng;
+    a.chunks = p.chunks;
+    a.cps = p.cps;
     a.m = mt;
     a.in = w0.in;
-    a.ng = ng;
+    a.ng = w0.in / kGroup;
     a.out = w0.out;
-    a.mcols = x_f32 ? 2 * mt : mt;
+    a.P = x_f32 ? 2 * mt : mt;
+    a.xf32 = x_f32 ? 1 : 0;
+    a.yf32 = y_f32 ? 1 : 0;
     a.stages = p.stages;
-    a.cb = p.ch;
-    const size_t smem = gemv_smem(p.stages, p.ch, gate_up, ng, a.mcols);
-    const bool f16 = w0.sb_dtype == THQ4_F16;
-    cudaError_t e;
-    if (x_f32)
-      e = f16 ? dispatch<true, true>(a, gate_up, y_f32, p.grid, smem, stream)
-              : dispatch<true, false>(a, gate_up, y_f32, p.grid, smem, stream);
-    else
-      e = f16 ? dispatch<false, true>(a, gate_up, y_f32, p.grid, smem, stream)
-              : dispatch<false, false>(a, gate_up, y_f32, p.grid, smem, stream);
+    a.xcap = p.xcap;
+    // a last pass with fewer tokens fits in the footprint planned for more
+    const size_t smem = gemv_smem(p.stages, p.ch, gate_up, p.xcap, a.P);
+    const int gw = window_groups(a.P);
+    const cudaError_t e = w0.sb_dtype == THQ4_F16 ? dispatch<true>(a, gate_up, p.ch, gw, p.grid, smem, stream)
+                                                  : dispatch<false>(a, gate_up, p.ch, gw, p.grid, smem, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

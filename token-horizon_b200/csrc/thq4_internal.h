@@ -47,7 +47,7 @@ uint32_t *status_word();
 
 // ---- GEMV / verify ---------------------------------------------------------
 struct GemvCfg {
-  int warps = 0;  // forced slab-groups per ring stage (0 = policy)
+  int warps = 0;  // forced slab-groups per ring stage, 2 or 4 (0 = policy)
   int depth = 0;  // forced ring stages (0 = policy)
   int grid = 0;   // forced CTAs (0 = policy)
 };
@@ -57,6 +57,8 @@ GemvCfg gemv_cfg_override();
 struct GemvPlan {
   bool ok;
   int threads, grid, pieces, tokens_per_pass, ch, stages;
+  int cps, xcap;     // chunks per slab, activation groups staged per CTA
+  long long chunks;  // chunks in the weight
   size_t smem;
 };
 // Workspace the decode/verify kernel needs for a weight of `rows` rows:

@@ -88,12 +88,8 @@ __global__ void repack_kernel(const RepackArgs a) {
   for (int j = 0; j < 4; ++j) {
     uint32_t word = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int k = 16 * j + 2 * c + 8 * (i >> 1) + h;
-        word |= nib(i & 1, k) << (16 * h + 4 * i);
-      }
+    for (int i = 0; i < 8; ++i)
+      word |= nib((i >> 1) & 1, frag_k(j, i, c)) << (4 * i);
     out[j] = word;
   }
   reinterpret_cast<uint4 *>(a.dq)[tid] = make_uint4(out[0], out[1], out[2], out[3]);
@@ -119,24 +115,21 @@ __global__ void dequant_kernel(const uint32_t *qw, const uint16_t *sb, int out, 
   if (tid >= (size_t)out * kb8) return;
   const int n = (int)(tid / kb8), k0 = (int)(tid % kb8) * 8;
   const int slab = n / kSlabRows, t = (n % kSlabRows) / kTileRows, rr = n % kTileRows, r = rr % 8, irow = rr / 8;
-  const int g = k0 / 64, kk = k0 % 64, j = kk / 16, ik = (kk % 16) / 8;
+  // eight consecutive k share the word (j) and the nibble row-half; element
+  // pair (2c', 2c'+1) sits at bits 4i and 4i+16 of lane column c'
+  const int g = k0 / 64, kk = k0 % 64, j = 2 * ((kk >> 5) & 1) + ((kk >> 3) & 1);
+  const int i = ((kk >> 4) & 1) + 2 * irow;
   const size_t chunk = ((size_t)slab * ng + g) * kSlabTiles + t;
   const uint2 quad = reinterpret_cast<const uint2 *>(sb)[chunk * 8 + r];
   const uint32_t qd = irow ? quad.y : quad.x;
   const float s = sb_to_f32<SF16>(qd & 0xffffu), b = sb_to_f32<SF16>(qd >> 16);
-  const int i = irow + 2 * ik;
   uint32_t o[4];
 #pragma unroll
-  for (int e = 0; e < 8; e += 2) {
-    float v[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = e / 2;  // (k % 16 within the half-step) / 2
-      const uint32_t word = qw[(chunk * 32 + 4 * r + c) * 4 + j];
-      const uint32_t q = (word >> (16 * h + 4 * i)) & 0xFu;
-      v[h] = fmaf((float)q, s, b);
-    }
-    o[e / 2] = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+  for (int cc = 0; cc < 4; ++cc) {
+    const uint32_t word = qw[(chunk * 32 + 4 * r + cc) * 4 + j];
+    const float v0 = fmaf((float)((word >> (4 * i)) & 0xFu), s, b);
+    const float v1 = fmaf((float)((word >> (4 * i + 16)) & 0xFu), s, b);
+    o[cc] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
   }
   y[tid] = make_uint4(o[0], o[1], o[2], o[3]);
 }
