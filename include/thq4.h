@@ -163,7 +163,7 @@ thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);
 
 /* ---- testing hooks -------------------------------------------------------
  * Forces the decode/verify kernel's launch shape for every later call in this
- * process: slab-groups per streamed stage (2 or 4), stages in the
+ * process: slab-groups per streamed stage (4 or 8), stages in the
  * shared-memory ring (2 .. 8) and CTAs in the grid (1 .. 2x SM count); 0
  * leaves a field to the policy, all zeros restore it.  The reference's tests
  * run every instantiated tile config the same way (qwen35.rs:6963-6989).

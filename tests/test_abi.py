@@ -107,6 +107,7 @@ def test_linear_requires_workspace():
 def test_debug_hook_validation():
     assert thq4.lib().thq4_debug_set_gemv(3, 0, 0, 0) == _lib.ERR_INVALID_ARGUMENT
     assert thq4.lib().thq4_debug_set_gemv(1, 0, 0, 0) == _lib.ERR_INVALID_ARGUMENT
+    assert thq4.lib().thq4_debug_set_gemv(2, 0, 0, 0) == _lib.ERR_INVALID_ARGUMENT
     assert thq4.lib().thq4_debug_set_gemv(0, 9, 0, 0) == _lib.ERR_INVALID_ARGUMENT
     assert thq4.lib().thq4_debug_set_gemv(0, 0, 0, 1) == _lib.ERR_INVALID_ARGUMENT
     assert thq4.lib().thq4_debug_set_gemv(0, 0, 0, 0) == _lib.OK

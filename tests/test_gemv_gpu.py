@@ -16,7 +16,7 @@ from helpers import assert_close_ref, assert_gate_up_close, assert_rms_close, de
 pytestmark = pytest.mark.gpu
 
 # (slab-groups per stage, ring stages, CTAs; 0 = policy)
-SPLITS = [(0, 0, 0), (2, 2, 0), (2, 6, 0), (4, 3, 7), (2, 8, 0), (4, 2, 3), (4, 4, 1), (2, 3, 296)]
+SPLITS = [(0, 0, 0), (4, 2, 0), (8, 3, 0), (4, 3, 7), (4, 6, 0), (8, 2, 3), (4, 4, 1), (4, 3, 296)]
 
 
 @pytest.fixture(autouse=True)
@@ -223,7 +223,7 @@ def test_tiny_and_ragged_weights(out, inp):
     xb = O.rand_x(inp, 3)
     want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(xb))[0]
     q = _qlin(wq, sb)
-    for chunk, stages, grid in [(0, 0, 0), (2, 2, 0), (4, 5, 5), (2, 2, 1)]:
+    for chunk, stages, grid in [(0, 0, 0), (4, 2, 0), (4, 5, 5), (8, 2, 1)]:
         thq4.check(thq4.lib().thq4_debug_set_gemv(chunk, stages, grid, 0))
         got = to_f32(q.linear(_x_bf16(xb).reshape(1, inp))).ravel()
         assert_close_ref(f"{out}x{inp} cb{chunk} st{stages} grid{grid}", got, want)

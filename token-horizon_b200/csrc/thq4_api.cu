@@ -275,10 +275,10 @@ thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream) {
 }
 
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
-  if (!(chunk == 0 || chunk == 2 || chunk == 4) || stages < 0 || stages == 1 || stages > 8 ||
+  if (!(chunk == 0 || chunk == 4 || chunk == 8) || stages < 0 || stages == 1 || stages > 8 ||
       grid < 0 || grid > 2 * device_sm_count() || reserved != 0)
     return set_error(THQ4_ERR_INVALID_ARGUMENT,
-                     "thq4_debug_set_gemv: chunk 0/2/4, stages 0 or 2..8, grid 0..2x SM count, reserved 0");
+                     "thq4_debug_set_gemv: chunk 0/4/8, stages 0 or 2..8, grid 0..2x SM count, reserved 0");
   g_force_warps.store(chunk, std::memory_order_relaxed);
   g_force_depth.store(stages, std::memory_order_relaxed);
   g_force_grid.store(grid, std::memory_order_relaxed);

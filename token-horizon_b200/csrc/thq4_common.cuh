@@ -22,16 +22,17 @@
 //            the nibble at bits 4i..4i+3 (i = 0..7) of word j holds
 //                row = 128 slab + 16 t + r + 8 ((i >> 1) & 1)
 //                k   = 64 g + 32 (j >> 1) + 8 (j & 1) + 16 (i & 1) + 2 c + (i >> 2)
-//            (frag_k below).  So for word w of k-step pair p = j >> 1:
-//              w & 0x000F000F         rows r   / k-step 2p   (low nibbles)
-//              (w >> 8) & 0x000F000F  rows r+8 / k-step 2p
-//              w & 0x00F000F0         rows r   / k-step 2p+1 (nibbles x 16)
+//            (frag_k below).  So for word w of k-step pair p = j >> 1,
+//            with the nibble moved to bits 4..7 of each 16-bit half:
+//              (w << 4) & 0x00F000F0  rows r   / k-step 2p
+//              (w >> 4) & 0x00F000F0  rows r+8 / k-step 2p
+//              w        & 0x00F000F0  rows r   / k-step 2p+1
 //              (w >> 8) & 0x00F000F0  rows r+8 / k-step 2p+1
-//            each a pair of adjacent k (2c, 2c+1) in the two 16-bit halves:
-//            exactly the A-fragment registers of mma.m16n8k16 (words j = 2p
-//            and 2p+1 give the k and k+8 halves).  OR-ing 0x64006400 makes
-//            each half the fp16 number 1024 + q (low nibbles) or 1024 + 16 q
-//            (high nibbles) -- exact, five ALU operations per word.
+//            each a pair of adjacent k (2c, 2c+1) in the two halves: exactly
+//            the A-fragment registers of mma.m16n8k16 (words j = 2p and
+//            2p+1 give the k and k+8 halves).  OR-ing 0x54005400 makes each
+//            half the fp16 number 64 + q -- exact (the unit in the last place
+//            of [64, 128) is 1/16) -- seven ALU operations per word.
 //   scales:  64 bytes at byte offset ch * 64: eight quads
 //            {s_r, b_r, s_r+8, b_r+8} (16-bit, bf16 or f16), quad r at + 8 r.
 //
@@ -86,14 +87,23 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return p;
 }
 
-// (w & mask) | 0x64006400 as one LOP3: with mask 0x000F000F the fp16 pair
-// (1024 + q0, 1024 + q1), with mask 0x00F000F0 the pair (1024 + 16 q0,
-// 1024 + 16 q1).  Both are exact (fp16 has a unit step on [1024, 2048)).
+// (w & 0x00F000F0) | 0x54005400 as one LOP3: the fp16 pair (64 + q0,
+// 64 + q1) of the nibbles in bits 4..7 and 20..23, exact.
 template <uint32_t MASK>
 __device__ __forceinline__ uint32_t nib_f16x2(uint32_t w) {
   uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(w), "n"(MASK), "n"(0x64006400));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(w), "n"(MASK), "n"(0x54005400));
   return r;
+}
+
+// D = A * B (C = 0), fp16 inputs, f32 accumulate, m16n8k16.
+__device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
 // D = A * B + C, fp16 inputs, f32 accumulate, m16n8k16.
@@ -104,6 +114,23 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Device-scope acquire-release atomic add (orders this thread's earlier
+// writes before it, and later reads after it).
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;\n" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+// Device-scope relaxed 16-byte load (not served from a stale L1 line).
+__device__ __forceinline__ float4 ld_relaxed_f4(const float *p) {
+  float4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
 }
 
 // ---- mbarrier / bulk-copy / PDL wrappers --------------------------------

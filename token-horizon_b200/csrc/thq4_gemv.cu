@@ -12,9 +12,9 @@
 //   - the weight is a stream of "slab-groups" (SG): 128 rows x 64 k, 4096
 //     bytes of nibbles + 512 bytes of scale/bias, slab-major, so any run of
 //     SGs is one contiguous byte range of the frag layout.  A persistent grid
-//     (one or two CTAs per SM) gives every CTA an equal run of "chunks" (CB
-//     consecutive SGs of one slab, CB-aligned); a run may start and end
-//     inside a slab;
+//     (one or two CTAs per SM) gives every CTA an equal run of "chunks" (CB =
+//     4 or 8 consecutive SGs of one slab, CB-aligned); a run may start and
+//     end inside a slab;
 //   - one producer warp per CTA streams the run into a ring of shared-memory
 //     stages with bulk copies (cp.async.bulk, evict-first in L2, no
 //     multicast) of one chunk each, completing on a "full" mbarrier per stage;
@@ -22,21 +22,24 @@
 //   - eight consumer warps each own one 16-row tile of every SG, so their
 //     output rows are disjoint and no reduction crosses warps.  Per SG a warp
 //     runs four mma.m16n8k16 (fp16 x fp16 -> f32) with the weight as the A
-//     operand (16 rows) and activation columns as N (8).  One LOP3 per
-//     register turns a nibble pair into the fp16 pair (1024 + q) or
-//     (1024 + 16 q) (frag layout, thq4_common.cuh); the two kinds accumulate
-//     in separate chains ("lo" and "hi") and meet in the epilogue as
-//     lo + hi / 16.  The 1024 offsets are removed by seeding the lo chain
-//     with -off, off = 1024 sum(x, lo k) + 64 sum(x, hi k), computed when x
-//     is staged.  The group's value is then the reference's per-group form
-//     (quant_kernel.rs:1994-2001, 2887-2890):  s * sum(q x) + b * sum(x);
+//     operand (16 rows) and activation columns as N (8).  A shift and one
+//     LOP3 per register put a nibble pair in mantissa bits 4..7 of the fp16
+//     pair 64 + q (exact; frag layout, thq4_common.cuh).  Two independent
+//     chains (k-steps 0, 2 and 1, 3) meet in the epilogue as
+//     acc0 + acc1 - off, off = 64 sum(x) computed when x is staged.  The
+//     group's value is then the reference's per-group form
+//     (quant_kernel.rs:1994-2001, 2887-2890):  s * sum(q x) + b * sum(x).
+//     (The offset enters the fp32 accumulation at 64x the size of the q
+//     signal; with the nibble in mantissa bits 0..3 it would be 1024x and
+//     cost ten bits of the accumulator instead of six);
 //   - with few tokens most of the 8 columns are free, so consecutive groups
 //     share one accumulator: in a "window" of GW groups (4 when a group
 //     needs <= 2 columns), group j's activation sits in columns
 //     [8j/GW, 8(j+1)/GW) and is zero elsewhere.  After the window each lane
 //     holds the sums of exactly one group (its own columns), so the scale /
 //     bias epilogue runs once per window with every lane busy -- 4x fewer
-//     epilogue instructions for a matvec;
+//     epilogue instructions for a matvec.  Windows never cross a chunk, so
+//     the epilogue reads its scales from the stage still held;
 //   - the activation is converted to fp16 per (group, token) with a power-of-
 //     two scale 2^e that puts the group's largest |x| in [2^14, 2^15): exact
 //     for bf16 input over 31 binades below the group maximum, no overflow at
@@ -67,7 +70,7 @@ constexpr int kConsumers = kSlabTiles;  // one consumer warp per tile of a slab
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kSgBytes = kSlabTiles * (kChunkBytes + kQuadBytes);  // 4608
 constexpr int kMaxStages = 8;
-constexpr uint32_t kLoMask = 0x000F000Fu, kHiMask = 0x00F000F0u;
+constexpr uint32_t kNibMask = 0x00F000F0u;  // mantissa bits 4..7 of both halves
 
 struct GemvArgs {
   const uint8_t *qw0;  // gate (or the only) weight: frag nibbles
@@ -88,11 +91,13 @@ struct GemvArgs {
   int xcap;            // activation groups staged per CTA
 };
 
-__host__ __device__ inline int colpairs(int P) { return (P + 1) / 2; }
+// columns with per-group metadata: P rounded up to even (lanes own pairs)
+__host__ __device__ inline int meta_cols(int P) { return (P + 1) & ~1; }
 // fp16 B fragments [slot][P][2][4] x 16 B, a 128-byte zero block, then per
-// (slot, column pair) {xs0, xs1, f0, f1} and {off0, off1}
+// (slot, column) {xs, f, off, 0}: the column's sum(x), its scale 2^e and
+// the magic-number offset 64 sum(x')
 __host__ __device__ inline size_t xstage_bytes(int xcap, int P) {
-  return (size_t)xcap * P * 128 + 128 + (size_t)xcap * colpairs(P) * 24;
+  return (size_t)xcap * P * 128 + 128 + (size_t)xcap * meta_cols(P) * 16;
 }
 __host__ __device__ inline size_t stage_bytes(int cb, bool gate_up) { return (size_t)(gate_up ? 2 : 1) * cb * kSgBytes; }
 __host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, int xcap, int P) {
@@ -125,17 +130,12 @@ __device__ __forceinline__ void consumer_sync() {
 // column q: token q (bf16 x) or token q/2's hi (even q) or lo (odd q) part
 // (f32 x), with x' = x 2^-e.  The 8 threads of one (slot, q) reduce the
 // group's max |x| and sums with a fixed shuffle tree (deterministic).
-__device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float *mxf, float *moff) {
+__device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
   const int tid = threadIdx.x, nthr = kConsumers * 32;
-  const int P = a.P, CP = colpairs(P);
+  const int P = a.P, P8 = meta_cols(P);
   if (tid < 8) zero[tid] = make_uint4(0, 0, 0, 0);
   if (P & 1)  // the unused column of the last pair contributes nothing
-    for (int i = tid; i < xcnt; i += nthr) {
-      const int e = i * CP + CP - 1;
-      mxf[e * 4 + 1] = 0.0f;
-      mxf[e * 4 + 3] = 0.0f;
-      moff[e * 2 + 1] = 0.0f;
-    }
+    for (int i = tid; i < xcnt; i += nthr) mx[i * P8 + P] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   const int entries = xcnt * P * 8;
   const int span = (entries + 31) / 32 * 32;
   for (int idx = tid; idx < span; idx += nthr) {
@@ -157,14 +157,14 @@ __device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *z
                     : __uint_as_float((uint32_t)static_cast<const uint16_t *>(a.x)[at] << 16);
       v[vv] = xv;
     }
-    float mx = 0.0f;
+    float amax = 0.0f;
 #pragma unroll
-    for (int vv = 0; vv < 8; ++vv) mx = fmaxf(mx, fabsf(v[vv]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    for (int vv = 0; vv < 8; ++vv) amax = fmaxf(amax, fabsf(v[vv]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
     // 2^e with the group max in [2^14, 2^15); e = 0 for an all-zero group
-    const int ex = (__float_as_int(mx) >> 23) & 0xff;
+    const int ex = (__float_as_int(amax) >> 23) & 0xff;
     const int e2 = ex == 0 ? 0 : min(max(ex - 127 - 14, -110), 114);
     const float dn = __int_as_float((127 - e2) << 23), f = __int_as_float((127 + e2) << 23);
     uint32_t hv[4] = {0, 0, 0, 0};
@@ -187,12 +187,7 @@ __device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *z
     shi += __shfl_xor_sync(0xffffffffu, shi, 2);
     slo += __shfl_xor_sync(0xffffffffu, slo, 4);
     shi += __shfl_xor_sync(0xffffffffu, shi, 4);
-    if (live && (idx & 7) == 0) {
-      const int pe = slot * CP + (q >> 1), w = q & 1;
-      mxf[pe * 4 + w] = f * (slo + shi);
-      mxf[pe * 4 + 2 + w] = f;
-      moff[pe * 2 + w] = 1024.0f * slo + 64.0f * shi;
-    }
+    if (live && (idx & 7) == 0) mx[slot * P8 + q] = make_float4(f * (slo + shi), f, 64.0f * (slo + shi), 0.0f);
   }
   consumer_sync();
 }
@@ -245,11 +240,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   uint64_t *empty = full + kMaxStages;
   unsigned char *ring = smem + 128;
   unsigned char *xt = ring + (size_t)R * SB;
-  const int P = a.P, CP = colpairs(P);
+  const int P = a.P, P8 = meta_cols(P);
   uint4 *xf = reinterpret_cast<uint4 *>(xt);
   uint4 *zero = reinterpret_cast<uint4 *>(xt + (size_t)a.xcap * P * 128);
-  float *mxf = reinterpret_cast<float *>(xt + (size_t)a.xcap * P * 128 + 128);
-  float *moff = mxf + (size_t)a.xcap * CP * 4;
+  float4 *mx = reinterpret_cast<float4 *>(xt + (size_t)a.xcap * P * 128 + 128);
 
   // this CTA's run of chunks
   const long long C0 = run_begin(blockIdx.x, a.chunks, gridDim.x), C1 = run_begin(blockIdx.x + 1, a.chunks, gridDim.x);
@@ -269,18 +263,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     // ---- producer: one elected lane streams the run -------------------------
     if (lane != 0) return;
     const uint64_t pol = evict_first_policy();
-    for (int n = 0; n < nch; ++n) {
-      const int s = n % R;
-      if (n >= R && !mbar_wait_bounded(&empty[s], (uint32_t)(((n / R) - 1) & 1), kWaitLimitNs)) {
+    long long sl = C0 / a.cps;  // slab and chunk-in-slab of chunk C0 + n
+    int cg = (int)(C0 - sl * a.cps);
+    int s = 0;
+    uint32_t par = 0;  // parity of this use of stage s
+    for (int n = 0; n < nch; ++n, ++cg) {
+      if (cg == a.cps) cg = 0, ++sl;
+      if (n >= R && !mbar_wait_bounded(&empty[s], par ^ 1u, kWaitLimitNs)) {
         raise_status(a.status, kStatusTimeout);
         // copies already issued must land before the CTA's memory is reused
         for (int k = n - R; k < n; ++k)
-          if (k >= 0) (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
+          (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
         return;
       }
-      const long long C = C0 + n;
-      const long long sl = C / a.cps;
-      const int g0c = (int)(C - sl * a.cps) * CB, cnt = min(CB, a.ng - g0c);
+      const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
       const long long sg = sl * a.ng + g0c;
       unsigned char *dst = ring + (size_t)s * SB;
       mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
@@ -290,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         bulk_g2s(dst + (size_t)CB * 4096, a.qw1 + sg * 4096, cnt * 4096, &full[s], pol);
         bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, a.sb1 + sg * 512, cnt * 512, &full[s], pol);
       }
+      if (++s == R) s = 0, par ^= 1u;
     }
     // the consumers wait for every chunk before they release it
     return;
@@ -297,93 +294,78 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 
   // ---- consumers: warp `warp` owns tile `warp` of every slab-group ----------
   pdl_wait();
-  const int gs = (int)(C0 % a.cps) * CB;
+  const int sl0 = (int)(C0 / a.cps), cg0 = (int)(C0 - (long long)sl0 * a.cps);
+  const int gs = cg0 * CB;
   const int xcnt =
       (int)min((long long)a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
-  stage_x(a, gs, xcnt, xf, zero, mxf, moff);
+  stage_x(a, gs, xcnt, xf, zero, mx);
 
   const int r = lane >> 2, c = lane & 3;
   const int jr = r / CPG, qr = r % CPG;  // this lane's B column: window position jr, column qr
-  const bool bq = qr < P;
   const int jc = c / LPJ, cp = c % LPJ;  // this lane's D columns 2c, 2c+1: position jc, pair cp
-  const bool colv = 2 * cp < P;
-  const int cpv = min(cp, CP - 1);
+  const bool colv = 2 * cp < P;          // the pair holds a column in use
+  const int xoff = qr * 8 + c;           // B entry of column qr within a slot
+  bool bsel[GW];                         // B of window position j is this lane's column
+#pragma unroll
+  for (int j = 0; j < GW; ++j) bsel[j] = jr == j && qr < P;
   auto slot_of = [&](int g) { return g >= gs ? g - gs : g + a.ng - gs; };
 
   float lo[NS][4], hi[NS][4], y[NS][4];
-  uint2 sc[NS];
 #pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    sc[s] = make_uint2(0, 0);
+  for (int s = 0; s < NS; ++s)
 #pragma unroll
     for (int e = 0; e < 4; ++e) lo[s][e] = hi[s][e] = y[s][e] = 0.0f;
-  }
-  int wlo = -1, whi = 0, wbase = 0;  // open window: first / last position, its group 0
-  bool seg_whole = (C0 % a.cps) == 0;  // the current slab segment began at the slab's start
+  bool seg_whole = cg0 == 0;  // the current slab segment began at the slab's start
   bool finished_any = false;
 
-  auto open_window = [&](int g, int j) {
-    wbase = g - j;
-    wlo = j;
-    const int gl = wbase + jc;
-    float o0 = 0.0f, o1 = 0.0f;
-    // a lane whose group lies outside this run's staged groups keeps 0 (it
-    // is not processed here, and close_window skips it)
-    const int gsl = gl < a.ng ? slot_of(gl) : xcnt;
-    if (colv && jc >= j && gsl < xcnt) {
-      const float2 o = *reinterpret_cast<const float2 *>(moff + (size_t)(gsl * CP + cpv) * 2);
-      o0 = o.x;
-      o1 = o.y;
-    }
-#pragma unroll
-    for (int s = 0; s < NS; ++s) {
-      lo[s][0] = -o0, lo[s][1] = -o1, lo[s][2] = -o0, lo[s][3] = -o1;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) hi[s][e] = 0.0f;
-    }
-  };
-  auto group = [&](const unsigned char *nib, const unsigned char *scl, int u, int g, int j) {
-    const uint4 *bp = (jr == j && bq) ? xf + ((size_t)slot_of(g) * P + qr) * 8 + c : zero + c;
+  // Group u of the chunk; `live`: this lane's B column holds it; `first`:
+  // the window's first group, which starts both chains from zero.
+  auto group = [&](const unsigned char *nib, const uint4 *xc, int u, bool live, bool first) {
+    const uint4 *bp = live ? xc + u * P * 8 : zero + c;
     const uint4 xa = bp[0], xb = bp[4];
-    if (jc == j) {
-#pragma unroll
-      for (int s = 0; s < NS; ++s)
-        sc[s] = *reinterpret_cast<const uint2 *>(scl + (size_t)(s * CB + u) * 512 + warp * 64 + r * 8);
-    }
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
       const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(s * CB + u) * 4096 + warp * 512 + lane * 16);
-      const uint32_t t0 = w.x >> 8, t1 = w.y >> 8, t2 = w.z >> 8, t3 = w.w >> 8;
-      mma_f16_16816(lo[s], nib_f16x2<kLoMask>(w.x), nib_f16x2<kLoMask>(t0), nib_f16x2<kLoMask>(w.y),
-                    nib_f16x2<kLoMask>(t1), xa.x, xa.y);
-      mma_f16_16816(hi[s], nib_f16x2<kHiMask>(w.x), nib_f16x2<kHiMask>(t0), nib_f16x2<kHiMask>(w.y),
-                    nib_f16x2<kHiMask>(t1), xa.z, xa.w);
-      mma_f16_16816(lo[s], nib_f16x2<kLoMask>(w.z), nib_f16x2<kLoMask>(t2), nib_f16x2<kLoMask>(w.w),
-                    nib_f16x2<kLoMask>(t3), xb.x, xb.y);
-      mma_f16_16816(hi[s], nib_f16x2<kHiMask>(w.z), nib_f16x2<kHiMask>(t2), nib_f16x2<kHiMask>(w.w),
-                    nib_f16x2<kHiMask>(t3), xb.z, xb.w);
+      // k-step 2p rows r / r+8: bits 0..3 / 8..11 of each half, moved up by
+      // 4 / down by 4; k-step 2p+1: bits 4..7 in place / 12..15 down by 8
+      const uint32_t a00 = nib_f16x2<kNibMask>(w.x << 4), a01 = nib_f16x2<kNibMask>(w.x >> 4);
+      const uint32_t a02 = nib_f16x2<kNibMask>(w.y << 4), a03 = nib_f16x2<kNibMask>(w.y >> 4);
+      const uint32_t a10 = nib_f16x2<kNibMask>(w.x), a11 = nib_f16x2<kNibMask>(w.x >> 8);
+      const uint32_t a12 = nib_f16x2<kNibMask>(w.y), a13 = nib_f16x2<kNibMask>(w.y >> 8);
+      const uint32_t a20 = nib_f16x2<kNibMask>(w.z << 4), a21 = nib_f16x2<kNibMask>(w.z >> 4);
+      const uint32_t a22 = nib_f16x2<kNibMask>(w.w << 4), a23 = nib_f16x2<kNibMask>(w.w >> 4);
+      const uint32_t a30 = nib_f16x2<kNibMask>(w.z), a31 = nib_f16x2<kNibMask>(w.z >> 8);
+      const uint32_t a32 = nib_f16x2<kNibMask>(w.w), a33 = nib_f16x2<kNibMask>(w.w >> 8);
+      if (first) {
+        mma_f16_16816_z(lo[s], a00, a01, a02, a03, xa.x, xa.y);
+        mma_f16_16816_z(hi[s], a10, a11, a12, a13, xa.z, xa.w);
+      } else {
+        mma_f16_16816(lo[s], a00, a01, a02, a03, xa.x, xa.y);
+        mma_f16_16816(hi[s], a10, a11, a12, a13, xa.z, xa.w);
+      }
+      mma_f16_16816(lo[s], a20, a21, a22, a23, xb.x, xb.y);
+      mma_f16_16816(hi[s], a30, a31, a32, a33, xb.z, xb.w);
     }
-    whi = j;
   };
-  auto close_window = [&]() {
-    const int gl = wbase + jc;
-    const bool valid = colv && jc >= wlo && jc <= whi;
-    float4 xm = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (valid) xm = *reinterpret_cast<const float4 *>(mxf + (size_t)(slot_of(gl) * CP + cpv) * 4);
+  // Epilogue of the window starting at chunk group w0: this lane's group is
+  // w0 + jc; its scales come from the stage, its activation sums from mc.
+  auto close_window = [&](const unsigned char *scl, const float4 *mc, int w0, bool valid) {
+    if (!valid) return;
+    const int gu = w0 + jc;
+    const float4 m0 = mc[gu * P8];
+    const float4 m1 = ONE ? m0 : mc[gu * P8 + 1];
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-      const float sr = sb_to_f32<SF16>(sc[s].x & 0xffffu), br = sb_to_f32<SF16>(sc[s].x >> 16);
-      const float s8 = sb_to_f32<SF16>(sc[s].y & 0xffffu), b8 = sb_to_f32<SF16>(sc[s].y >> 16);
-      if (valid) {
-        y[s][0] = fmaf(sr * xm.z, fmaf(hi[s][0], 0.0625f, lo[s][0]), fmaf(br, xm.x, y[s][0]));
-        y[s][2] = fmaf(s8 * xm.z, fmaf(hi[s][2], 0.0625f, lo[s][2]), fmaf(b8, xm.x, y[s][2]));
-        if constexpr (!ONE) {
-          y[s][1] = fmaf(sr * xm.w, fmaf(hi[s][1], 0.0625f, lo[s][1]), fmaf(br, xm.y, y[s][1]));
-          y[s][3] = fmaf(s8 * xm.w, fmaf(hi[s][3], 0.0625f, lo[s][3]), fmaf(b8, xm.y, y[s][3]));
-        }
+      const uint2 q = *reinterpret_cast<const uint2 *>(scl + (size_t)(s * CB + gu) * 512 + warp * 64 + r * 8);
+      const float sr = sb_to_f32<SF16>(q.x & 0xffffu), br = sb_to_f32<SF16>(q.x >> 16);
+      const float s8 = sb_to_f32<SF16>(q.y & 0xffffu), b8 = sb_to_f32<SF16>(q.y >> 16);
+      y[s][0] = fmaf(sr * m0.y, (lo[s][0] + hi[s][0]) - m0.z, fmaf(br, m0.x, y[s][0]));
+      y[s][2] = fmaf(s8 * m0.y, (lo[s][2] + hi[s][2]) - m0.z, fmaf(b8, m0.x, y[s][2]));
+      if constexpr (!ONE) {
+        y[s][1] = fmaf(sr * m1.y, (lo[s][1] + hi[s][1]) - m1.z, fmaf(br, m1.x, y[s][1]));
+        y[s][3] = fmaf(s8 * m1.y, (lo[s][3] + hi[s][3]) - m1.z, fmaf(b8, m1.x, y[s][3]));
       }
     }
-    wlo = -1;
   };
   // lanes of one column pair but different window positions hold disjoint
   // groups of the same outputs: add them (every such lane gets the same sum)
@@ -404,25 +386,27 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   };
 
   // The run's partial slabs: its first (if it began inside a slab) and its
-  // last (if it ended inside one).  Publish this CTA's part (side 0: the
-  // run's first segment, side 1: its last); the CTA that arrives last adds
-  // every part in CTA order and stores the tile.
-  auto hand_over = [&](int sl, int side, float (&v)[NS][4]) {
+  // last (if it ended inside one).  This CTA's part of each is stored to the
+  // workspace as soon as it is complete (side 0: the run's first segment,
+  // side 1: its last) with plain stores; at the end of the run one
+  // acquire-release increment per partial slab publishes them, and the CTA
+  // whose increment completes the count adds every part in CTA order and
+  // stores the tile.  Nothing waits, and the only fences are the two atomics.
+  auto publish = [&](int side, const float (&v)[NS][4]) {
     float *gslot = a.part + (((size_t)blockIdx.x * 2 + side) * kSlabTiles + warp) * (NS * 128) + lane * 4;
 #pragma unroll
     for (int si = 0; si < NS; ++si)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) gslot[si * 128 + e] = v[si][e];
-    __threadfence();
-    __syncwarp();
+      *reinterpret_cast<float4 *>(gslot + si * 128) = make_float4(v[si][0], v[si][1], v[si][2], v[si][3]);
+  };
+  auto contributors = [&](int sl, long long &clo, long long &chi) {
     const long long t0 = (long long)sl * a.cps, t1 = t0 + a.cps;
-    const long long clo = run_of(t0, a.chunks, gridDim.x), chi = run_of(t1 - 1, a.chunks, gridDim.x);
-    uint32_t old = 0;
-    uint32_t *cntp = &a.count[(size_t)sl * kSlabTiles + warp];
-    if (lane == 0) old = atomicAdd(cntp, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 != (uint32_t)(chi - clo + 1)) return;
-    __threadfence();
+    clo = run_of(t0, a.chunks, gridDim.x);
+    chi = run_of(t1 - 1, a.chunks, gridDim.x);
+  };
+  auto combine = [&](int sl) {
+    long long clo, chi;
+    contributors(sl, clo, chi);
+    const long long t0 = (long long)sl * a.cps;
     float acc[NS][4];
 #pragma unroll
     for (int si = 0; si < NS; ++si)
@@ -430,66 +414,58 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       for (int e = 0; e < 4; ++e) acc[si][e] = 0.0f;
     for (long long q = clo; q <= chi; ++q) {
       const int qs = (q == clo && run_begin(q, a.chunks, gridDim.x) < t0) ? 1 : 0;
-      const volatile float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
+      const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
 #pragma unroll
-      for (int si = 0; si < NS; ++si)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[si][e] += src[si * 128 + e];
+      for (int si = 0; si < NS; ++si) {
+        const float4 v = ld_relaxed_f4(src + si * 128);
+        acc[si][0] += v.x, acc[si][1] += v.y, acc[si][2] += v.z, acc[si][3] += v.w;
+      }
     }
-    if (lane == 0) *cntp = 0;  // ready for the next call
+    if (lane == 0) a.count[(size_t)sl * kSlabTiles + warp] = 0;  // ready for the next call
     store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, acc[0], acc[NS - 1]);
   };
+  int first_slab = -1;
+  int sl = sl0, cg = cg0 - 1, s = R - 1;
+  uint32_t par = 1;  // (stage, parity) of chunk n, kept incrementally
   for (int n = 0; n < nch; ++n) {
-    const int s = n % R;
-    if (!mbar_wait_bounded(&full[s], (uint32_t)((n / R) & 1), kWaitLimitNs)) {
+    if (++cg == a.cps) cg = 0, ++sl;
+    if (++s == R) s = 0, par ^= 1u;
+    if (!mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
       // the producer then times out on this stage's release and stops;
       // outputs of this call are undefined and the status word says so
       raise_status(a.status, kStatusTimeout);
       return;
     }
-    const long long C = C0 + n;
-    const int sl = (int)(C / a.cps), cg = (int)(C - (long long)sl * a.cps);
     const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
     const unsigned char *nib = ring + (size_t)s * SB;
     const unsigned char *scl = nib + (size_t)NS * CB * 4096;
+    // the chunk's groups are consecutive slots (gs is chunk-aligned)
+    const int slot0 = slot_of(g0c);
+    const uint4 *xc = xf + (size_t)slot0 * P * 8 + xoff;
+    const float4 *mc = mx + (size_t)slot0 * P8 + 2 * cp;
     if (cnt == CB) {
-      if constexpr (CB >= GW) {
-        // chunks are window-aligned: positions are compile-time
 #pragma unroll
-        for (int u = 0; u < CB; ++u) {
-          if (u % GW == 0) open_window(g0c + u, 0);
-          group(nib, scl, u, g0c + u, u % GW);
-          if (u % GW == GW - 1) close_window();
-        }
-      } else {  // two-group chunks of a four-group window
-        if ((g0c & 3) == 0) {
-          open_window(g0c, 0);
-          group(nib, scl, 0, g0c, 0);
-          group(nib, scl, 1, g0c + 1, 1);
-        } else {
-          if (wlo < 0) open_window(g0c, 2);
-          group(nib, scl, 0, g0c, 2);
-          group(nib, scl, 1, g0c + 1, 3);
-          close_window();
-        }
+      for (int u = 0; u < CB; ++u) {
+        group(nib, xc, u, bsel[u % GW], u % GW == 0);
+        if (u % GW == GW - 1) close_window(scl, mc, u - (GW - 1), colv);
       }
-    } else {
+    } else {  // the slab's last chunk when ng is not a multiple of CB
       for (int u = 0; u < cnt; ++u) {
-        const int g = g0c + u, j = g % GW;
-        if (wlo < 0) open_window(g, j);
-        group(nib, scl, u, g, j);
-        if (j == GW - 1) close_window();
+        const int j = u % GW;
+        group(nib, xc, u, jr == j && qr < P, j == 0);
+        if (j == GW - 1 || u == cnt - 1) close_window(scl, mc, u - j, colv && u - j + jc < cnt);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (cg == a.cps - 1) {  // slab end
-      if (wlo >= 0) close_window();
       reduce_y();
-      if (seg_whole)
+      if (seg_whole) {
         store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, y[0], y[NS - 1]);
-      else  // the run's first segment, partial
-        hand_over(sl, 0, y);
+      } else {  // the run's first segment, partial
+        publish(0, y);
+        first_slab = sl;
+      }
 #pragma unroll
       for (int si = 0; si < NS; ++si)
 #pragma unroll
@@ -499,11 +475,35 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     }
   }
 
-  if (nch > 0 && C1 % a.cps != 0) {  // the run ended inside a slab
-    if (wlo >= 0) close_window();
+  int last_slab = -1;
+  if (nch > 0 && cg != a.cps - 1) {  // the run ended inside a slab
     reduce_y();
-    hand_over((int)((C1 - 1) / a.cps), finished_any ? 1 : 0, y);
+    publish(finished_any ? 1 : 0, y);
+    last_slab = sl;
   }
+  if (first_slab < 0 && last_slab < 0) return;
+  // the lanes' stores above happen before lane 0's release increments
+  __syncwarp();
+  uint32_t done = 0;  // bit 0: first slab complete, bit 1: last slab complete
+  if (lane == 0) {
+    uint32_t o0 = 0, o1 = 0;
+    long long clo, chi;
+    if (first_slab >= 0) o0 = atom_add_acq_rel(&a.count[(size_t)first_slab * kSlabTiles + warp], 1u);
+    if (last_slab >= 0) o1 = atom_add_acq_rel(&a.count[(size_t)last_slab * kSlabTiles + warp], 1u);
+    if (first_slab >= 0) {
+      contributors(first_slab, clo, chi);
+      if (o0 + 1 == (uint32_t)(chi - clo + 1)) done |= 1u;
+    }
+    if (last_slab >= 0) {
+      contributors(last_slab, clo, chi);
+      if (o1 + 1 == (uint32_t)(chi - clo + 1)) done |= 2u;
+    }
+  }
+  done = __shfl_sync(0xffffffffu, done, 0);
+  // lane 0's acquire happens before the other lanes' loads
+  __syncwarp();
+  if (done & 1u) combine(first_slab);
+  if (done & 2u) combine(last_slab);
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
@@ -539,9 +539,9 @@ cudaError_t dispatch_gw(const GemvArgs &a, int gw, int grid, size_t smem, cudaSt
 template <bool SF16>
 cudaError_t dispatch(const GemvArgs &a, bool gate_up, int cb, int gw, int grid, size_t smem, cudaStream_t s) {
   if (gate_up)
-    return cb == 4 ? dispatch_gw<4, SF16, true>(a, gw, grid, smem, s) : dispatch_gw<2, SF16, true>(a, gw, grid, smem, s);
-  return cb == 4 ? dispatch_gw<4, SF16, false>(a, gw, grid, smem, s)
-                 : dispatch_gw<2, SF16, false>(a, gw, grid, smem, s);
+    return cb == 8 ? dispatch_gw<8, SF16, true>(a, gw, grid, smem, s) : dispatch_gw<4, SF16, true>(a, gw, grid, smem, s);
+  return cb == 8 ? dispatch_gw<8, SF16, false>(a, gw, grid, smem, s)
+                 : dispatch_gw<4, SF16, false>(a, gw, grid, smem, s);
 }
 
 int window_groups(int P) { return P <= 2 ? 4 : (P <= 4 ? 2 : 1); }
@@ -562,14 +562,17 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
   const int ng = in / kGroup;
   const int sms = device_sm_count();
   const GemvCfg cfg = gemv_cfg_override();
-  const int cb = cfg.warps > 0 ? cfg.warps : (gate_up ? 2 : 4);
+  const int cb = cfg.warps > 0 ? cfg.warps : 4;
   const int cps = (ng + cb - 1) / cb;
   const long long chunks = (long long)row_slabs(out) * cps;
   int per = x_f32 ? 4 : 8;  // tokens per launch: 8 B columns, two per f32 token
   if (per > m) per = m;
   for (;;) {
     const int P = x_f32 ? 2 * per : per;
-    for (int per_sm = 2; per_sm >= 1 && !p.ok; --per_sm) {
+    // one CTA per SM with a deep ring measured best for every decode shape;
+    // a forced grid above the SM count runs two per SM
+    {
+      const int per_sm = cfg.grid > sms ? 2 : 1;
       long long grid = cfg.grid > 0 ? cfg.grid : (long long)sms * per_sm;
       if (grid > (long long)sms * 2) grid = (long long)sms * 2;
       if (chunks < grid) grid = chunks;  // every CTA run holds at least one chunk
@@ -580,7 +583,7 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
       if (cfg.depth > 0) {
         if (gemv_smem(cfg.depth, cb, gate_up, xcap, P) <= limit) st = cfg.depth;
       } else {
-        for (int t = per_sm == 2 ? 6 : kMaxStages; t >= 2 && !st; --t)
+        for (int t = per_sm == 2 ? 6 : 5; t >= 2 && !st; --t)
           if (gemv_smem(t, cb, gate_up, xcap, P) <= limit) st = t;
       }
       if (st) {

@@ -47,7 +47,7 @@ uint32_t *status_word();
 
 // ---- GEMV / verify ---------------------------------------------------------
 struct GemvCfg {
-  int warps = 0;  // forced slab-groups per ring stage, 2 or 4 (0 = policy)
+  int warps = 0;  // forced slab-groups per ring stage, 4 or 8 (0 = policy)
   int depth = 0;  // forced ring stages (0 = policy)
   int grid = 0;   // forced CTAs (0 = policy)
 };
