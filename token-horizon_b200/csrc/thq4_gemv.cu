@@ -82,7 +82,8 @@ struct GemvArgs {
   uint32_t *status;    // device status word
   float *part;         // workspace: partials [cta][2 sides][8 tiles][NS][32 lanes][4]
   uint32_t *count;     // workspace: arrivals per (slab, tile) (zero between calls)
-  long long chunks;    // slabs * cps: the units CTA runs are cut in
+  int chunks;          // slabs * cps: the units CTA runs are cut in
+  int run_base, run_rem;  // chunks / grid, chunks % grid: run i holds base + (i < rem)
   int cps;             // chunks per slab, ceil(ng / cb)
   int m, in, ng, out;
   int P;               // B columns in use: m (bf16 x) or 2m (f32 x)
@@ -105,19 +106,17 @@ __host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, in
 }
 // floats of one CTA side's partial: 8 tiles x NS x 32 lanes x 4
 __host__ __device__ inline int side_floats(bool gate_up) { return kSlabTiles * (gate_up ? 2 : 1) * 32 * 4; }
-__host__ __device__ inline long long run_begin(long long i, long long total, long long parts) {
-  return i * total / parts;
-}
-// The run holding unit o (0 <= o < total): the largest i with
-// run_begin(i) <= o, which is never an empty run.
-__device__ __forceinline__ long long run_of(long long o, long long total, long long parts) {
-  return ((o + 1) * parts + total - 1) / total - 1;
+// First chunk of run i: runs hold base + 1 chunks for i < rem, base after.
+__device__ __forceinline__ int run_begin(const GemvArgs &a, int i) { return i * a.run_base + min(i, a.run_rem); }
+// The run holding chunk o (every run is non-empty: base >= 1).
+__device__ __forceinline__ int run_of(const GemvArgs &a, int o) {
+  const int big = a.run_rem * (a.run_base + 1);
+  return o < big ? o / (a.run_base + 1) : a.run_rem + (o - big) / a.run_base;
 }
 // slab-groups before chunk C
-__host__ __device__ inline long long sgs_before(long long C, int cps, int ng, int cb) {
-  const long long sl = C / cps;
-  const int cg = (int)(C - sl * cps);
-  return sl * ng + min(cg * cb, ng);
+__device__ __forceinline__ int sgs_before(int C, int cps, int ng, int cb) {
+  const int sl = C / cps;
+  return sl * ng + min((C - sl * cps) * cb, ng);
 }
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumers * 32) : "memory");
@@ -128,66 +127,94 @@ __device__ __forceinline__ void consumer_sync() {
 // + c (16 bytes) holds, for k-steps 2h and 2h+1 of the group, the fp16 pairs
 // {x'[2c], x'[2c+1]}, {x'[2c+8], x'[2c+9]} (k relative to the k-step) of
 // column q: token q (bf16 x) or token q/2's hi (even q) or lo (odd q) part
-// (f32 x), with x' = x 2^-e.  The 8 threads of one (slot, q) reduce the
-// group's max |x| and sums with a fixed shuffle tree (deterministic).
+// (f32 x), with x' = x 2^-e.  One item = 8 consecutive k of one (slot,
+// column), read with one vector load; the 8 items of a (slot, column) are 8
+// adjacent lanes, which reduce the group's max |x| and sum with a fixed
+// shuffle tree (deterministic).  Up to four items per thread are requested
+// before any is used.
 __device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
   const int tid = threadIdx.x, nthr = kConsumers * 32;
   const int P = a.P, P8 = meta_cols(P);
+  constexpr int kU = 4;
   if (tid < 8) zero[tid] = make_uint4(0, 0, 0, 0);
   if (P & 1)  // the unused column of the last pair contributes nothing
     for (int i = tid; i < xcnt; i += nthr) mx[i * P8 + P] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  const int entries = xcnt * P * 8;
-  const int span = (entries + 31) / 32 * 32;
-  for (int idx = tid; idx < span; idx += nthr) {
-    const bool live = idx < entries;
-    const int e = live ? idx : 0;
-    const int c = e & 3, h = (e >> 2) & 1, sq = e >> 3;
-    const int q = sq % P, slot = sq / P;
-    int g = gs + slot;
-    if (g >= a.ng) g -= a.ng;
-    const int t = a.xf32 ? q >> 1 : q, part = a.xf32 ? q & 1 : 0;
-    float v[8];
+  uint32_t *xw = reinterpret_cast<uint32_t *>(xf);
+  const int items = xcnt * P * 8;
+  const int span = (items + 31) / 32 * 32;  // whole warps: every lane takes part in the shuffles
+  for (int base = tid; base < span; base += kU * nthr) {
+    float v[kU][8];
 #pragma unroll
-    for (int vv = 0; vv < 8; ++vv) {
-      const int k = 16 * (2 * h + (vv >> 2)) + 2 * c + (vv & 1) + 8 * ((vv >> 1) & 1);
-      const size_t at = (size_t)t * a.in + (size_t)g * kGroup + k;
-      float xv = 0.0f;
-      if (live)
-        xv = a.xf32 ? static_cast<const float *>(a.x)[at]
-                    : __uint_as_float((uint32_t)static_cast<const uint16_t *>(a.x)[at] << 16);
-      v[vv] = xv;
+    for (int it = 0; it < kU; ++it) {
+      const int idx = base + it * nthr;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[it][e] = 0.0f;
+      if (idx >= items) continue;
+      const int h8 = idx & 7, sq = idx >> 3, q = sq % P, slot = sq / P;
+      int g = gs + slot;
+      if (g >= a.ng) g -= a.ng;
+      const int t = a.xf32 ? q >> 1 : q;
+      const size_t at = (size_t)t * a.in + (size_t)g * kGroup + 8 * h8;
+      if (a.xf32) {
+        const float4 *p4 = reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + at);
+        const float4 u0 = p4[0], u1 = p4[1];
+        v[it][0] = u0.x, v[it][1] = u0.y, v[it][2] = u0.z, v[it][3] = u0.w;
+        v[it][4] = u1.x, v[it][5] = u1.y, v[it][6] = u1.z, v[it][7] = u1.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) + at);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[it][2 * e] = __uint_as_float(w[e] << 16);
+          v[it][2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+        }
+      }
     }
-    float amax = 0.0f;
 #pragma unroll
-    for (int vv = 0; vv < 8; ++vv) amax = fmaxf(amax, fabsf(v[vv]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    // 2^e with the group max in [2^14, 2^15); e = 0 for an all-zero group
-    const int ex = (__float_as_int(amax) >> 23) & 0xff;
-    const int e2 = ex == 0 ? 0 : min(max(ex - 127 - 14, -110), 114);
-    const float dn = __int_as_float((127 - e2) << 23), f = __int_as_float((127 + e2) << 23);
-    uint32_t hv[4] = {0, 0, 0, 0};
-    float hf[8];
+    for (int it = 0; it < kU; ++it) {
+      const int idx = base + it * nthr;
+      if (idx >= span) break;  // uniform per warp
+      const bool live = idx < items;
+      const int h8 = idx & 7, sq = live ? idx >> 3 : 0, q = sq % P, slot = sq / P;
+      const int part = a.xf32 ? q & 1 : 0;
+      float amax = 0.0f;
 #pragma unroll
-    for (int vv = 0; vv < 8; ++vv) {
-      const float xs = v[vv] * dn;
-      const __half hi = __float2half_rn(xs);
-      const __half val = part ? __float2half_rn(xs - __half2float(hi)) : hi;
-      hf[vv] = __half2float(val);
-      hv[vv >> 1] |= (uint32_t)__half_as_ushort(val) << (16 * (vv & 1));
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[it][e]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      // 2^e with the group max in [2^14, 2^15); e = 0 for an all-zero group
+      const int ex = (__float_as_int(amax) >> 23) & 0xff;
+      const int e2 = ex == 0 ? 0 : min(max(ex - 127 - 14, -110), 114);
+      const float dn = __int_as_float((127 - e2) << 23), f = __int_as_float((127 + e2) << 23);
+      float sum = 0.0f;
+      uint32_t hv[4];
+#pragma unroll
+      for (int pr = 0; pr < 4; ++pr) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float xs = v[it][2 * pr + hh] * dn;
+          const __half hi = __float2half_rn(xs);
+          const __half val = part ? __float2half_rn(xs - __half2float(hi)) : hi;
+          sum += __half2float(val);
+          bits |= (uint32_t)__half_as_ushort(val) << (16 * hh);
+        }
+        hv[pr] = bits;
+      }
+      if (live) {
+        // k = 8 h8 + 2 pr + {0, 1}: k-step kp = h8 / 2, lane column pr, word
+        // 2 (kp & 1) + (h8 & 1) of entry ((slot*P + q)*2 + kp/2)*4 + pr
+        const int kp = h8 >> 1, wd = 2 * (kp & 1) + (h8 & 1);
+        const int e0 = ((slot * P + q) * 2 + (kp >> 1)) * 4;
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) xw[(e0 + pr) * 4 + wd] = hv[pr];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      if (live && h8 == 0) mx[slot * P8 + q] = make_float4(f * sum, f, 64.0f * sum, 0.0f);
     }
-    if (live) xf[idx] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-    // k-step 2h (lo chain) holds values 0..3, k-step 2h+1 (hi chain) 4..7
-    float slo = (hf[0] + hf[1]) + (hf[2] + hf[3]);
-    float shi = (hf[4] + hf[5]) + (hf[6] + hf[7]);
-    slo += __shfl_xor_sync(0xffffffffu, slo, 1);
-    shi += __shfl_xor_sync(0xffffffffu, shi, 1);
-    slo += __shfl_xor_sync(0xffffffffu, slo, 2);
-    shi += __shfl_xor_sync(0xffffffffu, shi, 2);
-    slo += __shfl_xor_sync(0xffffffffu, slo, 4);
-    shi += __shfl_xor_sync(0xffffffffu, shi, 4);
-    if (live && (idx & 7) == 0) mx[slot * P8 + q] = make_float4(f * (slo + shi), f, 64.0f * (slo + shi), 0.0f);
   }
   consumer_sync();
 }
@@ -246,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   float4 *mx = reinterpret_cast<float4 *>(xt + (size_t)a.xcap * P * 128 + 128);
 
   // this CTA's run of chunks
-  const long long C0 = run_begin(blockIdx.x, a.chunks, gridDim.x), C1 = run_begin(blockIdx.x + 1, a.chunks, gridDim.x);
-  const int nch = (int)(C1 - C0);
+  const int C0 = run_begin(a, blockIdx.x), C1 = run_begin(a, blockIdx.x + 1);
+  const int nch = C1 - C0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; ++s) {
@@ -263,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     // ---- producer: one elected lane streams the run -------------------------
     if (lane != 0) return;
     const uint64_t pol = evict_first_policy();
-    long long sl = C0 / a.cps;  // slab and chunk-in-slab of chunk C0 + n
-    int cg = (int)(C0 - sl * a.cps);
+    int sl = C0 / a.cps;  // slab and chunk-in-slab of chunk C0 + n
+    int cg = C0 - sl * a.cps;
     int s = 0;
     uint32_t par = 0;  // parity of this use of stage s
     for (int n = 0; n < nch; ++n, ++cg) {
@@ -277,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         return;
       }
       const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
-      const long long sg = sl * a.ng + g0c;
+      const long long sg = (long long)sl * a.ng + g0c;
       unsigned char *dst = ring + (size_t)s * SB;
       mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
       bulk_g2s(dst, a.qw0 + sg * 4096, cnt * 4096, &full[s], pol);
@@ -294,10 +321,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 
   // ---- consumers: warp `warp` owns tile `warp` of every slab-group ----------
   pdl_wait();
-  const int sl0 = (int)(C0 / a.cps), cg0 = (int)(C0 - (long long)sl0 * a.cps);
+  const int sl0 = C0 / a.cps, cg0 = C0 - sl0 * a.cps;
   const int gs = cg0 * CB;
   const int xcnt =
-      (int)min((long long)a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
+      min(a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
   stage_x(a, gs, xcnt, xf, zero, mx);
 
   const int r = lane >> 2, c = lane & 3;
@@ -398,27 +425,40 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     for (int si = 0; si < NS; ++si)
       *reinterpret_cast<float4 *>(gslot + si * 128) = make_float4(v[si][0], v[si][1], v[si][2], v[si][3]);
   };
-  auto contributors = [&](int sl, long long &clo, long long &chi) {
-    const long long t0 = (long long)sl * a.cps, t1 = t0 + a.cps;
-    clo = run_of(t0, a.chunks, gridDim.x);
-    chi = run_of(t1 - 1, a.chunks, gridDim.x);
+  auto contributors = [&](int sl, int &clo, int &chi) {
+    const int t0 = sl * a.cps;
+    clo = run_of(a, t0);
+    chi = run_of(a, t0 + a.cps - 1);
   };
   auto combine = [&](int sl) {
-    long long clo, chi;
+    int clo, chi;
     contributors(sl, clo, chi);
-    const long long t0 = (long long)sl * a.cps;
+    const int t0 = sl * a.cps;
     float acc[NS][4];
 #pragma unroll
     for (int si = 0; si < NS; ++si)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[si][e] = 0.0f;
-    for (long long q = clo; q <= chi; ++q) {
-      const int qs = (q == clo && run_begin(q, a.chunks, gridDim.x) < t0) ? 1 : 0;
-      const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
+    // up to kBatch contributors' parts are requested before any is added,
+    // so the loads overlap; the sum still runs in CTA order
+    constexpr int kBatch = 8 / NS;
+    for (int q0 = clo; q0 <= chi; q0 += kBatch) {
+      float4 v[kBatch][NS];
 #pragma unroll
-      for (int si = 0; si < NS; ++si) {
-        const float4 v = ld_relaxed_f4(src + si * 128);
-        acc[si][0] += v.x, acc[si][1] += v.y, acc[si][2] += v.z, acc[si][3] += v.w;
+      for (int i = 0; i < kBatch; ++i) {
+        const int q = q0 + i;
+        if (q > chi) break;
+        const int qs = (q == clo && run_begin(a, q) < t0) ? 1 : 0;
+        const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
+#pragma unroll
+        for (int si = 0; si < NS; ++si) v[i][si] = ld_relaxed_f4(src + si * 128);
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i > chi) break;
+#pragma unroll
+        for (int si = 0; si < NS; ++si)
+          acc[si][0] += v[i][si].x, acc[si][1] += v[i][si].y, acc[si][2] += v[i][si].z, acc[si][3] += v[i][si].w;
       }
     }
     if (lane == 0) a.count[(size_t)sl * kSlabTiles + warp] = 0;  // ready for the next call
@@ -487,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   uint32_t done = 0;  // bit 0: first slab complete, bit 1: last slab complete
   if (lane == 0) {
     uint32_t o0 = 0, o1 = 0;
-    long long clo, chi;
+    int clo, chi;
     if (first_slab >= 0) o0 = atom_add_acq_rel(&a.count[(size_t)first_slab * kSlabTiles + warp], 1u);
     if (last_slab >= 0) o1 = atom_add_acq_rel(&a.count[(size_t)last_slab * kSlabTiles + warp], 1u);
     if (first_slab >= 0) {
@@ -565,6 +605,8 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
   const int cb = cfg.warps > 0 ? cfg.warps : 4;
   const int cps = (ng + cb - 1) / cb;
   const long long chunks = (long long)row_slabs(out) * cps;
+  // run arithmetic on the device is 32-bit
+  if ((long long)row_slabs(out) * ng >= (1ll << 31)) return p;
   int per = x_f32 ? 4 : 8;  // tokens per launch: 8 B columns, two per f32 token
   if (per > m) per = m;
   for (;;) {
@@ -627,7 +669,9 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     a.status = status_word();
     a.part = static_cast<float *>(workspace);
     a.count = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + part_bytes);
-    a.chunks = p.chunks;
+    a.chunks = (int)p.chunks;
+    a.run_base = (int)(p.chunks / p.grid);
+    a.run_rem = (int)(p.chunks % p.grid);
     a.cps = p.cps;
     a.m = mt;
     a.in = w0.in;
