@@ -79,7 +79,7 @@ GemvCfg gemv_cfg_override() {
     if (s && *s) {
       int w = 0, d = 0, g = 0;
       if (std::sscanf(s, "%d,%d,%d", &w, &d, &g) >= 1) {
-        if (w == 1 || w == 2 || w == 4) e.warps = w;
+        if (w == 4 || w == 8) e.warps = w;
         if (d >= 2 && d <= 8) e.depth = d;
         if (g > 0) e.grid = g;
       }
