@@ -157,6 +157,36 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
  * call returns it zeroed, so one allocation serves every later call.  Calls
  * that may overlap on the GPU need separate workspaces. */
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
+/* thq4_linear without a workspace argument.  No reference counterpart: the
+ * reference's ops take scratch from candle's buffer pool.  The decode/verify
+ * kernel's split-K scratch (partial sums and arrival counters) comes from one
+ * 6 MiB buffer the library keeps in device memory per device, so the call
+ * allocates nothing and needs only the weight, x and y.
+ *
+ * For callers that cannot allocate or own device memory where they run a
+ * projection: a binding that only receives tensors from its host and has no
+ * device allocator of its own, or a serving loop whose device memory is fixed
+ * before the first request (a cudaMalloc there would also synchronise the
+ * device).
+ *
+ *   - The first call on a device, with that device current, looks up the
+ *     buffer's address once (cudaGetSymbolAddress); make that first call
+ *     before any stream capture.  Neither it nor any later call allocates:
+ *     no cudaMalloc / cudaFree and no allocating library call.
+ *   - A weight whose workspace (thq4_linear_workspace_bytes) is larger than
+ *     the buffer is rejected with THQ4_ERR_UNSUPPORTED before anything is
+ *     launched (at 148 SMs: above about 5.7 million rows).
+ *   - Must start at zero: the arrival counters.  The buffer is zero when the
+ *     library's module loads on a device, and every completed call leaves the
+ *     counters zero again.  A call whose kernel reported kStatusTimeout
+ *     (thq4_device_status) may leave them set; later calls of this entry
+ *     point in that process are then unreliable.
+ *   - Every call on a device shares the one buffer: calls that can overlap on
+ *     the GPU (streams not ordered with each other) race and produce wrong
+ *     results.  Order them on one stream, or use thq4_linear with a workspace
+ *     per stream. */
+thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype,
+                                int m, void *y, int y_dtype, void *stream);
 /* Replaces AffineDequant (quant_kernel.rs:1743-1782, 5836-5899): y bf16
  * [out][in] = bf16(q * s + b). */
 thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);

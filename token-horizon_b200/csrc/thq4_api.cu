@@ -138,6 +138,34 @@ thq4_status check_workspace(void *ws, size_t have, size_t need, const char *who)
 }  // namespace
 }  // namespace thq4
 
+namespace thq4 {
+namespace {
+
+// Scratch of thq4_linear_noalloc (the split-K partials and arrival counters
+// thq4_linear takes from its workspace argument): one buffer per device,
+// zero when the module loads; calls leave the counters zeroed.
+constexpr size_t kNoAllocScratchBytes = 6u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (nullptr and *err set when the lookup fails).
+void *noalloc_scratch(cudaError_t *err) {
+  static DeviceOnce once;
+  static void *addr[64] = {nullptr};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  *err = once.run([&] { return cudaGetSymbolAddress(&addr[dev], g_noalloc_scratch); });
+  return *err == cudaSuccess ? addr[dev] : nullptr;
+}
+
+}  // namespace
+}  // namespace thq4
+
 using namespace thq4;
 
 extern "C" {
@@ -244,6 +272,28 @@ thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
   cudaError_t e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, workspace,
                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, "thq4_linear");
+  return THQ4_OK;
+}
+
+thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
+                                void *stream) {
+  const char *who = "thq4_linear_noalloc";
+  thq4_status s = check_weight(w, who);
+  if (s != THQ4_OK) return s;
+  s = check_io(x, x_dtype, m, y, y_dtype, who);
+  if (s != THQ4_OK) return s;
+  const size_t need = gemv_workspace_bytes(w->out);
+  if (need > kNoAllocScratchBytes)
+    return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": a " + std::to_string(w->out) +
+                                               "-row weight needs " + std::to_string(need) +
+                                               " bytes of scratch, above the built-in " +
+                                               std::to_string(kNoAllocScratchBytes) + "; use thq4_linear");
+  cudaError_t e = cudaSuccess;
+  void *scratch = noalloc_scratch(&e);
+  if (!scratch) return cuda_error(e, "thq4_linear_noalloc: cudaGetSymbolAddress");
+  e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, scratch,
+                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
 }
 

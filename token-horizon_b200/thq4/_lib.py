@@ -65,6 +65,7 @@ SIGNATURES = {
     "thq4_weight_init": (c_int, [POINTER(thq4_weight), c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "thq4_linear": (c_int, [POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
                             c_size_t, c_void_p]),
+    "thq4_linear_noalloc": (c_int, [POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "thq4_gate_up": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
                              c_int, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_workspace_bytes": (c_size_t, [POINTER(thq4_weight), c_int]),
