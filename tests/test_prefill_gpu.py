@@ -1,0 +1,82 @@
+"""The prefill GEMM (m > 8 tokens, tcgen05) through the C ABI against the CPU
+oracle.  The cases are the reference's prefill tests (quant_kernel.rs:
+5428-5466, pf_vec_matches_legacy_bitwise): one LCG stream generates the tiled
+weights and activations of every case in order; gate/up cases are a fused
+[gate | up] weight of 2 x out rows.  The reference compares its kernel
+families with each other; here every output is held to the reference CPU
+path (bf16-dequantised weight, f32 accumulate)."""
+import numpy as np
+import pytest
+import torch
+
+import q4oracle as O
+import thq4
+from helpers import assert_close_ref, assert_gate_up_close, assert_rms_close, dev, dev_sb, to_f32
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def pf_cases():
+    st = O.PfStream()
+    cases = []
+    for out, inp, gu, m in O.PF_CASES:
+        total = 2 * out if gu else out
+        tw, tsb, x = st.case(total, inp, m)
+        wq, sb = O.tiled_to_mlx(tw, tsb, total, inp)
+        cases.append((out, inp, gu, m, tw, tsb, wq, sb, x))
+    return cases
+
+
+@pytest.mark.parametrize("idx", range(len(O.PF_CASES)))
+def test_prefill_matches_reference_cpu_path(pf_cases, idx):
+    out, inp, gu, m, tw, tsb, wq, sb, x = pf_cases[idx]
+    xd = dev(x)
+    xf = O.bf16_to_f32(x)
+    if not gu:
+        q = thq4.QLin.from_layout(thq4.SRC_TILED, dev(tw), dev(tsb), out, inp, thq4.BF16)
+        want = O.linear_dequant(wq, sb, O.SB_BF16, xf)
+        got32 = to_f32(q.linear_ps(xd, out_dtype=torch.float32))
+        assert got32.shape == (m, out)
+        assert_rms_close(f"prefill f32 {out}x{inp} m{m}", got32, want, rel=1e-3)
+        got = to_f32(q.linear(xd))
+        for t in range(m):
+            assert_close_ref(f"prefill bf16 {out}x{inp} m{m} t{t}", got[t], want[t])
+        again = to_f32(q.linear(xd))
+        assert np.array_equal(got, again), "not deterministic"
+    else:
+        q = thq4.QLin(dev(wq), dev(sb), 2 * out, inp, 64)
+        got = to_f32(q.gate_up_act(xd))
+        assert got.shape == (m, out)
+        g = O.linear_dequant(wq, sb, O.SB_BF16, xf)
+        for t in range(m):
+            assert_gate_up_close(f"prefill gate_up {out}x{inp} m{m} t{t}", got[t], g[t, :out], g[t, out:], inp)
+
+
+@pytest.mark.parametrize("m", [9, 16, 127, 300])
+def test_prefill_token_counts(m):
+    """Token counts around the decode/prefill boundary and tile edges."""
+    out, inp = 392, 640
+    wq, sb = O.synthetic_weight(out, inp, 900 + m, O.SB_F16)
+    rng = np.random.default_rng(m)
+    x = O.f32_to_bf16(rng.standard_normal((m, inp)).astype(np.float32))
+    q = thq4.QLin(dev(wq), dev_sb(sb, O.SB_F16), out, inp, 64).tiled()
+    got = to_f32(q.linear_ps(dev(x), out_dtype=torch.float32))
+    assert_rms_close(f"prefill m{m}", got, O.linear_dequant(wq, sb, O.SB_F16, O.bf16_to_f32(x)), rel=1e-3)
+
+
+@pytest.mark.parametrize("m", [512, 2048])
+def test_prefill_baseline_config(m):
+    """x [m x 4096] bf16 ~ N(0,1), W [12288 x 4096] ~
+    N(0, 0.02) with f16 scale/bias.  The whole product runs on the GPU; the
+    oracle checks 192 output columns (a block at each end and a seeded
+    sample) on every token."""
+    out, inp = 12288, 4096
+    wq, sb = O.synthetic_weight(out, inp, 77, O.SB_F16)
+    rng = np.random.default_rng(5 + m)
+    x = O.f32_to_bf16(rng.standard_normal((m, inp)).astype(np.float32))
+    q = thq4.QLin(dev(wq), dev_sb(sb, O.SB_F16), out, inp, 64).tiled()
+    got = to_f32(q.linear_ps(dev(x), out_dtype=torch.float32))
+    cols = np.unique(np.concatenate([np.arange(64), np.arange(out - 64, out), rng.choice(out, 64, replace=False)]))
+    want = O.linear_dequant(wq[cols], sb[cols], O.SB_F16, O.bf16_to_f32(x))
+    assert_rms_close(f"prefill C3 m{m}", got[:, cols], want, rel=1e-3)

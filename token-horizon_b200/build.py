@@ -61,7 +61,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             if p.returncode != 0:
                 raise RuntimeError("nvcc failed: " + " ".join(cmd))
     if force or jobs or _stale(OUT, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs, "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs]
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode != 0:
             sys.stderr.write(p.stdout + p.stderr)

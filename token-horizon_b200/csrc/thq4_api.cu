@@ -267,6 +267,11 @@ thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
   if (s != THQ4_OK) return s;
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_linear");
   if (s != THQ4_OK) return s;
+  if (prefill_supported(m, x_dtype == THQ4_F32)) {
+    const cudaError_t e = prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "thq4_linear (prefill)");
+    return THQ4_OK;
+  }
   s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(w->out), "thq4_linear");
   if (s != THQ4_OK) return s;
   cudaError_t e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, workspace,
@@ -307,6 +312,11 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const v
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_gate_up: gate and up halves differ in shape or dtype");
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_gate_up");
   if (s != THQ4_OK) return s;
+  if (prefill_supported(m, x_dtype == THQ4_F32)) {
+    const cudaError_t e = prefill_launch(*gate, up, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "thq4_gate_up (prefill)");
+    return THQ4_OK;
+  }
   s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(gate->out), "thq4_gate_up");
   if (s != THQ4_OK) return s;
   cudaError_t e = gemv_launch(*gate, up, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, workspace,

@@ -71,6 +71,12 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
                         int m, void *y, bool y_f32, void *workspace, cudaStream_t stream);
 
+// ---- prefill GEMM (tcgen05) -------------------------------------------------
+// The tensor-core path serves m > 8 tokens of bf16 x.
+bool prefill_supported(int m, bool x_f32);
+cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
+                           cudaStream_t stream);
+
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,
                           int row_begin, int rows, void *dst_qw, void *dst_sb, cudaStream_t stream);
