@@ -11,23 +11,28 @@
 // bf16(silu(bf16 g) * bf16 u) (qwen35.rs:711-884).
 //
 // Bound: tensor throughput (51.5 GFLOP per 512-token call of the BASELINE
-// 12288 x 4096 shape against 28 MB of weights).  Design:
-//   - persistent CTAs (one per SM) walk output tiles of 256 tokens x 128
-//     output rows (one frag slab); consecutive tiles share the slab, so the
-//     weight is fetched from HBM once and re-read from L2;
-//   - per 64-k stage (one quant group): a producer warp loads the x tile with
-//     a 2-D TMA (two 128-row boxes, 128-byte swizzle, zero fill past m) and
-//     the raw slab-group (4608 bytes of nibbles + scales) with one bulk copy;
-//   - four dequant warps turn the slab-group into the bf16 B tile in the
-//     K-major 128-byte-swizzled layout tcgen05 reads (each 4-byte store lands
-//     in a distinct bank), fence it to the async proxy and arrive;
+// 12288 x 4096 shape against 28 MB of weights).  The tensor core's operand
+// reads, the TMA fills and any dequantised tile written to shared memory all
+// share the SM's 128 bytes/clock of shared-memory bandwidth, which a design
+// with the bf16 weight tile in shared memory exhausts at ~55% of peak.  So:
+//   - the weights are the A operand and live in TMEM: eight dequant warps
+//     turn each raw slab-group (128 rows x 64 k: 4096 bytes of nibbles + 512
+//     of scales, one bulk copy) into bf16 in registers and store it straight
+//     into a TMEM ring (tcgen05.st, thread i -> row lane i).  A nibble
+//     becomes an f32 by OR-ing it into the mantissa of 2^23 and subtracting
+//     2^23 (exact); high nibbles stay in bits 4..7 and take s/16 (exact);
+//     pairs go through packed f32x2 add / fma and one cvt to bf16x2;
+//   - the activations are the B operand: x tiles of 256 (gate/up: 128)
+//     tokens x 64 k, loaded by a 2-D TMA with 128-byte swizzle (zero fill
+//     past m) into a shared-memory ring;
 //   - one thread issues tcgen05.mma.kind::f16 (bf16 in, f32 accumulate in
-//     TMEM): per k-step of 16, two M=128 x N=128 MMAs (the two token halves)
-//     sharing the B tile, and commits the stage back to the producer;
-//   - the accumulator is double-buffered in TMEM (2 x 256 of its 512
-//     columns), so four epilogue warps drain tile i (tcgen05.ld, convert,
-//     store) while tile i+1 accumulates; the gate/up form keeps gate and up
-//     accumulators side by side (all 512 columns) and drains between tiles;
+//     TMEM), M = 128 output rows x N = 256 tokens per k-step of 16, and
+//     commits each stage back to the producer;
+//   - persistent CTAs (one per SM) walk tiles of one slab (128 rows) x 256
+//     tokens, token tiles fastest, so a slab is fetched from HBM once and
+//     re-read from L2; eight epilogue warps drain D (tcgen05.ld) -- a warp's
+//     32 lanes hold 32 consecutive output rows, so each store of a token's
+//     values is one contiguous 64-byte segment of y;
 //   - every wait is bounded; a timeout raises kStatusTimeout, sets a CTA-wide
 //     abort flag that ends every role's loop, and the CTA still frees TMEM.
 #include <cuda.h>
@@ -42,16 +47,14 @@
 namespace thq4 {
 namespace {
 
-constexpr int kBM = 256;  // tokens per tile (two M = 128 MMAs)
-constexpr int kBN = 128;  // output rows per tile (one slab)
+constexpr int kBN = 128;  // output rows per tile (one slab): the MMA's M
 constexpr int kBK = 64;   // k per stage (one quant group)
-constexpr int kDeqWarps = 4, kEpiWarps = 4;
-constexpr int kWarpEpi0 = 4, kWarpProd = 8, kWarpMma = 9;  // dequant warps are 0..3
-constexpr int kPfThreads = 10 * 32;
-constexpr uint32_t kXBox = 128 * kBK * 2;        // one 128-row x box, bytes
-constexpr uint32_t kXStage = 2 * kXBox;          // 32 KB
-constexpr uint32_t kWStage = kBN * kBK * 2;      // bf16 B tile, 16 KB
-constexpr uint32_t kRawStage = 4096 + 512;       // one slab-group
+constexpr int kDeqWarps = 8, kEpiWarps = 8;
+constexpr int kWarpEpi0 = 8, kWarpProd = 16, kWarpMma = 17;  // dequant warps are 0..7
+constexpr int kPfThreads = 18 * 32;
+constexpr uint32_t kXBox = 128 * kBK * 2;   // one 128-token x box, bytes
+constexpr uint32_t kRawStage = 4096 + 512;  // one slab-group
+constexpr int kAcolsPerStage = kBK / 2;     // TMEM columns of one stage's A (bf16 pairs)
 
 struct PfArgs {
   const uint8_t *qw[2];  // gate (or the only) weight, up
@@ -63,16 +66,23 @@ struct PfArgs {
   int yf32;
 };
 
-template <int NS, int S>
-struct PfSmem {
+// NS weight streams (1, or 2 for gate/up), BT tokens per tile, S stages
+template <int NS, int BT, int S>
+struct PfCfg {
+  static constexpr uint32_t x_stage = BT * kBK * 2;
   static constexpr uint32_t x_off = 0;
-  static constexpr uint32_t w_off = x_off + S * kXStage;
-  static constexpr uint32_t raw_off = w_off + S * NS * kWStage;
+  static constexpr uint32_t raw_off = x_off + S * x_stage;
   static constexpr uint32_t bar_off = raw_off + S * NS * kRawStage;
-  // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf[2], acce[2]
-  static constexpr uint32_t misc_off = bar_off + (4 * S + 4) * 8;
+  // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf, acce
+  static constexpr uint32_t misc_off = bar_off + (4 * S + 2) * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t alloc = bytes + 1024;  // room to align the base to 1024
+  // TMEM: D (NS accumulators of BT columns), then the A ring
+  static constexpr int d_cols = NS * BT;
+  static constexpr int a_col0 = d_cols;
+  static constexpr int cols = d_cols + S * NS * kAcolsPerStage;
+  static_assert(cols <= 512, "TMEM holds 512 columns");
+  static_assert(alloc <= 227 * 1024, "shared memory");
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -81,14 +91,29 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::f16 instruction descriptor: bf16 A and B, f32 D, K-major, M = 128, N = kBN
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// kind::f16 instruction descriptor: bf16 A and B, f32 D, K-major, M = 128, N
+constexpr uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_bf16_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+// D[128 x N] (+)= A[128 x 16] . B[N x 16]^T with A in TMEM (lane = row, a
+// 32-bit column = two consecutive k) and B in shared memory.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// 16 columns of this warp's 32 TMEM lanes from registers (thread i -> lane i)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_addr(bar))
@@ -136,51 +161,58 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
   (void)mbar_wait_bounded(bar, parity, kWaitLimitNs);
 }
 
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ uint64_t u2(uint32_t lo, uint32_t hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+  return v;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// bf16x2 of the f32 pair {lo, hi}, round to nearest even
+__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// (w & mask) | 0x4B000000: the f32 2^23 + (w & mask)
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t magic23(uint32_t w) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(w), "n"(MASK), "n"(0x4B000000));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Stores 32 consecutive outputs of one token row.
-__device__ __forceinline__ void store_row32(const PfArgs &a, int token, int col, const float (&v)[32]) {
-  if (token >= a.m || col >= a.n) return;
-  const bool full = col + 32 <= a.n;
-  if (a.yf32) {
-    float *dst = static_cast<float *>(a.y) + (size_t)token * a.n + col;
-    if (full && (a.n & 3) == 0) {
-#pragma unroll
-      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4 *>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (col + e < a.n) dst[e] = v[e];
-    }
-  } else {
-    uint16_t *dst = static_cast<uint16_t *>(a.y) + (size_t)token * a.n + col;
-    if (full && (a.n & 7) == 0) {
-#pragma unroll
-      for (int e = 0; e < 32; e += 8)
-        *reinterpret_cast<uint4 *>(dst + e) = make_uint4(pack_bf16(v[e], v[e + 1]), pack_bf16(v[e + 2], v[e + 3]),
-                                                         pack_bf16(v[e + 4], v[e + 5]), pack_bf16(v[e + 6], v[e + 7]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (col + e < a.n) dst[e] = f32_to_bf16_bits(v[e]);
-    }
-  }
-}
-
-template <int NS, int S, bool SF16>
+template <int NS, int BT, int S, bool SF16>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap xmap, const PfArgs a) {
-  using L = PfSmem<NS, S>;
-  constexpr bool kDB = NS == 1;  // double-buffered accumulator
+  using C = PfCfg<NS, BT, S>;
+  constexpr uint32_t kIdesc = idesc_bf16(BT);
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::bar_off);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::bar_off);
   uint64_t *xfull = bars, *rawfull = bars + S, *deq = bars + 2 * S, *empty = bars + 3 * S;
-  uint64_t *accf = bars + 4 * S, *acce = accf + 2;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + L::misc_off);
-  volatile int *abort = reinterpret_cast<volatile int *>(sm + L::misc_off + 4);
+  uint64_t *accf = bars + 4 * S, *acce = accf + 1;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + C::misc_off);
+  volatile int *abort = reinterpret_cast<volatile int *>(sm + C::misc_off + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -190,13 +222,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       mbar_init(&deq[s], kDeqWarps);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kEpiWarps);
-    }
+    mbar_init(accf, 1);
+    mbar_init(acce, kEpiWarps);
     *abort = 0;
   }
-  if (warp == kWarpMma) {  // the whole of TMEM: two 256-column accumulators
+  if (warp == kWarpMma) {  // all of TMEM (one CTA per SM)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(smem_addr(tmem_holder)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
@@ -216,11 +246,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         for (int g = 0; g < a.ng; ++g, ++it) {
           const int s = it % S;
           if (it >= S && !pf_wait(&empty[s], (uint32_t)(((it / S) - 1) & 1), abort, a.status)) break;
-          unsigned char *xd = sm + L::x_off + (size_t)s * kXStage;
-          mbar_arrive_expect_tx(&xfull[s], kXStage);
-          tma_load_2d(xd, &xmap, g * kBK, mt * kBM, &xfull[s]);
-          tma_load_2d(xd + kXBox, &xmap, g * kBK, mt * kBM + 128, &xfull[s]);
-          unsigned char *rd = sm + L::raw_off + (size_t)s * NS * kRawStage;
+          unsigned char *xd = sm + C::x_off + (size_t)s * C::x_stage;
+          mbar_arrive_expect_tx(&xfull[s], C::x_stage);
+#pragma unroll
+          for (int bx = 0; bx < BT / 128; ++bx) tma_load_2d(xd + bx * kXBox, &xmap, g * kBK, mt * BT + bx * 128, &xfull[s]);
+          unsigned char *rd = sm + C::raw_off + (size_t)s * NS * kRawStage;
           const size_t sg = (size_t)nt * a.ng + g;
           mbar_arrive_expect_tx(&rawfull[s], NS * kRawStage);
 #pragma unroll
@@ -243,9 +273,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     if (lane == 0) {
       int it = 0, local = 0, committed = 0;
       for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, ++local) {
-        const int b = kDB ? (local & 1) : 0;
-        const int use = kDB ? (local >> 1) : local;  // earlier uses of accumulator b
-        if (use >= 1 && !pf_wait(&acce[b], (uint32_t)((use - 1) & 1), abort, a.status)) break;
+        if (local >= 1 && !pf_wait(acce, (uint32_t)((local - 1) & 1), abort, a.status)) break;
         tc_fence_after();
         bool ok = true;
         for (int g = 0; g < a.ng; ++g, ++it) {
@@ -256,31 +284,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
             break;
           }
           tc_fence_after();
-          const uint32_t xa = smem_addr(sm + L::x_off + (size_t)s * kXStage);
+          const uint32_t xa = smem_addr(sm + C::x_off + (size_t)s * C::x_stage);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t a0 = umma_desc_sw128(xa + kk * 32), a1 = umma_desc_sw128(xa + kXBox + kk * 32);
+            const uint64_t bd = umma_desc_sw128(xa + kk * 32);
+            const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
-            for (int si = 0; si < NS; ++si) {
-              const uint64_t bd = umma_desc_sw128(smem_addr(sm + L::w_off + (size_t)(s * NS + si) * kWStage) + kk * 32);
-              const uint32_t col = (uint32_t)((b * NS + si) * 2 * kBN);
-              const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
-              mma_bf16_ss(tmem + col, a0, bd, acc);
-              mma_bf16_ss(tmem + col + kBN, a1, bd, acc);
-            }
+            for (int si = 0; si < NS; ++si)
+              mma_bf16_ts(tmem + (uint32_t)(si * BT),
+                          tmem + (uint32_t)(C::a_col0 + (s * NS + si) * kAcolsPerStage + kk * 8), bd, kIdesc, acc);
           }
-          umma_commit(&empty[s]);  // frees the stage once these MMAs are done
+          umma_commit(&empty[s]);  // frees the x, raw and A slots once these MMAs are done
           committed = it + 1;
         }
         if (!ok) break;
-        umma_commit(&accf[b]);
+        umma_commit(accf);
       }
       if (*abort && committed > 0)
         drain_wait(&empty[(committed - 1) % S], (uint32_t)(((committed - 1) / S) & 1));
     }
   } else if (warp < kWarpEpi0) {
-    // ---- dequant: raw slab-group -> bf16 B tile (K-major, 128-byte swizzle) ----
-    const int t = threadIdx.x;  // 0..127
+    // ---- dequant: raw slab-group -> bf16 A in TMEM -----------------------------
+    // warp w: TMEM lane quarter q = w % 4 (rows 32q..32q+31, this thread row
+    // 32q + lane) and k half kh = w / 4 (k 32kh..32kh+31 = A columns 16kh..)
+    const int q = warp & 3, kh = warp >> 2;
+    const int row = 32 * q + lane;  // 0..127
+    const int tl = row >> 4, r = row & 7, hrow = (row >> 3) & 1;
+    const uint64_t m23 = f2(-8388608.0f, -8388608.0f);
     int it = 0;
     for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
       bool ok = true;
@@ -292,33 +322,34 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         }
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
-          const unsigned char *raw = sm + L::raw_off + (size_t)(s * NS + si) * kRawStage;
-          unsigned char *wt = sm + L::w_off + (size_t)(s * NS + si) * kWStage;
+          const unsigned char *raw = sm + C::raw_off + (size_t)(s * NS + si) * kRawStage;
+          const uint2 qd = *reinterpret_cast<const uint2 *>(raw + 4096 + tl * 64 + r * 8);
+          const uint32_t sbw = hrow ? qd.y : qd.x;
+          const float sv = sb_to_f32<SF16>(sbw & 0xffffu), bv = sb_to_f32<SF16>(sbw >> 16);
+          // low nibbles take s, high nibbles (kept x16) take s / 16
+          const uint64_t sc0 = f2(sv, sv), sc1 = f2(sv * 0.0625f, sv * 0.0625f), bb = f2(bv, bv);
+          uint32_t v[16];
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int ch = t + half * 128, tl = ch >> 5, ln = ch & 31, r = ln >> 2, c = ln & 3;
-            const uint4 w4 = *reinterpret_cast<const uint4 *>(raw + ch * 16);
-            const uint2 q = *reinterpret_cast<const uint2 *>(raw + 4096 + tl * 64 + r * 8);
-            const float s0 = sb_to_f32<SF16>(q.x & 0xffffu), b0 = sb_to_f32<SF16>(q.x >> 16);
-            const float s8 = sb_to_f32<SF16>(q.y & 0xffffu), b8 = sb_to_f32<SF16>(q.y >> 16);
-            const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          for (int c = 0; c < 4; ++c) {
+            // lane chunk (4r + c) of tile tl holds this row's k 2c, 2c+1 (+8,
+            // +16, +24) of words j = 2kh, 2kh+1
+            const uint2 wd = *reinterpret_cast<const uint2 *>(raw + tl * 512 + (4 * r + c) * 16 + kh * 8);
+            const uint32_t ww[2] = {wd.x, wd.y};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int hi8 = (i >> 1) & 1;
-                const float sc = hi8 ? s8 : s0, bi = hi8 ? b8 : b0;
-                const float v0 = fmaf((float)((wv[j] >> (4 * i)) & 0xFu), sc, bi);
-                const float v1 = fmaf((float)((wv[j] >> (4 * i + 16)) & 0xFu), sc, bi);
-                const int row = tl * 16 + r + 8 * hi8;                        // 0..127
-                const int chunk = 4 * (j >> 1) + (j & 1) + 2 * (i & 1);      // 16-byte column of the row
-                *reinterpret_cast<uint32_t *>(wt + (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4) +
-                                              4 * c) = pack_bf16(v0, v1);
-              }
+            for (int jj = 0; jj < 2; ++jj) {
+              // this row's nibbles: byte hrow (k pair +0) and byte hrow + 2
+              // (k pair +1), low half e = 0 (k + 0) and high half e = 1 (k + 16)
+              const uint32_t lo = ww[jj] >> (8 * hrow), hi = ww[jj] >> (8 * hrow + 16);
+              const uint64_t p0 = u2(magic23<0x0Fu>(lo), magic23<0x0Fu>(hi));
+              const uint64_t p1 = u2(magic23<0xF0u>(lo), magic23<0xF0u>(hi));
+              // k within the half: 8 jj + 16 e + 2c -> A column 4 jj + 8 e + c
+              v[4 * jj + c] = pack_bf16x2(fma2(add2(p0, m23), sc0, bb));
+              v[4 * jj + 8 + c] = pack_bf16x2(fma2(add2(p1, m23), sc1, bb));
             }
           }
+          tmem_st16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(C::a_col0 + (s * NS + si) * kAcolsPerStage + 16 * kh), v);
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> tcgen05 reads
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&deq[s]);
       }
@@ -326,38 +357,48 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     }
   } else {
     // ---- epilogue: TMEM -> registers -> y --------------------------------------
-    const int q4 = warp & 3;  // this warp's TMEM lane quarter
+    // warp: TMEM lane quarter q (rows 32q..), token half th of the tile
+    const int q = warp & 3, th = (warp - kWarpEpi0) >> 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, ++local) {
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
-      const int b = kDB ? (local & 1) : 0;
-      const int use = kDB ? (local >> 1) : local;
-      if (!pf_wait(&accf[b], (uint32_t)(use & 1), abort, a.status)) break;
+      if (!pf_wait(accf, (uint32_t)(local & 1), abort, a.status)) break;
       tc_fence_after();
+      const int n = nt * kBN + 32 * q + lane;
+      constexpr int kChunks = BT / 32 / 2;  // 32-token chunks per warp
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int token = mt * kBM + h * 128 + q4 * 32 + lane;
-#pragma unroll 1
-        for (int cc = 0; cc < kBN / 32; ++cc) {
-          const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-          uint32_t u[32];
-          float v[32];
-          tmem_ld32(tmem + lane_base + (uint32_t)(b * NS * 2 * kBN + h * kBN + cc * 32), u);
-          if constexpr (NS == 2) {
-            uint32_t uu[32];
-            tmem_ld32(tmem + lane_base + (uint32_t)(2 * kBN + h * kBN + cc * 32), uu);
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int t0 = mt * BT + (th * kChunks + cc) * 32;
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((th * kChunks + cc) * 32);
+        uint32_t u[32];
+        float v[32];
+        tmem_ld32(taddr, u);
+        if constexpr (NS == 2) {
+          uint32_t uu[32];
+          tmem_ld32(taddr + BT, uu);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = silu_mul(__uint_as_float(u[e]), __uint_as_float(uu[e]));
-          } else {
+          for (int e = 0; e < 32; ++e) v[e] = silu_mul(__uint_as_float(u[e]), __uint_as_float(uu[e]));
+        } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]);
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]);
+        }
+        // lanes hold 32 consecutive rows n: each token's store is contiguous
+        if (n < a.n) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int t = t0 + e;
+            if (t < a.m) {
+              if (a.yf32)
+                static_cast<float *>(a.y)[(size_t)t * a.n + n] = v[e];
+              else
+                static_cast<uint16_t *>(a.y)[(size_t)t * a.n + n] = f32_to_bf16_bits(v[e]);
+            }
           }
-          store_row32(a, token, nt * kBN + cc * 32, v);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[b]);
+      if (lane == 0) mbar_arrive(acce);
     }
   }
 
@@ -370,11 +411,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   }
 }
 
-template <int NS, int S, bool SF16>
+template <int NS, int BT, int S, bool SF16>
 cudaError_t prefill_launch_t(const CUtensorMap &map, const PfArgs &a, int grid, cudaStream_t stream) {
-  auto *k = &prefill_kernel<NS, S, SF16>;
+  auto *k = &prefill_kernel<NS, BT, S, SF16>;
   static DeviceOnce once;
-  const size_t smem = PfSmem<NS, S>::alloc;
+  const size_t smem = PfCfg<NS, BT, S>::alloc;
   cudaError_t e = once.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (e != cudaSuccess) return e;
   k<<<grid, kPfThreads, smem, stream>>>(map, a);
@@ -387,7 +428,6 @@ bool prefill_supported(int m, bool x_f32) { return m > 8 && !x_f32; }
 
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
                            cudaStream_t stream) {
-  // x [m][k] bf16 as a 2-D tensor (k innermost), 64 x 128 boxes, 128-byte swizzle
   // the driver's tensor-map encoder, looked up through the runtime so the
   // library needs no link-time driver dependency
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
@@ -400,18 +440,19 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
       encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   if (!encode) return cudaErrorNotSupported;
+  // x [m][k] bf16 as a 2-D tensor (k innermost), 64 x 128 boxes, 128-byte swizzle
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)w0.in, (cuuint64_t)m};
   const cuuint64_t strides[1] = {(cuuint64_t)w0.in * 2};
   const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims,
-                                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
   PfArgs a{};
   const bool gate_up = w1 != nullptr;
+  const int bt = gate_up ? 128 : 256;
   a.qw[0] = static_cast<const uint8_t *>(w0.qw);
   a.sb[0] = static_cast<const uint8_t *>(w0.sb);
   a.qw[1] = gate_up ? static_cast<const uint8_t *>(w1->qw) : nullptr;
@@ -421,7 +462,7 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   a.m = m;
   a.n = w0.out;
   a.ng = w0.in / kBK;
-  a.m_tiles = (m + kBM - 1) / kBM;
+  a.m_tiles = (m + bt - 1) / bt;
   const long long tiles = (long long)a.m_tiles * row_slabs(w0.out);
   if (tiles >= (1ll << 31)) return cudaErrorInvalidValue;
   a.tiles = (int)tiles;
@@ -429,8 +470,10 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   const int grid = (int)std::min<long long>(tiles, device_sm_count());
   const bool f16 = w0.sb_dtype == THQ4_F16;
   if (gate_up)
-    return f16 ? prefill_launch_t<2, 3, true>(map, a, grid, stream) : prefill_launch_t<2, 3, false>(map, a, grid, stream);
-  return f16 ? prefill_launch_t<1, 4, true>(map, a, grid, stream) : prefill_launch_t<1, 4, false>(map, a, grid, stream);
+    return f16 ? prefill_launch_t<2, 128, 4, true>(map, a, grid, stream)
+               : prefill_launch_t<2, 128, 4, false>(map, a, grid, stream);
+  return f16 ? prefill_launch_t<1, 256, 5, true>(map, a, grid, stream)
+             : prefill_launch_t<1, 256, 5, false>(map, a, grid, stream);
 }
 
 }  // namespace thq4
