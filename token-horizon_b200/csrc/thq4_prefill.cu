@@ -63,7 +63,7 @@ struct PfArgs {
   uint32_t *status;
   int m, n, ng;
   int m_tiles, tiles;
-  int yf32;
+  int yf32;  // unused by the kernels (a template parameter); kept for tracing
 };
 
 // NS weight streams (1, or 2 for gate/up), BT tokens per tile, S stages
@@ -72,9 +72,11 @@ struct PfCfg {
   static constexpr uint32_t x_stage = BT * kBK * 2;
   static constexpr uint32_t x_off = 0;
   static constexpr uint32_t raw_off = x_off + S * x_stage;
-  static constexpr uint32_t bar_off = raw_off + S * NS * kRawStage;
-  // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf, acce
-  static constexpr uint32_t misc_off = bar_off + (4 * S + 2) * 8;
+  // a bf16 output tile [BT tokens][128 rows], staged between TMEM and y
+  static constexpr uint32_t y_off = raw_off + S * NS * kRawStage;
+  static constexpr uint32_t bar_off = y_off + BT * kBN * 2;
+  // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf, acce, yfull, ydone
+  static constexpr uint32_t misc_off = bar_off + (4 * S + 4) * 8;
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t alloc = bytes + 1024;  // room to align the base to 1024
   // TMEM: D (NS accumulators of BT columns), then the A ring
@@ -202,7 +204,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int NS, int BT, int S, bool SF16>
+template <int NS, int BT, int S, bool SF16, bool YF32>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap xmap, const PfArgs a) {
   using C = PfCfg<NS, BT, S>;
   constexpr uint32_t kIdesc = idesc_bf16(BT);
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::bar_off);
   uint64_t *xfull = bars, *rawfull = bars + S, *deq = bars + 2 * S, *empty = bars + 3 * S;
-  uint64_t *accf = bars + 4 * S, *acce = accf + 1;
+  uint64_t *accf = bars + 4 * S, *acce = accf + 1, *yfull = accf + 2, *ydone = accf + 3;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + C::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(sm + C::misc_off + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -224,6 +226,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     }
     mbar_init(accf, 1);
     mbar_init(acce, kEpiWarps);
+    mbar_init(yfull, kEpiWarps);
+    mbar_init(ydone, kEpiWarps);
     *abort = 0;
   }
   if (warp == kWarpMma) {  // all of TMEM (one CTA per SM)
@@ -356,20 +360,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       if (!ok) break;
     }
   } else {
-    // ---- epilogue: TMEM -> registers -> y --------------------------------------
-    // warp: TMEM lane quarter q (rows 32q..), token half th of the tile
+    // ---- epilogue: TMEM -> registers -> (bf16 tile in SMEM) -> y --------------
+    // warp: TMEM lane quarter q (rows 32q..), token half th of the tile.  For
+    // a bf16 y the accumulator is released as soon as it sits in the SMEM
+    // tile, and y is then written in 16-byte pieces, a token's 128 values
+    // (256 contiguous bytes) at a time; an f32 y is stored straight from
+    // registers, a warp's 32 rows of one token being one contiguous segment.
     const int q = warp & 3, th = (warp - kWarpEpi0) >> 2;
+    const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..255
+    uint16_t *ytile = reinterpret_cast<uint16_t *>(sm + C::y_off);
     int local = 0;
     for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, ++local) {
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
       if (!pf_wait(accf, (uint32_t)(local & 1), abort, a.status)) break;
+      // the SMEM tile is free once every warp stored the previous one
+      if (!YF32 && local >= 1 && !pf_wait(ydone, (uint32_t)((local - 1) & 1), abort, a.status)) break;
       tc_fence_after();
-      const int n = nt * kBN + 32 * q + lane;
+      const int nl = 32 * q + lane, n = nt * kBN + nl;
       constexpr int kChunks = BT / 32 / 2;  // 32-token chunks per warp
 #pragma unroll 1
       for (int cc = 0; cc < kChunks; ++cc) {
-        const int t0 = mt * BT + (th * kChunks + cc) * 32;
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((th * kChunks + cc) * 32);
+        const int tc0 = (th * kChunks + cc) * 32;  // first token of the chunk within the tile
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)tc0;
         uint32_t u[32];
         float v[32];
         tmem_ld32(taddr, u);
@@ -382,23 +394,47 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]);
         }
-        // lanes hold 32 consecutive rows n: each token's store is contiguous
-        if (n < a.n) {
+        if constexpr (YF32) {
+          if (n < a.n) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int t = t0 + e;
-            if (t < a.m) {
-              if (a.yf32)
-                static_cast<float *>(a.y)[(size_t)t * a.n + n] = v[e];
-              else
-                static_cast<uint16_t *>(a.y)[(size_t)t * a.n + n] = f32_to_bf16_bits(v[e]);
+            for (int e = 0; e < 32; ++e) {
+              const int t = mt * BT + tc0 + e;
+              if (t < a.m) static_cast<float *>(a.y)[(size_t)t * a.n + n] = v[e];
             }
           }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ytile[(tc0 + e) * kBN + nl] = f32_to_bf16_bits(v[e]);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce);
+      if (lane == 0) mbar_arrive(acce);  // the MMA may overwrite D from here on
+      if constexpr (!YF32) {
+        if (lane == 0) mbar_arrive(yfull);
+        if (!pf_wait(yfull, (uint32_t)(local & 1), abort, a.status)) break;
+        // BT token rows of 256 bytes; 256 threads, 16-byte pieces
+        constexpr int kPer = BT * 16 / (kEpiWarps * 32);  // pieces per thread
+        const bool vec = (a.n & 7) == 0 && nt * kBN + kBN <= a.n;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int piece = et + i * kEpiWarps * 32, tt = piece >> 4, col = (piece & 15) * 8;
+          const int t = mt * BT + tt;
+          if (t >= a.m) continue;
+          const uint4 val = *reinterpret_cast<const uint4 *>(ytile + tt * kBN + col);
+          uint16_t *dst = static_cast<uint16_t *>(a.y) + (size_t)t * a.n + nt * kBN + col;
+          if (vec) {
+            *reinterpret_cast<uint4 *>(dst) = val;
+          } else {
+            const uint16_t *h = reinterpret_cast<const uint16_t *>(&val);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (nt * kBN + col + e < a.n) dst[e] = h[e];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ydone);
+      }
     }
   }
 
@@ -411,9 +447,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   }
 }
 
-template <int NS, int BT, int S, bool SF16>
+template <int NS, int BT, int S, bool SF16, bool YF32>
 cudaError_t prefill_launch_t(const CUtensorMap &map, const PfArgs &a, int grid, cudaStream_t stream) {
-  auto *k = &prefill_kernel<NS, BT, S, SF16>;
+  auto *k = &prefill_kernel<NS, BT, S, SF16, YF32>;
   static DeviceOnce once;
   const size_t smem = PfCfg<NS, BT, S>::alloc;
   cudaError_t e = once.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
@@ -469,11 +505,14 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   a.yf32 = y_f32 ? 1 : 0;
   const int grid = (int)std::min<long long>(tiles, device_sm_count());
   const bool f16 = w0.sb_dtype == THQ4_F16;
-  if (gate_up)
-    return f16 ? prefill_launch_t<2, 128, 4, true>(map, a, grid, stream)
-               : prefill_launch_t<2, 128, 4, false>(map, a, grid, stream);
-  return f16 ? prefill_launch_t<1, 256, 5, true>(map, a, grid, stream)
-             : prefill_launch_t<1, 256, 5, false>(map, a, grid, stream);
+#define THQ4_PF(NS_, BT_, S_)                                                                         \
+  return f16 ? (y_f32 ? prefill_launch_t<NS_, BT_, S_, true, true>(map, a, grid, stream)                  \
+                      : prefill_launch_t<NS_, BT_, S_, true, false>(map, a, grid, stream))                \
+             : (y_f32 ? prefill_launch_t<NS_, BT_, S_, false, true>(map, a, grid, stream)                 \
+                      : prefill_launch_t<NS_, BT_, S_, false, false>(map, a, grid, stream));
+  if (gate_up) THQ4_PF(2, 128, 4)
+  THQ4_PF(1, 256, 4)
+#undef THQ4_PF
 }
 
 }  // namespace thq4
