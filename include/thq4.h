@@ -191,6 +191,40 @@ thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype
  * [out][in] = bf16(q * s + b). */
 thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);
 
+/* ---- MoE (replaces Splash MoE::add, docs/splash/runtime/ops/MoE.cpp:119-231,
+ * and its kernels in docs/splash/runtime/metal/kernels/shared/moe.metal) ---- */
+
+/* Group tiles (of 32 routes each) the routing of T tokens to k of E experts
+ * can produce: min(T*k/32 + E, T*k) (moeMaximumTiles, MoE.hpp:72-77, without
+ * a shared expert). */
+uint32_t thq4_moe_max_tiles(int T, int E, int k);
+/* Routing on the device (moe_route_select_q8 + moe_group_routes,
+ * moe.metal:270-449).  logits bf16 [T][E]; outputs: ids u32 [T][k] (experts by
+ * descending score, lowest id first among equal scores), weights bf16 [T][k]
+ * (softmax over the k selected scores), tiles u32 [max_tiles][2] = {expert,
+ * live rows}, grouped_routes u32 [max_tiles*32] (route t*k+slot, padding
+ * 0xFFFFFFFF), route_rows u32 [T*k] (the inverse map), ntiles u32 [1].  Within
+ * an expert, routes ascend by route index: the permutation is deterministic
+ * and bit-exact.  max_tiles >= thq4_moe_max_tiles(T, E, k); E <= 1024,
+ * 1 <= k <= min(E, 32). */
+thq4_status thq4_moe_route(const void *logits, int T, int E, int k, uint32_t *ids, void *weights,
+                           uint32_t *tiles, uint32_t *grouped_routes, uint32_t *route_rows,
+                           uint32_t *ntiles, int max_tiles, void *stream);
+/* Workspace bytes of thq4_moe (routing tables, the gathered rows and the
+ * per-route intermediates). */
+size_t thq4_moe_workspace_bytes(int T, int H, int I, int E, int k);
+/* One MoE layer: y bf16 [T][H] = residual (optional, bf16 [T][H]) + sum over
+ * the k routes of each token, in slot order, of w * down(bf16(silu(bf16 g) *
+ * bf16 u)), g = gate x, u = up x, accumulated in f32 (moe_combine,
+ * moe.metal:642-664).  x bf16 [T][H], logits bf16 [T][E]; gate and up:
+ * E experts of I x H, down: E experts of H x I, one scale dtype.  All sizes
+ * are checked before anything is launched (MoE::add throws the same way,
+ * MoE.cpp:119-144). */
+thq4_status thq4_moe(const void *x, const void *residual, const void *logits, int T, int H, int I,
+                     int E, int k, const thq4_experts *gate, const thq4_experts *up,
+                     const thq4_experts *down, void *y, void *workspace, size_t workspace_bytes,
+                     void *stream);
+
 /* ---- testing hooks -------------------------------------------------------
  * Forces the decode/verify kernel's launch shape for every later call in this
  * process: slab-groups per streamed stage (4 or 8), stages in the

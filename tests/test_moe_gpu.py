@@ -1,0 +1,129 @@
+"""The MoE layer on the device through the C ABI against the CPU oracle
+(Splash moe_metal_test.mm: routing order and softmax weights :362-398, the
+grouping round trip :330-360, and the per-expert tolerance 0.02 + 0.01|ref|
+:429-441).  The routing permutation must be bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import q4oracle as O
+import thq4
+from helpers import dev, dev_sb
+from thq4 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _logits(T, E, seed, mode="normal"):
+    rng = np.random.default_rng(seed)
+    z = rng.standard_normal((T, E)).astype(np.float32)
+    if mode == "ties":  # a handful of distinct scores: ties everywhere
+        z = np.round(z * 2.0) / 2.0
+    if mode == "neg_inf":  # some experts masked out, a few tokens almost entirely
+        z[rng.random((T, E)) < 0.3] = -np.inf
+        z[0, :] = -np.inf
+        z[0, 1] = 0.5
+    return O.f32_to_bf16(z)
+
+
+def _u32(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().numpy().view(np.uint32)
+
+
+@pytest.mark.parametrize("T,E,k,mode", [(256, 128, 8, "normal"), (37, 8, 2, "normal"), (64, 16, 4, "ties"),
+                                        (33, 12, 3, "neg_inf"), (1, 4, 4, "normal"), (300, 64, 6, "ties")])
+def test_routing_is_bit_exact(T, E, k, mode):
+    logits = _logits(T, E, T * 31 + E, mode)
+    ids_w, w_w = O.moe_select(logits, k)
+    tiles_w, n_w, grouped_w, rows_w = O.moe_group(ids_w, E, 32)
+    ids, w, tiles, grouped, rows = thq4.moe_route(dev(logits), k)
+    assert np.array_equal(_u32(ids), ids_w), "expert ids / order differ"
+    got_w = w.cpu().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
+    # softmax weights: expf on the device may differ from the host's by an f32 ulp
+    assert np.abs(got_w - w_w.astype(np.int32)).max() <= 1, "routing weights off by more than one bf16 ulp"
+    assert tiles.shape[0] == n_w
+    assert np.array_equal(_u32(tiles).reshape(-1), tiles_w[:n_w].reshape(-1))
+    assert np.array_equal(_u32(grouped), grouped_w[:n_w * 32])
+    assert np.array_equal(_u32(rows), rows_w)
+    # the round trip the reference tests: every route lands on the row that lists it
+    g = _u32(grouped)
+    assert all(g[r] == i for i, r in enumerate(_u32(rows)))
+
+
+def _experts(E, out, inp, sb_dtype, seed):
+    wqs, sbs = [], []
+    for e in range(E):
+        wq, sb = O.synthetic_weight(out, inp, seed + e, sb_dtype)
+        wqs.append(wq)
+        sbs.append(sb)
+    return np.stack(wqs), np.stack(sbs)
+
+
+def _close(tag, got, want):
+    got = got.astype(np.float64)
+    want = want.astype(np.float64)
+    bad = np.abs(got - want) > 0.02 + 0.01 * np.abs(want)
+    assert not bad.any(), f"{tag}: {bad.sum()} elements off, e.g. got {got[bad][:4]} want {want[bad][:4]}"
+
+
+@pytest.mark.parametrize("sb_dtype", [O.SB_BF16, O.SB_F16])
+def test_moe_layer_matches_oracle(sb_dtype):
+    """moe_metal_test's shape: H = 1024, I = 512, E = 8, k = 2."""
+    T, H, I, E, k = 130, 1024, 512, 8, 2
+    gu_wq, gu_sb = _experts(E, 2 * I, H, sb_dtype, 100)
+    dn_wq, dn_sb = _experts(E, H, I, sb_dtype, 200)
+    rng = np.random.default_rng(7)
+    x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    res = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    logits = _logits(T, E, 8)
+    ids, w = O.moe_select(logits, k)
+    y_ref = O.moe_forward(x, res, ids, w, gu_wq, gu_sb, dn_wq, dn_sb, sb_dtype, I)[0]
+    gate = thq4.PackedExperts.from_mlx(dev(gu_wq), dev_sb(gu_sb, sb_dtype), sb_dtype, 0, I)
+    up = thq4.PackedExperts.from_mlx(dev(gu_wq), dev_sb(gu_sb, sb_dtype), sb_dtype, I, I)
+    down = thq4.PackedExperts.from_mlx(dev(dn_wq), dev_sb(dn_sb, sb_dtype), sb_dtype)
+    y = thq4.moe(dev(x), dev(logits), k, gate, up, down, residual=dev(res))
+    got = O.bf16_to_f32(y.cpu().view(torch.int16).numpy().view(np.uint16))
+    _close(f"moe sb{sb_dtype}", got, O.bf16_to_f32(y_ref))
+    again = thq4.moe(dev(x), dev(logits), k, gate, up, down, residual=dev(res))
+    assert torch.equal(y.view(torch.int16), again.view(torch.int16)), "not deterministic"
+
+
+def test_moe_baseline_config():
+    """T = 256, H = 2048, E = 128, k = 8, I = 768, f16
+    scale/bias, x and logits ~ N(0, 1).  The whole layer runs on the GPU; the
+    oracle recomputes the first 24 tokens (their 192 routes)."""
+    T, H, I, E, k = 256, 2048, 768, 128, 8
+    d = torch.device("cuda")
+    gu = [synth.normal_weight(2 * I, H, 1000 + e, d) for e in range(E)]
+    dn = [synth.normal_weight(H, I, 5000 + e, d) for e in range(E)]
+    gu_wq, gu_sb = torch.stack([a for a, _ in gu]), torch.stack([b for _, b in gu])
+    dn_wq, dn_sb = torch.stack([a for a, _ in dn]), torch.stack([b for _, b in dn])
+    gate = thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, 0, I)
+    up = thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, I, I)
+    down = thq4.PackedExperts.from_mlx(dn_wq, dn_sb, thq4.F16)
+    rng = np.random.default_rng(11)
+    x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    logits = _logits(T, E, 12)
+    y = thq4.moe(dev(x), dev(logits), k, gate, up, down)
+    got = O.bf16_to_f32(y.cpu().view(torch.int16).numpy().view(np.uint16))
+    ids, w = O.moe_select(logits, k)
+    sub = 24
+    y_ref = O.moe_forward(x[:sub], None, ids[:sub], w[:sub], gu_wq.cpu().numpy().view(np.uint32),
+                          gu_sb.cpu().view(torch.int16).numpy().view(np.uint16), dn_wq.cpu().numpy().view(np.uint32),
+                          dn_sb.cpu().view(torch.int16).numpy().view(np.uint16), O.SB_F16, I)[0]
+    _close("moe C5", got[:sub], O.bf16_to_f32(y_ref))
+
+
+def test_moe_rejects_bad_shapes():
+    T, H, I, E, k = 4, 128, 64, 2, 1
+    gu_wq, gu_sb = _experts(E, 2 * I, H, O.SB_BF16, 1)
+    dn_wq, dn_sb = _experts(E, H, I, O.SB_BF16, 2)
+    gate = thq4.PackedExperts.from_mlx(dev(gu_wq), dev(gu_sb), thq4.BF16, 0, I)
+    up = thq4.PackedExperts.from_mlx(dev(gu_wq), dev(gu_sb), thq4.BF16, I, I)
+    down = thq4.PackedExperts.from_mlx(dev(dn_wq), dev(dn_sb), thq4.BF16)
+    x = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
+    logits = torch.zeros((T, E), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(thq4.Thq4Error, match="experts are"):
+        thq4.moe(x, logits, k, gate, down, down)  # up has the down shape
+    with pytest.raises(thq4.Thq4Error, match="k <= min"):
+        thq4.moe(x, logits, 3, gate, up, down)

@@ -334,6 +334,95 @@ thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream) {
   return THQ4_OK;
 }
 
+uint32_t thq4_moe_max_tiles(int T, int E, int k) {
+  if (T <= 0 || E <= 0 || k <= 0) return 0;
+  return moe_max_tiles(T, E, k);
+}
+
+namespace {
+thq4_status check_route_args(int T, int E, int k, const char *who) {
+  if (T < 1 || E < 1 || E > 1024 || k < 1 || k > E || k > 32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": need T >= 1, 1 <= E <= 1024, 1 <= k <= min(E, 32) "
+                                                                   "(T " + std::to_string(T) + ", E " +
+                                                    std::to_string(E) + ", k " + std::to_string(k) + ")");
+  if (moe_group_smem(T * k, E) > 200 * 1024)
+    return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": " + std::to_string((long long)T * k) +
+                                               " routes exceed the grouping kernel's shared memory");
+  return THQ4_OK;
+}
+thq4_status check_experts(const thq4_experts *w, int E, int out, int in, const char *what, const char *who) {
+  const std::string pre = std::string(who) + ": " + what;
+  if (!w) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + " experts are NULL");
+  if (w->experts != E || w->out != out || w->in != in)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + " experts are " + std::to_string(w->experts) + " x " +
+                                                    std::to_string(w->out) + " x " + std::to_string(w->in) +
+                                                    ", expected " + std::to_string(E) + " x " + std::to_string(out) +
+                                                    " x " + std::to_string(in));
+  if (w->gs != kGroup) return set_error(THQ4_ERR_UNSUPPORTED, pre + ": only group size 64 is packed");
+  if (w->sb_dtype != THQ4_BF16 && w->sb_dtype != THQ4_F16)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + ": scale dtype must be bf16 or f16");
+  size_t qb = 0, sbb = 0;
+  thq4_weight_bytes(out, in, kGroup, &qb, &sbb);
+  if (!w->qw || !w->sb || !aligned(w->qw, 16) || !aligned(w->sb, 16) || w->qw_stride % 16 || w->sb_stride % 16 ||
+      w->qw_stride < qb || w->sb_stride < sbb)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + ": buffers must be 16-byte aligned with per-expert strides >= " +
+                                                    std::to_string(qb) + " / " + std::to_string(sbb) + " bytes");
+  return THQ4_OK;
+}
+}  // namespace
+
+thq4_status thq4_moe_route(const void *logits, int T, int E, int k, uint32_t *ids, void *weights, uint32_t *tiles,
+                           uint32_t *grouped_routes, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
+                           void *stream) {
+  const char *who = "thq4_moe_route";
+  thq4_status s = check_route_args(T, E, k, who);
+  if (s != THQ4_OK) return s;
+  if (!logits || !ids || !weights || !tiles || !grouped_routes || !route_rows || !ntiles)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route: pointers must be non-NULL");
+  if (!aligned(logits, 2) || !aligned(weights, 2) || !aligned(ids, 4) || !aligned(tiles, 4) ||
+      !aligned(grouped_routes, 4) || !aligned(route_rows, 4) || !aligned(ntiles, 4))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route: misaligned buffer");
+  if (max_tiles < (int)moe_max_tiles(T, E, k))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route: max_tiles below thq4_moe_max_tiles(T, E, k) = " +
+                                                    std::to_string(moe_max_tiles(T, E, k)));
+  cudaError_t e = moe_route_launch(static_cast<const uint16_t *>(logits), T, E, k, ids, static_cast<uint16_t *>(weights),
+                                   tiles, grouped_routes, route_rows, ntiles, max_tiles, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+size_t thq4_moe_workspace_bytes(int T, int H, int I, int E, int k) {
+  if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return 0;
+  return moe_workspace(T, H, I, E, k, nullptr).bytes;
+}
+
+thq4_status thq4_moe(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
+                     const thq4_experts *gate, const thq4_experts *up, const thq4_experts *down, void *y,
+                     void *workspace, size_t workspace_bytes, void *stream) {
+  const char *who = "thq4_moe";
+  thq4_status s = check_route_args(T, E, k, who);
+  if (s != THQ4_OK) return s;
+  if (H <= 0 || I <= 0 || H % kGroup || I % kGroup)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe: H and I must be positive multiples of 64");
+  if ((s = check_experts(gate, E, I, H, "gate", who)) != THQ4_OK) return s;
+  if ((s = check_experts(up, E, I, H, "up", who)) != THQ4_OK) return s;
+  if ((s = check_experts(down, E, H, I, "down", who)) != THQ4_OK) return s;
+  if (gate->sb_dtype != up->sb_dtype || gate->sb_dtype != down->sb_dtype)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe: gate, up and down differ in scale dtype");
+  if (!x || !y || !logits || !aligned(x, 16) || !aligned(y, 16) || !aligned(logits, 2) ||
+      (residual && !aligned(residual, 16)))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe: x, y (and residual) must be 16-byte aligned, logits non-NULL");
+  const MoeWorkspace need = moe_workspace(T, H, I, E, k, nullptr);
+  if (!workspace || workspace_bytes < need.bytes || !aligned(workspace, 256))
+    return set_error(THQ4_ERR_WORKSPACE, "thq4_moe: needs a 256-byte aligned workspace of " + std::to_string(need.bytes) +
+                                             " bytes (thq4_moe_workspace_bytes), got " + std::to_string(workspace_bytes));
+  const MoeWorkspace w = moe_workspace(T, H, I, E, k, workspace);
+  cudaError_t e = moe_launch(x, residual, logits, T, H, I, E, k, *gate, *up, *down, y, w,
+                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
   if (!(chunk == 0 || chunk == 4 || chunk == 8) || stages < 0 || stages == 1 || stages > 8 ||
       grid < 0 || grid > 2 * device_sm_count() || reserved != 0)

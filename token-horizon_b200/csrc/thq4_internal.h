@@ -77,6 +77,41 @@ bool prefill_supported(int m, bool x_f32);
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
                            cudaStream_t stream);
 
+// ---- MoE -------------------------------------------------------------------
+// Routes are grouped by expert into tiles of this many activation rows.
+constexpr int kMoeTileRows = 32;
+// The grouped expert product on the tcgen05 path: for every group tile gt <
+// *count, y rows [gt*32, gt*32 + live) = x rows . expert(tiles[2gt])^T (w1:
+// the fused SwiGLU with w0 = gate, w1 = up).  x, y: [max_tiles*32][k], [..][n].
+struct GroupedGemm {
+  const void *x;
+  void *y;
+  const thq4_experts *w0, *w1;
+  const uint32_t *tiles, *count;
+  int max_tiles;
+};
+cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream);
+
+// Upper bound on group tiles for T tokens routed to k of E experts.
+uint32_t moe_max_tiles(int T, int E, int k);
+// Shared memory of the grouping kernel for R routes and E experts.
+size_t moe_group_smem(int R, int E);
+// Select (top-k, softmax weights) and group (stable counting sort) on the device.
+cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
+                             uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
+                             cudaStream_t stream);
+// The MoE layer's scratch, carved from one caller buffer (nullptr: sizes only).
+struct MoeWorkspace {
+  uint32_t *ids, *tiles, *grouped, *route_rows, *ntiles;
+  uint16_t *weights, *xg, *h, *d;
+  size_t bytes;
+  int max_tiles;
+};
+MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base);
+cudaError_t moe_launch(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
+                       const thq4_experts &gate, const thq4_experts &up, const thq4_experts &down, void *y,
+                       const MoeWorkspace &w, cudaStream_t stream);
+
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,
                           int row_begin, int rows, void *dst_qw, void *dst_sb, cudaStream_t stream);

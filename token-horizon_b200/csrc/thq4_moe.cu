@@ -1,0 +1,258 @@
+// thq4_moe.cu -- the MoE layer: routing, grouping, the grouped expert
+// products and the weighted combine.
+//
+// Replaces Splash's MoE::add (docs/splash/runtime/ops/MoE.cpp:119-231) and
+// its kernels (docs/splash/runtime/metal/kernels/shared/moe.metal):
+//   select   moe_route_select_q8 (:270-361): per token the top k experts by
+//            descending score, lowest id first among equal scores, weights
+//            exp(s_r - s_0) / sum_selected exp(s_o - s_0) rounded to bf16;
+//   group    moe_group_routes (:368-449): a counting sort of the T*k routes
+//            by expert into tiles of kMoeTileRows rows ({expert, live rows}
+//            descriptors, MoeTileDescriptor abi/MoE.h:26-29), padding rows
+//            ~0u, and the inverse map route -> grouped row.  The reference's
+//            atomic cursors leave the order of routes within an expert open;
+//            this library fixes it to ascending route index, so the
+//            permutation is bit-exact and reproducible;
+//   experts  moe_gather_rows + moe_expert_tile / q4_mpp_tile (:453-640): the
+//            gathered rows go through the tcgen05 grouped GEMM (gate/up with
+//            the SwiGLU epilogue, then down), bf16 at each boundary;
+//   combine  moe_combine (:642-664): y = residual + sum over the k slots in
+//            slot order of w * d, in f32 (separate multiply and add), one bf16
+//            rounding.
+//
+// Select runs one warp per token; group runs in one CTA (one thread per
+// expert, routes staged in shared memory); gather and combine move 16-byte
+// pieces.  All of it is negligible next to the expert products, which stream
+// every touched expert's weights from HBM once per group tile.
+#include <algorithm>
+
+#include "thq4_common.cuh"
+#include "thq4_internal.h"
+
+namespace thq4 {
+namespace {
+
+constexpr uint32_t kPad = 0xFFFFFFFFu;
+
+__device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+// One warp per token.  Repeated arg-max over the warp: candidates are the
+// experts not yet taken whose score is not -inf; ties go to the lower id; a
+// token without a candidate takes expert 0 (the oracle's rule).
+__global__ void select_kernel(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const uint16_t *row = logits + (size_t)warp * E;
+  float top[32];
+  uint32_t taken = 0;  // bit j: this lane's expert lane + 32 j is taken (E <= 1024)
+  for (int r = 0; r < k; ++r) {
+    float bv = 0.0f;
+    int bi = -1;
+    for (int j = 0, e = lane; e < E; ++j, e += 32) {
+      if ((taken >> j) & 1u) continue;
+      const float v = bf16f(row[e]);
+      if (v == -INFINITY) continue;
+      if (bi < 0 || v > bv) bv = v, bi = e;  // ascending e within the lane
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) bv = ov, bi = oi;
+    }
+    const int best = bi < 0 ? 0 : bi;
+    if (bi >= 0 && (best & 31) == lane) taken |= 1u << (best >> 5);
+    if (lane == 0) ids[(size_t)warp * k + r] = (uint32_t)best;
+    // without a candidate every remaining score is -inf, expert 0's included
+    top[r & 31] = bi < 0 ? -INFINITY : bv;
+  }
+  if (lane == 0) {
+    float den = 0.0f;
+    for (int o = 0; o < k; ++o) den = __fadd_rn(den, expf(__fsub_rn(top[o], top[0])));
+    for (int r = 0; r < k; ++r)
+      weights[(size_t)warp * k + r] = f32_to_bf16_bits(__fdiv_rn(expf(__fsub_rn(top[r], top[0])), den));
+  }
+}
+
+// One CTA, one thread per expert (E <= blockDim).  Routes in ascending order
+// within each expert.
+__global__ void group_kernel(const uint32_t *ids, int R, int E, int max_tiles, uint32_t *tiles, uint32_t *grouped,
+                             uint32_t *route_rows, uint32_t *ntiles, uint32_t *status) {
+  extern __shared__ uint32_t sm[];  // ids staged (R <= capacity), then counts / offsets
+  uint32_t *sids = sm, *cnt = sm + R, *off = cnt + E;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const uint32_t e = ids[r];
+    sids[r] = e;
+    if (e >= (uint32_t)E) {  // such a route is dropped: combine skips it
+      raise_status(status, kStatusBadExpert);
+      route_rows[r] = kPad;
+    }
+  }
+  __syncthreads();
+  const int e = threadIdx.x;
+  uint32_t c = 0;
+  if (e < E)
+    for (int r = 0; r < R; ++r) c += sids[r] == (uint32_t)e;
+  if (e < E) cnt[e] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (int x = 0; x < E; ++x) {
+      off[x] = acc;
+      acc += (cnt[x] + kMoeTileRows - 1) / kMoeTileRows;
+    }
+    *ntiles = acc <= (uint32_t)max_tiles ? acc : 0u;
+    if (acc > (uint32_t)max_tiles) raise_status(status, kStatusBounds);
+    off[E] = acc;
+  }
+  __syncthreads();
+  if (off[E] > (uint32_t)max_tiles || e >= E) return;
+  const uint32_t t0 = off[e], nt = (c + kMoeTileRows - 1) / kMoeTileRows;
+  for (uint32_t t = 0; t < nt; ++t) {
+    tiles[2 * (t0 + t)] = (uint32_t)e;
+    tiles[2 * (t0 + t) + 1] = min((uint32_t)kMoeTileRows, c - t * kMoeTileRows);
+  }
+  uint32_t cur = 0;
+  for (int r = 0; r < R; ++r)
+    if (sids[r] == (uint32_t)e) {
+      const uint32_t row = t0 * kMoeTileRows + cur++;
+      grouped[row] = (uint32_t)r;
+      route_rows[r] = row;
+    }
+  for (uint32_t row = t0 * kMoeTileRows + c; row < (t0 + nt) * kMoeTileRows; ++row) grouped[row] = kPad;
+}
+
+// xg[row] = x[route / k] for the live rows of the live tiles, zero for padding.
+__global__ void gather_kernel(const uint16_t *x, int H, int k, const uint32_t *grouped, const uint32_t *ntiles,
+                              uint16_t *xg) {
+  const int pieces = H / 8;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t row = i / pieces;
+  if (row >= (size_t)(*ntiles) * kMoeTileRows) return;
+  const int p = (int)(i % pieces);
+  const uint32_t route = grouped[row];
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (route != kPad) v = reinterpret_cast<const uint4 *>(x + (size_t)(route / k) * H)[p];
+  reinterpret_cast<uint4 *>(xg + row * H)[p] = v;
+}
+
+// y[t] = residual[t] + sum_s w[t][s] * d[route_rows[t*k + s]], slot order, f32.
+__global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const uint32_t *route_rows,
+                               const uint16_t *residual, int T, int H, int k, uint16_t *y) {
+  const int pieces = H / 8;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)T * pieces) return;
+  const int t = (int)(i / pieces), p = (int)(i % pieces);
+  float v[8];
+  if (residual) {
+    const uint4 r = reinterpret_cast<const uint4 *>(residual + (size_t)t * H)[p];
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = bf16f((uint16_t)(w[e >> 1] >> (16 * (e & 1))));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+  }
+  for (int s = 0; s < k; ++s) {
+    const uint32_t row = route_rows[(size_t)t * k + s];
+    if (row == kPad) continue;
+    const float ws = bf16f(weights[(size_t)t * k + s]);
+    const uint4 dv = reinterpret_cast<const uint4 *>(d + (size_t)row * H)[p];
+    const uint32_t w[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __fmul_rn(ws, bf16f((uint16_t)(w[e >> 1] >> (16 * (e & 1))))));
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    o[e] = (uint32_t)f32_to_bf16_bits(v[2 * e]) | ((uint32_t)f32_to_bf16_bits(v[2 * e + 1]) << 16);
+  reinterpret_cast<uint4 *>(y + (size_t)t * H)[p] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+uint32_t moe_max_tiles(int T, int E, int k) {
+  const uint64_t routed = (uint64_t)T * (uint64_t)k;
+  const uint64_t bound = routed / kMoeTileRows + (uint64_t)E;
+  return (uint32_t)std::min(bound, routed);
+}
+
+size_t moe_group_smem(int R, int E) { return ((size_t)R + 2 * (size_t)E + 1) * 4; }
+
+cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
+                             uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
+                             cudaStream_t stream) {
+  const int threads = 256, warps = threads / 32;
+  select_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int R = T * k;
+  const size_t smem = moe_group_smem(R, E);
+  static DeviceOnce once;
+  e = once.run([] { return cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
+  if (e != cudaSuccess) return e;
+  const int gthreads = std::max(32, (E + 31) / 32 * 32);
+  group_kernel<<<1, gthreads, smem, stream>>>(ids, R, E, max_tiles, tiles, grouped, route_rows, ntiles, status_word());
+  return cudaGetLastError();
+}
+
+MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base) {
+  MoeWorkspace w{};
+  const size_t R = (size_t)T * k, mt = moe_max_tiles(T, E, k), rows = mt * kMoeTileRows;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += align256(bytes);
+    return base ? static_cast<char *>(base) + at : nullptr;
+  };
+  w.ids = reinterpret_cast<uint32_t *>(take(R * 4));
+  w.weights = reinterpret_cast<uint16_t *>(take(R * 2));
+  w.tiles = reinterpret_cast<uint32_t *>(take(mt * 8));
+  w.grouped = reinterpret_cast<uint32_t *>(take(rows * 4));
+  w.route_rows = reinterpret_cast<uint32_t *>(take(R * 4));
+  w.ntiles = reinterpret_cast<uint32_t *>(take(4));
+  w.xg = reinterpret_cast<uint16_t *>(take(rows * H * 2));
+  w.h = reinterpret_cast<uint16_t *>(take(rows * I * 2));
+  w.d = reinterpret_cast<uint16_t *>(take(rows * H * 2));
+  w.bytes = o;
+  w.max_tiles = (int)mt;
+  return w;
+}
+
+cudaError_t moe_launch(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
+                       const thq4_experts &gate, const thq4_experts &up, const thq4_experts &down, void *y,
+                       const MoeWorkspace &w, cudaStream_t stream) {
+  cudaError_t e = moe_route_launch(static_cast<const uint16_t *>(logits), T, E, k, w.ids, w.weights, w.tiles, w.grouped,
+                                   w.route_rows, w.ntiles, w.max_tiles, stream);
+  if (e != cudaSuccess) return e;
+  const size_t rows = (size_t)w.max_tiles * kMoeTileRows;
+  {
+    const size_t n = rows * (H / 8);
+    gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const uint16_t *>(x), H, k, w.grouped,
+                                                                    w.ntiles, w.xg);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  GroupedGemm g{};
+  g.x = w.xg;
+  g.y = w.h;
+  g.w0 = &gate;
+  g.w1 = &up;
+  g.tiles = w.tiles;
+  g.count = w.ntiles;
+  g.max_tiles = w.max_tiles;
+  if ((e = grouped_launch(g, stream)) != cudaSuccess) return e;
+  g.x = w.h;
+  g.y = w.d;
+  g.w0 = &down;
+  g.w1 = nullptr;
+  if ((e = grouped_launch(g, stream)) != cudaSuccess) return e;
+  const size_t n = (size_t)T * (H / 8);
+  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w.d, w.weights, w.route_rows,
+                                                                   static_cast<const uint16_t *>(residual), T, H, k,
+                                                                   static_cast<uint16_t *>(y));
+  return cudaGetLastError();
+}
+
+}  // namespace thq4

@@ -63,8 +63,49 @@ struct PfArgs {
   uint32_t *status;
   int m, n, ng;
   int m_tiles, tiles;
-  int yf32;  // unused by the kernels (a template parameter); kept for tracing
+  // grouped (MoE expert) mode when gtiles != nullptr: unit u is group tile
+  // gt = u / n_slabs (activation rows [gt*BT, gt*BT + live) of the gathered
+  // x) times slab u % n_slabs of expert gtiles[2 gt]; gtiles[2 gt + 1] =
+  // live rows; *gcount = group tiles in use (written on the device)
+  const uint32_t *gtiles;
+  const uint32_t *gcount;
+  uint64_t qw_stride[2], sb_stride[2];
+  int n_slabs, max_units;
 };
+
+// One unit of work: output slab nt for activation rows [row0, row_end).
+struct PfUnit {
+  int nt, row0, row_end;
+  const uint8_t *qw[2];
+  const uint8_t *sb[2];
+};
+template <int BT>
+__device__ __forceinline__ PfUnit pf_unit(const PfArgs &a, int u) {
+  PfUnit x;
+  if (a.gtiles) {
+    const int gt = u / a.n_slabs;
+    const uint32_t e = a.gtiles[2 * gt];
+    x.nt = u - gt * a.n_slabs;
+    x.row0 = gt * BT;
+    x.row_end = x.row0 + (int)a.gtiles[2 * gt + 1];
+#pragma unroll
+    for (int si = 0; si < 2; ++si) {
+      x.qw[si] = a.qw[si] ? a.qw[si] + e * a.qw_stride[si] : nullptr;
+      x.sb[si] = a.sb[si] ? a.sb[si] + e * a.sb_stride[si] : nullptr;
+    }
+  } else {
+    const int mt = u % a.m_tiles;
+    x.nt = u / a.m_tiles;
+    x.row0 = mt * BT;
+    x.row_end = a.m;
+#pragma unroll
+    for (int si = 0; si < 2; ++si) {
+      x.qw[si] = a.qw[si];
+      x.sb[si] = a.sb[si];
+    }
+  }
+  return x;
+}
 
 // NS weight streams (1, or 2 for gate/up), BT tokens per tile, S stages
 template <int NS, int BT, int S>
@@ -77,6 +118,7 @@ struct PfCfg {
   static constexpr uint32_t bar_off = y_off + BT * kBN * 2;
   // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf, acce, yfull, ydone
   static constexpr uint32_t misc_off = bar_off + (4 * S + 4) * 8;
+  static constexpr int box_rows = BT < 128 ? BT : 128;  // x rows per TMA box
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t alloc = bytes + 1024;  // room to align the base to 1024
   // TMEM: D (NS accumulators of BT columns), then the A ring
@@ -131,6 +173,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
         "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+// 16 columns of this warp's 32 TMEM lanes into registers
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -215,6 +266,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   uint64_t *accf = bars + 4 * S, *acce = accf + 1, *yfull = accf + 2, *ydone = accf + 3;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + C::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(sm + C::misc_off + 4);
+  int *units_sm = reinterpret_cast<int *>(sm + C::misc_off + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -229,6 +281,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     mbar_init(yfull, kEpiWarps);
     mbar_init(ydone, kEpiWarps);
     *abort = 0;
+    // units of work: the plain GEMM's tiles, or the group tiles in use
+    units_sm[0] = a.gtiles ? min(a.max_units, (int)*a.gcount * a.n_slabs) : a.tiles;
   }
   if (warp == kWarpMma) {  // all of TMEM (one CTA per SM)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(smem_addr(tmem_holder)));
@@ -239,28 +293,30 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  const int units = units_sm[0];
 
   if (warp == kWarpProd) {
     // ---- producer ------------------------------------------------------------
     if (lane == 0) {
       const uint64_t pol = evict_first_policy();
       int it = 0, issued = 0;
-      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
-        const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+      for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x) {
+        const PfUnit un = pf_unit<BT>(a, tile);
         for (int g = 0; g < a.ng; ++g, ++it) {
           const int s = it % S;
           if (it >= S && !pf_wait(&empty[s], (uint32_t)(((it / S) - 1) & 1), abort, a.status)) break;
           unsigned char *xd = sm + C::x_off + (size_t)s * C::x_stage;
           mbar_arrive_expect_tx(&xfull[s], C::x_stage);
 #pragma unroll
-          for (int bx = 0; bx < BT / 128; ++bx) tma_load_2d(xd + bx * kXBox, &xmap, g * kBK, mt * BT + bx * 128, &xfull[s]);
+          for (int bx = 0; bx < BT / C::box_rows; ++bx)
+            tma_load_2d(xd + bx * C::box_rows * kBK * 2, &xmap, g * kBK, un.row0 + bx * C::box_rows, &xfull[s]);
           unsigned char *rd = sm + C::raw_off + (size_t)s * NS * kRawStage;
-          const size_t sg = (size_t)nt * a.ng + g;
+          const size_t sg = (size_t)un.nt * a.ng + g;
           mbar_arrive_expect_tx(&rawfull[s], NS * kRawStage);
 #pragma unroll
           for (int si = 0; si < NS; ++si) {
-            bulk_g2s(rd + si * kRawStage, a.qw[si] + sg * 4096, 4096, &rawfull[s], pol);
-            bulk_g2s(rd + si * kRawStage + 4096, a.sb[si] + sg * 512, 512, &rawfull[s], pol);
+            bulk_g2s(rd + si * kRawStage, un.qw[si] + sg * 4096, 4096, &rawfull[s], pol);
+            bulk_g2s(rd + si * kRawStage + 4096, un.sb[si] + sg * 512, 512, &rawfull[s], pol);
           }
           issued = it + 1;
         }
@@ -276,7 +332,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     // ---- MMA issuer ------------------------------------------------------------
     if (lane == 0) {
       int it = 0, local = 0, committed = 0;
-      for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, ++local) {
+      for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x, ++local) {
         if (local >= 1 && !pf_wait(acce, (uint32_t)((local - 1) & 1), abort, a.status)) break;
         tc_fence_after();
         bool ok = true;
@@ -316,7 +372,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     const int tl = row >> 4, r = row & 7, hrow = (row >> 3) & 1;
     const uint64_t m23 = f2(-8388608.0f, -8388608.0f);
     int it = 0;
-    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x) {
       bool ok = true;
       for (int g = 0; g < a.ng; ++g, ++it) {
         const int s = it % S;
@@ -370,41 +426,40 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..255
     uint16_t *ytile = reinterpret_cast<uint16_t *>(sm + C::y_off);
     int local = 0;
-    for (int tile = blockIdx.x; tile < a.tiles && !*abort; tile += gridDim.x, ++local) {
-      const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+    for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x, ++local) {
+      const PfUnit un = pf_unit<BT>(a, tile);
+      const int nt = un.nt;
       if (!pf_wait(accf, (uint32_t)(local & 1), abort, a.status)) break;
       // the SMEM tile is free once every warp stored the previous one
       if (!YF32 && local >= 1 && !pf_wait(ydone, (uint32_t)((local - 1) & 1), abort, a.status)) break;
       tc_fence_after();
       const int nl = 32 * q + lane, n = nt * kBN + nl;
-      constexpr int kChunks = BT / 32 / 2;  // 32-token chunks per warp
 #pragma unroll 1
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int tc0 = (th * kChunks + cc) * 32;  // first token of the chunk within the tile
+      for (int tc0 = th * (BT / 2); tc0 < (th + 1) * (BT / 2); tc0 += 16) {  // 16 tokens at a time
         const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)tc0;
-        uint32_t u[32];
-        float v[32];
-        tmem_ld32(taddr, u);
+        uint32_t u[16];
+        float v[16];
+        tmem_ld16(taddr, u);
         if constexpr (NS == 2) {
-          uint32_t uu[32];
-          tmem_ld32(taddr + BT, uu);
+          uint32_t uu[16];
+          tmem_ld16(taddr + BT, uu);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = silu_mul(__uint_as_float(u[e]), __uint_as_float(uu[e]));
+          for (int e = 0; e < 16; ++e) v[e] = silu_mul(__uint_as_float(u[e]), __uint_as_float(uu[e]));
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]);
+          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(u[e]);
         }
         if constexpr (YF32) {
           if (n < a.n) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int t = mt * BT + tc0 + e;
-              if (t < a.m) static_cast<float *>(a.y)[(size_t)t * a.n + n] = v[e];
+            for (int e = 0; e < 16; ++e) {
+              const int t = un.row0 + tc0 + e;
+              if (t < un.row_end) static_cast<float *>(a.y)[(size_t)t * a.n + n] = v[e];
             }
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ytile[(tc0 + e) * kBN + nl] = f32_to_bf16_bits(v[e]);
+          for (int e = 0; e < 16; ++e) ytile[(tc0 + e) * kBN + nl] = f32_to_bf16_bits(v[e]);
         }
       }
       tc_fence_before();
@@ -419,8 +474,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
           const int piece = et + i * kEpiWarps * 32, tt = piece >> 4, col = (piece & 15) * 8;
-          const int t = mt * BT + tt;
-          if (t >= a.m) continue;
+          const int t = un.row0 + tt;
+          if (t >= un.row_end) continue;
           const uint4 val = *reinterpret_cast<const uint4 *>(ytile + tt * kBN + col);
           uint16_t *dst = static_cast<uint16_t *>(a.y) + (size_t)t * a.n + nt * kBN + col;
           if (vec) {
@@ -460,12 +515,11 @@ cudaError_t prefill_launch_t(const CUtensorMap &map, const PfArgs &a, int grid, 
 
 }  // namespace
 
-bool prefill_supported(int m, bool x_f32) { return m > 8 && !x_f32; }
+namespace {
 
-cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
-                           cudaStream_t stream) {
-  // the driver's tensor-map encoder, looked up through the runtime so the
-  // library needs no link-time driver dependency
+// The driver's tensor-map encoder, looked up through the runtime so the
+// library needs no link-time driver dependency.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -475,20 +529,44 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
         q == cudaDriverEntryPointSuccess)
       encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
+  return encode;
+}
+
+// x [rows][k] bf16 as a 2-D tensor (k innermost), 64 x box_rows boxes,
+// 128-byte swizzle
+cudaError_t make_xmap(const void *x, int k, int rows, int box_rows, CUtensorMap *map) {
+  const auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
-  // x [m][k] bf16 as a 2-D tensor (k innermost), 64 x 128 boxes, 128-byte swizzle
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)w0.in, (cuuint64_t)m};
-  const cuuint64_t strides[1] = {(cuuint64_t)w0.in * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+  const CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  PfArgs a{};
+  return cr == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int NS, int BT, int S>
+cudaError_t launch_cfg(const CUtensorMap &map, const PfArgs &a, int grid, bool f16, bool y_f32, cudaStream_t stream) {
+  return f16 ? (y_f32 ? prefill_launch_t<NS, BT, S, true, true>(map, a, grid, stream)
+                      : prefill_launch_t<NS, BT, S, true, false>(map, a, grid, stream))
+             : (y_f32 ? prefill_launch_t<NS, BT, S, false, true>(map, a, grid, stream)
+                      : prefill_launch_t<NS, BT, S, false, false>(map, a, grid, stream));
+}
+
+}  // namespace
+
+bool prefill_supported(int m, bool x_f32) { return m > 8 && !x_f32; }
+
+cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
+                           cudaStream_t stream) {
   const bool gate_up = w1 != nullptr;
   const int bt = gate_up ? 128 : 256;
+  CUtensorMap map;
+  cudaError_t e = make_xmap(x, w0.in, m, 128, &map);
+  if (e != cudaSuccess) return e;
+  PfArgs a{};
   a.qw[0] = static_cast<const uint8_t *>(w0.qw);
   a.sb[0] = static_cast<const uint8_t *>(w0.sb);
   a.qw[1] = gate_up ? static_cast<const uint8_t *>(w1->qw) : nullptr;
@@ -502,17 +580,41 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   const long long tiles = (long long)a.m_tiles * row_slabs(w0.out);
   if (tiles >= (1ll << 31)) return cudaErrorInvalidValue;
   a.tiles = (int)tiles;
-  a.yf32 = y_f32 ? 1 : 0;
   const int grid = (int)std::min<long long>(tiles, device_sm_count());
   const bool f16 = w0.sb_dtype == THQ4_F16;
-#define THQ4_PF(NS_, BT_, S_)                                                                         \
-  return f16 ? (y_f32 ? prefill_launch_t<NS_, BT_, S_, true, true>(map, a, grid, stream)                  \
-                      : prefill_launch_t<NS_, BT_, S_, true, false>(map, a, grid, stream))                \
-             : (y_f32 ? prefill_launch_t<NS_, BT_, S_, false, true>(map, a, grid, stream)                 \
-                      : prefill_launch_t<NS_, BT_, S_, false, false>(map, a, grid, stream));
-  if (gate_up) THQ4_PF(2, 128, 4)
-  THQ4_PF(1, 256, 4)
-#undef THQ4_PF
+  if (gate_up) return launch_cfg<2, 128, 4>(map, a, grid, f16, y_f32, stream);
+  return launch_cfg<1, 256, 4>(map, a, grid, f16, y_f32, stream);
+}
+
+cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream) {
+  CUtensorMap map;
+  cudaError_t e = make_xmap(g.x, g.w0->in, g.max_tiles * kMoeTileRows, kMoeTileRows, &map);
+  if (e != cudaSuccess) return e;
+  const bool gate_up = g.w1 != nullptr;
+  PfArgs a{};
+  a.qw[0] = static_cast<const uint8_t *>(g.w0->qw);
+  a.sb[0] = static_cast<const uint8_t *>(g.w0->sb);
+  a.qw[1] = gate_up ? static_cast<const uint8_t *>(g.w1->qw) : nullptr;
+  a.sb[1] = gate_up ? static_cast<const uint8_t *>(g.w1->sb) : nullptr;
+  a.qw_stride[0] = g.w0->qw_stride;
+  a.sb_stride[0] = g.w0->sb_stride;
+  a.qw_stride[1] = gate_up ? g.w1->qw_stride : 0;
+  a.sb_stride[1] = gate_up ? g.w1->sb_stride : 0;
+  a.y = g.y;
+  a.status = status_word();
+  a.m = g.max_tiles * kMoeTileRows;
+  a.n = g.w0->out;
+  a.ng = g.w0->in / kBK;
+  a.gtiles = g.tiles;
+  a.gcount = g.count;
+  a.n_slabs = row_slabs(g.w0->out);
+  const long long units = (long long)g.max_tiles * a.n_slabs;
+  if (units >= (1ll << 31)) return cudaErrorInvalidValue;
+  a.max_units = (int)units;
+  const int grid = (int)std::min<long long>(units, device_sm_count());
+  const bool f16 = g.w0->sb_dtype == THQ4_F16;
+  if (gate_up) return launch_cfg<2, kMoeTileRows, 6>(map, a, grid, f16, false, stream);
+  return launch_cfg<1, kMoeTileRows, 6>(map, a, grid, f16, false, stream);
 }
 
 }  // namespace thq4

@@ -70,6 +70,12 @@ SIGNATURES = {
                              c_int, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_workspace_bytes": (c_size_t, [POINTER(thq4_weight), c_int]),
     "thq4_dequant": (c_int, [POINTER(thq4_weight), c_void_p, c_void_p]),
+    "thq4_moe_max_tiles": (c_uint32, [c_int, c_int, c_int]),
+    "thq4_moe_route": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_int, c_void_p]),
+    "thq4_moe_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "thq4_moe": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(thq4_experts),
+                         POINTER(thq4_experts), POINTER(thq4_experts), c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
 }
 

@@ -227,3 +227,81 @@ def lin_apply_ps(x: torch.Tensor, l: QLin, presum: bool = False) -> torch.Tensor
 
 def lin_apply(x: torch.Tensor, l: QLin) -> torch.Tensor:
     return lin_apply_ps(x, l, False)
+
+
+# -- MoE (Splash MoE::add, docs/splash/runtime/ops/MoE.cpp:119-231) ------------
+
+class PackedExperts:
+    """E experts of one shape (rows x inp), packed back to back in the frag
+    layout; the host mirror of Splash's ExpertQ4Projection
+    (docs/splash/runtime/ops/Linear.hpp:37-43)."""
+
+    def __init__(self, experts: int, rows: int, inp: int, sb_dtype: int, device: torch.device):
+        qb, sbb = ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.lib().thq4_weight_bytes(rows, inp, 64, ctypes.byref(qb), ctypes.byref(sbb))
+        self.experts, self.rows, self.inp, self.sb_dtype = experts, rows, inp, sb_dtype
+        self.qw_stride, self.sb_stride = qb.value, sbb.value
+        self.qw = torch.empty(experts * qb.value, dtype=torch.uint8, device=device)
+        self.sb = torch.empty(experts * sbb.value, dtype=torch.uint8, device=device)
+        self.desc = _lib.thq4_experts()
+        self.desc.experts, self.desc.out, self.desc.in_, self.desc.gs = experts, rows, inp, 64
+        self.desc.sb_dtype, self.desc.reserved = sb_dtype, 0
+        self.desc.qw, self.desc.sb = self.qw.data_ptr(), self.sb.data_ptr()
+        self.desc.qw_stride, self.desc.sb_stride = qb.value, sbb.value
+
+    @classmethod
+    def from_mlx(cls, wq: torch.Tensor, sb: torch.Tensor, sb_dtype: int, row_begin: int = 0,
+                 rows: Optional[int] = None) -> "PackedExperts":
+        """wq u32 [E, src_out, inp/8], sb [E, src_out, 2*inp/64]: rows
+        [row_begin, row_begin + rows) of every expert (e.g. the gate or the up
+        half of a fused [gate | up] expert)."""
+        E, src_out, inp = wq.shape[0], wq.shape[1], wq.shape[2] * 8
+        rows = src_out - row_begin if rows is None else rows
+        p = cls(E, rows, inp, sb_dtype, wq.device)
+        for e in range(E):
+            check(_lib.lib().thq4_repack(SRC_MLX, _ptr(wq[e].contiguous()), _ptr(sb[e].contiguous()), src_out, inp, 64,
+                                         sb_dtype, row_begin, rows,
+                                         ctypes.c_void_p(p.qw.data_ptr() + e * p.qw_stride), p.qw_stride,
+                                         ctypes.c_void_p(p.sb.data_ptr() + e * p.sb_stride), p.sb_stride, _stream()))
+        return p
+
+
+_MOE_WS: dict = {}
+
+
+def moe_route(logits: torch.Tensor, k: int):
+    """Device routing (moe.metal:270-449): ids [T, k] u32, weights [T, k] bf16,
+    tiles [n, 2] u32, grouped_routes [n*32] u32, route_rows [T*k] u32."""
+    T, E = logits.shape
+    L = _lib.lib()
+    mt = L.thq4_moe_max_tiles(T, E, k)
+    dev = logits.device
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.bfloat16, device=dev)
+    tiles = torch.empty((mt, 2), dtype=torch.int32, device=dev)
+    grouped = torch.empty(mt * 32, dtype=torch.int32, device=dev)
+    rows = torch.empty(T * k, dtype=torch.int32, device=dev)
+    n = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(L.thq4_moe_route(_ptr(logits.contiguous()), T, E, k, _ptr(ids), _ptr(w), _ptr(tiles), _ptr(grouped),
+                           _ptr(rows), _ptr(n), mt, _stream()))
+    nt = int(n.item())
+    return ids, w, tiles[:nt], grouped[:nt * 32], rows
+
+
+def moe(x: torch.Tensor, logits: torch.Tensor, k: int, gate: PackedExperts, up: PackedExperts,
+        down: PackedExperts, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One MoE layer: residual + sum_slot w * down(silu(gate x) * up x), bf16 [T, H]."""
+    T, H = x.shape
+    E, I = gate.experts, gate.rows
+    L = _lib.lib()
+    need = L.thq4_moe_workspace_bytes(T, H, I, E, k)
+    key = (x.device.index, torch.cuda.current_stream(x.device).cuda_stream)
+    ws = _MOE_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        _MOE_WS[key] = ws
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    check(L.thq4_moe(_ptr(x.contiguous()), _ptr(residual), _ptr(logits.contiguous()), T, H, I, E, k,
+                     ctypes.byref(gate.desc), ctypes.byref(up.desc), ctypes.byref(down.desc), _ptr(y), _ptr(ws),
+                     ws.numel(), _stream()))
+    return y
