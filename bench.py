@@ -146,12 +146,6 @@ def dist_env():
     return world, rank, local
 
 
-def shard_rows(total: int, world: int, rank: int):
-    per = total // world
-    assert per * world == total and per % 16 == 0, f"{total} rows do not split into {world} x 16k"
-    return rank * per, per
-
-
 # ---------------------------------------------------------------------------
 # the thq4 arm
 # ---------------------------------------------------------------------------
@@ -160,6 +154,7 @@ def run_thq4(args):
     import torch.distributed as dist
     import thq4
     from thq4 import synth
+    from thq4.shard import shard_rows
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -346,9 +341,14 @@ def run_thq4(args):
     except Exception:
         pass
 
-    prefill = None
-    if rank == 0 and not args.skip_prefill:
+    prefill = moe = None
+    if rank == 0 and world == 1 and not args.skip_prefill:
+        # the decode weights go first: these measurements have their own working sets
+        layers = None
+        torch.cuda.empty_cache()
         prefill = bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind)
+        torch.cuda.empty_cache()
+        moe = bench_moe(torch, thq4, synth, dev, hbm_peak)
 
     # free graphs holding NCCL work before the process group goes away
     graph = g2 = None
@@ -393,6 +393,7 @@ def run_thq4(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "prefill": prefill,
+            "moe": moe,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -400,37 +401,82 @@ def run_thq4(args):
         dist.destroy_process_group()
 
 
-def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
-    """x [512 x 4096] bf16, W [12288 x 4096] Q4 -> TFLOP/s."""
-    M, N, K = 512, 12288, 4096
-    wq, sb = synth.normal_weight(N, K, 99, dev)
-    w = thq4.PackedWeight.repack(thq4.SRC_MLX, wq, sb, N, K, thq4.F16)
-    x = torch.randn((M, K), device=dev).to(torch.bfloat16)
-    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    lib = thq4.lib()
-    need = lib.thq4_linear_workspace_bytes(ctypes.byref(w.desc), M)
-    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
-
-    def call():
-        thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, M,
-                                   ctypes.c_void_p(y.data_ptr()), thq4.BF16, ctypes.c_void_p(ws.data_ptr()), need,
-                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
-
+def _time_ms(torch, fn, reps):
+    """Mean ms per call: CUDA events on the current stream after 3 warm-up
+    calls (the callers rotate operands larger than L2)."""
     for _ in range(3):
-        call()
+        fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
     a.record()
     for _ in range(reps):
-        call()
+        fn()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-    return {"config": "x 512x4096 bf16, W 12288x4096 Q4 (f16 scale/bias)", "tflops": round(tflops, 2),
-            "ms": round(ms, 4), "peak_tflops": tc_peak, "frac": round(tflops / tc_peak, 4), "peak_kind": peak_kind,
-            "kernel": "verify-kernel token passes (no tcgen05 prefill kernel yet)"}
+    return a.elapsed_time(b) / reps
+
+
+def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
+    """x [M x 4096] bf16 ~ N(0,1), W [12288 x 4096] Q4
+    with f16 scale/bias, M = 512 (headline) and 2048 -> TFLOP/s.  Four weight
+    copies (113 MB) rotate so the weight stream is not served from L2."""
+    N, K = 12288, 4096
+    ws = []
+    for i in range(4):
+        wq, sb = synth.normal_weight(N, K, 99 + i, dev)
+        ws.append(thq4.PackedWeight.repack(thq4.SRC_MLX, wq, sb, N, K, thq4.F16))
+        del wq, sb
+    lib = thq4.lib()
+    out = {"kernel": "prefill_kernel (tcgen05.mma kind::f16, dequantised weights in TMEM, x by TMA)",
+           "peak_tflops": tc_peak, "peak_kind": peak_kind}
+    for M in (512, 2048):
+        x = torch.randn((M, K), device=dev).to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+        def call():
+            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for w in ws:
+                thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, M,
+                                           ctypes.c_void_p(y.data_ptr()), thq4.BF16, None, 0, s))
+
+        ms = _time_ms(torch, call, 10) / len(ws)
+        tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        out[f"m{M}"] = {"config": f"x {M}x4096 bf16, W 12288x4096 Q4 (f16 scale/bias)", "tflops": round(tflops, 2),
+                        "us": round(ms * 1e3, 2), "frac": round(tflops / tc_peak, 4)}
+    return out
+
+
+def bench_moe(torch, thq4, synth, dev, hbm_peak):
+    """T = 256 tokens, H = 2048, E = 128 experts, top-8,
+    I = 768, Q4 f16 scale/bias -> expert-weight GB/s (339,738,624 algorithmic
+    bytes, every expert touched) and us per layer (routing, gather, grouped
+    gate/up and down products, combine).  Two expert sets (680 MB) rotate."""
+    T, H, I, E, k = 256, 2048, 768, 128, 8
+    sets = []
+    for s in range(2):
+        gu = [synth.normal_weight(2 * I, H, 10_000 * (s + 1) + e, dev) for e in range(E)]
+        gu_wq, gu_sb = torch.stack([a for a, _ in gu]), torch.stack([b for _, b in gu])
+        del gu
+        dn = [synth.normal_weight(H, I, 20_000 * (s + 1) + e, dev) for e in range(E)]
+        dn_wq, dn_sb = torch.stack([a for a, _ in dn]), torch.stack([b for _, b in dn])
+        del dn
+        sets.append((thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, 0, I),
+                     thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, I, I),
+                     thq4.PackedExperts.from_mlx(dn_wq, dn_sb, thq4.F16)))
+        del gu_wq, gu_sb, dn_wq, dn_sb
+    x = torch.randn((T, H), device=dev).to(torch.bfloat16)
+    logits = torch.randn((T, E), device=dev).to(torch.bfloat16)
+
+    def call():
+        for g, u, d in sets:
+            thq4.moe(x, logits, k, g, u, d)
+
+    ms = _time_ms(torch, call, 10) / len(sets)
+    nbytes = E * (2 * I * H + H * I) * Q4_BYTES_PER_WEIGHT
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"config": "T 256, H 2048, E 128, k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
+            "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
+            "kernel": "grouped prefill_kernel (tcgen05) + routing / gather / combine"}
 
 
 # ---------------------------------------------------------------------------
