@@ -228,8 +228,9 @@ thq4_status thq4_moe(const void *x, const void *residual, const void *logits, in
 /* ---- testing hooks -------------------------------------------------------
  * Forces the decode/verify kernel's launch shape for every later call in this
  * process: slab-groups per streamed stage (4 or 8), stages in the
- * shared-memory ring (2 .. 8) and CTAs in the grid (1 .. 2x SM count); 0
- * leaves a field to the policy, all zeros restore it.  The reference's tests
+ * shared-memory ring (2 .. 8; an upper bound, lowered to what fits) and CTAs
+ * in the grid (1 .. 2x SM count, capped at one per SM); 0 leaves a field to
+ * the policy, all zeros restore it.  The reference's tests
  * run every instantiated tile config the same way (qwen35.rs:6963-6989).
  * Returns THQ4_ERR_INVALID_ARGUMENT for other values; `reserved` must be 0. */
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved);

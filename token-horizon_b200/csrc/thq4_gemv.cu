@@ -12,15 +12,18 @@
 //   - the weight is a stream of "slab-groups" (SG): 128 rows x 64 k, 4096
 //     bytes of nibbles + 512 bytes of scale/bias, slab-major, so any run of
 //     SGs is one contiguous byte range of the frag layout.  A persistent grid
-//     (one or two CTAs per SM) gives every CTA an equal run of "chunks" (CB =
-//     4 or 8 consecutive SGs of one slab, CB-aligned); a run may start and
-//     end inside a slab;
+//     (one CTA per SM) gives every CTA an equal run of "chunks" (CB = 8, or 4,
+//     consecutive SGs of one slab, CB-aligned); a run may start and end
+//     inside a slab.  Where whole slabs per CTA still fill >= 85% of the SMs
+//     the grid is the slab count instead, and nothing is split;
 //   - one producer warp per CTA streams the run into a ring of shared-memory
 //     stages with bulk copies (cp.async.bulk, evict-first in L2, no
 //     multicast) of one chunk each, completing on a "full" mbarrier per stage;
 //     the first stages are requested before the kernel waits for its input;
 //   - eight consumer warps each own one 16-row tile of every SG, so their
-//     output rows are disjoint and no reduction crosses warps.  Per SG a warp
+//     output rows are disjoint and no reduction crosses warps (sixteen, two
+//     per tile, measured no faster: the LOP3 work of the in-register dequant
+//     fills the ALU pipe either way).  Per SG a warp
 //     runs four mma.m16n8k16 (fp16 x fp16 -> f32) with the weight as the A
 //     operand (16 rows) and activation columns as N (8).  A shift and one
 //     LOP3 per register put a nibble pair in mantissa bits 4..7 of the fp16
@@ -170,10 +173,11 @@ __device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *z
         }
       }
     }
+    // all kU items go through the shuffle trees together (independent
+    // chains); an item past `span` is a whole warp's, whose results are dropped
 #pragma unroll
     for (int it = 0; it < kU; ++it) {
       const int idx = base + it * nthr;
-      if (idx >= span) break;  // uniform per warp
       const bool live = idx < items;
       const int h8 = idx & 7, sq = live ? idx >> 3 : 0, q = sq % P, slot = sq / P;
       const int part = a.xf32 ? q & 1 : 0;
@@ -319,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     return;
   }
 
-  // ---- consumers: warp `warp` owns tile `warp` of every slab-group ----------
+  // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
+  const int tile = warp;
   pdl_wait();
   const int sl0 = C0 / a.cps, cg0 = C0 - sl0 * a.cps;
   const int gs = cg0 * CB;
@@ -352,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     const uint4 xa = bp[0], xb = bp[4];
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-      const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(s * CB + u) * 4096 + warp * 512 + lane * 16);
+      const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(s * CB + u) * 4096 + tile * 512 + lane * 16);
       // k-step 2p rows r / r+8: bits 0..3 / 8..11 of each half, moved up by
       // 4 / down by 4; k-step 2p+1: bits 4..7 in place / 12..15 down by 8
       const uint32_t a00 = nib_f16x2<kNibMask>(w.x << 4), a01 = nib_f16x2<kNibMask>(w.x >> 4);
@@ -383,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     const float4 m1 = ONE ? m0 : mc[gu * P8 + 1];
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-      const uint2 q = *reinterpret_cast<const uint2 *>(scl + (size_t)(s * CB + gu) * 512 + warp * 64 + r * 8);
+      const uint2 q = *reinterpret_cast<const uint2 *>(scl + (size_t)(s * CB + gu) * 512 + tile * 64 + r * 8);
       const float sr = sb_to_f32<SF16>(q.x & 0xffffu), br = sb_to_f32<SF16>(q.x >> 16);
       const float s8 = sb_to_f32<SF16>(q.y & 0xffffu), b8 = sb_to_f32<SF16>(q.y >> 16);
       y[s][0] = fmaf(sr * m0.y, (lo[s][0] + hi[s][0]) - m0.z, fmaf(br, m0.x, y[s][0]));
@@ -418,9 +423,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   // side 1: its last) with plain stores; at the end of the run one
   // acquire-release increment per partial slab publishes them, and the CTA
   // whose increment completes the count adds every part in CTA order and
-  // stores the tile.  Nothing waits, and the only fences are the two atomics.
+  // stores the tile.  Nothing waits; one release fence before the (relaxed)
+  // increments and one acquire fence in the completing CTA order the parts.
   auto publish = [&](int side, const float (&v)[NS][4]) {
-    float *gslot = a.part + (((size_t)blockIdx.x * 2 + side) * kSlabTiles + warp) * (NS * 128) + lane * 4;
+    float *gslot = a.part + (((size_t)blockIdx.x * 2 + side) * kSlabTiles + tile) * (NS * 128) + lane * 4;
 #pragma unroll
     for (int si = 0; si < NS; ++si)
       *reinterpret_cast<float4 *>(gslot + si * 128) = make_float4(v[si][0], v[si][1], v[si][2], v[si][3]);
@@ -449,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         const int q = q0 + i;
         if (q > chi) break;
         const int qs = (q == clo && run_begin(a, q) < t0) ? 1 : 0;
-        const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + warp) * (NS * 128) + lane * 4;
+        const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + tile) * (NS * 128) + lane * 4;
 #pragma unroll
         for (int si = 0; si < NS; ++si) v[i][si] = ld_relaxed_f4(src + si * 128);
       }
@@ -461,20 +467,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
           acc[si][0] += v[i][si].x, acc[si][1] += v[i][si].y, acc[si][2] += v[i][si].z, acc[si][3] += v[i][si].w;
       }
     }
-    if (lane == 0) a.count[(size_t)sl * kSlabTiles + warp] = 0;  // ready for the next call
-    store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, acc[0], acc[NS - 1]);
+    if (lane == 0) a.count[(size_t)sl * kSlabTiles + tile] = 0;  // ready for the next call
+    store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, acc[0], acc[NS - 1]);
   };
   int first_slab = -1;
   int sl = sl0, cg = cg0 - 1, s = R - 1;
   uint32_t par = 1;  // (stage, parity) of chunk n, kept incrementally
+  // A warp whose wait times out stops computing and releasing stages; the
+  // producer then times out on the stage's release and stops.  Outputs of
+  // the call are undefined and the status word says so.
+  bool aborted = false;
   for (int n = 0; n < nch; ++n) {
     if (++cg == a.cps) cg = 0, ++sl;
     if (++s == R) s = 0, par ^= 1u;
-    if (!mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
-      // the producer then times out on this stage's release and stops;
-      // outputs of this call are undefined and the status word says so
+    if (!aborted && !mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
       raise_status(a.status, kStatusTimeout);
-      return;
+      aborted = true;
     }
     const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
     const unsigned char *nib = ring + (size_t)s * SB;
@@ -483,7 +491,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     const int slot0 = slot_of(g0c);
     const uint4 *xc = xf + (size_t)slot0 * P * 8 + xoff;
     const float4 *mc = mx + (size_t)slot0 * P8 + 2 * cp;
-    if (cnt == CB) {
+    if (aborted) {
+    } else if (cnt == CB) {
 #pragma unroll
       for (int u = 0; u < CB; ++u) {
         group(nib, xc, u, bsel[u % GW], u % GW == 0);
@@ -497,15 +506,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0 && !aborted) mbar_arrive(&empty[s]);
     if (cg == a.cps - 1) {  // slab end
       reduce_y();
-      if (seg_whole) {
-        store_tile<GW, GATE_UP>(a, sl * kSlabTiles + warp, lane, y[0], y[NS - 1]);
+      if (aborted) {
+      } else if (seg_whole) {
+        store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, y[0], y[NS - 1]);
       } else {  // the run's first segment, partial
         publish(0, y);
-        first_slab = sl;
       }
+      if (!seg_whole) first_slab = sl;
 #pragma unroll
       for (int si = 0; si < NS; ++si)
 #pragma unroll
@@ -518,18 +528,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   int last_slab = -1;
   if (nch > 0 && cg != a.cps - 1) {  // the run ended inside a slab
     reduce_y();
-    publish(finished_any ? 1 : 0, y);
+    if (!aborted) publish(finished_any ? 1 : 0, y);
     last_slab = sl;
   }
-  if (first_slab < 0 && last_slab < 0) return;
-  // the lanes' stores above happen before lane 0's release increments
+  if (aborted || (first_slab < 0 && last_slab < 0)) return;
+  // the lanes' stores above happen before lane 0's release fence; one fence
+  // covers both increments, which are then in flight together
   __syncwarp();
   uint32_t done = 0;  // bit 0: first slab complete, bit 1: last slab complete
   if (lane == 0) {
     uint32_t o0 = 0, o1 = 0;
     int clo, chi;
-    if (first_slab >= 0) o0 = atom_add_acq_rel(&a.count[(size_t)first_slab * kSlabTiles + warp], 1u);
-    if (last_slab >= 0) o1 = atom_add_acq_rel(&a.count[(size_t)last_slab * kSlabTiles + warp], 1u);
+    fence_acq_rel_gpu();
+    if (first_slab >= 0) o0 = atom_add_relaxed(&a.count[(size_t)first_slab * kSlabTiles + tile], 1u);
+    if (last_slab >= 0) o1 = atom_add_relaxed(&a.count[(size_t)last_slab * kSlabTiles + tile], 1u);
     if (first_slab >= 0) {
       contributors(first_slab, clo, chi);
       if (o0 + 1 == (uint32_t)(chi - clo + 1)) done |= 1u;
@@ -538,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       contributors(last_slab, clo, chi);
       if (o1 + 1 == (uint32_t)(chi - clo + 1)) done |= 2u;
     }
+    if (done) fence_acq_rel_gpu();  // acquire: every other part is visible
   }
   done = __shfl_sync(0xffffffffu, done, 0);
   // lane 0's acquire happens before the other lanes' loads
@@ -602,7 +615,7 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
   const int ng = in / kGroup;
   const int sms = device_sm_count();
   const GemvCfg cfg = gemv_cfg_override();
-  const int cb = cfg.warps > 0 ? cfg.warps : 4;
+  const int cb = cfg.warps > 0 ? cfg.warps : 8;
   const int cps = (ng + cb - 1) / cb;
   const long long chunks = (long long)row_slabs(out) * cps;
   // run arithmetic on the device is 32-bit
@@ -611,23 +624,27 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
   if (per > m) per = m;
   for (;;) {
     const int P = x_f32 ? 2 * per : per;
-    // one CTA per SM with a deep ring measured best for every decode shape;
-    // a forced grid above the SM count runs two per SM
+    // one CTA per SM with a deep ring of 8-group chunks measured best for
+    // every decode shape
     {
-      const int per_sm = cfg.grid > sms ? 2 : 1;
-      long long grid = cfg.grid > 0 ? cfg.grid : (long long)sms * per_sm;
-      if (grid > (long long)sms * 2) grid = (long long)sms * 2;
+      // one CTA per SM (a CTA holds 17 warps and most of the shared memory)
+      long long grid = cfg.grid > 0 ? std::min(cfg.grid, sms) : (long long)sms;
+      // Whole slabs per CTA when that still fills >= 85% of the SMs: no
+      // slab is split, so there is no split-K fix-up at the end of the run
+      // (the fused gate/up of a 17408-wide MLP: 136 slabs on 148 SMs).
+      if (cfg.grid <= 0) {
+        const int slabs = row_slabs(out);
+        const int j = (slabs + sms - 1) / sms;
+        if (slabs % j == 0 && (long long)(slabs / j) * 100 >= (long long)sms * 85) grid = slabs / j;
+      }
       if (chunks < grid) grid = chunks;  // every CTA run holds at least one chunk
       const long long max_run = (chunks + grid - 1) / grid;
       const int xcap = (int)std::min<long long>(ng, max_run * cb);
-      const size_t limit = per_sm == 2 ? (size_t)kGemvHalfSmem : (size_t)kGemvMaxSmem;
+      const size_t limit = (size_t)kGemvMaxSmem;
+      // the deepest ring that fits, up to a forced depth
       int st = 0;
-      if (cfg.depth > 0) {
-        if (gemv_smem(cfg.depth, cb, gate_up, xcap, P) <= limit) st = cfg.depth;
-      } else {
-        for (int t = per_sm == 2 ? 6 : 5; t >= 2 && !st; --t)
-          if (gemv_smem(t, cb, gate_up, xcap, P) <= limit) st = t;
-      }
+      for (int t = cfg.depth > 0 ? cfg.depth : 5; t >= 2 && !st; --t)
+        if (gemv_smem(t, cb, gate_up, xcap, P) <= limit) st = t;
       if (st) {
         p.ok = true;
         p.stages = st;

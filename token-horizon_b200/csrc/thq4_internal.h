@@ -13,9 +13,6 @@ namespace thq4 {
 
 // Dynamic shared memory the GEMV may use per CTA (B200: 227 KB opt-in).
 constexpr int kGemvMaxSmem = 227 * 1024;
-// Half of it: the decode kernel sizes its rings so two CTAs share an SM.
-constexpr int kGemvHalfSmem = 113 * 1024;
-
 
 // Runs `fn` once per device (e.g. a cudaFuncSetAttribute), remembering
 // success; a failure is returned and retried on the next call.

@@ -20,9 +20,9 @@
 //            slot order of w * d, in f32 (separate multiply and add), one bf16
 //            rounding.
 //
-// Select runs one warp per token; group runs in one CTA (one thread per
-// expert, routes staged in shared memory); gather and combine move 16-byte
-// pieces.  All of it is negligible next to the expert products, which stream
+// Select runs one warp per token; group runs in one CTA (a two-pass stable
+// counting sort over warp segments of the routes); gather and combine move
+// 16-byte pieces.  All of it is negligible next to the expert products, which stream
 // every touched expert's weights from HBM once per group tile.
 #include <algorithm>
 
@@ -74,52 +74,105 @@ __global__ void select_kernel(const uint16_t *logits, int T, int E, int k, uint3
   }
 }
 
-// One CTA, one thread per expert (E <= blockDim).  Routes in ascending order
-// within each expert.
+// Warps of the grouping kernel: each owns a contiguous segment of the routes
+// and one row of per-expert counters in shared memory.
+__host__ __device__ inline int group_warps(int E) { return E <= 512 ? 32 : 16; }
+
+// One CTA.  A stable counting sort of the routes by expert:
+//   1. every warp counts its segment's routes per expert (32 routes at a
+//      time; lanes holding the same expert find each other with match.any);
+//   2. per expert, the warps' counts become exclusive prefixes in warp order
+//      and the expert's total; the experts' tile counts are scanned into
+//      their first tile;
+//   3. every warp walks its segment again and places each route after the
+//      earlier ones of its expert (its rank among the 32 plus the running
+//      count), so routes stay in ascending order within an expert.
+// Routes whose expert id is out of range are dropped (combine skips them).
 __global__ void group_kernel(const uint32_t *ids, int R, int E, int max_tiles, uint32_t *tiles, uint32_t *grouped,
                              uint32_t *route_rows, uint32_t *ntiles, uint32_t *status) {
-  extern __shared__ uint32_t sm[];  // ids staged (R <= capacity), then counts / offsets
-  uint32_t *sids = sm, *cnt = sm + R, *off = cnt + E;
-  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+  extern __shared__ uint32_t sm[];
+  const int W = blockDim.x >> 5;
+  uint32_t *cw = sm;            // [W][E]: counts, then each warp's running base
+  uint32_t *off = sm + W * E;   // [E + 1]: first tile of each expert, tiles in use
+  uint32_t *tot = off + E + 1;  // [E]: routes of each expert
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int i = threadIdx.x; i < W * E; i += blockDim.x) cw[i] = 0;
+  __syncthreads();
+  const int seg = (R + W - 1) / W;
+  const int r0 = min(R, warp * seg), r1 = min(R, r0 + seg);
+  auto expert_of = [&](int r) -> uint32_t {
+    if (r >= r1) return kPad;
     const uint32_t e = ids[r];
-    sids[r] = e;
-    if (e >= (uint32_t)E) {  // such a route is dropped: combine skips it
+    return e < (uint32_t)E ? e : kPad;
+  };
+  for (int b = r0; b < r1; b += 32) {
+    const int r = b + lane;
+    const uint32_t e = expert_of(r);
+    if (r < r1 && e == kPad) {
       raise_status(status, kStatusBadExpert);
       route_rows[r] = kPad;
     }
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    if (e != kPad && (peers & lt) == 0) cw[warp * E + e] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
-  const int e = threadIdx.x;
-  uint32_t c = 0;
-  if (e < E)
-    for (int r = 0; r < R; ++r) c += sids[r] == (uint32_t)e;
-  if (e < E) cnt[e] = c;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
     uint32_t acc = 0;
-    for (int x = 0; x < E; ++x) {
-      off[x] = acc;
-      acc += (cnt[x] + kMoeTileRows - 1) / kMoeTileRows;
+    for (int w = 0; w < W; ++w) {
+      const uint32_t c = cw[w * E + e];
+      cw[w * E + e] = acc;
+      acc += c;
     }
-    *ntiles = acc <= (uint32_t)max_tiles ? acc : 0u;
-    if (acc > (uint32_t)max_tiles) raise_status(status, kStatusBounds);
-    off[E] = acc;
+    tot[e] = acc;
   }
   __syncthreads();
-  if (off[E] > (uint32_t)max_tiles || e >= E) return;
-  const uint32_t t0 = off[e], nt = (c + kMoeTileRows - 1) / kMoeTileRows;
-  for (uint32_t t = 0; t < nt; ++t) {
-    tiles[2 * (t0 + t)] = (uint32_t)e;
-    tiles[2 * (t0 + t) + 1] = min((uint32_t)kMoeTileRows, c - t * kMoeTileRows);
+  if (warp == 0) {
+    uint32_t carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const uint32_t nt = e < E ? (tot[e] + kMoeTileRows - 1) / kMoeTileRows : 0u;
+      uint32_t v = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (e < E) off[e] = carry + v - nt;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) {
+      off[E] = carry;
+      *ntiles = carry <= (uint32_t)max_tiles ? carry : 0u;
+      if (carry > (uint32_t)max_tiles) raise_status(status, kStatusBounds);
+    }
   }
-  uint32_t cur = 0;
-  for (int r = 0; r < R; ++r)
-    if (sids[r] == (uint32_t)e) {
-      const uint32_t row = t0 * kMoeTileRows + cur++;
+  __syncthreads();
+  if (off[E] > (uint32_t)max_tiles) return;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const uint32_t t0 = off[e], c = tot[e], nt = (c + kMoeTileRows - 1) / kMoeTileRows;
+    for (uint32_t t = 0; t < nt; ++t) {
+      tiles[2 * (t0 + t)] = (uint32_t)e;
+      tiles[2 * (t0 + t) + 1] = min((uint32_t)kMoeTileRows, c - t * kMoeTileRows);
+    }
+    for (uint32_t row = t0 * kMoeTileRows + c; row < (t0 + nt) * kMoeTileRows; ++row) grouped[row] = kPad;
+  }
+  for (int b = r0; b < r1; b += 32) {
+    const int r = b + lane;
+    const uint32_t e = expert_of(r);
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    uint32_t base = 0;
+    if (e != kPad) {
+      base = cw[warp * E + e];
+      const uint32_t row = off[e] * kMoeTileRows + base + __popc(peers & lt);
       grouped[row] = (uint32_t)r;
       route_rows[r] = row;
     }
-  for (uint32_t row = t0 * kMoeTileRows + c; row < (t0 + nt) * kMoeTileRows; ++row) grouped[row] = kPad;
+    __syncwarp();
+    if (e != kPad && (peers & lt) == 0) cw[warp * E + e] = base + __popc(peers);
+    __syncwarp();
+  }
 }
 
 // xg[row] = x[route / k] for the live rows of the live tiles, zero for padding.
@@ -179,7 +232,10 @@ uint32_t moe_max_tiles(int T, int E, int k) {
   return (uint32_t)std::min(bound, routed);
 }
 
-size_t moe_group_smem(int R, int E) { return ((size_t)R + 2 * (size_t)E + 1) * 4; }
+size_t moe_group_smem(int R, int E) {
+  (void)R;  // the routes are read from global memory twice, never staged
+  return ((size_t)group_warps(E) * E + 2 * (size_t)E + 1) * 4;
+}
 
 cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
                              uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
@@ -193,8 +249,7 @@ cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32
   static DeviceOnce once;
   e = once.run([] { return cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
   if (e != cudaSuccess) return e;
-  const int gthreads = std::max(32, (E + 31) / 32 * 32);
-  group_kernel<<<1, gthreads, smem, stream>>>(ids, R, E, max_tiles, tiles, grouped, route_rows, ntiles, status_word());
+  group_kernel<<<1, group_warps(E) * 32, smem, stream>>>(ids, R, E, max_tiles, tiles, grouped, route_rows, ntiles, status_word());
   return cudaGetLastError();
 }
 

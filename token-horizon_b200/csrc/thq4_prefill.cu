@@ -25,12 +25,18 @@
 //   - the activations are the B operand: x tiles of 256 (gate/up: 128)
 //     tokens x 64 k, loaded by a 2-D TMA with 128-byte swizzle (zero fill
 //     past m) into a shared-memory ring;
+//   - a second producer warp streams the raw slab-groups into their own,
+//     deeper ring, released as soon as the dequant warps have read a stage
+//     (not when the MMA is done), so HBM requests stay in flight even when
+//     a tile has few tokens (the MoE expert tiles of 32);
 //   - one thread issues tcgen05.mma.kind::f16 (bf16 in, f32 accumulate in
 //     TMEM), M = 128 output rows x N = 256 tokens per k-step of 16, and
 //     commits each stage back to the producer;
 //   - persistent CTAs (one per SM) walk tiles of one slab (128 rows) x 256
 //     tokens, token tiles fastest, so a slab is fetched from HBM once and
-//     re-read from L2; eight epilogue warps drain D (tcgen05.ld) -- a warp's
+//     re-read from L2; D has one or two TMEM buffers (two where TMEM has
+//     room, so the next tile's MMAs overlap this tile's epilogue); eight
+//     epilogue warps drain D (tcgen05.ld) -- a warp's
 //     32 lanes hold 32 consecutive output rows, so each store of a token's
 //     values is one contiguous 64-byte segment of y;
 //   - every wait is bounded; a timeout raises kStatusTimeout, sets a CTA-wide
@@ -39,6 +45,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "thq4_common.cuh"
@@ -50,8 +57,9 @@ namespace {
 constexpr int kBN = 128;  // output rows per tile (one slab): the MMA's M
 constexpr int kBK = 64;   // k per stage (one quant group)
 constexpr int kDeqWarps = 8, kEpiWarps = 8;
-constexpr int kWarpEpi0 = 8, kWarpProd = 16, kWarpMma = 17;  // dequant warps are 0..7
-constexpr int kPfThreads = 18 * 32;
+// dequant warps are 0..7; the x producer, the MMA issuer and the weight producer follow the epilogue warps
+constexpr int kWarpEpi0 = 8, kWarpProd = 16, kWarpMma = 17, kWarpRaw = 18;
+constexpr int kPfThreads = 19 * 32;
 constexpr uint32_t kXBox = 128 * kBK * 2;   // one 128-token x box, bytes
 constexpr uint32_t kRawStage = 4096 + 512;  // one slab-group
 constexpr int kAcolsPerStage = kBK / 2;     // TMEM columns of one stage's A (bf16 pairs)
@@ -107,26 +115,34 @@ __device__ __forceinline__ PfUnit pf_unit(const PfArgs &a, int u) {
   return x;
 }
 
-// NS weight streams (1, or 2 for gate/up), BT tokens per tile, S stages
-template <int NS, int BT, int S>
+// NS weight streams (1, or 2 for gate/up), BT tokens per tile, S stages of
+// x (shared memory) and of dequantised A (TMEM), RW stages of raw weights
+// (shared memory), NB accumulator buffers in TMEM.  The raw ring is released
+// as soon as the dequant warps have read a stage, so it can run far ahead of
+// the tensor core: it is what keeps HBM requests in flight when a tile has
+// few tokens.
+template <int NS, int BT, int S, int RW, int NB>
 struct PfCfg {
   static constexpr uint32_t x_stage = BT * kBK * 2;
   static constexpr uint32_t x_off = 0;
   static constexpr uint32_t raw_off = x_off + S * x_stage;
   // a bf16 output tile [BT tokens][128 rows], staged between TMEM and y
-  static constexpr uint32_t y_off = raw_off + S * NS * kRawStage;
+  static constexpr uint32_t y_off = raw_off + RW * NS * kRawStage;
   static constexpr uint32_t bar_off = y_off + BT * kBN * 2;
-  // barriers: xfull[S], rawfull[S], deq[S], empty[S], accf, acce, yfull, ydone
-  static constexpr uint32_t misc_off = bar_off + (4 * S + 4) * 8;
+  // barriers: xfull[S], deq[S], empty[S], rawfull[RW], rawempty[RW],
+  // accf[NB], acce[NB], yfull, ydone
+  static constexpr int n_bars = 3 * S + 2 * RW + 2 * NB + 2;
+  static constexpr uint32_t misc_off = bar_off + n_bars * 8;
   static constexpr int box_rows = BT < 128 ? BT : 128;  // x rows per TMA box
   static constexpr uint32_t bytes = misc_off + 16;
   static constexpr uint32_t alloc = bytes + 1024;  // room to align the base to 1024
-  // TMEM: D (NS accumulators of BT columns), then the A ring
+  // TMEM: NB buffers of D (NS accumulators of BT columns each), then the A ring
   static constexpr int d_cols = NS * BT;
-  static constexpr int a_col0 = d_cols;
-  static constexpr int cols = d_cols + S * NS * kAcolsPerStage;
+  static constexpr int a_col0 = NB * d_cols;
+  static constexpr int cols = a_col0 + S * NS * kAcolsPerStage;
   static_assert(cols <= 512, "TMEM holds 512 columns");
   static_assert(alloc <= 227 * 1024, "shared memory");
+  static_assert(RW >= S, "the raw ring is at least as deep as the A ring");
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -255,15 +271,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int NS, int BT, int S, bool SF16, bool YF32>
+template <int NS, int BT, int S, int RW, int NB, bool SF16, bool YF32>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap xmap, const PfArgs a) {
-  using C = PfCfg<NS, BT, S>;
+  using C = PfCfg<NS, BT, S, RW, NB>;
   constexpr uint32_t kIdesc = idesc_bf16(BT);
   extern __shared__ unsigned char smem_raw[];
   unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::bar_off);
-  uint64_t *xfull = bars, *rawfull = bars + S, *deq = bars + 2 * S, *empty = bars + 3 * S;
-  uint64_t *accf = bars + 4 * S, *acce = accf + 1, *yfull = accf + 2, *ydone = accf + 3;
+  uint64_t *xfull = bars, *deq = bars + S, *empty = bars + 2 * S;
+  uint64_t *rawfull = bars + 3 * S, *rawempty = rawfull + RW;
+  uint64_t *accf = rawempty + RW, *acce = accf + NB, *yfull = acce + NB, *ydone = yfull + 1;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + C::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(sm + C::misc_off + 4);
   int *units_sm = reinterpret_cast<int *>(sm + C::misc_off + 8);
@@ -272,12 +289,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&rawfull[s], 1);
       mbar_init(&deq[s], kDeqWarps);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
-    mbar_init(acce, kEpiWarps);
+    for (int r = 0; r < RW; ++r) {
+      mbar_init(&rawfull[r], 1);
+      mbar_init(&rawempty[r], kDeqWarps);
+    }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], kEpiWarps);
+    }
     mbar_init(yfull, kEpiWarps);
     mbar_init(ydone, kEpiWarps);
     *abort = 0;
@@ -296,9 +318,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   const int units = units_sm[0];
 
   if (warp == kWarpProd) {
-    // ---- producer ------------------------------------------------------------
+    // ---- x producer: TMA tiles of the activations ------------------------------
     if (lane == 0) {
-      const uint64_t pol = evict_first_policy();
       int it = 0, issued = 0;
       for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x) {
         const PfUnit un = pf_unit<BT>(a, tile);
@@ -310,31 +331,47 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
           for (int bx = 0; bx < BT / C::box_rows; ++bx)
             tma_load_2d(xd + bx * C::box_rows * kBK * 2, &xmap, g * kBK, un.row0 + bx * C::box_rows, &xfull[s]);
-          unsigned char *rd = sm + C::raw_off + (size_t)s * NS * kRawStage;
-          const size_t sg = (size_t)un.nt * a.ng + g;
-          mbar_arrive_expect_tx(&rawfull[s], NS * kRawStage);
-#pragma unroll
-          for (int si = 0; si < NS; ++si) {
-            bulk_g2s(rd + si * kRawStage, un.qw[si] + sg * 4096, 4096, &rawfull[s], pol);
-            bulk_g2s(rd + si * kRawStage + 4096, un.sb[si] + sg * 512, 512, &rawfull[s], pol);
-          }
           issued = it + 1;
         }
       }
       if (*abort)
         for (int k = issued - S; k < issued; ++k)
-          if (k >= 0) {
-            drain_wait(&xfull[k % S], (uint32_t)((k / S) & 1));
-            drain_wait(&rawfull[k % S], (uint32_t)((k / S) & 1));
+          if (k >= 0) drain_wait(&xfull[k % S], (uint32_t)((k / S) & 1));
+    }
+  } else if (warp == kWarpRaw) {
+    // ---- weight producer: one bulk copy per raw slab-group and stream ---------
+    if (lane == 0) {
+      const uint64_t pol = evict_first_policy();
+      int it = 0, issued = 0;
+      for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x) {
+        const PfUnit un = pf_unit<BT>(a, tile);
+        for (int g = 0; g < a.ng; ++g, ++it) {
+          const int r = it % RW;
+          if (it >= RW && !pf_wait(&rawempty[r], (uint32_t)(((it / RW) - 1) & 1), abort, a.status)) break;
+          unsigned char *rd = sm + C::raw_off + (size_t)r * NS * kRawStage;
+          const size_t sg = (size_t)un.nt * a.ng + g;
+          mbar_arrive_expect_tx(&rawfull[r], NS * kRawStage);
+#pragma unroll
+          for (int si = 0; si < NS; ++si) {
+            bulk_g2s(rd + si * kRawStage, un.qw[si] + sg * 4096, 4096, &rawfull[r], pol);
+            bulk_g2s(rd + si * kRawStage + 4096, un.sb[si] + sg * 512, 512, &rawfull[r], pol);
           }
+          issued = it + 1;
+        }
+      }
+      if (*abort)
+        for (int k = issued - RW; k < issued; ++k)
+          if (k >= 0) drain_wait(&rawfull[k % RW], (uint32_t)((k / RW) & 1));
     }
   } else if (warp == kWarpMma) {
     // ---- MMA issuer ------------------------------------------------------------
     if (lane == 0) {
       int it = 0, local = 0, committed = 0;
       for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x, ++local) {
-        if (local >= 1 && !pf_wait(acce, (uint32_t)((local - 1) & 1), abort, a.status)) break;
+        const int b = local % NB;
+        if (local >= NB && !pf_wait(&acce[b], (uint32_t)(((local / NB) - 1) & 1), abort, a.status)) break;
         tc_fence_after();
+        const uint32_t dcol = (uint32_t)(b * C::d_cols);
         bool ok = true;
         for (int g = 0; g < a.ng; ++g, ++it) {
           const int s = it % S;
@@ -351,14 +388,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
             const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
             for (int si = 0; si < NS; ++si)
-              mma_bf16_ts(tmem + (uint32_t)(si * BT),
+              mma_bf16_ts(tmem + dcol + (uint32_t)(si * BT),
                           tmem + (uint32_t)(C::a_col0 + (s * NS + si) * kAcolsPerStage + kk * 8), bd, kIdesc, acc);
           }
-          umma_commit(&empty[s]);  // frees the x, raw and A slots once these MMAs are done
+          umma_commit(&empty[s]);  // frees x slot s and A slot s once these MMAs are done
           committed = it + 1;
         }
         if (!ok) break;
-        umma_commit(accf);
+        umma_commit(&accf[b]);
       }
       if (*abort && committed > 0)
         drain_wait(&empty[(committed - 1) % S], (uint32_t)(((committed - 1) / S) & 1));
@@ -375,14 +412,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x) {
       bool ok = true;
       for (int g = 0; g < a.ng; ++g, ++it) {
-        const int s = it % S;
-        if (!pf_wait(&rawfull[s], (uint32_t)((it / S) & 1), abort, a.status)) {
+        const int s = it % S, rs = it % RW;
+        // the raw stage has landed and the MMAs that read A slot s last are done
+        if (!pf_wait(&rawfull[rs], (uint32_t)((it / RW) & 1), abort, a.status) ||
+            (it >= S && !pf_wait(&empty[s], (uint32_t)(((it / S) - 1) & 1), abort, a.status))) {
           ok = false;
           break;
         }
+        tc_fence_after();
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
-          const unsigned char *raw = sm + C::raw_off + (size_t)(s * NS + si) * kRawStage;
+          const unsigned char *raw = sm + C::raw_off + (size_t)(rs * NS + si) * kRawStage;
           const uint2 qd = *reinterpret_cast<const uint2 *>(raw + 4096 + tl * 64 + r * 8);
           const uint32_t sbw = hrow ? qd.y : qd.x;
           const float sv = sb_to_f32<SF16>(sbw & 0xffffu), bv = sb_to_f32<SF16>(sbw >> 16);
@@ -411,7 +451,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&deq[s]);
+        if (lane == 0) {
+          mbar_arrive(&rawempty[rs]);
+          mbar_arrive(&deq[s]);
+        }
       }
       if (!ok) break;
     }
@@ -429,14 +472,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     for (int tile = blockIdx.x; tile < units && !*abort; tile += gridDim.x, ++local) {
       const PfUnit un = pf_unit<BT>(a, tile);
       const int nt = un.nt;
-      if (!pf_wait(accf, (uint32_t)(local & 1), abort, a.status)) break;
+      const int b = local % NB;
+      if (!pf_wait(&accf[b], (uint32_t)((local / NB) & 1), abort, a.status)) break;
       // the SMEM tile is free once every warp stored the previous one
       if (!YF32 && local >= 1 && !pf_wait(ydone, (uint32_t)((local - 1) & 1), abort, a.status)) break;
       tc_fence_after();
       const int nl = 32 * q + lane, n = nt * kBN + nl;
 #pragma unroll 1
       for (int tc0 = th * (BT / 2); tc0 < (th + 1) * (BT / 2); tc0 += 16) {  // 16 tokens at a time
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)tc0;
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * C::d_cols + tc0);
         uint32_t u[16];
         float v[16];
         tmem_ld16(taddr, u);
@@ -464,7 +508,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce);  // the MMA may overwrite D from here on
+      if (lane == 0) mbar_arrive(&acce[b]);  // the MMA may overwrite this D buffer from here on
       if constexpr (!YF32) {
         if (lane == 0) mbar_arrive(yfull);
         if (!pf_wait(yfull, (uint32_t)(local & 1), abort, a.status)) break;
@@ -502,11 +546,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   }
 }
 
-template <int NS, int BT, int S, bool SF16, bool YF32>
+template <int NS, int BT, int S, int RW, int NB, bool SF16, bool YF32>
 cudaError_t prefill_launch_t(const CUtensorMap &map, const PfArgs &a, int grid, cudaStream_t stream) {
-  auto *k = &prefill_kernel<NS, BT, S, SF16, YF32>;
+  auto *k = &prefill_kernel<NS, BT, S, RW, NB, SF16, YF32>;
   static DeviceOnce once;
-  const size_t smem = PfCfg<NS, BT, S>::alloc;
+  const size_t smem = PfCfg<NS, BT, S, RW, NB>::alloc;
   cudaError_t e = once.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (e != cudaSuccess) return e;
   k<<<grid, kPfThreads, smem, stream>>>(map, a);
@@ -547,22 +591,39 @@ cudaError_t make_xmap(const void *x, int k, int rows, int box_rows, CUtensorMap 
   return cr == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int NS, int BT, int S>
+template <int NS, int BT, int S, int RW, int NB>
 cudaError_t launch_cfg(const CUtensorMap &map, const PfArgs &a, int grid, bool f16, bool y_f32, cudaStream_t stream) {
-  return f16 ? (y_f32 ? prefill_launch_t<NS, BT, S, true, true>(map, a, grid, stream)
-                      : prefill_launch_t<NS, BT, S, true, false>(map, a, grid, stream))
-             : (y_f32 ? prefill_launch_t<NS, BT, S, false, true>(map, a, grid, stream)
-                      : prefill_launch_t<NS, BT, S, false, false>(map, a, grid, stream));
+  return f16 ? (y_f32 ? prefill_launch_t<NS, BT, S, RW, NB, true, true>(map, a, grid, stream)
+                      : prefill_launch_t<NS, BT, S, RW, NB, true, false>(map, a, grid, stream))
+             : (y_f32 ? prefill_launch_t<NS, BT, S, RW, NB, false, true>(map, a, grid, stream)
+                      : prefill_launch_t<NS, BT, S, RW, NB, false, false>(map, a, grid, stream));
 }
 
 }  // namespace
 
 bool prefill_supported(int m, bool x_f32) { return m > 8 && !x_f32; }
 
+namespace {
+// Token-tile width of the one-weight form: THQ4_PREFILL_BT=128 forces
+// 128-token tiles with two D buffers (a tuning switch read once).  256 is
+// the default: the dequant warps, not the tensor core, bound a tile, and a
+// 128-token tile spends the same dequant work on half the product (at
+// M = 512 it measured 1.5x slower despite the fuller last wave).
+int prefill_bt(int m) {
+  (void)m;
+  static const int forced = [] {
+    const char *s = std::getenv("THQ4_PREFILL_BT");
+    const int v = s ? std::atoi(s) : 0;
+    return v == 128 ? v : 0;
+  }();
+  return forced ? forced : 256;
+}
+}  // namespace
+
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
                            cudaStream_t stream) {
   const bool gate_up = w1 != nullptr;
-  const int bt = gate_up ? 128 : 256;
+  const int bt = gate_up ? 128 : prefill_bt(m);
   CUtensorMap map;
   cudaError_t e = make_xmap(x, w0.in, m, 128, &map);
   if (e != cudaSuccess) return e;
@@ -582,8 +643,9 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   a.tiles = (int)tiles;
   const int grid = (int)std::min<long long>(tiles, device_sm_count());
   const bool f16 = w0.sb_dtype == THQ4_F16;
-  if (gate_up) return launch_cfg<2, 128, 4>(map, a, grid, f16, y_f32, stream);
-  return launch_cfg<1, 256, 4>(map, a, grid, f16, y_f32, stream);
+  if (gate_up) return launch_cfg<2, 128, 4, 4, 1>(map, a, grid, f16, y_f32, stream);
+  if (bt == 128) return launch_cfg<1, 128, 8, 8, 2>(map, a, grid, f16, y_f32, stream);
+  return launch_cfg<1, 256, 4, 4, 1>(map, a, grid, f16, y_f32, stream);
 }
 
 cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream) {
@@ -613,8 +675,8 @@ cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream) {
   a.max_units = (int)units;
   const int grid = (int)std::min<long long>(units, device_sm_count());
   const bool f16 = g.w0->sb_dtype == THQ4_F16;
-  if (gate_up) return launch_cfg<2, kMoeTileRows, 6>(map, a, grid, f16, false, stream);
-  return launch_cfg<1, kMoeTileRows, 6>(map, a, grid, f16, false, stream);
+  if (gate_up) return launch_cfg<2, kMoeTileRows, 6, 20, 2>(map, a, grid, f16, false, stream);
+  return launch_cfg<1, kMoeTileRows, 6, 36, 2>(map, a, grid, f16, false, stream);
 }
 
 }  // namespace thq4
