@@ -476,7 +476,7 @@ def bench_moe(torch, thq4, synth, dev, hbm_peak):
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"config": "T 256, H 2048, E 128, k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
             "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
-            "kernel": "grouped prefill_kernel (tcgen05) + routing / gather / combine"}
+            "kernel": "moe_gemv_kernel (grouped small-tile mma.sync experts) + routing / gather / combine"}
 
 
 # ---------------------------------------------------------------------------

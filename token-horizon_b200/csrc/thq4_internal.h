@@ -9,6 +9,8 @@
 
 #include "../../include/thq4.h"
 
+struct CUtensorMap_st;  // cuda.h's tensor map (only pointers to it cross files)
+
 namespace thq4 {
 
 // Dynamic shared memory the GEMV may use per CTA (B200: 227 KB opt-in).
@@ -74,20 +76,29 @@ bool prefill_supported(int m, bool x_f32);
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
                            cudaStream_t stream);
 
+// bf16 x [rows][k] (k innermost) as a 2-D tensor map with 64 x box_rows
+// boxes and 128-byte swizzle; `map` points to a CUtensorMap.
+cudaError_t make_xmap(const void *x, int k, int rows, int box_rows, ::CUtensorMap_st *map);
+
 // ---- MoE -------------------------------------------------------------------
 // Routes are grouped by expert into tiles of this many activation rows.
 constexpr int kMoeTileRows = 32;
-// The grouped expert product on the tcgen05 path: for every group tile gt <
-// *count, y rows [gt*32, gt*32 + live) = x rows . expert(tiles[2gt])^T (w1:
-// the fused SwiGLU with w0 = gate, w1 = up).  x, y: [max_tiles*32][k], [..][n].
-struct GroupedGemm {
+
+// The expert products for small group tiles (csrc/thq4_moe_gemv.cu): for
+// every group tile gt < *count, y rows [gt*32, gt*32 + 32) = x rows .
+// expert(tiles[2gt])^T (w1: the fused SwiGLU with w0 = gate, w1 = up).
+// xsum [tile][in/64][32] holds the sum of each x row's 64-groups; ysum
+// (optional) receives the same for y.  x, y: [max_tiles*32][in], [..][out].
+struct MoeExperts {
   const void *x;
   void *y;
   const thq4_experts *w0, *w1;
   const uint32_t *tiles, *count;
+  const float *xsum;
+  float *ysum;
   int max_tiles;
 };
-cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream);
+cudaError_t moe_expert_launch(const MoeExperts &g, cudaStream_t stream);
 
 // Upper bound on group tiles for T tokens routed to k of E experts.
 uint32_t moe_max_tiles(int T, int E, int k);
@@ -101,6 +112,7 @@ cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32
 struct MoeWorkspace {
   uint32_t *ids, *tiles, *grouped, *route_rows, *ntiles;
   uint16_t *weights, *xg, *h, *d;
+  float *xsum, *hsum;  // group sums of xg and h: [tile][groups][32]
   size_t bytes;
   int max_tiles;
 };

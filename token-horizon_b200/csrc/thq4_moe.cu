@@ -14,8 +14,9 @@
 //            this library fixes it to ascending route index, so the
 //            permutation is bit-exact and reproducible;
 //   experts  moe_gather_rows + moe_expert_tile / q4_mpp_tile (:453-640): the
-//            gathered rows go through the tcgen05 grouped GEMM (gate/up with
-//            the SwiGLU epilogue, then down), bf16 at each boundary;
+//            gathered rows (with their 64-group sums) go through the grouped
+//            small-tile kernel of thq4_moe_gemv.cu (gate/up with the SwiGLU
+//            epilogue, then down), bf16 at each boundary;
 //   combine  moe_combine (:642-664): y = residual + sum over the k slots in
 //            slot order of w * d, in f32 (separate multiply and add), one bf16
 //            rounding.
@@ -175,18 +176,31 @@ __global__ void group_kernel(const uint32_t *ids, int R, int E, int max_tiles, u
   }
 }
 
-// xg[row] = x[route / k] for the live rows of the live tiles, zero for padding.
+// xg[row] = x[route / k] for the live rows of the live tiles, zero for
+// padding, and xsum[tile][g][row % 32] = the sum of the row's 64-group g in
+// f32.  One thread per 16-byte piece (8 values, summed in order); the 8
+// pieces of a group are 8 aligned lanes, which add their sums with a fixed
+// shuffle tree (deterministic).
 __global__ void gather_kernel(const uint16_t *x, int H, int k, const uint32_t *grouped, const uint32_t *ntiles,
-                              uint16_t *xg) {
+                              uint16_t *xg, float *xsum) {
   const int pieces = H / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t row = i / pieces;
-  if (row >= (size_t)(*ntiles) * kMoeTileRows) return;
+  if (row >= (size_t)(*ntiles) * kMoeTileRows) return;  // whole 8-lane groups leave together
   const int p = (int)(i % pieces);
   const uint32_t route = grouped[row];
   uint4 v = make_uint4(0, 0, 0, 0);
   if (route != kPad) v = reinterpret_cast<const uint4 *>(x + (size_t)(route / k) * H)[p];
   reinterpret_cast<uint4 *>(xg + row * H)[p] = v;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float sum = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) sum = (sum + bf16f((uint16_t)(w[e] & 0xffffu))) + bf16f((uint16_t)(w[e] >> 16));
+  const unsigned lane = threadIdx.x & 31, gmask = 0xFFu << (lane & ~7u);
+  sum += __shfl_xor_sync(gmask, sum, 1);
+  sum += __shfl_xor_sync(gmask, sum, 2);
+  sum += __shfl_xor_sync(gmask, sum, 4);
+  if ((p & 7) == 0) xsum[((row / kMoeTileRows) * (H / 64) + p / 8) * kMoeTileRows + row % kMoeTileRows] = sum;
 }
 
 // y[t] = residual[t] + sum_s w[t][s] * d[route_rows[t*k + s]], slot order, f32.
@@ -271,6 +285,8 @@ MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base) {
   w.xg = reinterpret_cast<uint16_t *>(take(rows * H * 2));
   w.h = reinterpret_cast<uint16_t *>(take(rows * I * 2));
   w.d = reinterpret_cast<uint16_t *>(take(rows * H * 2));
+  w.xsum = reinterpret_cast<float *>(take(rows * (H / 64) * 4));
+  w.hsum = reinterpret_cast<float *>(take(rows * (I / 64) * 4));
   w.bytes = o;
   w.max_tiles = (int)mt;
   return w;
@@ -286,23 +302,27 @@ cudaError_t moe_launch(const void *x, const void *residual, const void *logits, 
   {
     const size_t n = rows * (H / 8);
     gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const uint16_t *>(x), H, k, w.grouped,
-                                                                    w.ntiles, w.xg);
+                                                                    w.ntiles, w.xg, w.xsum);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  GroupedGemm g{};
+  MoeExperts g{};
   g.x = w.xg;
   g.y = w.h;
   g.w0 = &gate;
   g.w1 = &up;
   g.tiles = w.tiles;
   g.count = w.ntiles;
+  g.xsum = w.xsum;
+  g.ysum = w.hsum;
   g.max_tiles = w.max_tiles;
-  if ((e = grouped_launch(g, stream)) != cudaSuccess) return e;
+  if ((e = moe_expert_launch(g, stream)) != cudaSuccess) return e;
   g.x = w.h;
   g.y = w.d;
   g.w0 = &down;
   g.w1 = nullptr;
-  if ((e = grouped_launch(g, stream)) != cudaSuccess) return e;
+  g.xsum = w.hsum;
+  g.ysum = nullptr;
+  if ((e = moe_expert_launch(g, stream)) != cudaSuccess) return e;
   const size_t n = (size_t)T * (H / 8);
   combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w.d, w.weights, w.route_rows,
                                                                    static_cast<const uint16_t *>(residual), T, H, k,

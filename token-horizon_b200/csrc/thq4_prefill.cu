@@ -25,10 +25,9 @@
 //   - the activations are the B operand: x tiles of 256 (gate/up: 128)
 //     tokens x 64 k, loaded by a 2-D TMA with 128-byte swizzle (zero fill
 //     past m) into a shared-memory ring;
-//   - a second producer warp streams the raw slab-groups into their own,
-//     deeper ring, released as soon as the dequant warps have read a stage
-//     (not when the MMA is done), so HBM requests stay in flight even when
-//     a tile has few tokens (the MoE expert tiles of 32);
+//   - a second producer warp streams the raw slab-groups into their own
+//     ring, released as soon as the dequant warps have read a stage (not
+//     when the MMA is done);
 //   - one thread issues tcgen05.mma.kind::f16 (bf16 in, f32 accumulate in
 //     TMEM), M = 128 output rows x N = 256 tokens per k-step of 16, and
 //     commits each stage back to the producer;
@@ -71,14 +70,6 @@ struct PfArgs {
   uint32_t *status;
   int m, n, ng;
   int m_tiles, tiles;
-  // grouped (MoE expert) mode when gtiles != nullptr: unit u is group tile
-  // gt = u / n_slabs (activation rows [gt*BT, gt*BT + live) of the gathered
-  // x) times slab u % n_slabs of expert gtiles[2 gt]; gtiles[2 gt + 1] =
-  // live rows; *gcount = group tiles in use (written on the device)
-  const uint32_t *gtiles;
-  const uint32_t *gcount;
-  uint64_t qw_stride[2], sb_stride[2];
-  int n_slabs, max_units;
 };
 
 // One unit of work: output slab nt for activation rows [row0, row_end).
@@ -90,27 +81,14 @@ struct PfUnit {
 template <int BT>
 __device__ __forceinline__ PfUnit pf_unit(const PfArgs &a, int u) {
   PfUnit x;
-  if (a.gtiles) {
-    const int gt = u / a.n_slabs;
-    const uint32_t e = a.gtiles[2 * gt];
-    x.nt = u - gt * a.n_slabs;
-    x.row0 = gt * BT;
-    x.row_end = x.row0 + (int)a.gtiles[2 * gt + 1];
+  const int mt = u % a.m_tiles;
+  x.nt = u / a.m_tiles;
+  x.row0 = mt * BT;
+  x.row_end = a.m;
 #pragma unroll
-    for (int si = 0; si < 2; ++si) {
-      x.qw[si] = a.qw[si] ? a.qw[si] + e * a.qw_stride[si] : nullptr;
-      x.sb[si] = a.sb[si] ? a.sb[si] + e * a.sb_stride[si] : nullptr;
-    }
-  } else {
-    const int mt = u % a.m_tiles;
-    x.nt = u / a.m_tiles;
-    x.row0 = mt * BT;
-    x.row_end = a.m;
-#pragma unroll
-    for (int si = 0; si < 2; ++si) {
-      x.qw[si] = a.qw[si];
-      x.sb[si] = a.sb[si];
-    }
+  for (int si = 0; si < 2; ++si) {
+    x.qw[si] = a.qw[si];
+    x.sb[si] = a.sb[si];
   }
   return x;
 }
@@ -201,13 +179,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(
-          smem_addr(dst)),
-      "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
-      : "memory");
-}
 
 // Bounded wait that also gives up once another role has aborted the CTA.
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *status) {
@@ -283,7 +254,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   uint64_t *accf = rawempty + RW, *acce = accf + NB, *yfull = acce + NB, *ydone = yfull + 1;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sm + C::misc_off);
   volatile int *abort = reinterpret_cast<volatile int *>(sm + C::misc_off + 4);
-  int *units_sm = reinterpret_cast<int *>(sm + C::misc_off + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -303,8 +273,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     mbar_init(yfull, kEpiWarps);
     mbar_init(ydone, kEpiWarps);
     *abort = 0;
-    // units of work: the plain GEMM's tiles, or the group tiles in use
-    units_sm[0] = a.gtiles ? min(a.max_units, (int)*a.gcount * a.n_slabs) : a.tiles;
   }
   if (warp == kWarpMma) {  // all of TMEM (one CTA per SM)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(smem_addr(tmem_holder)));
@@ -315,7 +283,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int units = units_sm[0];
+  const int units = a.tiles;
 
   if (warp == kWarpProd) {
     // ---- x producer: TMA tiles of the activations ------------------------------
@@ -576,6 +544,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return encode;
 }
 
+}  // namespace
+
 // x [rows][k] bf16 as a 2-D tensor (k innermost), 64 x box_rows boxes,
 // 128-byte swizzle
 cudaError_t make_xmap(const void *x, int k, int rows, int box_rows, CUtensorMap *map) {
@@ -590,6 +560,8 @@ cudaError_t make_xmap(const void *x, int k, int rows, int box_rows, CUtensorMap 
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return cr == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
+
+namespace {
 
 template <int NS, int BT, int S, int RW, int NB>
 cudaError_t launch_cfg(const CUtensorMap &map, const PfArgs &a, int grid, bool f16, bool y_f32, cudaStream_t stream) {
@@ -646,37 +618,6 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
   if (gate_up) return launch_cfg<2, 128, 4, 4, 1>(map, a, grid, f16, y_f32, stream);
   if (bt == 128) return launch_cfg<1, 128, 8, 8, 2>(map, a, grid, f16, y_f32, stream);
   return launch_cfg<1, 256, 4, 4, 1>(map, a, grid, f16, y_f32, stream);
-}
-
-cudaError_t grouped_launch(const GroupedGemm &g, cudaStream_t stream) {
-  CUtensorMap map;
-  cudaError_t e = make_xmap(g.x, g.w0->in, g.max_tiles * kMoeTileRows, kMoeTileRows, &map);
-  if (e != cudaSuccess) return e;
-  const bool gate_up = g.w1 != nullptr;
-  PfArgs a{};
-  a.qw[0] = static_cast<const uint8_t *>(g.w0->qw);
-  a.sb[0] = static_cast<const uint8_t *>(g.w0->sb);
-  a.qw[1] = gate_up ? static_cast<const uint8_t *>(g.w1->qw) : nullptr;
-  a.sb[1] = gate_up ? static_cast<const uint8_t *>(g.w1->sb) : nullptr;
-  a.qw_stride[0] = g.w0->qw_stride;
-  a.sb_stride[0] = g.w0->sb_stride;
-  a.qw_stride[1] = gate_up ? g.w1->qw_stride : 0;
-  a.sb_stride[1] = gate_up ? g.w1->sb_stride : 0;
-  a.y = g.y;
-  a.status = status_word();
-  a.m = g.max_tiles * kMoeTileRows;
-  a.n = g.w0->out;
-  a.ng = g.w0->in / kBK;
-  a.gtiles = g.tiles;
-  a.gcount = g.count;
-  a.n_slabs = row_slabs(g.w0->out);
-  const long long units = (long long)g.max_tiles * a.n_slabs;
-  if (units >= (1ll << 31)) return cudaErrorInvalidValue;
-  a.max_units = (int)units;
-  const int grid = (int)std::min<long long>(units, device_sm_count());
-  const bool f16 = g.w0->sb_dtype == THQ4_F16;
-  if (gate_up) return launch_cfg<2, kMoeTileRows, 6, 20, 2>(map, a, grid, f16, false, stream);
-  return launch_cfg<1, kMoeTileRows, 6, 36, 2>(map, a, grid, f16, false, stream);
 }
 
 }  // namespace thq4
