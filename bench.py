@@ -35,6 +35,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import datetime as _dt
+import gc
 import json
 import os
 import statistics
@@ -350,8 +351,17 @@ def run_thq4(args):
         torch.cuda.empty_cache()
         moe = bench_moe(torch, thq4, synth, dev, hbm_peak)
 
-    # free graphs holding NCCL work before the process group goes away
+    # Release the graphs (they hold NCCL work) before the process group goes
+    # away, or its teardown waits for good: reset them and drop every
+    # reference, the bound `replay` methods included.
+    cuda_graph_used = graph is not None
+    torch.cuda.synchronize()
+    for gr in (graph, g2):
+        if gr is not None:
+            gr.reset()
+    run = run_gu = None
     graph = g2 = None
+    gc.collect()
     torch.cuda.synchronize()
 
     cpu = None
@@ -380,7 +390,7 @@ def run_thq4(args):
                 "l2": f"inputs larger than L2: {total_bytes / 1e9:.2f} GB of weights per step "
                       f"({rank_bytes / 1e9:.2f} GB per GPU), no flush",
                 "parallelism": f"column-shard x{world}" + (" + NCCL all-gather per projection" if world > 1 else ""),
-                "cuda_graph": graph is not None or not args.no_graph,
+                "cuda_graph": cuda_graph_used,
             },
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue)",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
