@@ -66,6 +66,9 @@ def parse():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--skip-prefill", action="store_true")
+    p.add_argument("--nccl-gather", action="store_true",
+                   help="N > 1: gather each projection's output with NCCL all-gather (the baseline) instead of "
+                        "the GEMV epilogue's NVLink stores")
     return p.parse_args()
 
 
@@ -217,7 +220,38 @@ def run_thq4(args):
     def stream():
         return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
+    # N > 1: each projection's epilogue stores its rows into every rank's full
+    # vector over NVLink (IPC-mapped buffers) and raises this rank's flag on
+    # every peer; the next projection waits for the peers' flags before it
+    # reads x.  No collective runs in the step.
+    peer = None
+    if world > 1 and not args.nccl_gather:
+        from thq4.shard import PeerGroup
+
+        peer = PeerGroup((3 * HIDDEN + INTER) * 2 + 4 * 256, dev)
+        off_q, off_o = peer.buffer(HIDDEN * 2), peer.buffer(HIDDEN * 2)
+        off_h, off_y = peer.buffer(INTER * 2), peer.buffer(HIDDEN * 2)
+        g_qkv = peer.gather(off_q, qn, q0, HIDDEN, wait=True)
+        g_o = peer.gather(off_o, qn, q0, HIDDEN, wait=True)
+        g_gu = peer.gather(off_h, inn, i0, INTER, wait=True)
+        g_dn = peer.gather(off_y, qn, q0, HIDDEN, wait=True)
+        V = lambda off: ctypes.c_void_p(peer.ptr(off))  # noqa: E731
+
+    def step_peer():
+        s = stream()
+        for (qkv, o, gate, up, down) in layers:
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, P(x_in), BF, 1, P(t_qkv), P(ws), ws_bytes,
+                                            ctypes.byref(g_qkv), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, V(off_q), BF, 1, P(t_o), P(ws), ws_bytes,
+                                            ctypes.byref(g_o), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(off_o), BF, 1, P(t_h),
+                                            P(ws), ws_bytes, ctypes.byref(g_gu), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, V(off_h), BF, 1, P(t_d), P(ws), ws_bytes,
+                                            ctypes.byref(g_dn), s))
+
     def step():
+        if peer is not None:
+            return step_peer()
         s = stream()
         for (qkv, o, gate, up, down) in layers:
             thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
@@ -301,7 +335,10 @@ def run_thq4(args):
     def e2e_body():
         x_in.copy_(x_host, non_blocking=True)
         run()
-        y_host.copy_(y_out, non_blocking=True)
+        if peer is not None:
+            thq4.check(lib.thq4_copy(P(y_host), V(off_y), HIDDEN * 2, stream()))
+        else:
+            y_host.copy_(y_out, non_blocking=True)
 
     for _ in range(3):
         e2e_body()
@@ -363,6 +400,8 @@ def run_thq4(args):
     graph = g2 = None
     gc.collect()
     torch.cuda.synchronize()
+    if peer is not None:
+        peer.close()
 
     cpu = None
     if rank == 0 and world == 1:
@@ -389,7 +428,9 @@ def run_thq4(args):
                 "intermediate": INTER, "group": 64, "scale_dtype": "f16",
                 "l2": f"inputs larger than L2: {total_bytes / 1e9:.2f} GB of weights per step "
                       f"({rank_bytes / 1e9:.2f} GB per GPU), no flush",
-                "parallelism": f"column-shard x{world}" + (" + NCCL all-gather per projection" if world > 1 else ""),
+                "parallelism": f"column-shard x{world}" + (
+                    "" if world == 1 else " + NCCL all-gather per projection" if args.nccl_gather else
+                    ", outputs gathered by the GEMV epilogue (NVLink stores to IPC-mapped buffers + flags)"),
                 "cuda_graph": cuda_graph_used,
             },
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue)",

@@ -225,6 +225,51 @@ thq4_status thq4_moe(const void *x, const void *residual, const void *logits, in
                      const thq4_experts *down, void *y, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ---- multi-GPU column shards --------------------------------------------
+ * The reference engine is single-device; these entry points are the sharded
+ * extension.  Each rank (one process per GPU) holds a contiguous range of a
+ * projection's output rows; instead of an all-gather after the projection,
+ * the GEMV's epilogue stores its rows straight into every rank's copy of the
+ * full vector (NVLink stores through IPC mappings), and the grid's last CTA
+ * then writes this rank's completed-gather count into its slot of every
+ * peer's flag words (system-scope release).  A projection whose x is such a
+ * full vector waits (wait = 1, before it reads x; bounded, kStatusTimeout
+ * bit 2 of thq4_device_status) until every peer's flag has reached this
+ * rank's own count.  Every rank must make the same sequence of gathered
+ * calls.  The flag and count words live in memory every rank maps
+ * (thq4_ipc_alloc / thq4_ipc_open) and start at 0. */
+typedef struct thq4_peer_gather {
+  int32_t world;           /* ranks, 1 .. 8 */
+  int32_t rank;
+  int32_t rows;            /* the first `rows` outputs of the call are gathered ... */
+  int32_t offset;          /* ... to full[t * stride + offset + row] on every rank */
+  int32_t stride;          /* full-vector length per token */
+  int32_t wait;            /* 1: wait for the peers' gathers before reading x */
+  void *const *dst;        /* device array [world]: rank r's full vector (bf16), as mapped here */
+  uint32_t *const *flags;  /* device array [world]: rank r's flag words (u32 [world]), as mapped here */
+  uint32_t *count;         /* this rank's completed-gather count (one device word) */
+  uint32_t *arrive;        /* this rank's CTA arrival counter (one device word, left at 0) */
+} thq4_peer_gather;
+
+/* thq4_linear (up == NULL) or thq4_gate_up with the all-gather fused in; y is
+ * bf16 [m][out] (the local rows), m <= 8 for bf16 x (4 for f32 x). */
+thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const void *x, int x_dtype, int m,
+                             void *y, void *workspace, size_t workspace_bytes, const thq4_peer_gather *g,
+                             void *stream);
+/* On `stream`, waits until every peer has completed as many gathers as this
+ * rank (for a gathered vector read by something other than thq4_linear_peer). */
+thq4_status thq4_peer_wait(const thq4_peer_gather *g, void *stream);
+
+#define THQ4_IPC_HANDLE_BYTES 64
+/* Device memory another process of this node can map: cudaMalloc'd, zeroed,
+ * with its IPC handle (THQ4_IPC_HANDLE_BYTES bytes) written to `handle`. */
+thq4_status thq4_ipc_alloc(size_t bytes, void **ptr, void *handle);
+thq4_status thq4_ipc_open(const void *handle, void **ptr);
+thq4_status thq4_ipc_close(void *ptr);
+thq4_status thq4_ipc_free(void *ptr);
+/* Stream-ordered copy between any two addresses (cudaMemcpyAsync, default kind). */
+thq4_status thq4_copy(void *dst, const void *src, size_t bytes, void *stream);
+
 /* ---- testing hooks -------------------------------------------------------
  * Forces the decode/verify kernel's launch shape for every later call in this
  * process: slab-groups per streamed stage (4 or 8), stages in the

@@ -1,0 +1,114 @@
+"""Column shards over two GPUs with the all-gather fused into the projection:
+two ranks (one process per GPU) each own half the rows of two chained
+projections; the first gathers its output into both ranks' full vectors over
+NVLink, the second reads that vector (after waiting for the peer's flag) and
+gathers again.  Both ranks' full outputs must match the CPU oracle's
+unsharded chain.  Skipped with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, ret):
+    import ctypes
+    import datetime
+
+    import torch.distributed as dist
+
+    import q4oracle as O
+    import thq4
+    from helpers import dev
+    from thq4.shard import PeerGroup, shard_rows
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    d = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=d,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        n1, k1, n2 = 1024, 768, 512  # y1 = W1 x (1024 x 768), y2 = W2 y1 (512 x 1024)
+        w1q, w1s = O.rand_qlin(n1, k1, 31)
+        w2q, w2s = O.rand_qlin(n2, n1, 32)
+        x = O.rand_x(k1, 33)
+        b1, r1 = shard_rows(n1, world, rank)
+        b2, r2 = shard_rows(n2, world, rank)
+        q1 = thq4.QLin(dev(w1q[b1:b1 + r1]).to(d), dev(w1s[b1:b1 + r1]).to(d), r1, k1, 64).tiled()
+        q2 = thq4.QLin(dev(w2q[b2:b2 + r2]).to(d), dev(w2s[b2:b2 + r2]).to(d), r2, n1, 64).tiled()
+        L = thq4.lib()
+        grp = PeerGroup((n1 + n2) * 2 + 512, d)
+        o1, o2 = grp.buffer(n1 * 2), grp.buffer(n2 * 2)
+        g1 = grp.gather(o1, r1, b1, n1, wait=True)
+        g2 = grp.gather(o2, r2, b2, n2, wait=True)
+        ws = thq4.qlin.workspace(q1.packed.desc, d)
+        ws2 = torch.zeros_like(ws)
+        xt = dev(x.reshape(1, k1)).to(d)
+        y1 = torch.empty((1, r1), dtype=torch.bfloat16, device=d)
+        y2 = torch.empty((1, r2), dtype=torch.bfloat16, device=d)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):  # the flags count up across repeated chains
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q1.packed.desc), None, P(xt), thq4.BF16, 1, P(y1), P(ws),
+                                          ws.numel(), ctypes.byref(g1), s))
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q2.packed.desc), None, ctypes.c_void_p(grp.ptr(o1)),
+                                          thq4.BF16, 1, P(y2), P(ws2), ws2.numel(), ctypes.byref(g2), s))
+        thq4.check(L.thq4_peer_wait(ctypes.byref(g2), s))  # the peer's last slice has landed
+        full1 = torch.empty((1, n1), dtype=torch.bfloat16, device=d)
+        full2 = torch.empty((1, n2), dtype=torch.bfloat16, device=d)
+        thq4.check(L.thq4_copy(P(full1), ctypes.c_void_p(grp.ptr(o1)), n1 * 2, s))
+        thq4.check(L.thq4_copy(P(full2), ctypes.c_void_p(grp.ptr(o2)), n2 * 2, s))
+        torch.cuda.synchronize()
+        st = ctypes.c_uint32()
+        thq4.check(L.thq4_device_status(ctypes.byref(st), None))
+        out = (full1.float().cpu().numpy().ravel(), full2.float().cpu().numpy().ravel(), int(st.value))
+        grp.close()
+        ret.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_chain_matches_oracle():
+    import torch.multiprocessing as mp
+
+    import q4oracle as O
+    from helpers import assert_close_ref
+
+    paths = [HERE, ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "token-horizon_b200")]
+    os.environ["PYTHONPATH"] = os.pathsep.join(paths + [os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(ret.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    n1, k1, n2 = 1024, 768, 512
+    w1q, w1s = O.rand_qlin(n1, k1, 31)
+    w2q, w2s = O.rand_qlin(n2, n1, 32)
+    x = O.bf16_to_f32(O.rand_x(k1, 33))
+    y1 = O.linear_group(w1q, w1s, O.SB_BF16, x.reshape(1, k1))
+    y1b = O.bf16_to_f32(O.f32_to_bf16(y1))
+    y2 = O.linear_group(w2q, w2s, O.SB_BF16, y1b)
+    for rank in range(2):
+        f1, f2, status = got[rank]
+        assert status == 0, f"rank {rank}: device status {status:#x}"
+        assert_close_ref(f"rank {rank} gathered y1", f1, y1[0])
+        assert_close_ref(f"rank {rank} gathered y2", f2, y2[0])
+    assert np.array_equal(got[0][0], got[1][0]) and np.array_equal(got[0][1], got[1][1]), "ranks disagree"

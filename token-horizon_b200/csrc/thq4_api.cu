@@ -325,6 +325,105 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const v
   return THQ4_OK;
 }
 
+namespace {
+thq4_status check_peer(const thq4_peer_gather *g, const char *who) {
+  const std::string pre = std::string(who) + ": ";
+  if (!g) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "peer gather is NULL");
+  if (g->world < 1 || g->world > 8 || g->rank < 0 || g->rank >= g->world)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "need 1 <= world <= 8 and 0 <= rank < world (world " +
+                                                    std::to_string(g->world) + ", rank " + std::to_string(g->rank) + ")");
+  if (!g->dst || !g->flags || !g->count || !g->arrive)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "dst, flags, count and arrive must be device pointers");
+  if (g->wait != 0 && g->wait != 1) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "wait must be 0 or 1");
+  return THQ4_OK;
+}
+}  // namespace
+
+thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const void *x, int x_dtype, int m, void *y,
+                             void *workspace, size_t workspace_bytes, const thq4_peer_gather *g, void *stream) {
+  const char *who = "thq4_linear_peer";
+  thq4_status s = check_weight(w, who);
+  if (s != THQ4_OK) return s;
+  if (up) {
+    if ((s = check_weight(up, who)) != THQ4_OK) return s;
+    if (w->out != up->out || w->in != up->in || w->sb_dtype != up->sb_dtype)
+      return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: gate and up halves differ in shape or dtype");
+  }
+  if ((s = check_io(x, x_dtype, m, y, THQ4_BF16, who)) != THQ4_OK) return s;
+  if ((s = check_peer(g, who)) != THQ4_OK) return s;
+  const int per = x_dtype == THQ4_F32 ? 4 : 8;
+  if (m > per)
+    return set_error(THQ4_ERR_UNSUPPORTED, "thq4_linear_peer: m " + std::to_string(m) + " > " + std::to_string(per) +
+                                               " (one decode/verify launch per gathered call)");
+  if (g->rows < 0 || g->rows > w->out || g->offset < 0 || g->stride < 1 || (long long)g->offset + g->rows > g->stride)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: need 0 <= rows <= out and offset + rows <= stride");
+  if ((s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(w->out), who)) != THQ4_OK) return s;
+  PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
+                g->rows, g->offset, g->stride, g->wait};
+  const cudaError_t e = gemv_launch(*w, up, x, x_dtype == THQ4_F32, m, y, false, workspace,
+                                    static_cast<cudaStream_t>(stream), &pg);
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+thq4_status thq4_peer_wait(const thq4_peer_gather *g, void *stream) {
+  thq4_status s = check_peer(g, "thq4_peer_wait");
+  if (s != THQ4_OK) return s;
+  PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
+                g->rows, g->offset, g->stride, g->wait};
+  const cudaError_t e = peer_wait_launch(pg, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "thq4_peer_wait");
+  return THQ4_OK;
+}
+
+thq4_status thq4_ipc_alloc(size_t bytes, void **ptr, void *handle) {
+  if (!ptr || !handle || bytes == 0) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_ipc_alloc: bad arguments");
+  static_assert(sizeof(cudaIpcMemHandle_t) == THQ4_IPC_HANDLE_BYTES, "IPC handle size");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_error(e, "thq4_ipc_alloc");
+  if ((e = cudaMemset(p, 0, bytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_error(e, "thq4_ipc_alloc");
+  }
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_error(e, "thq4_ipc_alloc");
+  }
+  std::memcpy(handle, &h, sizeof h);
+  *ptr = p;
+  return THQ4_OK;
+}
+
+thq4_status thq4_ipc_open(const void *handle, void **ptr) {
+  if (!ptr || !handle) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_error(e, "thq4_ipc_open");
+  return THQ4_OK;
+}
+
+thq4_status thq4_ipc_close(void *ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_error(e, "thq4_ipc_close");
+  return THQ4_OK;
+}
+
+thq4_status thq4_ipc_free(void *ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_error(e, "thq4_ipc_free");
+  return THQ4_OK;
+}
+
+thq4_status thq4_copy(void *dst, const void *src, size_t bytes, void *stream) {
+  if ((!dst || !src) && bytes) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_copy: NULL pointer");
+  const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "thq4_copy");
+  return THQ4_OK;
+}
+
 thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream) {
   thq4_status s = check_weight(w, "thq4_dequant");
   if (s != THQ4_OK) return s;

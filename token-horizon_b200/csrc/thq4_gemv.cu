@@ -93,6 +93,13 @@ struct GemvArgs {
   int xf32, yf32;
   int stages;          // ring stages
   int xcap;            // activation groups staged per CTA
+  // fused all-gather of column shards (g_dst null: none): the first g_rows
+  // outputs also go to full[t * g_stride + g_off + row] on every rank, and
+  // the grid's last CTA raises this rank's flag on every peer
+  uint16_t *const *g_dst;
+  uint32_t *const *g_flags;
+  uint32_t *g_count, *g_arrive;
+  int g_world, g_rank, g_rows, g_off, g_stride, g_wait;
 };
 
 // columns with per-group metadata: P rounded up to even (lanes own pairs)
@@ -250,12 +257,52 @@ __device__ __forceinline__ void store_tile(const GemvArgs &a, int rt, int lane, 
       }
       if (t >= a.m) continue;
       if constexpr (GATE_UP) v = silu_mul(v, u);
-      if (a.yf32)
+      if (a.yf32) {
         static_cast<float *>(a.y)[(size_t)t * a.out + row] = v;
-      else
-        static_cast<uint16_t *>(a.y)[(size_t)t * a.out + row] = f32_to_bf16_bits(v);
+      } else {
+        const uint16_t bits = f32_to_bf16_bits(v);
+        static_cast<uint16_t *>(a.y)[(size_t)t * a.out + row] = bits;
+        if (a.g_dst && row < a.g_rows)  // the shard's slice of the full vector, on every rank (NVLink stores)
+          for (int rk = 0; rk < a.g_world; ++rk) a.g_dst[rk][(size_t)t * a.g_stride + a.g_off + row] = bits;
+      }
     }
   }
+}
+
+// Until every peer has completed as many gathers as this rank (its own
+// count is final: the previous projection on this stream has completed), or
+// kWaitLimitNs, after which the status word says kStatusTimeout.
+__device__ void peer_wait(uint32_t *const *flags, const uint32_t *count, int world, int rank, uint32_t *status) {
+  const uint32_t target = *reinterpret_cast<const volatile uint32_t *>(count);
+  const uint32_t *mine = flags[rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int rk = 0; rk < world; ++rk) {
+    if (rk == rank) continue;
+    while ((int32_t)(ld_acquire_sys(mine + rk) - target) < 0) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        raise_status(status, kStatusTimeout);
+        return;
+      }
+    }
+  }
+}
+// After every consumer warp's stores: the grid's last CTA bumps this rank's
+// gather count and writes it into this rank's slot of every peer's flags.
+__device__ void peer_signal(const GemvArgs &a) {
+  consumer_sync();
+  if (threadIdx.x != 0) return;
+  fence_acq_rel_sys();  // this CTA's stores, local and remote, before its arrival
+  if (atom_add_acq_rel(a.g_arrive, 1u) + 1u != gridDim.x) return;
+  *a.g_arrive = 0;
+  const uint32_t c = *a.g_count + 1u;  // only the last CTA of each launch touches it
+  *a.g_count = c;
+  fence_acq_rel_sys();  // every CTA's stores (acquired through the counter) before the flags
+  for (int rk = 0; rk < a.g_world; ++rk)
+    if (rk != a.g_rank) st_release_sys(a.g_flags[rk] + a.g_rank, c);
+}
+
+__global__ void peer_wait_kernel(uint32_t *const *flags, const uint32_t *count, int world, int rank, uint32_t *status) {
+  if (threadIdx.x == 0) peer_wait(flags, count, world, rank, status);
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
@@ -326,6 +373,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
   const int tile = warp;
   pdl_wait();
+  if (a.g_dst && a.g_wait) {  // x holds the peers' slices: wait until they have landed
+    if (threadIdx.x == 0) peer_wait(a.g_flags, a.g_count, a.g_world, a.g_rank, a.status);
+    consumer_sync();
+  }
   const int sl0 = C0 / a.cps, cg0 = C0 - sl0 * a.cps;
   const int gs = cg0 * CB;
   const int xcnt =
@@ -531,32 +582,34 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     if (!aborted) publish(finished_any ? 1 : 0, y);
     last_slab = sl;
   }
-  if (aborted || (first_slab < 0 && last_slab < 0)) return;
-  // the lanes' stores above happen before lane 0's release fence; one fence
-  // covers both increments, which are then in flight together
-  __syncwarp();
-  uint32_t done = 0;  // bit 0: first slab complete, bit 1: last slab complete
-  if (lane == 0) {
-    uint32_t o0 = 0, o1 = 0;
-    int clo, chi;
-    fence_acq_rel_gpu();
-    if (first_slab >= 0) o0 = atom_add_relaxed(&a.count[(size_t)first_slab * kSlabTiles + tile], 1u);
-    if (last_slab >= 0) o1 = atom_add_relaxed(&a.count[(size_t)last_slab * kSlabTiles + tile], 1u);
-    if (first_slab >= 0) {
-      contributors(first_slab, clo, chi);
-      if (o0 + 1 == (uint32_t)(chi - clo + 1)) done |= 1u;
+  if (!aborted && (first_slab >= 0 || last_slab >= 0)) {
+    // the lanes' stores above happen before lane 0's release fence; one
+    // fence covers both increments, which are then in flight together
+    __syncwarp();
+    uint32_t done = 0;  // bit 0: first slab complete, bit 1: last slab complete
+    if (lane == 0) {
+      uint32_t o0 = 0, o1 = 0;
+      int clo, chi;
+      fence_acq_rel_gpu();
+      if (first_slab >= 0) o0 = atom_add_relaxed(&a.count[(size_t)first_slab * kSlabTiles + tile], 1u);
+      if (last_slab >= 0) o1 = atom_add_relaxed(&a.count[(size_t)last_slab * kSlabTiles + tile], 1u);
+      if (first_slab >= 0) {
+        contributors(first_slab, clo, chi);
+        if (o0 + 1 == (uint32_t)(chi - clo + 1)) done |= 1u;
+      }
+      if (last_slab >= 0) {
+        contributors(last_slab, clo, chi);
+        if (o1 + 1 == (uint32_t)(chi - clo + 1)) done |= 2u;
+      }
+      if (done) fence_acq_rel_gpu();  // acquire: every other part is visible
     }
-    if (last_slab >= 0) {
-      contributors(last_slab, clo, chi);
-      if (o1 + 1 == (uint32_t)(chi - clo + 1)) done |= 2u;
-    }
-    if (done) fence_acq_rel_gpu();  // acquire: every other part is visible
+    done = __shfl_sync(0xffffffffu, done, 0);
+    // lane 0's acquire happens before the other lanes' loads
+    __syncwarp();
+    if (done & 1u) combine(first_slab);
+    if (done & 2u) combine(last_slab);
   }
-  done = __shfl_sync(0xffffffffu, done, 0);
-  // lane 0's acquire happens before the other lanes' loads
-  __syncwarp();
-  if (done & 1u) combine(first_slab);
-  if (done & 2u) combine(last_slab);
+  if (a.g_dst) peer_signal(a);  // every consumer warp gets here
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
@@ -667,10 +720,12 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
 }
 
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32, int m, void *y,
-                        bool y_f32, void *workspace, cudaStream_t stream) {
+                        bool y_f32, void *workspace, cudaStream_t stream, const PeerGather *peer) {
   const bool gate_up = w1 != nullptr;
   const GemvPlan p = gemv_plan(w0.out, w0.in, m, x_f32, gate_up);
   if (!p.ok) return cudaErrorInvalidConfiguration;
+  // a gathered call is one launch (one signal per call)
+  if (peer && (m > p.tokens_per_pass || y_f32)) return cudaErrorInvalidValue;
   const int xb = x_f32 ? 4 : 2, yb = y_f32 ? 4 : 2;
   const size_t part_bytes =
       gemv_workspace_bytes(w0.out) - ((size_t)row_slabs(w0.out) * kSlabTiles * 4 + 255) / 256 * 256;
@@ -699,6 +754,18 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     a.yf32 = y_f32 ? 1 : 0;
     a.stages = p.stages;
     a.xcap = p.xcap;
+    if (peer) {
+      a.g_dst = peer->dst;
+      a.g_flags = peer->flags;
+      a.g_count = peer->count;
+      a.g_arrive = peer->arrive;
+      a.g_world = peer->world;
+      a.g_rank = peer->rank;
+      a.g_rows = peer->rows;
+      a.g_off = peer->offset;
+      a.g_stride = peer->stride;
+      a.g_wait = peer->wait;
+    }
     // a last pass with fewer tokens fits in the footprint planned for more
     const size_t smem = gemv_smem(p.stages, p.ch, gate_up, p.xcap, a.P);
     const int gw = window_groups(a.P);
@@ -707,6 +774,11 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t peer_wait_launch(const PeerGather &g, cudaStream_t stream) {
+  peer_wait_kernel<<<1, 32, 0, stream>>>(g.flags, g.count, g.world, g.rank, status_word());
+  return cudaGetLastError();
 }
 
 }  // namespace thq4

@@ -67,8 +67,20 @@ size_t gemv_workspace_bytes(int rows);
 // Programmatic dependent launch for the GEMV (THQ4_PDL=0 disables; read once).
 bool gemv_pdl_enabled();
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
+// The all-gather of column shards fused into the projection (thq4_peer_gather).
+struct PeerGather {
+  uint16_t *const *dst;     // device array [world]: each rank's full-vector buffer
+  uint32_t *const *flags;   // device array [world]: each rank's flag words [world]
+  uint32_t *count, *arrive;
+  int world, rank, rows, offset, stride, wait;
+};
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
-                        int m, void *y, bool y_f32, void *workspace, cudaStream_t stream);
+                        int m, void *y, bool y_f32, void *workspace, cudaStream_t stream,
+                        const PeerGather *peer = nullptr);
+// Waits (one thread, bounded) until every peer has completed as many gathers
+// as this rank, then returns; used where a gathered vector is consumed by
+// something other than the next projection.
+cudaError_t peer_wait_launch(const PeerGather &g, cudaStream_t stream);
 
 // ---- prefill GEMM (tcgen05) -------------------------------------------------
 // The tensor-core path serves m > 8 tokens of bf16 x.

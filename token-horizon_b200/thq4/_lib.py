@@ -52,6 +52,14 @@ class thq4_experts(ctypes.Structure):
                 ("sb_stride", ctypes.c_uint64)]
 
 
+class thq4_peer_gather(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("rows", ctypes.c_int32),
+                ("offset", ctypes.c_int32), ("stride", ctypes.c_int32), ("wait", ctypes.c_int32),
+                ("dst", c_void_p), ("flags", c_void_p), ("count", c_void_p), ("arrive", c_void_p)]
+
+
+IPC_HANDLE_BYTES = 64
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/thq4.h declares
@@ -76,6 +84,14 @@ SIGNATURES = {
     "thq4_moe_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "thq4_moe": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(thq4_experts),
                          POINTER(thq4_experts), POINTER(thq4_experts), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "thq4_linear_peer": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
+                                 c_void_p, c_size_t, POINTER(thq4_peer_gather), c_void_p]),
+    "thq4_peer_wait": (c_int, [POINTER(thq4_peer_gather), c_void_p]),
+    "thq4_ipc_alloc": (c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "thq4_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "thq4_ipc_close": (c_int, [c_void_p]),
+    "thq4_ipc_free": (c_int, [c_void_p]),
+    "thq4_copy": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
 }
 

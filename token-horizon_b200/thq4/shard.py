@@ -7,12 +7,18 @@ The fused [gate | up] weight shards both halves with the same row range, so
 the SwiGLU epilogue stays local.  Shards are multiples of 16 rows (one MMA
 tile) and equal in size, the layout `all_gather_into_tensor` concatenates.
 
+`PeerGroup` sets up the fused alternative to that all-gather
+(`thq4_linear_peer`): one region of device memory per rank, mapped by every
+other rank through CUDA IPC, holding the gather flags and the full-vector
+buffers that the projections write into directly over NVLink.
+
 The reference engine is single-device; this module is the host logic of the
 multi-GPU extension and carries no arithmetic of its own.
 """
 from __future__ import annotations
 
-from typing import Optional
+import ctypes
+from typing import List, Optional
 
 import torch
 
@@ -43,3 +49,88 @@ def gather_rows(local: torch.Tensor, full: Optional[torch.Tensor] = None, group=
         full.copy_(out)
         return full
     return out
+
+
+class PeerGroup:
+    """One IPC-mapped region per rank: [0, 256) control words (flags[world]
+    u32 at 0, the gather count at 64, the CTA arrival counter at 128), then
+    full-vector buffers placed by `buffer` at the same offset on every rank
+    (every rank makes the same calls in the same order)."""
+
+    CONTROL = 256
+
+    def __init__(self, nbytes: int, device: torch.device, group=None):
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._lib = _lib.lib()
+        self._L = _lib
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device
+        self.size = self.CONTROL + nbytes
+        self._next = self.CONTROL
+        base, handle = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        _lib.check(self._lib.thq4_ipc_alloc(self.size, ctypes.byref(base), handle))
+        self.local = base.value
+        handles: List[bytes] = [handle.raw]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases: List[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(self.local)
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(self._lib.thq4_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p)))
+            self.bases.append(p.value)
+        self._flags = self._ptr_array([b for b in self.bases])
+        self.count = self.local + 64
+        self.arrive = self.local + 128
+        self._keep = []
+
+    def _ptr_array(self, ptrs) -> torch.Tensor:
+        t = torch.tensor(list(ptrs), dtype=torch.int64, device=self.device)
+        return t
+
+    def buffer(self, nbytes: int) -> int:
+        """Offset of a new buffer of `nbytes` (256-byte aligned) in every rank's region."""
+        off = self._next
+        self._next = (off + nbytes + 255) // 256 * 256
+        if self._next > self.size:
+            raise ValueError(f"PeerGroup region of {self.size} bytes is full")
+        return off
+
+    def ptr(self, offset: int) -> int:
+        """This rank's address of the buffer at `offset`."""
+        return self.local + offset
+
+    def gather(self, offset: int, rows: int, at: int, stride: int, wait: bool):
+        """A thq4_peer_gather for a projection whose first `rows` outputs go to
+        full[t * stride + at + row] in the buffer at `offset` on every rank."""
+        dst = self._ptr_array([b + offset for b in self.bases])
+        self._keep.append(dst)
+        g = self._L.thq4_peer_gather()
+        g.world, g.rank, g.rows, g.offset, g.stride, g.wait = self.world, self.rank, rows, at, stride, int(wait)
+        g.dst, g.flags = dst.data_ptr(), self._flags.data_ptr()
+        g.count, g.arrive = self.count, self.arrive
+        return g
+
+    def close(self) -> None:
+        """Unmap the peers' regions, then free this rank's (after every rank
+        has unmapped it).  Collective."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for r, b in enumerate(self.bases):
+            if r != self.rank:
+                self._L.check(self._lib.thq4_ipc_close(ctypes.c_void_p(b)))
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self._L.check(self._lib.thq4_ipc_free(ctypes.c_void_p(self.local)))
+        self.bases, self._keep = [], []
