@@ -380,6 +380,11 @@ def run_thq4(args):
         pass
 
     prefill = moe = None
+    if world > 1 and not args.skip_prefill:
+        # every rank: the MoE layer with its experts sharded over the GPUs
+        layers = None
+        torch.cuda.empty_cache()
+        moe = bench_moe_sharded(torch, thq4, synth, dev, hbm_peak, world, rank, local)
     if rank == 0 and world == 1 and not args.skip_prefill:
         # the decode weights go first: these measurements have their own working sets
         layers = None
@@ -528,6 +533,59 @@ def bench_moe(torch, thq4, synth, dev, hbm_peak):
     return {"config": "T 256, H 2048, E 128, k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
             "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
             "kernel": "moe_gemv_kernel (grouped small-tile mma.sync experts) + routing / gather / combine"}
+
+
+def bench_moe_sharded(torch, thq4, synth, dev, hbm_peak, world, rank, local):
+    """BASELINE configs[4] with the experts split E/N per GPU: every rank
+    routes all 256 tokens (bit-identically), runs its experts' routes
+    (thq4_moe_partial, f32 partial) and one NCCL all-reduce sums the
+    partials; whole-job expert-weight GB/s and us per layer, max over ranks.
+    Two expert sets rotate."""
+    import torch.distributed as dist
+
+    from thq4.shard import expert_range, moe_sharded
+
+    T, H, I, E, k = 256, 2048, 768, 128, 8
+    e0, n = expert_range(E, world, rank)
+    sets = []
+    for s in range(2):
+        gu = [synth.normal_weight(2 * I, H, 10_000 * (s + 1) + e0 + e, dev) for e in range(n)]
+        gu_wq, gu_sb = torch.stack([a for a, _ in gu]), torch.stack([b for _, b in gu])
+        del gu
+        dn = [synth.normal_weight(H, I, 20_000 * (s + 1) + e0 + e, dev) for e in range(n)]
+        dn_wq, dn_sb = torch.stack([a for a, _ in dn]), torch.stack([b for _, b in dn])
+        del dn
+        sets.append((thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, 0, I),
+                     thq4.PackedExperts.from_mlx(gu_wq, gu_sb, thq4.F16, I, I),
+                     thq4.PackedExperts.from_mlx(dn_wq, dn_sb, thq4.F16)))
+        del gu_wq, gu_sb, dn_wq, dn_sb
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)  # the same activations and logits on every rank
+    x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn((T, E), device=dev, generator=g).to(torch.bfloat16)
+
+    def call():
+        for gt, up, dn in sets:
+            moe_sharded(x, logits, k, e0, gt, up, dn)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local])
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(10):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / (10 * len(sets))], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    nbytes = E * (2 * I * H + H * I) * Q4_BYTES_PER_WEIGHT
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"config": f"T 256, H 2048, E 128 ({n} per GPU), k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
+            "weight_gbs": round(gbs, 1), "frac": round(gbs / (hbm_peak * world), 4), "bytes": int(nbytes),
+            "kernel": "moe_gemv_kernel per expert shard + NCCL all-reduce of the f32 partials"}
 
 
 # ---------------------------------------------------------------------------

@@ -260,6 +260,19 @@ thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const 
  * rank (for a gathered vector read by something other than thq4_linear_peer). */
 thq4_status thq4_peer_wait(const thq4_peer_gather *g, void *stream);
 
+/* Expert-sharded MoE: this rank holds experts [e0, e1) of E (gate, up and
+ * down describe just those, e1 - e0 experts each).  Routing runs over all E
+ * experts, bit-identical on every rank given the same logits; only the
+ * routes to local experts are computed.  y_part f32 [T][H] = residual (if
+ * not NULL; pass it on one rank only) + the sum over each token's local
+ * routes, in slot order, of w * down(bf16(silu(bf16 g) * bf16 u)).  Summing
+ * y_part over the ranks (one all-reduce) and rounding once to bf16 gives the
+ * layer's output.  Workspace: thq4_moe_workspace_bytes(T, H, I, e1 - e0, k). */
+thq4_status thq4_moe_partial(const void *x, const void *residual, const void *logits, int T, int H, int I, int E,
+                             int k, int e0, int e1, const thq4_experts *gate, const thq4_experts *up,
+                             const thq4_experts *down, float *y_part, void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 #define THQ4_IPC_HANDLE_BYTES 64
 /* Device memory another process of this node can map: cudaMalloc'd, zeroed,
  * with its IPC handle (THQ4_IPC_HANDLE_BYTES bytes) written to `handle`. */

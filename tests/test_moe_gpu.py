@@ -2,6 +2,8 @@
 (Splash moe_metal_test.mm: routing order and softmax weights :362-398, the
 grouping round trip :330-360, and the per-expert tolerance 0.02 + 0.01|ref|
 :429-441).  The routing permutation must be bit-exact."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -127,3 +129,37 @@ def test_moe_rejects_bad_shapes():
         thq4.moe(x, logits, k, gate, down, down)  # up has the down shape
     with pytest.raises(thq4.Thq4Error, match="k <= min"):
         thq4.moe(x, logits, 3, gate, up, down)
+
+
+def test_expert_shards_sum_to_the_layer():
+    """Expert sharding (thq4_moe_partial): the whole expert range with the
+    residual rounds to the unsharded layer bit for bit; two halves summed in
+    f32 match the oracle within the expert tolerance; routes to the other
+    shard's experts are dropped without a bad-expert status."""
+    T, H, I, E, k = 96, 512, 256, 8, 2
+    gu_wq, gu_sb = _experts(E, 2 * I, H, O.SB_BF16, 300)
+    dn_wq, dn_sb = _experts(E, H, I, O.SB_BF16, 400)
+    rng = np.random.default_rng(17)
+    x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    res = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    logits = _logits(T, E, 18)
+
+    def packed(e0, e1):
+        return (thq4.PackedExperts.from_mlx(dev(gu_wq[e0:e1]), dev(gu_sb[e0:e1]), thq4.BF16, 0, I),
+                thq4.PackedExperts.from_mlx(dev(gu_wq[e0:e1]), dev(gu_sb[e0:e1]), thq4.BF16, I, I),
+                thq4.PackedExperts.from_mlx(dev(dn_wq[e0:e1]), dev(dn_sb[e0:e1]), thq4.BF16))
+
+    full = packed(0, E)
+    y = thq4.moe(dev(x), dev(logits), k, *full, residual=dev(res))
+    whole = thq4.moe_partial(dev(x), dev(logits), k, 0, *full, residual=dev(res))
+    assert torch.equal(whole.to(torch.bfloat16).view(torch.int16), y.view(torch.int16)), "full range != thq4_moe"
+    st = ctypes.c_uint32()
+    thq4.check(thq4.lib().thq4_device_status(ctypes.byref(st), None))
+    a = thq4.moe_partial(dev(x), dev(logits), k, 0, *packed(0, E // 2), residual=dev(res))
+    b = thq4.moe_partial(dev(x), dev(logits), k, E // 2, *packed(E // 2, E))
+    thq4.check(thq4.lib().thq4_device_status(ctypes.byref(st), None))
+    assert st.value == 0, f"status {st.value:#x}: dropped routes are not bad experts"
+    got = O.bf16_to_f32((a + b).to(torch.bfloat16).cpu().view(torch.int16).numpy().view(np.uint16))
+    ids, w = O.moe_select(logits, k)
+    want = O.moe_forward(x, res, ids, w, gu_wq, gu_sb, dn_wq, dn_sb, O.SB_BF16, I)[0]
+    _close("two expert shards", got, O.bf16_to_f32(want))

@@ -3,7 +3,9 @@ two ranks (one process per GPU) each own half the rows of two chained
 projections; the first gathers its output into both ranks' full vectors over
 NVLink, the second reads that vector (after waiting for the peer's flag) and
 gathers again.  Both ranks' full outputs must match the CPU oracle's
-unsharded chain.  Skipped with fewer than two GPUs."""
+unsharded chain.  The MoE layer with its experts split over the two ranks
+(each rank's f32 partial, one NCCL all-reduce) must match the oracle's
+layer.  Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -112,3 +114,73 @@ def test_two_gpu_chain_matches_oracle():
         assert_close_ref(f"rank {rank} gathered y1", f1, y1[0])
         assert_close_ref(f"rank {rank} gathered y2", f2, y2[0])
     assert np.array_equal(got[0][0], got[1][0]) and np.array_equal(got[0][1], got[1][1]), "ranks disagree"
+
+
+def _moe_rank(rank, world, port, ret):
+    import datetime
+
+    import torch.distributed as dist
+
+    import q4oracle as O
+    import thq4
+    from helpers import dev
+    from thq4.shard import expert_range, moe_sharded
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    d = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=d,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        T, H, I, E, k = 64, 256, 128, 8, 2
+        gu = [O.synthetic_weight(2 * I, H, 900 + e, O.SB_BF16) for e in range(E)]
+        dn = [O.synthetic_weight(H, I, 950 + e, O.SB_BF16) for e in range(E)]
+        gq, gs = np.stack([a for a, _ in gu]), np.stack([b for _, b in gu])
+        dq, ds = np.stack([a for a, _ in dn]), np.stack([b for _, b in dn])
+        e0, n = expert_range(E, world, rank)
+        gate = thq4.PackedExperts.from_mlx(dev(gq[e0:e0 + n]).to(d), dev(gs[e0:e0 + n]).to(d), thq4.BF16, 0, I)
+        up = thq4.PackedExperts.from_mlx(dev(gq[e0:e0 + n]).to(d), dev(gs[e0:e0 + n]).to(d), thq4.BF16, I, I)
+        down = thq4.PackedExperts.from_mlx(dev(dq[e0:e0 + n]).to(d), dev(ds[e0:e0 + n]).to(d), thq4.BF16)
+        rng = np.random.default_rng(3)
+        x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+        res = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+        lg = O.f32_to_bf16(rng.standard_normal((T, E)).astype(np.float32))
+        y = moe_sharded(dev(x).to(d), dev(lg).to(d), k, e0, gate, up, down, residual=dev(res).to(d))
+        torch.cuda.synchronize()
+        ret.put((rank, y.cpu().view(torch.int16).numpy().view(np.uint16)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_expert_shards_match_oracle():
+    import torch.multiprocessing as mp
+
+    import q4oracle as O
+
+    paths = [HERE, ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "token-horizon_b200")]
+    os.environ["PYTHONPATH"] = os.pathsep.join(paths + [os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_moe_rank, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(ret.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    T, H, I, E, k = 64, 256, 128, 8, 2
+    gu = [O.synthetic_weight(2 * I, H, 900 + e, O.SB_BF16) for e in range(E)]
+    dn = [O.synthetic_weight(H, I, 950 + e, O.SB_BF16) for e in range(E)]
+    gq, gs = np.stack([a for a, _ in gu]), np.stack([b for _, b in gu])
+    dq, ds = np.stack([a for a, _ in dn]), np.stack([b for _, b in dn])
+    rng = np.random.default_rng(3)
+    x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    res = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    lg = O.f32_to_bf16(rng.standard_normal((T, E)).astype(np.float32))
+    ids, w = O.moe_select(lg, k)
+    want = O.bf16_to_f32(O.moe_forward(x, res, ids, w, gq, gs, dq, ds, O.SB_BF16, I)[0]).astype(np.float64)
+    assert np.array_equal(got[0], got[1]), "ranks disagree after the all-reduce"
+    y = O.bf16_to_f32(got[0]).astype(np.float64)
+    assert np.all(np.abs(y - want) <= 0.02 + 0.01 * np.abs(want)), "sharded MoE differs from the oracle"

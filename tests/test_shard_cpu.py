@@ -72,3 +72,15 @@ def test_two_gloo_ranks_reassemble_y():
     x = O.bf16_to_f32(np.stack([O.rand_x(inp, 50 + t) for t in range(m)]))
     want = O.linear_group(wq, sb, O.SB_BF16, x).astype(np.float32)
     assert np.array_equal(got, want)
+
+
+def test_expert_ranges_partition_the_experts():
+    from thq4.shard import expert_range
+    for E, world in [(128, 2), (128, 8), (8, 4), (64, 1)]:
+        seen = np.zeros(E, dtype=np.int32)
+        for r in range(world):
+            e0, n = expert_range(E, world, r)
+            seen[e0:e0 + n] += 1
+        assert (seen == 1).all()
+    with pytest.raises(ValueError):
+        expert_range(10, 4, 0)

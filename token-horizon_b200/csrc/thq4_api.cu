@@ -522,6 +522,41 @@ thq4_status thq4_moe(const void *x, const void *residual, const void *logits, in
   return THQ4_OK;
 }
 
+thq4_status thq4_moe_partial(const void *x, const void *residual, const void *logits, int T, int H, int I, int E,
+                             int k, int e0, int e1, const thq4_experts *gate, const thq4_experts *up,
+                             const thq4_experts *down, float *y_part, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  const char *who = "thq4_moe_partial";
+  thq4_status s = check_route_args(T, E, k, who);
+  if (s != THQ4_OK) return s;
+  if (e0 < 0 || e1 <= e0 || e1 > E)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_partial: need 0 <= e0 < e1 <= E (e0 " + std::to_string(e0) +
+                                                    ", e1 " + std::to_string(e1) + ", E " + std::to_string(E) + ")");
+  if (H <= 0 || I <= 0 || H % kGroup || I % kGroup)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_partial: H and I must be positive multiples of 64");
+  const int El = e1 - e0;
+  if ((s = check_experts(gate, El, I, H, "gate", who)) != THQ4_OK) return s;
+  if ((s = check_experts(up, El, I, H, "up", who)) != THQ4_OK) return s;
+  if ((s = check_experts(down, El, H, I, "down", who)) != THQ4_OK) return s;
+  if (gate->sb_dtype != up->sb_dtype || gate->sb_dtype != down->sb_dtype)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_partial: gate, up and down differ in scale dtype");
+  if (!x || !y_part || !logits || !aligned(x, 16) || !aligned(y_part, 16) || !aligned(logits, 2) ||
+      (residual && !aligned(residual, 16)))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_moe_partial: x, y_part (and residual) must be 16-byte aligned, logits non-NULL");
+  const MoeWorkspace need = moe_workspace(T, H, I, El, k, nullptr);
+  if (!workspace || workspace_bytes < need.bytes || !aligned(workspace, 256))
+    return set_error(THQ4_ERR_WORKSPACE, "thq4_moe_partial: needs a 256-byte aligned workspace of " +
+                                             std::to_string(need.bytes) +
+                                             " bytes (thq4_moe_workspace_bytes with E = e1 - e0), got " +
+                                             std::to_string(workspace_bytes));
+  const MoeWorkspace w = moe_workspace(T, H, I, El, k, workspace);
+  cudaError_t e = moe_launch(x, residual, logits, T, H, I, E, k, *gate, *up, *down, y_part, w,
+                             static_cast<cudaStream_t>(stream), e0, e1, true);
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
   if (!(chunk == 0 || chunk == 4 || chunk == 8) || stages < 0 || stages == 1 || stages > 8 ||
       grid < 0 || grid > 2 * device_sm_count() || reserved != 0)

@@ -117,9 +117,10 @@ uint32_t moe_max_tiles(int T, int E, int k);
 // Shared memory of the grouping kernel for R routes and E experts.
 size_t moe_group_smem(int R, int E);
 // Select (top-k, softmax weights) and group (stable counting sort) on the device.
+// Experts [e0, e1) of E are grouped (e1 < 0: all); the tiles hold local ids.
 cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
                              uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
-                             cudaStream_t stream);
+                             cudaStream_t stream, int e0 = 0, int e1 = -1);
 // The MoE layer's scratch, carved from one caller buffer (nullptr: sizes only).
 struct MoeWorkspace {
   uint32_t *ids, *tiles, *grouped, *route_rows, *ntiles;
@@ -129,9 +130,10 @@ struct MoeWorkspace {
   int max_tiles;
 };
 MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base);
+// The layer (y bf16) or, for an expert shard [e0, e1), its f32 partial.
 cudaError_t moe_launch(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
                        const thq4_experts &gate, const thq4_experts &up, const thq4_experts &down, void *y,
-                       const MoeWorkspace &w, cudaStream_t stream);
+                       const MoeWorkspace &w, cudaStream_t stream, int e0 = 0, int e1 = -1, bool y_f32 = false);
 
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,

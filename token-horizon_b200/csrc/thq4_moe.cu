@@ -89,8 +89,10 @@ __host__ __device__ inline int group_warps(int E) { return E <= 512 ? 32 : 16; }
 //      earlier ones of its expert (its rank among the 32 plus the running
 //      count), so routes stay in ascending order within an expert.
 // Routes whose expert id is out of range are dropped (combine skips them).
-__global__ void group_kernel(const uint32_t *ids, int R, int E, int max_tiles, uint32_t *tiles, uint32_t *grouped,
-                             uint32_t *route_rows, uint32_t *ntiles, uint32_t *status) {
+// Experts [e0, e0 + E) of E_all are grouped (local ids e - e0); routes to
+// other valid experts are dropped silently (another rank computes them).
+__global__ void group_kernel(const uint32_t *ids, int R, int E_all, int e0, int E, int max_tiles, uint32_t *tiles,
+                             uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, uint32_t *status) {
   extern __shared__ uint32_t sm[];
   const int W = blockDim.x >> 5;
   uint32_t *cw = sm;            // [W][E]: counts, then each warp's running base
@@ -104,14 +106,14 @@ __global__ void group_kernel(const uint32_t *ids, int R, int E, int max_tiles, u
   const int r0 = min(R, warp * seg), r1 = min(R, r0 + seg);
   auto expert_of = [&](int r) -> uint32_t {
     if (r >= r1) return kPad;
-    const uint32_t e = ids[r];
+    const uint32_t e = ids[r] - (uint32_t)e0;  // wraps for e < e0
     return e < (uint32_t)E ? e : kPad;
   };
   for (int b = r0; b < r1; b += 32) {
     const int r = b + lane;
     const uint32_t e = expert_of(r);
     if (r < r1 && e == kPad) {
-      raise_status(status, kStatusBadExpert);
+      if (ids[r] >= (uint32_t)E_all) raise_status(status, kStatusBadExpert);
       route_rows[r] = kPad;
     }
     const uint32_t peers = __match_any_sync(0xffffffffu, e);
@@ -204,8 +206,10 @@ __global__ void gather_kernel(const uint16_t *x, int H, int k, const uint32_t *g
 }
 
 // y[t] = residual[t] + sum_s w[t][s] * d[route_rows[t*k + s]], slot order, f32.
+// F32: y is f32 (an expert shard's partial, summed over the ranks later).
+template <bool F32>
 __global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const uint32_t *route_rows,
-                               const uint16_t *residual, int T, int H, int k, uint16_t *y) {
+                               const uint16_t *residual, int T, int H, int k, void *y) {
   const int pieces = H / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)T * pieces) return;
@@ -229,11 +233,17 @@ __global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __fmul_rn(ws, bf16f((uint16_t)(w[e >> 1] >> (16 * (e & 1))))));
   }
-  uint32_t o[4];
+  if constexpr (F32) {
+    float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(y) + (size_t)t * H) + 2 * p;
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint32_t o[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e)
-    o[e] = (uint32_t)f32_to_bf16_bits(v[2 * e]) | ((uint32_t)f32_to_bf16_bits(v[2 * e + 1]) << 16);
-  reinterpret_cast<uint4 *>(y + (size_t)t * H)[p] = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int e = 0; e < 4; ++e)
+      o[e] = (uint32_t)f32_to_bf16_bits(v[2 * e]) | ((uint32_t)f32_to_bf16_bits(v[2 * e + 1]) << 16);
+    reinterpret_cast<uint4 *>(static_cast<uint16_t *>(y) + (size_t)t * H)[p] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -253,17 +263,20 @@ size_t moe_group_smem(int R, int E) {
 
 cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
                              uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, int e0, int e1) {
+  if (e1 < 0) e1 = E;
   const int threads = 256, warps = threads / 32;
   select_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(logits, T, E, k, ids, weights);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int R = T * k;
-  const size_t smem = moe_group_smem(R, E);
+  const int E_loc = e1 - e0;
+  const size_t smem = moe_group_smem(R, E_loc);
   static DeviceOnce once;
   e = once.run([] { return cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
   if (e != cudaSuccess) return e;
-  group_kernel<<<1, group_warps(E) * 32, smem, stream>>>(ids, R, E, max_tiles, tiles, grouped, route_rows, ntiles, status_word());
+  group_kernel<<<1, group_warps(E_loc) * 32, smem, stream>>>(ids, R, E, e0, E_loc, max_tiles, tiles, grouped, route_rows,
+                                                               ntiles, status_word());
   return cudaGetLastError();
 }
 
@@ -294,9 +307,9 @@ MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base) {
 
 cudaError_t moe_launch(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
                        const thq4_experts &gate, const thq4_experts &up, const thq4_experts &down, void *y,
-                       const MoeWorkspace &w, cudaStream_t stream) {
+                       const MoeWorkspace &w, cudaStream_t stream, int e0, int e1, bool y_f32) {
   cudaError_t e = moe_route_launch(static_cast<const uint16_t *>(logits), T, E, k, w.ids, w.weights, w.tiles, w.grouped,
-                                   w.route_rows, w.ntiles, w.max_tiles, stream);
+                                   w.route_rows, w.ntiles, w.max_tiles, stream, e0, e1 < 0 ? E : e1);
   if (e != cudaSuccess) return e;
   const size_t rows = (size_t)w.max_tiles * kMoeTileRows;
   {
@@ -324,9 +337,12 @@ cudaError_t moe_launch(const void *x, const void *residual, const void *logits, 
   g.ysum = nullptr;
   if ((e = moe_expert_launch(g, stream)) != cudaSuccess) return e;
   const size_t n = (size_t)T * (H / 8);
-  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w.d, w.weights, w.route_rows,
-                                                                   static_cast<const uint16_t *>(residual), T, H, k,
-                                                                   static_cast<uint16_t *>(y));
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  const uint16_t *res = static_cast<const uint16_t *>(residual);
+  if (y_f32)
+    combine_kernel<true><<<blocks, 256, 0, stream>>>(w.d, w.weights, w.route_rows, res, T, H, k, y);
+  else
+    combine_kernel<false><<<blocks, 256, 0, stream>>>(w.d, w.weights, w.route_rows, res, T, H, k, y);
   return cudaGetLastError();
 }
 

@@ -5,8 +5,9 @@ host-side mirror of the reference's operator API on top of it.
 """
 from ._lib import (BF16, F16, F32, SRC_FRAG, SRC_MLX, SRC_SLAB, SRC_TILED, Thq4Error, check, last_error,
                    lib, version)
-from .qlin import PackedExperts, PackedWeight, QLin, fuse_lins, lin_apply, lin_apply_ps, maybe_tiled, moe, moe_route
+from .qlin import (PackedExperts, PackedWeight, QLin, fuse_lins, lin_apply, lin_apply_ps, maybe_tiled, moe, moe_partial,
+                   moe_route)
 
 __all__ = ["BF16", "F16", "F32", "SRC_FRAG", "SRC_MLX", "SRC_SLAB", "SRC_TILED", "Thq4Error", "check",
            "last_error", "lib", "version", "PackedWeight", "QLin", "fuse_lins", "lin_apply", "lin_apply_ps",
-           "maybe_tiled", "PackedExperts", "moe", "moe_route"]
+           "maybe_tiled", "PackedExperts", "moe", "moe_partial", "moe_route"]

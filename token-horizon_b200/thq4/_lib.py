@@ -84,6 +84,9 @@ SIGNATURES = {
     "thq4_moe_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "thq4_moe": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(thq4_experts),
                          POINTER(thq4_experts), POINTER(thq4_experts), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "thq4_moe_partial": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                 POINTER(thq4_experts), POINTER(thq4_experts), POINTER(thq4_experts), c_void_p,
+                                 c_void_p, c_size_t, c_void_p]),
     "thq4_linear_peer": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
                                  c_void_p, c_size_t, POINTER(thq4_peer_gather), c_void_p]),
     "thq4_peer_wait": (c_int, [POINTER(thq4_peer_gather), c_void_p]),

@@ -288,6 +288,29 @@ def moe_route(logits: torch.Tensor, k: int):
     return ids, w, tiles[:nt], grouped[:nt * 32], rows
 
 
+def moe_partial(x: torch.Tensor, logits: torch.Tensor, k: int, e0: int, gate: PackedExperts, up: PackedExperts,
+                down: PackedExperts, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """An expert shard's part of one MoE layer: gate/up/down hold experts
+    [e0, e0 + gate.experts) of logits.shape[1]; returns f32 [T, H] (plus the
+    residual where given).  The layer's output is the ranks' sum, rounded
+    once to bf16."""
+    T, H = x.shape
+    E = logits.shape[1]
+    El, I = gate.experts, gate.rows
+    L = _lib.lib()
+    need = L.thq4_moe_workspace_bytes(T, H, I, El, k)
+    key = ("partial", x.device.index, torch.cuda.current_stream(x.device).cuda_stream)
+    ws = _MOE_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        _MOE_WS[key] = ws
+    y = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    check(L.thq4_moe_partial(_ptr(x.contiguous()), _ptr(residual), _ptr(logits.contiguous()), T, H, I, E, k, e0,
+                             e0 + El, ctypes.byref(gate.desc), ctypes.byref(up.desc), ctypes.byref(down.desc), _ptr(y),
+                             _ptr(ws), ws.numel(), _stream()))
+    return y
+
+
 def moe(x: torch.Tensor, logits: torch.Tensor, k: int, gate: PackedExperts, up: PackedExperts,
         down: PackedExperts, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One MoE layer: residual + sum_slot w * down(silu(gate x) * up x), bf16 [T, H]."""

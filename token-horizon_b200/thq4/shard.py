@@ -51,6 +51,31 @@ def gather_rows(local: torch.Tensor, full: Optional[torch.Tensor] = None, group=
     return out
 
 
+def expert_range(E: int, world: int, rank: int):
+    """(first expert, experts) of `rank`'s equal share of E experts."""
+    per, rem = divmod(E, world)
+    if rem or not 0 <= rank < world:
+        raise ValueError(f"{E} experts do not split into {world} equal shards")
+    return rank * per, per
+
+
+def moe_sharded(x: torch.Tensor, logits: torch.Tensor, k: int, e0: int, gate, up, down,
+                residual: Optional[torch.Tensor] = None, group=None) -> torch.Tensor:
+    """One MoE layer with the experts sharded over the ranks: each rank runs
+    its experts' routes (thq4_moe_partial, f32 partial [T, H]; the residual is
+    added on rank 0 only), one all-reduce sums the partials, and the sum is
+    rounded once to bf16."""
+    import torch.distributed as dist
+
+    from .qlin import moe_partial
+
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    part = moe_partial(x, logits, k, e0, gate, up, down, residual if rank == 0 else None)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(part, group=group)
+    return part.to(torch.bfloat16)
+
+
 class PeerGroup:
     """One IPC-mapped region per rank: [0, 256) control words (flags[world]
     u32 at 0, the gather count at 64, the CTA arrival counter at 128), then
