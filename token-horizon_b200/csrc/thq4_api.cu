@@ -71,17 +71,18 @@ GemvCfg gemv_cfg_override() {
   c.depth = g_force_depth.load(std::memory_order_relaxed);
   c.grid = g_force_grid.load(std::memory_order_relaxed);
   if (c.warps || c.depth || c.grid) return c;
-  // THQ4_GEMV="chunk,stages,grid", read once (the reference reads its TH_QMVT /
+  // THQ4_GEMV="chunk,stages,grid,pre", read once (the reference reads its TH_QMVT /
   // TH_Q4_POLICY switches once the same way, quant_kernel.rs:41-78, 367-432)
   static const GemvCfg env = [] {
     GemvCfg e;
     const char *s = std::getenv("THQ4_GEMV");
     if (s && *s) {
-      int w = 0, d = 0, g = 0;
-      if (std::sscanf(s, "%d,%d,%d", &w, &d, &g) >= 1) {
+      int w = 0, d = 0, g = 0, pre = 0;
+      if (std::sscanf(s, "%d,%d,%d,%d", &w, &d, &g, &pre) >= 1) {
         if (w == 4 || w == 8) e.warps = w;
         if (d >= 2 && d <= 8) e.depth = d;
         if (g > 0) e.grid = g;
+        if (pre > 0 && pre <= 8) e.pre = pre;
       }
     }
     return e;

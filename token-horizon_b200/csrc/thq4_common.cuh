@@ -124,6 +124,22 @@ __device__ __forceinline__ uint32_t atom_add_relaxed(uint32_t *p, uint32_t v) {
   asm volatile("atom.relaxed.gpu.global.add.u32 %0, [%1], %2;\n" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
+// Thread-block clusters: every thread of every CTA of the cluster arrives
+// (release) and waits (acquire); DSMEM stores into another CTA's shared
+// memory at the same offset (mapa).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr_local, uint32_t cta_rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_addr_local), "r"(cta_rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
 // System-scope ordering for flags that other GPUs read over NVLink.
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;\n" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {

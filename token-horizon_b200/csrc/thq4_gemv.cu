@@ -61,6 +61,7 @@
 //     output writes.  Every mbarrier wait is bounded in time and reports
 //     kStatusTimeout instead of hanging.
 #include <algorithm>
+#include <atomic>
 
 #include "thq4_common.cuh"
 #include "thq4_internal.h"
@@ -93,6 +94,8 @@ struct GemvArgs {
   int xf32, yf32;
   int stages;          // ring stages
   int xcap;            // activation groups staged per CTA
+  int pre;             // stages requested before x is staged (0: all)
+  int cl_j;            // > 1: slab-split mode, j CTAs per slab in one cluster
   // fused all-gather of column shards (g_dst null: none): the first g_rows
   // outputs also go to full[t * g_stride + g_off + row] on every rank, and
   // the grid's last CTA raises this rank's flag on every peer
@@ -112,7 +115,7 @@ __host__ __device__ inline size_t xstage_bytes(int xcap, int P) {
 }
 __host__ __device__ inline size_t stage_bytes(int cb, bool gate_up) { return (size_t)(gate_up ? 2 : 1) * cb * kSgBytes; }
 __host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, int xcap, int P) {
-  return 128 + (size_t)stages * stage_bytes(cb, gate_up) + xstage_bytes(xcap, P);
+  return 256 + (size_t)stages * stage_bytes(cb, gate_up) + xstage_bytes(xcap, P);
 }
 // floats of one CTA side's partial: 8 tiles x NS x 32 lanes x 4
 __host__ __device__ inline int side_floats(bool gate_up) { return kSlabTiles * (gate_up ? 2 : 1) * 32 * 4; }
@@ -305,6 +308,45 @@ __global__ void peer_wait_kernel(uint32_t *const *flags, const uint32_t *count, 
   if (threadIdx.x == 0) peer_wait(flags, count, world, rank, status);
 }
 
+// The producer lane: streams the run's nch chunks from chunk C0 into the
+// ring.  On a timeout it waits (bounded) for the copies it issued and stops.
+template <int CB, bool GATE_UP>
+__device__ __forceinline__ void produce_run(const GemvArgs &a, int C0, int nch, int R, uint64_t *full, uint64_t *empty,
+                                            uint64_t *xready, unsigned char *ring) {
+  constexpr int NS = GATE_UP ? 2 : 1;
+  constexpr size_t SB = (size_t)NS * CB * kSgBytes;
+  const uint64_t pol = evict_first_policy();
+  int sl = C0 / a.cps;  // slab and chunk-in-slab of chunk C0 + n
+  int cg = C0 - sl * a.cps;
+  int s = 0;
+  uint32_t par = 0;  // parity of this use of stage s
+  for (int n = 0; n < nch; ++n, ++cg) {
+    if (cg == a.cps) cg = 0, ++sl;
+    // Only the first a.pre stages go out before the consumers have staged
+    // x: the activation loads then do not queue behind the whole ring's
+    // weight burst.  (A timeout here only delays the stream.)
+    if (n == a.pre && a.pre > 0) (void)mbar_wait_bounded(xready, 0, kWaitLimitNs);
+    if (n >= R && !mbar_wait_bounded(&empty[s], par ^ 1u, kWaitLimitNs)) {
+      raise_status(a.status, kStatusTimeout);
+      // copies already issued must land before the CTA's memory is reused
+      for (int k = n - R; k < n; ++k) (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
+      return;
+    }
+    const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
+    const long long sg = (long long)sl * a.ng + g0c;
+    unsigned char *dst = ring + (size_t)s * SB;
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
+    bulk_g2s(dst, a.qw0 + sg * 4096, cnt * 4096, &full[s], pol);
+    bulk_g2s(dst + (size_t)NS * CB * 4096, a.sb0 + sg * 512, cnt * 512, &full[s], pol);
+    if constexpr (GATE_UP) {
+      bulk_g2s(dst + (size_t)CB * 4096, a.qw1 + sg * 4096, cnt * 4096, &full[s], pol);
+      bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, a.sb1 + sg * 512, cnt * 512, &full[s], pol);
+    }
+    if (++s == R) s = 0, par ^= 1u;
+  }
+  // the consumers wait for every chunk before they release it
+}
+
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr int NS = GATE_UP ? 2 : 1;
@@ -316,15 +358,27 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr size_t SB = (size_t)NS * CB * kSgBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
-  unsigned char *ring = smem + 128;
+  uint64_t *xready = empty + kMaxStages;  // the consumers have staged x
+  unsigned char *ring = smem + 256;
   unsigned char *xt = ring + (size_t)R * SB;
   const int P = a.P, P8 = meta_cols(P);
   uint4 *xf = reinterpret_cast<uint4 *>(xt);
   uint4 *zero = reinterpret_cast<uint4 *>(xt + (size_t)a.xcap * P * 128);
   float4 *mx = reinterpret_cast<float4 *>(xt + (size_t)a.xcap * P * 128 + 128);
 
-  // this CTA's run of chunks
-  const int C0 = run_begin(a, blockIdx.x), C1 = run_begin(a, blockIdx.x + 1);
+  // this CTA's run of chunks: an equal share of the flattened chunk space,
+  // or (slab-split mode) part `part` of the chunks of slab blockIdx / j
+  const bool clustered = a.cl_j > 1;
+  const int part = clustered ? (int)(blockIdx.x % (unsigned)a.cl_j) : 0;
+  int C0, C1;
+  if (clustered) {
+    const int slab = blockIdx.x / a.cl_j;
+    C0 = slab * a.cps + part * a.cps / a.cl_j;
+    C1 = slab * a.cps + (part + 1) * a.cps / a.cl_j;
+  } else {
+    C0 = run_begin(a, blockIdx.x);
+    C1 = run_begin(a, blockIdx.x + 1);
+  }
   const int nch = C1 - C0;
 
   if (threadIdx.x == 0) {
@@ -332,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
+    mbar_init(xready, 1);
   }
   fence_mbar_init();
   __syncthreads();
@@ -339,37 +394,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 
   if (warp == kConsumers) {
     // ---- producer: one elected lane streams the run -------------------------
-    if (lane != 0) return;
-    const uint64_t pol = evict_first_policy();
-    int sl = C0 / a.cps;  // slab and chunk-in-slab of chunk C0 + n
-    int cg = C0 - sl * a.cps;
-    int s = 0;
-    uint32_t par = 0;  // parity of this use of stage s
-    for (int n = 0; n < nch; ++n, ++cg) {
-      if (cg == a.cps) cg = 0, ++sl;
-      if (n >= R && !mbar_wait_bounded(&empty[s], par ^ 1u, kWaitLimitNs)) {
-        raise_status(a.status, kStatusTimeout);
-        // copies already issued must land before the CTA's memory is reused
-        for (int k = n - R; k < n; ++k)
-          (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
-        return;
-      }
-      const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
-      const long long sg = (long long)sl * a.ng + g0c;
-      unsigned char *dst = ring + (size_t)s * SB;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
-      bulk_g2s(dst, a.qw0 + sg * 4096, cnt * 4096, &full[s], pol);
-      bulk_g2s(dst + (size_t)NS * CB * 4096, a.sb0 + sg * 512, cnt * 512, &full[s], pol);
-      if constexpr (GATE_UP) {
-        bulk_g2s(dst + (size_t)CB * 4096, a.qw1 + sg * 4096, cnt * 4096, &full[s], pol);
-        bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, a.sb1 + sg * 512, cnt * 512, &full[s], pol);
-      }
-      if (++s == R) s = 0, par ^= 1u;
+    // (in slab-split mode the whole warp stays for the final cluster barrier)
+    if (lane == 0) produce_run<CB, GATE_UP>(a, C0, nch, R, full, empty, xready, ring);
+    __syncwarp();
+    if (clustered) {  // the consumers' two cluster barriers (below)
+      cluster_sync_all();
+      cluster_sync_all();
     }
-    // the consumers wait for every chunk before they release it
     return;
   }
-
   // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
   const int tile = warp;
   pdl_wait();
@@ -382,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   const int xcnt =
       min(a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
   stage_x(a, gs, xcnt, xf, zero, mx);
+  if (threadIdx.x == 0) mbar_arrive(xready);
 
   const int r = lane >> 2, c = lane & 3;
   const int jr = r / CPG, qr = r % CPG;  // this lane's B column: window position jr, column qr
@@ -558,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     }
     __syncwarp();
     if (lane == 0 && !aborted) mbar_arrive(&empty[s]);
-    if (cg == a.cps - 1) {  // slab end
+    if (!clustered && cg == a.cps - 1) {  // slab end
       reduce_y();
       if (aborted) {
       } else if (seg_whole) {
@@ -574,6 +608,35 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       seg_whole = true;
       finished_any = true;
     }
+  }
+
+  if (clustered) {
+    // Slab-split mode: this CTA holds part `part` of one slab.  Once every
+    // CTA of the cluster is past its stream (barrier 1) the leader's ring is
+    // free; the other parts go there through DSMEM (barrier 2), and the
+    // leader adds them in part order and stores the tile.
+    reduce_y();
+    float4 *xb = reinterpret_cast<float4 *>(ring);
+    cluster_sync_all();
+    if (part > 0) {
+#pragma unroll
+      for (int si = 0; si < NS; ++si) {
+        const uint32_t at = smem_addr(xb + (((size_t)part * kSlabTiles + tile) * NS + si) * 32 + lane);
+        st_cluster_f4(cluster_map(at, 0), make_float4(y[si][0], y[si][1], y[si][2], y[si][3]));
+      }
+    }
+    cluster_sync_all();
+    if (part == 0) {
+      for (int pp = 1; pp < a.cl_j; ++pp)
+#pragma unroll
+        for (int si = 0; si < NS; ++si) {
+          const float4 v = xb[(((size_t)pp * kSlabTiles + tile) * NS + si) * 32 + lane];
+          y[si][0] += v.x, y[si][1] += v.y, y[si][2] += v.z, y[si][3] += v.w;
+        }
+      if (!aborted) store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
+    }
+    if (a.g_dst) peer_signal(a);
+    return;
   }
 
   int last_slab = -1;
@@ -625,11 +688,35 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = gemv_pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (a.cl_j > 1) {  // the j CTAs of a slab form one cluster
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)a.cl_j;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    // all clusters must be resident at once (one wave): how many fit depends
+    // on how the SMs group into GPCs; asked once per (instance, size, smem)
+    static std::atomic<uint64_t> key{0};
+    static std::atomic<int> fits{0};
+    const uint64_t want = ((uint64_t)smem << 8) | (uint64_t)a.cl_j;
+    int n = 0;
+    if (key.load(std::memory_order_acquire) == want) {
+      n = fits.load(std::memory_order_relaxed);
+    } else {
+      if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+      }
+      fits.store(n, std::memory_order_relaxed);
+      key.store(want, std::memory_order_release);
+    }
+    if (n * a.cl_j < grid) return cudaErrorCooperativeLaunchTooLarge;  // the caller re-plans without clusters
+  }
   return cudaLaunchKernelEx(&cfg, k, a);
 }
 
@@ -685,10 +772,23 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
       // Whole slabs per CTA when that still fills >= 85% of the SMs: no
       // slab is split, so there is no split-K fix-up at the end of the run
       // (the fused gate/up of a 17408-wide MLP: 136 slabs on 148 SMs).
+      // Otherwise, with fewer slabs than SMs, each slab is split among j
+      // CTAs of one cluster when that fills >= 75% of the SMs: the parts
+      // meet in shared memory (DSMEM) instead of the workspace (hidden-5120
+      // q/k/v: 56 slabs x 2; o and down: 40 slabs x 3).
+      p.cl_j = 1;
       if (cfg.grid <= 0) {
         const int slabs = row_slabs(out);
         const int j = (slabs + sms - 1) / sms;
-        if (slabs % j == 0 && (long long)(slabs / j) * 100 >= (long long)sms * 85) grid = slabs / j;
+        if (slabs % j == 0 && (long long)(slabs / j) * 100 >= (long long)sms * 85) {
+          grid = slabs / j;
+        } else if (slabs < sms) {
+          const int jc = std::min(std::min(8, sms / slabs), cps);
+          if (jc >= 2 && (long long)slabs * jc * 100 >= (long long)sms * 75) {
+            grid = (long long)slabs * jc;
+            p.cl_j = jc;
+          }
+        }
       }
       if (chunks < grid) grid = chunks;  // every CTA run holds at least one chunk
       const long long max_run = (chunks + grid - 1) / grid;
@@ -754,6 +854,8 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     a.yf32 = y_f32 ? 1 : 0;
     a.stages = p.stages;
     a.xcap = p.xcap;
+    a.pre = gemv_cfg_override().pre;
+    a.cl_j = p.cl_j;
     if (peer) {
       a.g_dst = peer->dst;
       a.g_flags = peer->flags;
@@ -769,8 +871,17 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     // a last pass with fewer tokens fits in the footprint planned for more
     const size_t smem = gemv_smem(p.stages, p.ch, gate_up, p.xcap, a.P);
     const int gw = window_groups(a.P);
-    const cudaError_t e = w0.sb_dtype == THQ4_F16 ? dispatch<true>(a, gate_up, p.ch, gw, p.grid, smem, stream)
-                                                  : dispatch<false>(a, gate_up, p.ch, gw, p.grid, smem, stream);
+    cudaError_t e = w0.sb_dtype == THQ4_F16 ? dispatch<true>(a, gate_up, p.ch, gw, p.grid, smem, stream)
+                                            : dispatch<false>(a, gate_up, p.ch, gw, p.grid, smem, stream);
+    if (e == cudaErrorCooperativeLaunchTooLarge && a.cl_j > 1) {
+      // the clusters do not fit in one wave: one CTA per SM with split-K
+      const int grid = (int)std::min<long long>(p.chunks, device_sm_count());
+      a.cl_j = 1;
+      a.run_base = (int)(p.chunks / grid);
+      a.run_rem = (int)(p.chunks % grid);
+      e = w0.sb_dtype == THQ4_F16 ? dispatch<true>(a, gate_up, p.ch, gw, grid, smem, stream)
+                                  : dispatch<false>(a, gate_up, p.ch, gw, grid, smem, stream);
+    }
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -49,6 +49,7 @@ struct GemvCfg {
   int warps = 0;  // forced slab-groups per ring stage, 4 or 8 (0 = policy)
   int depth = 0;  // forced ring stages (0 = policy)
   int grid = 0;   // forced CTAs (0 = policy)
+  int pre = 0;    // ring stages requested before x is staged (0 = all)
 };
 // The testing hook's forced shape, else THQ4_GEMV (read once), else none.
 GemvCfg gemv_cfg_override();
@@ -57,6 +58,7 @@ struct GemvPlan {
   bool ok;
   int threads, grid, pieces, tokens_per_pass, ch, stages;
   int cps, xcap;     // chunks per slab, activation groups staged per CTA
+  int cl_j;          // > 1: each slab split among cl_j CTAs of one cluster
   long long chunks;  // chunks in the weight
   size_t smem;
 };
