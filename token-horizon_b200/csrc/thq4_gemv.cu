@@ -62,6 +62,7 @@
 //     kStatusTimeout instead of hanging.
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "thq4_common.cuh"
 #include "thq4_internal.h"
@@ -741,6 +742,39 @@ int window_groups(int P) { return P <= 2 ? 4 : (P <= 4 ? 2 : 1); }
 
 }  // namespace
 
+namespace {
+// Clusters of j CTAs (one CTA per SM, the GEMV's footprint) that can be
+// resident at once: it depends on how the SMs group into GPCs.  Asked once
+// per device and j.
+int cluster_capacity(int j) {
+  static std::mutex mu;
+  static int cache[64][9];
+  int dev = 0;
+  if (j < 2 || j > 8 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev][j]) return cache[dev][j] - 1;
+  auto *k = &gemv_kernel<8, 4, true, true, false>;
+  int n = 0;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(j * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 150 * 1024;  // any footprint that allows one CTA per SM
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)j;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+  }
+  (void)cudaGetLastError();
+  cache[dev][j] = n + 1;
+  return n;
+}
+}  // namespace
+
 size_t gemv_workspace_bytes(int rows) {
   // one partial per CTA side (at most two CTAs per SM), sized for gate and
   // up, then one counter per (slab, tile)
@@ -783,10 +817,14 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
         if (slabs % j == 0 && (long long)(slabs / j) * 100 >= (long long)sms * 85) {
           grid = slabs / j;
         } else if (slabs < sms) {
-          const int jc = std::min(std::min(8, sms / slabs), cps);
-          if (jc >= 2 && (long long)slabs * jc * 100 >= (long long)sms * 75) {
-            grid = (long long)slabs * jc;
-            p.cl_j = jc;
+          // the largest j whose clusters all fit at once and fill >= 75%
+          for (int jc = std::min(std::min(8, sms / slabs), cps); jc >= 2; --jc) {
+            if ((long long)slabs * jc * 100 < (long long)sms * 75) break;
+            if (cluster_capacity(jc) >= slabs) {
+              grid = (long long)slabs * jc;
+              p.cl_j = jc;
+              break;
+            }
           }
         }
       }

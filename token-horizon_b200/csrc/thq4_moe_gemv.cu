@@ -110,6 +110,20 @@ __device__ __forceinline__ uint32_t nib_bf16x2(uint32_t v) {
   asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(v), "n"(0x000F000F), "n"(0x43004300));
   return r;
 }
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ void unpk2(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// a * b + c on both f32 lanes, round to nearest (one instruction)
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 __device__ __forceinline__ void mg_consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"r"(kMgConsumers * 32) : "memory");
 }
@@ -173,15 +187,22 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
         else
           mma_bf16(acc[si][nb], A[0], A[1], A[2], A[3], bq[nb][2 * ks], bq[nb][2 * ks + 1]);
       }
+  // the same two FMAs per output, in packed f32x2 form: {y0, y1} (row r,
+  // tokens 2c and 2c + 1) and {y2, y3} (row r + 8)
 #pragma unroll
-  for (int si = 0; si < NS; ++si)
+  for (int si = 0; si < NS; ++si) {
+    const uint64_t srr = pk2(sr[si], sr[si]), crr = pk2(cr[si], cr[si]);
+    const uint64_t s88 = pk2(s8[si], s8[si]), c88 = pk2(c8[si], c8[si]);
 #pragma unroll
     for (int nb = 0; nb < NL; ++nb) {
-      y[si][nb][0] = fmaf(sr[si], acc[si][nb][0], fmaf(cr[si], sx[nb].x, y[si][nb][0]));
-      y[si][nb][1] = fmaf(sr[si], acc[si][nb][1], fmaf(cr[si], sx[nb].y, y[si][nb][1]));
-      y[si][nb][2] = fmaf(s8[si], acc[si][nb][2], fmaf(c8[si], sx[nb].x, y[si][nb][2]));
-      y[si][nb][3] = fmaf(s8[si], acc[si][nb][3], fmaf(c8[si], sx[nb].y, y[si][nb][3]));
+      const uint64_t xs2 = pk2(sx[nb].x, sx[nb].y);
+      uint64_t lo = pk2(y[si][nb][0], y[si][nb][1]), hi = pk2(y[si][nb][2], y[si][nb][3]);
+      lo = ffma2(srr, pk2(acc[si][nb][0], acc[si][nb][1]), ffma2(crr, xs2, lo));
+      hi = ffma2(s88, pk2(acc[si][nb][2], acc[si][nb][3]), ffma2(c88, xs2, hi));
+      unpk2(lo, y[si][nb][0], y[si][nb][1]);
+      unpk2(hi, y[si][nb][2], y[si][nb][3]);
     }
+  }
 }
 
 // The groups of a stage holding `cnt` groups.
