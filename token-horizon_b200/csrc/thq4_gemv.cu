@@ -776,8 +776,8 @@ int cluster_capacity(int j) {
 }  // namespace
 
 size_t gemv_workspace_bytes(int rows) {
-  // one partial per CTA side (at most two CTAs per SM), sized for gate and
-  // up, then one counter per (slab, tile)
+  // one partial per CTA side, sized for gate and up (room for two CTAs per
+  // SM; the grid is at most one per SM), then one counter per (slab, tile)
   const size_t ctas = (size_t)device_sm_count() * 2;
   return ctas * 2 * side_floats(true) * sizeof(float) +
          ((size_t)row_slabs(rows) * kSlabTiles * 4 + 255) / 256 * 256;

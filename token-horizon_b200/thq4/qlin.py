@@ -266,6 +266,22 @@ class PackedExperts:
         return p
 
 
+
+def _experts_from_slabs(cls, slabs: torch.Tensor, out: int, inp: int, sb_dtype: int) -> "PackedExperts":
+    """slabs u8 [E, out*inp/16*9] on the device: Splash expert slabs (a
+    package's expert section, docs/splash/runtime/model/WeightStore.cpp:
+    284-299), repacked expert by expert (THQ4_SRC_SLAB)."""
+    E = slabs.shape[0]
+    p = cls(E, out, inp, sb_dtype, slabs.device)
+    for e in range(E):
+        check(_lib.lib().thq4_repack(SRC_SLAB, _ptr(slabs[e].contiguous()), None, out, inp, 64, sb_dtype, 0, out,
+                                     ctypes.c_void_p(p.qw.data_ptr() + e * p.qw_stride), p.qw_stride,
+                                     ctypes.c_void_p(p.sb.data_ptr() + e * p.sb_stride), p.sb_stride, _stream()))
+    return p
+
+
+PackedExperts.from_slabs = classmethod(_experts_from_slabs)
+
 _MOE_WS: dict = {}
 
 
