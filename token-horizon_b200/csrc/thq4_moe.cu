@@ -34,16 +34,15 @@ namespace thq4 {
 namespace {
 
 constexpr uint32_t kPad = 0xFFFFFFFFu;
-constexpr int kFusedSelectTokens = 512;
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 
-// Token `warp` selected by one warp.  Repeated arg-max over the warp:
-// candidates are the experts not yet taken whose score is not -inf; ties go
-// to the lower id; a token without a candidate takes expert 0 (the oracle's
-// rule).
-__device__ void select_token(const uint16_t *logits, int warp, int E, int k, uint32_t *ids, uint16_t *weights,
-                             int lane) {
+// One warp per token.  Repeated arg-max over the warp: candidates are the
+// experts not yet taken whose score is not -inf; ties go to the lower id; a
+// token without a candidate takes expert 0 (the oracle's rule).
+__global__ void select_kernel(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
   const uint16_t *row = logits + (size_t)warp * E;
   float top[32];
   uint32_t taken = 0;  // bit j: this lane's expert lane + 32 j is taken (E <= 1024)
@@ -76,13 +75,6 @@ __device__ void select_token(const uint16_t *logits, int warp, int E, int k, uin
   }
 }
 
-// One warp per token.
-__global__ void select_kernel(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  select_token(logits, warp, E, k, ids, weights, lane);
-}
-
 // Warps of the grouping kernel: each owns a contiguous segment of the routes
 // and one row of per-expert counters in shared memory.
 __host__ __device__ inline int group_warps(int E) { return E <= 512 ? 32 : 16; }
@@ -99,19 +91,10 @@ __host__ __device__ inline int group_warps(int E) { return E <= 512 ? 32 : 16; }
 // Routes whose expert id is out of range are dropped (combine skips them).
 // Experts [e0, e0 + E) of E_all are grouped (local ids e - e0); routes to
 // other valid experts are dropped silently (another rank computes them).
-// With `logits` (few tokens) the same CTA first selects every token's
-// experts (warp w takes tokens w, w + W, ...), saving a launch.
 __global__ void group_kernel(const uint32_t *ids, int R, int E_all, int e0, int E, int max_tiles, uint32_t *tiles,
-                             uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, uint32_t *status,
-                             const uint16_t *logits, int k, uint16_t *weights) {
+                             uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, uint32_t *status) {
   extern __shared__ uint32_t sm[];
   const int W = blockDim.x >> 5;
-  if (logits) {
-    const int T = R / k;
-    for (int t = threadIdx.x >> 5; t < T; t += W)
-      select_token(logits, t, E_all, k, const_cast<uint32_t *>(ids), weights, threadIdx.x & 31);
-    __syncthreads();  // the ids written above are read by other warps below
-  }
   uint32_t *cw = sm;            // [W][E]: counts, then each warp's running base
   uint32_t *off = sm + W * E;   // [E + 1]: first tile of each expert, tiles in use
   uint32_t *tot = off + E + 1;  // [E]: routes of each expert
@@ -282,14 +265,10 @@ cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32
                              uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
                              cudaStream_t stream, int e0, int e1) {
   if (e1 < 0) e1 = E;
-  // up to kFusedSelectTokens tokens the grouping CTA selects them itself
-  const bool fused = T <= kFusedSelectTokens;
-  cudaError_t e = cudaSuccess;
-  if (!fused) {
-    const int threads = 256, warps = threads / 32;
-    select_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(logits, T, E, k, ids, weights);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
+  const int threads = 256, warps = threads / 32;
+  select_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   const int R = T * k;
   const int E_loc = e1 - e0;
   const size_t smem = moe_group_smem(R, E_loc);
@@ -297,8 +276,7 @@ cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32
   e = once.run([] { return cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
   if (e != cudaSuccess) return e;
   group_kernel<<<1, group_warps(E_loc) * 32, smem, stream>>>(ids, R, E, e0, E_loc, max_tiles, tiles, grouped, route_rows,
-                                                               ntiles, status_word(), fused ? logits : nullptr, k,
-                                                               weights);
+                                                               ntiles, status_word());
   return cudaGetLastError();
 }
 
