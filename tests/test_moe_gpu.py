@@ -33,7 +33,8 @@ def _u32(t: torch.Tensor) -> np.ndarray:
 
 
 @pytest.mark.parametrize("T,E,k,mode", [(256, 128, 8, "normal"), (37, 8, 2, "normal"), (64, 16, 4, "ties"),
-                                        (33, 12, 3, "neg_inf"), (1, 4, 4, "normal"), (300, 64, 6, "ties")])
+                                        (33, 12, 3, "neg_inf"), (1, 4, 4, "normal"), (300, 64, 6, "ties"),
+                                        (700, 128, 8, "ties"), (1200, 32, 2, "neg_inf")])
 def test_routing_is_bit_exact(T, E, k, mode):
     logits = _logits(T, E, T * 31 + E, mode)
     ids_w, w_w = O.moe_select(logits, k)
