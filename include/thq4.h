@@ -225,6 +225,80 @@ thq4_status thq4_moe(const void *x, const void *residual, const void *logits, in
                      const thq4_experts *down, void *y, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ---- the Splash MoE layer with its Q8 router and shared expert ---------- */
+
+/* An 8-bit affine projection in Splash's StorageN = 256 order (replaces
+ * Q8Projection, docs/splash/runtime/ops/Linear.hpp:27-33): output n < 256 of
+ * input k has its byte q at ((k/64)*256 + n)*64 + k%64 and its bf16 scale and
+ * bias at (k/64)*256 + n, value q * scale + bias.  out is 256; in % 64 == 0;
+ * q, scales and biases 16-byte aligned. */
+typedef struct thq4_q8_weight {
+  int32_t out;
+  int32_t in;
+  const void *q;
+  const void *scales;
+  const void *biases;
+} thq4_q8_weight;
+
+/* All weights of one sparse MoE block (replaces MoeWeights, MoE.hpp:35-44):
+ * the router (scores of experts 0..E-1 are its rows 0..E-1), E routed experts,
+ * and the shared expert -- three one-expert projections of the routed
+ * shapes, weighted per token by the sigmoid of row 0 of
+ * shared_expert_gate.  A layer without a shared expert passes
+ * shared_gate.qw == NULL and shared_expert_gate.q == NULL. */
+typedef struct thq4_moe_weights {
+  thq4_q8_weight router;
+  thq4_experts gate, up, down;
+  thq4_experts shared_gate, shared_up, shared_down;
+  thq4_q8_weight shared_expert_gate;
+} thq4_moe_weights;
+
+/* Router scores (moe_route_scores_q8_m8 / _m32, moe.metal:34-262): scores
+ * bf16 [T][ld] columns 0..ncols-1 = bf16 of, over eight K slices in order
+ * (slice s: groups [s*G/8, (s+1)*G/8) of G = in/64), the sum in group order
+ * of fma(dot, scale, sum * bias); dot = sum over the group's 64 k in k order
+ * of x * q (f32), sum = the group's 64 x as 32 pairs (x[l] + x[l+32])
+ * combined by xor butterfly (partners 16, 8, 4, 2, 1).  x bf16 [T][in],
+ * 16-byte aligned; 1 <= ncols <= 256, ld >= ncols.  Workspace:
+ * thq4_moe_scores_workspace_bytes(T, ncols) (the eight slices' f32 sums). */
+size_t thq4_moe_scores_workspace_bytes(int T, int ncols);
+thq4_status thq4_moe_scores_q8(const void *x, int T, const thq4_q8_weight *router, int ncols, void *scores, int ld,
+                               void *workspace, size_t workspace_bytes, void *stream);
+
+/* Group tiles of MoE::add for T tokens, k of E experts, plus ceil(T/32)
+ * tiles of the shared expert when shared != 0 (moeMaximumTiles, MoE.hpp:
+ * 72-77). */
+uint32_t thq4_moe_add_max_tiles(int T, int E, int k, int shared);
+/* The routing of MoE::add on the device (the router, moe_route_select_q8 and
+ * moe_group_routes, moe.metal:34-449): scores as thq4_moe_scores_q8, top k
+ * by descending score (lowest id first among equal scores) with softmax
+ * weights; with a shared expert gate (not NULL) a last route per token holds
+ * expert E with weight bf16(1 / (1 + exp(-g))), g = x . row 0 of the gate
+ * dequantised (thread v of 256 accumulates k = v, v + 256, ... by fma, warps
+ * by xor butterfly, the eight warp sums in order).  rpr = k (+1 with the
+ * shared expert) routes per token: ids u32 [T][rpr], weights bf16 [T][rpr],
+ * tiles u32 [max_tiles][2], grouped_routes u32 [max_tiles*32], route_rows
+ * u32 [T*rpr], ntiles u32 [1]; the shared expert's tiles follow the routed
+ * ones and hold every token in order.  Workspace:
+ * thq4_moe_scores_workspace_bytes(T, E). */
+thq4_status thq4_moe_route_q8(const void *x, int T, int E, int k, const thq4_q8_weight *router,
+                              const thq4_q8_weight *shared_expert_gate, uint32_t *ids, void *weights, uint32_t *tiles,
+                              uint32_t *grouped_routes, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
+                              void *workspace, size_t workspace_bytes, void *stream);
+/* Workspace bytes of thq4_moe_add / thq4_moe_add_partial (E = the experts
+ * this call holds; shared: it runs the shared expert). */
+size_t thq4_moe_add_workspace_bytes(int T, int H, int I, int E, int k, int shared);
+/* One MoE block (replaces MoE::add, MoE.cpp:119-231): routing as
+ * thq4_moe_route_q8, then y bf16 [T][H] = residual (optional) + the sum over
+ * each token's routes in slot order (the shared expert last) of
+ * w * down(bf16(silu(bf16 g) * bf16 u)), f32, one bf16 rounding.  Checked
+ * before anything is launched as MoE::add validates (MoE.cpp:43-58):
+ * H and I multiples of 256, 1 <= k <= E <= 256, router and shared gate
+ * 256 x H, experts E x I x H (gate, up) and E x H x I (down), the shared
+ * projections one expert each. */
+thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int I, int E, int k,
+                         const thq4_moe_weights *w, void *y, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- multi-GPU column shards --------------------------------------------
  * The reference engine is single-device; these entry points are the sharded
  * extension.  Each rank (one process per GPU) holds a contiguous range of a
@@ -272,6 +346,16 @@ thq4_status thq4_moe_partial(const void *x, const void *residual, const void *lo
                              int k, int e0, int e1, const thq4_experts *gate, const thq4_experts *up,
                              const thq4_experts *down, float *y_part, void *workspace, size_t workspace_bytes,
                              void *stream);
+
+/* thq4_moe_add for an expert shard: w holds routed experts [e0, e1) of E
+ * (gate, up, down: e1 - e0 experts), the full router and, when
+ * shared_expert_gate.q is not NULL, the layer's shared expert gate (every
+ * token then has k + 1 routes); the shard runs the shared expert when
+ * w->shared_gate.qw is not NULL (one rank of the group).  y_part f32 [T][H]
+ * as thq4_moe_partial. */
+thq4_status thq4_moe_add_partial(const void *x, const void *residual, int T, int H, int I, int E, int k, int e0,
+                                 int e1, const thq4_moe_weights *w, float *y_part, void *workspace,
+                                 size_t workspace_bytes, void *stream);
 
 #define THQ4_IPC_HANDLE_BYTES 64
 /* Device memory another process of this node can map: cudaMalloc'd, zeroed,

@@ -132,3 +132,62 @@ def moe_group(ids: np.ndarray, E: int, tile_rows: int):
             grouped.extend(int(r) for r in chunk)
             grouped.extend([0xFFFFFFFF] * (tile_rows - len(chunk)))
     return tiles, np.array(grouped, dtype=np.uint32), route_rows
+
+
+# ---- the Q8 router and the shared expert's gate (moe.metal:1-361) -------------
+
+def _fma32(a, b, c):
+    """f32 fma of f32 arrays whose product a*b is exact in f64 (it is for the
+    router's bf16/u8/f32 operands); the f64 sum then rounds once to f32
+    except in the rare double-rounding case."""
+    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(np.float32)
+
+
+def _butterfly32(v: np.ndarray) -> np.ndarray:
+    """Xor-butterfly sum over the last axis (32 lanes), partners 16 .. 1."""
+    for o in (16, 8, 4, 2, 1):
+        v = (v + v[..., np.arange(32) ^ o]).astype(np.float32)
+    return v[..., 0]
+
+
+def moe_scores_q8(x_bf16, q, scales, biases, ncols: int) -> np.ndarray:
+    """Router scores bf16 [T][ncols], array at a time over (token, column)."""
+    x = bf16_to_f32(np.asarray(x_bf16, dtype=np.uint16))
+    T, H = x.shape
+    G = H // 64
+    pairs = (x.reshape(T, G, 64)[:, :, :32] + x.reshape(T, G, 64)[:, :, 32:]).astype(np.float32)
+    sums = _butterfly32(pairs)  # [T][G]
+    qv = np.asarray(q, dtype=np.uint8).reshape(G, 256, 64)[:, :ncols, :].astype(np.float32)
+    sc = bf16_to_f32(np.asarray(scales, dtype=np.uint16).reshape(G, 256)[:, :ncols])
+    bi = bf16_to_f32(np.asarray(biases, dtype=np.uint16).reshape(G, 256)[:, :ncols])
+    total = np.zeros((T, ncols), np.float32)
+    for s in range(8):
+        sl = np.zeros((T, ncols), np.float32)
+        for g in range(s * G // 8, (s + 1) * G // 8):
+            dot = np.zeros((T, ncols), np.float32)
+            for j in range(64):
+                dot = (dot + x[:, 64 * g + j, None] * qv[g, None, :, j]).astype(np.float32)
+            c = (sums[:, g, None] * bi[g][None, :]).astype(np.float32)
+            sl = (sl + _fma32(dot, np.broadcast_to(sc[g], dot.shape), c)).astype(np.float32)
+        total = (total + sl).astype(np.float32)
+    return f32_to_bf16(total)
+
+
+def moe_shared_gate(x_bf16, q, scales, biases):
+    """(weights bf16 [T], logits f32 [T]) of the shared expert's scalar gate."""
+    x = bf16_to_f32(np.asarray(x_bf16, dtype=np.uint16))
+    T, H = x.shape
+    G = H // 64
+    qv = np.asarray(q, dtype=np.uint8).reshape(G, 256, 64)[:, 0, :].astype(np.float32).reshape(H)
+    sc = np.repeat(bf16_to_f32(np.asarray(scales, dtype=np.uint16).reshape(G, 256)[:, 0]), 64)
+    bi = np.repeat(bf16_to_f32(np.asarray(biases, dtype=np.uint16).reshape(G, 256)[:, 0]), 64)
+    deq = _fma32(qv, sc, bi)
+    acc = np.zeros((T, 256), np.float32)
+    for base in range(0, H, 256):
+        n = min(256, H - base)
+        acc[:, :n] = _fma32(x[:, base:base + n], np.broadcast_to(deq[base:base + n], (T, n)), acc[:, :n])
+    warps = _butterfly32(acc.reshape(T, 8, 32))  # [T][8]
+    total = np.zeros(T, np.float32)
+    for w in range(8):
+        total = (total + warps[:, w]).astype(np.float32)
+    return f32_to_bf16((np.float32(1) / (np.float32(1) + np.exp(-total))).astype(np.float32)), total

@@ -585,12 +585,15 @@ int q4o_moe_group(const uint32_t *ids, int T, int k, int E, int tile_rows,
 
 typedef struct {
   const uint16_t *x;
-  int T, H, I, k;
+  int T, H, I, k; /* k: routes per token (the routed slots plus a shared one) */
   const uint32_t *ids;
   const uint32_t *gu_wq, *dn_wq;
   const uint16_t *gu_sb, *dn_sb;
   int sb_dtype;
   uint16_t *h_out, *d_out;
+  uint32_t E; /* expert id E selects the shared expert */
+  const uint32_t *sh_gu_wq, *sh_dn_wq;
+  const uint16_t *sh_gu_sb, *sh_dn_sb;
 } moe_ctx;
 
 /* The CPU `project` of moe_metal_test.mm:147-165 (fp32 group dot and sum,
@@ -625,14 +628,19 @@ static void moe_routes(void *p, int r0, int r1) {
   for (int r = r0; r < r1; ++r) {
     int t = r / c->k;
     uint32_t e = c->ids[r];
+    int sh = e == c->E;
+    const uint32_t *gw = sh ? c->sh_gu_wq : c->gu_wq + e * gu_words;
+    const uint16_t *gs = sh ? c->sh_gu_sb : c->gu_sb + e * gu_sbn;
+    const uint32_t *dw = sh ? c->sh_dn_wq : c->dn_wq + e * dn_words;
+    const uint16_t *ds = sh ? c->sh_dn_sb : c->dn_sb + e * dn_sbn;
     for (int i = 0; i < H; ++i) x[i] = q4o_bf16_to_f32(c->x[(size_t)t * H + i]);
-    project_row(c->gu_wq + e * gu_words, c->gu_sb + e * gu_sbn, c->sb_dtype, 2 * I, H, x, gu);
+    project_row(gw, gs, c->sb_dtype, 2 * I, H, x, gu);
     for (int i = 0; i < I; ++i) {
       uint16_t hv = q4o_silu_mul_bf16(gu[i], gu[I + i]);
       h[i] = q4o_bf16_to_f32(hv);
       if (c->h_out) c->h_out[(size_t)r * I + i] = hv;
     }
-    project_row(c->dn_wq + e * dn_words, c->dn_sb + e * dn_sbn, c->sb_dtype, H, I, h, d);
+    project_row(dw, ds, c->sb_dtype, H, I, h, d);
     for (int i = 0; i < H; ++i) c->d_out[(size_t)r * H + i] = q4o_f32_to_bf16(d[i]);
   }
   free(x);
@@ -647,10 +655,20 @@ void q4o_moe_forward(const uint16_t *x, const uint16_t *residual, int T, int H,
                      const uint16_t *gu_sb, const uint32_t *dn_wq,
                      const uint16_t *dn_sb, int sb_dtype, uint16_t *h_out,
                      uint16_t *d_out, uint16_t *y, int nthreads) {
-  (void)E;
+  q4o_moe_forward_shared(x, residual, T, H, I, E, k, ids, weights, gu_wq, gu_sb, dn_wq, dn_sb, NULL, NULL,
+                         NULL, NULL, sb_dtype, h_out, d_out, y, nthreads);
+}
+
+void q4o_moe_forward_shared(const uint16_t *x, const uint16_t *residual, int T, int H, int I, int E, int k,
+                            const uint32_t *ids, const uint16_t *weights, const uint32_t *gu_wq,
+                            const uint16_t *gu_sb, const uint32_t *dn_wq, const uint16_t *dn_sb,
+                            const uint32_t *sh_gu_wq, const uint16_t *sh_gu_sb, const uint32_t *sh_dn_wq,
+                            const uint16_t *sh_dn_sb, int sb_dtype, uint16_t *h_out, uint16_t *d_out,
+                            uint16_t *y, int nthreads) {
   int own_d = d_out == NULL;
   if (own_d) d_out = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)T * k * H);
-  moe_ctx c = {x, T, H, I, k, ids, gu_wq, dn_wq, gu_sb, dn_sb, sb_dtype, h_out, d_out};
+  moe_ctx c = {x, T, H, I, k, ids, gu_wq, dn_wq, gu_sb, dn_sb, sb_dtype, h_out, d_out,
+               sh_gu_wq ? (uint32_t)E : 0xFFFFFFFFu, sh_gu_wq, sh_dn_wq, sh_gu_sb, sh_dn_sb};
   parallel_for(T * k, nthreads, moe_routes, &c);
   /* moe_combine (moe.metal:642-664): value = residual, then += w * d over
    * the slots in order, f32, one bf16 rounding. */
@@ -663,4 +681,231 @@ void q4o_moe_forward(const uint16_t *x, const uint16_t *residual, int T, int H,
       y[(size_t)t * H + i] = q4o_f32_to_bf16(v);
     }
   if (own_d) free(d_out);
+}
+
+/* ---- the Q8 router and the shared expert's gate (moe.metal:1-361) ------ */
+
+/* A Q8 projection in StorageN = 256 order (Linear.hpp:27-33, read by
+ * moe.metal:70-121): byte q of output n and input k at ((k/64)*256 + n)*64 +
+ * k%64; bf16 scale and bias at (k/64)*256 + n. */
+#define Q8_STORAGE_N 256
+#define ROUTE_SLICES 8
+
+/* A 64-value group's sum in the router's fixed order: lane l of a warp adds
+ * x[l] and x[l + 32] (moe_route_row_sum, moe.metal:22-25), then the lanes
+ * combine by xor butterfly, partners 16, 8, 4, 2, 1 (every lane ends with the
+ * same value since each step adds a pair in either order). */
+static float route_group_sum(const float *x) {
+  float v[32], w[32];
+  for (int l = 0; l < 32; ++l) v[l] = x[l] + x[l + 32];
+  for (int o = 16; o > 0; o >>= 1) {
+    for (int l = 0; l < 32; ++l) w[l] = v[l] + v[l ^ o];
+    memcpy(v, w, sizeof v);
+  }
+  return v[0];
+}
+
+typedef struct {
+  const uint16_t *x;
+  int H, ncols;
+  const uint8_t *q;
+  const uint16_t *scales, *biases;
+  uint16_t *scores;
+} scores_ctx;
+
+static void scores_rows(void *p, int t0, int t1) {
+  scores_ctx *c = (scores_ctx *)p;
+  int H = c->H, G = H / 64;
+  float *x = (float *)malloc(sizeof(float) * (size_t)H);
+  float *sums = (float *)malloc(sizeof(float) * (size_t)G);
+  for (int t = t0; t < t1; ++t) {
+    for (int i = 0; i < H; ++i) x[i] = q4o_bf16_to_f32(c->x[(size_t)t * H + i]);
+    for (int g = 0; g < G; ++g) sums[g] = route_group_sum(x + 64 * g);
+    for (int n = 0; n < c->ncols; ++n) {
+      float total = 0.0f;
+      for (int s = 0; s < ROUTE_SLICES; ++s) {
+        /* moe_route_slice (moe.metal:17-20): groups [s*G/8, (s+1)*G/8) */
+        int g0 = s * G / ROUTE_SLICES, g1 = (s + 1) * G / ROUTE_SLICES;
+        float slice = 0.0f;
+        for (int g = g0; g < g1; ++g) {
+          const uint8_t *qg = c->q + ((size_t)g * Q8_STORAGE_N + n) * 64;
+          float dot = 0.0f;
+          for (int j = 0; j < 64; ++j) dot = fmaf(x[64 * g + j], (float)qg[j], dot);
+          size_t prm = (size_t)g * Q8_STORAGE_N + n;
+          float b = q4o_bf16_to_f32(c->biases[prm]);
+          /* moe_route_group_term (moe.metal:29-32): fma(dot, scale, sum*bias) */
+          slice = slice + fmaf(dot, q4o_bf16_to_f32(c->scales[prm]), sums[g] * b);
+        }
+        total = total + slice;
+      }
+      c->scores[(size_t)t * c->ncols + n] = q4o_f32_to_bf16(total);
+    }
+  }
+  free(x);
+  free(sums);
+}
+
+/* moe_route_scores_q8_m8 / _m32 (moe.metal:34-262): per row and expert the
+ * sum over eight K slices, in slice order, of the slice's groups' terms
+ * fma(dot, scale, sum * bias) in group order; a group's dot is the f32 sum of
+ * x[k] * q[k] in k order (each product is exact: bf16 x 8-bit integer).  The
+ * reference's matmul2d leaves the order inside a group's dot to the
+ * hardware; the order above is the one this library's router kernel uses.
+ * x bf16 [T][H]; scores bf16 [T][ncols]. */
+void q4o_moe_scores_q8(const uint16_t *x, int T, int H, const uint8_t *q, const uint16_t *scales,
+                       const uint16_t *biases, int ncols, uint16_t *scores, int nthreads) {
+  scores_ctx c = {x, H, ncols, q, scales, biases, scores};
+  parallel_for(T, nthreads, scores_rows, &c);
+}
+
+/* The shared expert's scalar gate of moe_route_select_q8 (moe.metal:297-322):
+ * thread v of 256 accumulates, for d = v, v + 256, ..., x[d] * (q * s + b)
+ * with row 0's parameters of group d/64, each step one fma of the dequantised
+ * weight (itself fma(q, s, b)); each warp of 32 threads combines by xor
+ * butterfly (partners 16 .. 1); the eight warp sums add in warp order.
+ * weight = bf16(1 / (1 + exp(-total))).  logit (optional) = total. */
+void q4o_moe_shared_gate(const uint16_t *x, int T, int H, const uint8_t *q, const uint16_t *scales,
+                         const uint16_t *biases, uint16_t *weights, float *logit) {
+  for (int t = 0; t < T; ++t) {
+    const uint16_t *row = x + (size_t)t * H;
+    float total = 0.0f;
+    for (int w = 0; w < Q8_STORAGE_N / 32; ++w) {
+      float v[32], u[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int d = 32 * w + l; d < H; d += Q8_STORAGE_N) {
+          int g = d / 64, j = d % 64;
+          size_t prm = (size_t)g * Q8_STORAGE_N;
+          float deq = fmaf((float)q[prm * 64 + j], q4o_bf16_to_f32(scales[prm]), q4o_bf16_to_f32(biases[prm]));
+          acc = fmaf(q4o_bf16_to_f32(row[d]), deq, acc);
+        }
+        v[l] = acc;
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; ++l) u[l] = v[l] + v[l ^ o];
+        memcpy(v, u, sizeof v);
+      }
+      total = total + v[0];
+    }
+    if (logit) logit[t] = total;
+    weights[t] = q4o_f32_to_bf16(1.0f / (1.0f + expf(-total)));
+  }
+}
+
+/* moe_group_routes with the shared expert (moe.metal:368-449): every token
+ * carries k routed slots and, when rpr == k + 1, a shared slot last.  The
+ * routed slots sort as in q4o_moe_group; then ceil(T/tile_rows) tiles of
+ * expert E hold the shared routes of tokens 0..T-1 in order.  ids [T][rpr];
+ * route_rows [T*rpr].  Returns the tile count or -1. */
+int q4o_moe_group_shared(const uint32_t *ids, int T, int k, int rpr, int E, int tile_rows, int max_tiles,
+                         uint32_t *tiles, uint32_t *grouped_routes, uint32_t *route_rows) {
+  int routes = T * rpr;
+  uint32_t *count = (uint32_t *)calloc((size_t)E, sizeof(uint32_t));
+  uint32_t *offset = (uint32_t *)calloc((size_t)E, sizeof(uint32_t));
+  uint32_t *cursor = (uint32_t *)calloc((size_t)E, sizeof(uint32_t));
+  for (int r = 0; r < routes; ++r)
+    if (r % rpr < k) count[ids[r]]++;
+  uint32_t ntiles = 0;
+  for (int e = 0; e < E; ++e) {
+    offset[e] = ntiles;
+    ntiles += (count[e] + (uint32_t)tile_rows - 1) / (uint32_t)tile_rows;
+  }
+  uint32_t routed = ntiles;
+  uint32_t shared_tiles = rpr > k ? ((uint32_t)T + (uint32_t)tile_rows - 1) / (uint32_t)tile_rows : 0u;
+  ntiles += shared_tiles;
+  if ((int)ntiles > max_tiles) {
+    free(count);
+    free(offset);
+    free(cursor);
+    return -1;
+  }
+  for (size_t i = 0; i < (size_t)max_tiles * tile_rows; ++i) grouped_routes[i] = 0xFFFFFFFFu;
+  for (size_t i = 0; i < (size_t)max_tiles * 2; ++i) tiles[i] = 0;
+  for (int e = 0; e < E; ++e) {
+    uint32_t nt = (count[e] + (uint32_t)tile_rows - 1) / (uint32_t)tile_rows;
+    for (uint32_t t = 0; t < nt; ++t) {
+      uint32_t live = count[e] - t * (uint32_t)tile_rows;
+      tiles[(offset[e] + t) * 2] = (uint32_t)e;
+      tiles[(offset[e] + t) * 2 + 1] = live < (uint32_t)tile_rows ? live : (uint32_t)tile_rows;
+    }
+  }
+  for (int r = 0; r < routes; ++r) {
+    if (r % rpr >= k) continue;
+    uint32_t e = ids[r];
+    uint32_t row = offset[e] * (uint32_t)tile_rows + cursor[e]++;
+    grouped_routes[row] = (uint32_t)r;
+    route_rows[r] = row;
+  }
+  for (uint32_t t = 0; t < shared_tiles; ++t) {
+    uint32_t live = (uint32_t)T - t * (uint32_t)tile_rows;
+    tiles[(routed + t) * 2] = (uint32_t)E;
+    tiles[(routed + t) * 2 + 1] = live < (uint32_t)tile_rows ? live : (uint32_t)tile_rows;
+  }
+  if (rpr > k)
+    for (int t = 0; t < T; ++t) {
+      uint32_t row = routed * (uint32_t)tile_rows + (uint32_t)t;
+      grouped_routes[row] = (uint32_t)(t * rpr + k);
+      route_rows[t * rpr + k] = row;
+    }
+  free(count);
+  free(offset);
+  free(cursor);
+  return (int)ntiles;
+}
+
+/* ---- the reference MoE test's fixture (moe_metal_test.mm:46-271) -------- */
+
+static uint32_t splash_next(uint64_t *s) { return (uint32_t)q4o_lcg(s); }
+/* Random::unit (moe_metal_test.mm:74) */
+static float splash_unit(uint64_t *s) { return (float)(splash_next(s) & 0xFFFFFFu) / 8388608.0f - 1.0f; }
+
+/* randomSlab + packSlab (moe_metal_test.mm:108-145): nibbles n-major, then
+ * per parameter index a scale bf16(0.01 + 0.01 (unit + 1)) and a bias
+ * bf16(-0.2 + 0.05 unit), drawn in that order; packed into a Splash slab.
+ * The multiply-adds are single fmas, as clang contracts them on arm64. */
+static void splash_random_slab(uint64_t *s, int out, int in, uint8_t *slab) {
+  size_t elements = (size_t)out * in;
+  int groups = in / 64;
+  uint8_t *nib = (uint8_t *)malloc(elements);
+  for (size_t i = 0; i < elements; ++i) nib[i] = (uint8_t)(splash_next(s) & 15u);
+  size_t params = elements / 64;
+  uint16_t *sc = (uint16_t *)(slab + elements / 2);
+  uint16_t *bi = (uint16_t *)(slab + elements / 2 + elements / 32);
+  for (size_t i = 0; i < params; ++i) {
+    sc[i] = q4o_f32_to_bf16(fmaf(0.01f, splash_unit(s) + 1.0f, 0.01f));
+    bi[i] = q4o_f32_to_bf16(fmaf(0.05f, splash_unit(s), -0.2f));
+  }
+  memset(slab, 0, elements / 2);
+  for (int n = 0; n < out; ++n)
+    for (int k = 0; k < in; ++k) {
+      size_t prm = ((size_t)(n / 256) * groups + (size_t)(k / 64)) * 256 + (size_t)(n % 256);
+      size_t idx = prm * 64 + (size_t)(k % 64);
+      uint8_t v = nib[(size_t)n * in + k];
+      slab[idx / 2] |= (uint8_t)((idx & 1) ? v << 4 : v);
+    }
+  free(nib);
+}
+
+/* makeFixture (moe_metal_test.mm:217-271) with Random(seed): E gate, E up, E
+ * down slabs, then the shared gate, up and down slabs (one each), then per
+ * row and column an input bf16(sign * (0.55 + 0.45 unit)) (sign -1 on every
+ * third row) and a residual bf16(0.1 unit). */
+void q4o_splash_moe_fixture(int H, int I, int E, int rows, uint64_t seed, uint8_t *gate, uint8_t *up,
+                            uint8_t *down, uint8_t *shared_gate, uint8_t *shared_up, uint8_t *shared_down,
+                            uint16_t *x, uint16_t *residual) {
+  uint64_t s = seed;
+  size_t gs = q4o_slab_bytes(I, H), ds = q4o_slab_bytes(H, I);
+  for (int e = 0; e < E; ++e) splash_random_slab(&s, I, H, gate + (size_t)e * gs);
+  for (int e = 0; e < E; ++e) splash_random_slab(&s, I, H, up + (size_t)e * gs);
+  for (int e = 0; e < E; ++e) splash_random_slab(&s, H, I, down + (size_t)e * ds);
+  splash_random_slab(&s, I, H, shared_gate);
+  splash_random_slab(&s, I, H, shared_up);
+  splash_random_slab(&s, H, I, shared_down);
+  for (int r = 0; r < rows; ++r) {
+    float sign = r % 3 == 0 ? -1.0f : 1.0f;
+    for (int c = 0; c < H; ++c) {
+      x[(size_t)r * H + c] = q4o_f32_to_bf16(sign * fmaf(0.45f, splash_unit(&s), 0.55f));
+      residual[(size_t)r * H + c] = q4o_f32_to_bf16(0.1f * splash_unit(&s));
+    }
+  }
 }

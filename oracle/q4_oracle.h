@@ -155,6 +155,34 @@ void q4o_moe_forward(const uint16_t *x, const uint16_t *residual, int T, int H,
                      const uint16_t *dn_sb, int sb_dtype, uint16_t *h_out,
                      uint16_t *d_out, uint16_t *y, int nthreads);
 
+/* q4o_moe_forward with a shared expert: ids [T][k] hold routed experts and,
+ * in any slot, expert id E for the shared expert, whose weights are the sh_*
+ * arguments (MLX row-major like the routed ones; NULL: no shared expert). */
+void q4o_moe_forward_shared(const uint16_t *x, const uint16_t *residual, int T, int H, int I, int E, int k,
+                            const uint32_t *ids, const uint16_t *weights, const uint32_t *gu_wq,
+                            const uint16_t *gu_sb, const uint32_t *dn_wq, const uint16_t *dn_sb,
+                            const uint32_t *sh_gu_wq, const uint16_t *sh_gu_sb, const uint32_t *sh_dn_wq,
+                            const uint16_t *sh_dn_sb, int sb_dtype, uint16_t *h_out, uint16_t *d_out,
+                            uint16_t *y, int nthreads);
+/* Router scores of a Q8 projection in StorageN = 256 order (moe.metal:34-262),
+ * bf16 [T][ncols]; the fixed summation order is documented in q4_oracle.c. */
+void q4o_moe_scores_q8(const uint16_t *x, int T, int H, const uint8_t *q, const uint16_t *scales,
+                       const uint16_t *biases, int ncols, uint16_t *scores, int nthreads);
+/* The shared expert's routing weight (moe.metal:297-322): bf16 [T] sigmoid of
+ * the scalar gate (row 0 of a Q8 projection); logit [T] optional. */
+void q4o_moe_shared_gate(const uint16_t *x, int T, int H, const uint8_t *q, const uint16_t *scales,
+                         const uint16_t *biases, uint16_t *weights, float *logit);
+/* Grouping with a shared slot last in each token's rpr = k + 1 routes
+ * (moe.metal:368-449); rpr == k: as q4o_moe_group. */
+int q4o_moe_group_shared(const uint32_t *ids, int T, int k, int rpr, int E, int tile_rows, int max_tiles,
+                         uint32_t *tiles, uint32_t *grouped_routes, uint32_t *route_rows);
+/* The reference MoE test's fixture (moe_metal_test.mm:46-271): Splash slabs
+ * (q4o_slab_bytes each) of E gate, up and down experts and the shared
+ * expert's three projections, inputs and residuals bf16 [rows][H]. */
+void q4o_splash_moe_fixture(int H, int I, int E, int rows, uint64_t seed, uint8_t *gate, uint8_t *up,
+                            uint8_t *down, uint8_t *shared_gate, uint8_t *shared_up, uint8_t *shared_down,
+                            uint16_t *x, uint16_t *residual);
+
 /* ---- CPU baseline (the reference arm of bench.py) ---------------------- */
 /* The reference CPU semantics (dequantise on the fly, accumulate in f32),
  * vectorised and threaded over output rows.  y [m][out] f32.  Returns the

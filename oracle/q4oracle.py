@@ -108,6 +108,12 @@ def _declare(L) -> None:
         "q4o_moe_group": (c_int, [v, c_int, c_int, c_int, c_int, c_int, v, v, v]),
         "q4o_moe_forward": (None, [v, v, c_int, c_int, c_int, c_int, c_int, v, v, v, v, v, v,
                                    c_int, v, v, v, c_int]),
+        "q4o_moe_forward_shared": (None, [v, v, c_int, c_int, c_int, c_int, c_int, v, v, v, v, v, v,
+                                          v, v, v, v, c_int, v, v, v, c_int]),
+        "q4o_moe_scores_q8": (None, [v, c_int, c_int, v, v, v, c_int, v, c_int]),
+        "q4o_moe_shared_gate": (None, [v, c_int, c_int, v, v, v, v, v]),
+        "q4o_moe_group_shared": (c_int, [v, c_int, c_int, c_int, c_int, c_int, c_int, v, v, v]),
+        "q4o_splash_moe_fixture": (None, [c_int, c_int, c_int, c_int, c_uint64, v, v, v, v, v, v, v, v]),
         "q4o_cpu_linear": (c_int, [v, v, c_int, c_int, c_int, v, c_int, v, c_int]),
     }
     for name, (res, args) in sig.items():
@@ -337,8 +343,10 @@ def moe_group(ids, E: int, tile_rows: int, max_tiles: int | None = None):
 
 
 def moe_forward(x_bf16, residual_bf16, ids, weights_bf16, gu_wq, gu_sb, dn_wq, dn_sb, sb_dtype: int,
-                I: int, want_h: bool = False):
-    """One MoE layer on MLX row-major experts; returns (y, h, d) as bf16."""
+                I: int, want_h: bool = False, shared=None):
+    """One MoE layer on MLX row-major experts; returns (y, h, d) as bf16.
+    ``shared`` = (gu_wq, gu_sb, dn_wq, dn_sb) of the shared expert (one
+    expert, same shapes), which the id E selects in ``ids``."""
     x_bf16 = np.ascontiguousarray(x_bf16, dtype=np.uint16)
     T, H = x_bf16.shape
     k = ids.shape[1]
@@ -347,13 +355,100 @@ def moe_forward(x_bf16, residual_bf16, ids, weights_bf16, gu_wq, gu_sb, dn_wq, d
     d = np.empty((T * k, H), dtype=np.uint16)
     h = np.empty((T * k, I), dtype=np.uint16) if want_h else None
     res = None if residual_bf16 is None else np.ascontiguousarray(residual_bf16, dtype=np.uint16)
-    lib().q4o_moe_forward(_p(x_bf16), None if res is None else _p(res), T, H, I, E, k,
-                          _p(np.ascontiguousarray(ids, dtype=np.uint32)),
-                          _p(np.ascontiguousarray(weights_bf16, dtype=np.uint16)),
-                          _p(np.ascontiguousarray(gu_wq)), _p(np.ascontiguousarray(gu_sb)),
-                          _p(np.ascontiguousarray(dn_wq)), _p(np.ascontiguousarray(dn_sb)), sb_dtype,
-                          None if h is None else _p(h), _p(d), _p(y), threads())
+    sh = [None] * 4 if shared is None else [_p(np.ascontiguousarray(a)) for a in shared]
+    keep = shared
+    lib().q4o_moe_forward_shared(_p(x_bf16), None if res is None else _p(res), T, H, I, E, k,
+                                 _p(np.ascontiguousarray(ids, dtype=np.uint32)),
+                                 _p(np.ascontiguousarray(weights_bf16, dtype=np.uint16)),
+                                 _p(np.ascontiguousarray(gu_wq)), _p(np.ascontiguousarray(gu_sb)),
+                                 _p(np.ascontiguousarray(dn_wq)), _p(np.ascontiguousarray(dn_sb)),
+                                 sh[0], sh[1], sh[2], sh[3], sb_dtype,
+                                 None if h is None else _p(h), _p(d), _p(y), threads())
+    del keep
     return y, h, d
+
+
+# ---- the Q8 router and the shared expert (moe.metal:1-361) ---------------------
+
+Q8_STORAGE_N = 256
+
+
+def moe_scores_q8(x_bf16, q, scales, biases, ncols: int):
+    """Router scores bf16 [T][ncols] of a Q8 projection in StorageN = 256
+    order (q u8 [H/64 * 256 * 64], scales and biases bf16 [H/64 * 256])."""
+    x_bf16 = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T, H = x_bf16.shape
+    out = np.empty((T, ncols), dtype=np.uint16)
+    lib().q4o_moe_scores_q8(_p(x_bf16), T, H, _p(np.ascontiguousarray(q, dtype=np.uint8)),
+                            _p(np.ascontiguousarray(scales, dtype=np.uint16)),
+                            _p(np.ascontiguousarray(biases, dtype=np.uint16)), ncols, _p(out), threads())
+    return out
+
+
+def moe_shared_gate(x_bf16, q, scales, biases):
+    """The shared expert's routing weights bf16 [T] and gate logits f32 [T]."""
+    x_bf16 = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T, H = x_bf16.shape
+    w = np.empty(T, dtype=np.uint16)
+    logit = np.empty(T, dtype=np.float32)
+    lib().q4o_moe_shared_gate(_p(x_bf16), T, H, _p(np.ascontiguousarray(q, dtype=np.uint8)),
+                              _p(np.ascontiguousarray(scales, dtype=np.uint16)),
+                              _p(np.ascontiguousarray(biases, dtype=np.uint16)), _p(w), _p(logit))
+    return w, logit
+
+
+def moe_route_q8(x_bf16, E: int, k: int, router, shared_gate=None):
+    """The whole routing of Splash's MoE::add: scores from the Q8 router
+    (a (q, scales, biases) triple), top k of the E experts, and with a shared
+    expert gate a last slot per token holding expert E and its sigmoid weight.
+    Returns ids [T][rpr] u32, weights [T][rpr] bf16, scores bf16 [T][E]."""
+    scores = moe_scores_q8(x_bf16, *router, E)
+    ids, w = moe_select(scores, k)
+    if shared_gate is not None:
+        sw, _ = moe_shared_gate(x_bf16, *shared_gate)
+        ids = np.concatenate([ids, np.full((ids.shape[0], 1), E, dtype=np.uint32)], axis=1)
+        w = np.concatenate([w, sw[:, None]], axis=1)
+    return ids, w, scores
+
+
+def moe_max_tiles_shared(T: int, E: int, k: int, tile_rows: int, shared: bool) -> int:
+    """moeMaximumTiles (MoE.hpp:72-77): the routed bound plus the shared tiles."""
+    return moe_max_tiles(T, E, k, tile_rows) + ((T + tile_rows - 1) // tile_rows if shared else 0)
+
+
+def moe_group_shared(ids, k: int, E: int, tile_rows: int, max_tiles: int | None = None):
+    """Grouping of ids [T][rpr] whose slots past k are the shared expert's."""
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    T, rpr = ids.shape
+    if max_tiles is None:
+        max_tiles = moe_max_tiles_shared(T, E, k, tile_rows, rpr > k)
+    tiles = np.empty((max_tiles, 2), dtype=np.uint32)
+    grouped = np.empty(max_tiles * tile_rows, dtype=np.uint32)
+    route_rows = np.empty(T * rpr, dtype=np.uint32)
+    n = lib().q4o_moe_group_shared(_p(ids), T, k, rpr, E, tile_rows, max_tiles, _p(tiles), _p(grouped),
+                                   _p(route_rows))
+    if n < 0:
+        raise ValueError("max_tiles too small")
+    return tiles, n, grouped, route_rows
+
+
+SPLASH_MOE_SEED = 0x0E5
+
+
+def splash_moe_fixture(H: int, I: int, E: int, rows: int, seed: int = SPLASH_MOE_SEED):
+    """The expert slabs and rows of moe_metal_test.mm's makeFixture: a dict of
+    Splash slab arrays u8 ``gate``/``up``/``down`` [E, bytes] and
+    ``shared_gate``/``shared_up``/``shared_down`` [1, bytes], ``x`` and
+    ``residual`` bf16 [rows][H]."""
+    gs, ds = lib().q4o_slab_bytes(I, H), lib().q4o_slab_bytes(H, I)
+    f = {"gate": np.empty((E, gs), np.uint8), "up": np.empty((E, gs), np.uint8), "down": np.empty((E, ds), np.uint8),
+         "shared_gate": np.empty((1, gs), np.uint8), "shared_up": np.empty((1, gs), np.uint8),
+         "shared_down": np.empty((1, ds), np.uint8), "x": np.empty((rows, H), np.uint16),
+         "residual": np.empty((rows, H), np.uint16)}
+    lib().q4o_splash_moe_fixture(H, I, E, rows, seed, *[_p(f[n]) for n in ("gate", "up", "down", "shared_gate",
+                                                                             "shared_up", "shared_down", "x",
+                                                                             "residual")])
+    return f
 
 
 # ---- CPU baseline ---------------------------------------------------------------

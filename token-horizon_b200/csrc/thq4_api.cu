@@ -485,8 +485,10 @@ thq4_status thq4_moe_route(const void *logits, int T, int E, int k, uint32_t *id
   if (max_tiles < (int)moe_max_tiles(T, E, k))
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route: max_tiles below thq4_moe_max_tiles(T, E, k) = " +
                                                     std::to_string(moe_max_tiles(T, E, k)));
-  cudaError_t e = moe_route_launch(static_cast<const uint16_t *>(logits), T, E, k, ids, static_cast<uint16_t *>(weights),
-                                   tiles, grouped_routes, route_rows, ntiles, max_tiles, static_cast<cudaStream_t>(stream));
+  MoeRouting rt{};
+  rt.logits = static_cast<const uint16_t *>(logits);
+  cudaError_t e = moe_route_launch(rt, T, E, k, ids, static_cast<uint16_t *>(weights), tiles, grouped_routes, route_rows,
+                                   ntiles, max_tiles, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
 }
@@ -517,8 +519,10 @@ thq4_status thq4_moe(const void *x, const void *residual, const void *logits, in
     return set_error(THQ4_ERR_WORKSPACE, "thq4_moe: needs a 256-byte aligned workspace of " + std::to_string(need.bytes) +
                                              " bytes (thq4_moe_workspace_bytes), got " + std::to_string(workspace_bytes));
   const MoeWorkspace w = moe_workspace(T, H, I, E, k, workspace);
-  cudaError_t e = moe_launch(x, residual, logits, T, H, I, E, k, *gate, *up, *down, y, w,
-                             static_cast<cudaStream_t>(stream));
+  MoeRouting rt{};
+  rt.logits = static_cast<const uint16_t *>(logits);
+  const MoeSets sets{gate, up, down, nullptr, nullptr, nullptr};
+  cudaError_t e = moe_launch(x, residual, rt, T, H, I, E, k, sets, y, w, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
 }
@@ -552,10 +556,189 @@ thq4_status thq4_moe_partial(const void *x, const void *residual, const void *lo
                                              " bytes (thq4_moe_workspace_bytes with E = e1 - e0), got " +
                                              std::to_string(workspace_bytes));
   const MoeWorkspace w = moe_workspace(T, H, I, El, k, workspace);
-  cudaError_t e = moe_launch(x, residual, logits, T, H, I, E, k, *gate, *up, *down, y_part, w,
-                             static_cast<cudaStream_t>(stream), e0, e1, true);
+  MoeRouting rt{};
+  rt.logits = static_cast<const uint16_t *>(logits);
+  const MoeSets sets{gate, up, down, nullptr, nullptr, nullptr};
+  cudaError_t e = moe_launch(x, residual, rt, T, H, I, E, k, sets, y_part, w, static_cast<cudaStream_t>(stream), e0,
+                             e1, true);
   if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
+}
+
+// ---- the Splash MoE block: Q8 router, shared expert --------------------------
+
+namespace {
+thq4_status check_q8(const thq4_q8_weight *w, int in, const char *what, const char *who) {
+  const std::string pre = std::string(who) + ": " + what;
+  if (!w) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + " is NULL");
+  if (w->out != 256 || w->in != in)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + " is " + std::to_string(w->out) + " x " + std::to_string(w->in) +
+                                                    ", expected 256 x " + std::to_string(in));
+  if (!w->q || !w->scales || !w->biases || !aligned(w->q, 16) || !aligned(w->scales, 2) || !aligned(w->biases, 2))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + ": q must be 16-byte aligned, scales and biases non-NULL");
+  return THQ4_OK;
+}
+
+bool has_shared(const thq4_moe_weights *w) { return w->shared_expert_gate.q != nullptr; }
+bool runs_shared(const thq4_moe_weights *w) { return w->shared_gate.qw != nullptr; }
+
+// MoE::add's validate (MoE.cpp:14-58) for a call holding experts [e0, e1) of E.
+thq4_status check_moe_add(int T, int H, int I, int E, int k, int e0, int e1, const thq4_moe_weights *w,
+                          const char *who) {
+  if (!w) return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": weights are NULL");
+  if (T < 1 || H <= 0 || H % 256 || I <= 0 || I % 256 || E < 1 || E > 256 || k < 1 || k > E || k > 32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     std::string(who) + ": MoE weights do not match execution shape (need T >= 1, H and I multiples "
+                                        "of 256, 1 <= k <= E <= 256, k <= 32; T " + std::to_string(T) + ", H " +
+                         std::to_string(H) + ", I " + std::to_string(I) + ", E " + std::to_string(E) + ", k " +
+                         std::to_string(k) + ")");
+  if (e0 < 0 || e1 <= e0 || e1 > E)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": need 0 <= e0 < e1 <= E");
+  const int El = e1 - e0, rpr = k + (has_shared(w) ? 1 : 0);
+  if (moe_group_smem(T * rpr, El) > 200 * 1024)
+    return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": " + std::to_string((long long)T * rpr) +
+                                               " routes exceed the grouping kernel's shared memory");
+  thq4_status s;
+  if ((s = check_q8(&w->router, H, "router", who)) != THQ4_OK) return s;
+  if ((s = check_experts(&w->gate, El, I, H, "gate", who)) != THQ4_OK) return s;
+  if ((s = check_experts(&w->up, El, I, H, "up", who)) != THQ4_OK) return s;
+  if ((s = check_experts(&w->down, El, H, I, "down", who)) != THQ4_OK) return s;
+  const int dt = w->gate.sb_dtype;
+  if (w->up.sb_dtype != dt || w->down.sb_dtype != dt)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": expert scale dtypes differ");
+  if (runs_shared(w) && !has_shared(w))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": a shared expert needs its shared_expert_gate");
+  if (has_shared(w) && (s = check_q8(&w->shared_expert_gate, H, "shared_expert_gate", who)) != THQ4_OK) return s;
+  if (runs_shared(w)) {
+    if ((s = check_experts(&w->shared_gate, 1, I, H, "shared gate", who)) != THQ4_OK) return s;
+    if ((s = check_experts(&w->shared_up, 1, I, H, "shared up", who)) != THQ4_OK) return s;
+    if ((s = check_experts(&w->shared_down, 1, H, I, "shared down", who)) != THQ4_OK) return s;
+    if (w->shared_gate.sb_dtype != dt || w->shared_up.sb_dtype != dt || w->shared_down.sb_dtype != dt)
+      return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": expert scale dtypes differ");
+  }
+  return THQ4_OK;
+}
+
+thq4_status moe_add_common(const void *x, const void *residual, int T, int H, int I, int E, int k, int e0, int e1,
+                           const thq4_moe_weights *w, void *y, bool y_f32, void *workspace, size_t workspace_bytes,
+                           void *stream, const char *who) {
+  thq4_status s = check_moe_add(T, H, I, E, k, e0, e1, w, who);
+  if (s != THQ4_OK) return s;
+  if (!x || !y || !aligned(x, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": x, y (and residual) must be 16-byte aligned");
+  const int El = e1 - e0, rpr = k + (has_shared(w) ? 1 : 0);
+  const MoeWorkspace need = moe_workspace(T, H, I, El, k, nullptr, rpr, runs_shared(w), E);
+  if (!workspace || workspace_bytes < need.bytes || !aligned(workspace, 256))
+    return set_error(THQ4_ERR_WORKSPACE, std::string(who) + ": MoE grouped scratch is smaller than its bound (needs a "
+                                                            "256-byte aligned workspace of " +
+                                             std::to_string(need.bytes) + " bytes, thq4_moe_add_workspace_bytes; got " +
+                                             std::to_string(workspace_bytes) + ")");
+  const MoeWorkspace ws = moe_workspace(T, H, I, El, k, workspace, rpr, runs_shared(w), E);
+  MoeRouting rt{};
+  rt.x = x;
+  rt.H = H;
+  rt.router = &w->router;
+  rt.shared_gate = has_shared(w) ? &w->shared_expert_gate : nullptr;
+  rt.shared_local = runs_shared(w);
+  rt.partial = ws.partial;
+  const MoeSets sets{&w->gate, &w->up, &w->down, &w->shared_gate, &w->shared_up, &w->shared_down};
+  cudaError_t e = moe_launch(x, residual, rt, T, H, I, E, k, sets, y, ws, static_cast<cudaStream_t>(stream), e0, e1,
+                             y_f32);
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+}  // namespace
+
+size_t thq4_moe_scores_workspace_bytes(int T, int ncols) {
+  if (T <= 0 || ncols <= 0) return 0;
+  return moe_scores_bytes(T, ncols);
+}
+
+thq4_status thq4_moe_scores_q8(const void *x, int T, const thq4_q8_weight *router, int ncols, void *scores, int ld,
+                               void *workspace, size_t workspace_bytes, void *stream) {
+  const char *who = "thq4_moe_scores_q8";
+  if (!router) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_scores_q8: router is NULL");
+  if (T < 1 || ncols < 1 || ncols > 256 || ld < ncols || router->in <= 0 || router->in % kGroup)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_scores_q8: need T >= 1, 1 <= ncols <= 256, ld >= ncols, "
+                                                "router input a positive multiple of 64");
+  thq4_status s = check_q8(router, router->in, "router", who);
+  if (s != THQ4_OK) return s;
+  if (!x || !scores || !aligned(x, 16) || !aligned(scores, 2))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_scores_q8: x must be 16-byte aligned, scores non-NULL");
+  if (!workspace || workspace_bytes < moe_scores_bytes(T, ncols) || !aligned(workspace, 16))
+    return set_error(THQ4_ERR_WORKSPACE, "thq4_moe_scores_q8: needs a 16-byte aligned workspace of " +
+                                             std::to_string(moe_scores_bytes(T, ncols)) + " bytes");
+  cudaError_t e = moe_scores_launch(x, T, router->in, *router, ncols, static_cast<float *>(workspace),
+                                    static_cast<uint16_t *>(scores), ld, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+uint32_t thq4_moe_add_max_tiles(int T, int E, int k, int shared) {
+  if (T <= 0 || E <= 0 || k <= 0) return 0;
+  return moe_max_tiles(T, E, k, shared != 0);
+}
+
+thq4_status thq4_moe_route_q8(const void *x, int T, int E, int k, const thq4_q8_weight *router,
+                              const thq4_q8_weight *shared_expert_gate, uint32_t *ids, void *weights, uint32_t *tiles,
+                              uint32_t *grouped_routes, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
+                              void *workspace, size_t workspace_bytes, void *stream) {
+  const char *who = "thq4_moe_route_q8";
+  if (T < 1 || E < 1 || E > 256 || k < 1 || k > E || k > 32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route_q8: need T >= 1, 1 <= k <= E <= 256, k <= 32");
+  if (!router) return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route_q8: router is NULL");
+  const int H = router->in;
+  if (H <= 0 || H % kGroup)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route_q8: router input must be a positive multiple of 64");
+  thq4_status s = check_q8(router, H, "router", who);
+  if (s != THQ4_OK) return s;
+  if (shared_expert_gate && (s = check_q8(shared_expert_gate, H, "shared_expert_gate", who)) != THQ4_OK) return s;
+  const int rpr = k + (shared_expert_gate ? 1 : 0);
+  if (moe_group_smem(T * rpr, E) > 200 * 1024)
+    return set_error(THQ4_ERR_UNSUPPORTED, "thq4_moe_route_q8: too many routes for the grouping kernel");
+  if (!x || !ids || !weights || !tiles || !grouped_routes || !route_rows || !ntiles || !aligned(x, 16) ||
+      !aligned(weights, 2) || !aligned(ids, 4) || !aligned(tiles, 4) || !aligned(grouped_routes, 4) ||
+      !aligned(route_rows, 4) || !aligned(ntiles, 4))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route_q8: NULL or misaligned buffer");
+  const uint32_t need_tiles = moe_max_tiles(T, E, k, shared_expert_gate != nullptr);
+  if (max_tiles < (int)need_tiles)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_moe_route_q8: max_tiles below thq4_moe_add_max_tiles = " +
+                                                    std::to_string(need_tiles));
+  if (!workspace || workspace_bytes < moe_scores_bytes(T, E) || !aligned(workspace, 16))
+    return set_error(THQ4_ERR_WORKSPACE, "thq4_moe_route_q8: needs a 16-byte aligned workspace of " +
+                                             std::to_string(moe_scores_bytes(T, E)) + " bytes");
+  MoeRouting rt{};
+  rt.x = x;
+  rt.H = H;
+  rt.router = router;
+  rt.shared_gate = shared_expert_gate;
+  rt.shared_local = true;
+  rt.partial = static_cast<float *>(workspace);
+  cudaError_t e = moe_route_launch(rt, T, E, k, ids, static_cast<uint16_t *>(weights), tiles, grouped_routes,
+                                   route_rows, ntiles, max_tiles, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+size_t thq4_moe_add_workspace_bytes(int T, int H, int I, int E, int k, int shared) {
+  if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return 0;
+  return moe_workspace(T, H, I, E, k, nullptr, k + (shared ? 1 : 0), shared != 0, E).bytes;
+}
+
+thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int I, int E, int k,
+                         const thq4_moe_weights *w, void *y, void *workspace, size_t workspace_bytes, void *stream) {
+  const char *who = "thq4_moe_add";
+  if (w && has_shared(w) != runs_shared(w))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_moe_add: MoE weights do not match execution shape (shared expert and its gate go together)");
+  return moe_add_common(x, residual, T, H, I, E, k, 0, E, w, y, false, workspace, workspace_bytes, stream, who);
+}
+
+thq4_status thq4_moe_add_partial(const void *x, const void *residual, int T, int H, int I, int E, int k, int e0,
+                                 int e1, const thq4_moe_weights *w, float *y_part, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+  return moe_add_common(x, residual, T, H, I, E, k, e0, e1, w, y_part, true, workspace, workspace_bytes, stream,
+                        "thq4_moe_add_partial");
 }
 
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {

@@ -103,10 +103,13 @@ constexpr int kMoeTileRows = 32;
 // expert(tiles[2gt])^T (w1: the fused SwiGLU with w0 = gate, w1 = up).
 // xsum [tile][in/64][32] holds the sum of each x row's 64-groups; ysum
 // (optional) receives the same for y.  x, y: [max_tiles*32][in], [..][out].
+// Tiles of expert id n_experts run the shared expert (sw0, sw1: one expert each).
 struct MoeExperts {
   const void *x;
   void *y;
   const thq4_experts *w0, *w1;
+  const thq4_experts *sw0, *sw1;
+  int n_experts;
   const uint32_t *tiles, *count;
   const float *xsum;
   float *ysum;
@@ -114,28 +117,61 @@ struct MoeExperts {
 };
 cudaError_t moe_expert_launch(const MoeExperts &g, cudaStream_t stream);
 
-// Upper bound on group tiles for T tokens routed to k of E experts.
-uint32_t moe_max_tiles(int T, int E, int k);
+// Upper bound on group tiles for T tokens routed to k of E experts, plus
+// ceil(T/32) tiles of a shared expert.
+uint32_t moe_max_tiles(int T, int E, int k, bool shared = false);
 // Shared memory of the grouping kernel for R routes and E experts.
 size_t moe_group_smem(int R, int E);
-// Select (top-k, softmax weights) and group (stable counting sort) on the device.
-// Experts [e0, e1) of E are grouped (e1 < 0: all); the tiles hold local ids.
-cudaError_t moe_route_launch(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights,
+// Eight K slices of router partial sums per (token, column).
+constexpr int kRouteSlices = 8;
+size_t moe_scores_bytes(int T, int ncols);
+
+// Where a layer's routing comes from: bf16 logits [T][E], or the Q8 router
+// applied to x (partial: [8][T][E] f32 scratch).  With a shared expert gate
+// every token gets a last route (id E); shared_local: this call runs the
+// shared expert (its tiles carry the local id e1 - e0), otherwise that route
+// is dropped here.
+struct MoeRouting {
+  const uint16_t *logits;
+  const void *x;
+  int H;
+  const thq4_q8_weight *router;
+  const thq4_q8_weight *shared_gate;
+  bool shared_local;
+  float *partial;
+};
+// Router partial sums and, when scores is not null, the bf16 scores.
+cudaError_t moe_scores_launch(const void *x, int T, int H, const thq4_q8_weight &router, int ncols, float *partial,
+                              uint16_t *scores, int ld, cudaStream_t stream);
+// Select (top-k, softmax weights, the shared route) and group (stable
+// counting sort) on the device.  Experts [e0, e1) of E are grouped (e1 < 0:
+// all); the tiles hold local ids.
+cudaError_t moe_route_launch(const MoeRouting &r, int T, int E, int k, uint32_t *ids, uint16_t *weights,
                              uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
                              cudaStream_t stream, int e0 = 0, int e1 = -1);
 // The MoE layer's scratch, carved from one caller buffer (nullptr: sizes only).
+// rpr routes per token (k, or k + 1 with a shared expert); shared_local adds
+// the shared expert's tiles; router_cols > 0 reserves the router's partials.
 struct MoeWorkspace {
   uint32_t *ids, *tiles, *grouped, *route_rows, *ntiles;
   uint16_t *weights, *xg, *h, *d;
   float *xsum, *hsum;  // group sums of xg and h: [tile][groups][32]
+  float *partial;      // router partials [8][T][router_cols]
   size_t bytes;
   int max_tiles;
 };
-MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base);
+MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base, int rpr = -1, bool shared_local = false,
+                           int router_cols = 0);
+// The expert sets of one call: routed (gate, up, down) and, optionally, the
+// shared expert's (one expert each).
+struct MoeSets {
+  const thq4_experts *gate, *up, *down;
+  const thq4_experts *sgate, *sup, *sdown;
+};
 // The layer (y bf16) or, for an expert shard [e0, e1), its f32 partial.
-cudaError_t moe_launch(const void *x, const void *residual, const void *logits, int T, int H, int I, int E, int k,
-                       const thq4_experts &gate, const thq4_experts &up, const thq4_experts &down, void *y,
-                       const MoeWorkspace &w, cudaStream_t stream, int e0 = 0, int e1 = -1, bool y_f32 = false);
+cudaError_t moe_launch(const void *x, const void *residual, const MoeRouting &r, int T, int H, int I, int E, int k,
+                       const MoeSets &sets, void *y, const MoeWorkspace &w, cudaStream_t stream, int e0 = 0,
+                       int e1 = -1, bool y_f32 = false);
 
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,

@@ -52,6 +52,8 @@ struct MgArgs {
   const uint8_t *qw[2];  // gate (or the only) experts, up experts: expert e at + e * stride
   const uint8_t *sb[2];
   uint64_t qw_stride[2], sb_stride[2];
+  const uint8_t *shq[2], *shsb[2];  // the shared expert's, which tiles of id n_experts run
+  int n_experts;
   const uint32_t *tiles;   // [2 gt]: expert, [2 gt + 1]: live rows
   const uint32_t *ntiles;  // group tiles in use (device)
   const float *xsum;       // [tile][ng][32]: sum of each row's group of x
@@ -246,7 +248,12 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
     int it = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int gt = u / a.n_slabs, sl = u - gt * a.n_slabs;
-      const uint32_t e = a.tiles[2 * gt];
+      uint32_t e = a.tiles[2 * gt];
+      const bool shared = e == (uint32_t)a.n_experts && a.shq[0] != nullptr;
+      if (e >= (uint32_t)a.n_experts && !shared) {  // never produced by the grouping kernel
+        raise_status(a.status, kStatusBadExpert);
+        e = 0;
+      }
       for (int c = 0; c < cpu; ++c, ++it) {
         const int s = it % R;
         if (it >= R && !mbar_wait_bounded(&empty[s], (uint32_t)(((it / R) - 1) & 1), kWaitLimitNs)) {
@@ -261,9 +268,10 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
         const size_t sg = (size_t)sl * a.ng + g0;
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
-          bulk_g2s(st + St::nib_off + si * kMgCB * 4096, a.qw[si] + e * a.qw_stride[si] + sg * 4096, cnt * 4096, &full[s],
-                   pol);
-          bulk_g2s(st + St::sb_off + si * kMgCB * 512, a.sb[si] + e * a.sb_stride[si] + sg * 512, cnt * 512, &full[s], pol);
+          const uint8_t *qb = shared ? a.shq[si] : a.qw[si] + e * a.qw_stride[si];
+          const uint8_t *sbb = shared ? a.shsb[si] : a.sb[si] + e * a.sb_stride[si];
+          bulk_g2s(st + St::nib_off + si * kMgCB * 4096, qb + sg * 4096, cnt * 4096, &full[s], pol);
+          bulk_g2s(st + St::sb_off + si * kMgCB * 512, sbb + sg * 512, cnt * 512, &full[s], pol);
         }
         bulk_g2s_plain(st + St::xs_off, a.xsum + ((size_t)gt * a.ng + g0) * kMoeTileRows, cnt * 128, &full[s]);
       }
@@ -375,6 +383,12 @@ cudaError_t moe_expert_launch(const MoeExperts &g, cudaStream_t stream) {
   a.sb_stride[0] = g.w0->sb_stride;
   a.qw_stride[1] = gate_up ? g.w1->qw_stride : 0;
   a.sb_stride[1] = gate_up ? g.w1->sb_stride : 0;
+  a.n_experts = g.n_experts > 0 ? g.n_experts : g.w0->experts;
+  a.shq[0] = g.sw0 ? static_cast<const uint8_t *>(g.sw0->qw) : nullptr;
+  a.shsb[0] = g.sw0 ? static_cast<const uint8_t *>(g.sw0->sb) : nullptr;
+  a.shq[1] = g.sw1 ? static_cast<const uint8_t *>(g.sw1->qw) : nullptr;
+  a.shsb[1] = g.sw1 ? static_cast<const uint8_t *>(g.sw1->sb) : nullptr;
+  if (gate_up && (a.shq[0] != nullptr) != (a.shq[1] != nullptr)) return cudaErrorInvalidValue;
   a.tiles = g.tiles;
   a.ntiles = g.count;
   a.xsum = g.xsum;

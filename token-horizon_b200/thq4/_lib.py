@@ -52,6 +52,17 @@ class thq4_experts(ctypes.Structure):
                 ("sb_stride", ctypes.c_uint64)]
 
 
+class thq4_q8_weight(ctypes.Structure):
+    _fields_ = [("out", ctypes.c_int32), ("in_", ctypes.c_int32), ("q", c_void_p), ("scales", c_void_p),
+                ("biases", c_void_p)]
+
+
+class thq4_moe_weights(ctypes.Structure):
+    _fields_ = [("router", thq4_q8_weight), ("gate", thq4_experts), ("up", thq4_experts), ("down", thq4_experts),
+                ("shared_gate", thq4_experts), ("shared_up", thq4_experts), ("shared_down", thq4_experts),
+                ("shared_expert_gate", thq4_q8_weight)]
+
+
 class thq4_peer_gather(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("rows", ctypes.c_int32),
                 ("offset", ctypes.c_int32), ("stride", ctypes.c_int32), ("wait", ctypes.c_int32),
@@ -87,6 +98,18 @@ SIGNATURES = {
     "thq4_moe_partial": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  POINTER(thq4_experts), POINTER(thq4_experts), POINTER(thq4_experts), c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
+    "thq4_moe_scores_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "thq4_moe_scores_q8": (c_int, [c_void_p, c_int, POINTER(thq4_q8_weight), c_int, c_void_p, c_int, c_void_p,
+                                   c_size_t, c_void_p]),
+    "thq4_moe_add_max_tiles": (c_uint32, [c_int, c_int, c_int, c_int]),
+    "thq4_moe_route_q8": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(thq4_q8_weight), POINTER(thq4_q8_weight),
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                                  c_size_t, c_void_p]),
+    "thq4_moe_add_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "thq4_moe_add": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(thq4_moe_weights),
+                             c_void_p, c_void_p, c_size_t, c_void_p]),
+    "thq4_moe_add_partial": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                     POINTER(thq4_moe_weights), c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_peer": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
                                  c_void_p, c_size_t, POINTER(thq4_peer_gather), c_void_p]),
     "thq4_peer_wait": (c_int, [POINTER(thq4_peer_gather), c_void_p]),

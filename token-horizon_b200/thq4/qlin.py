@@ -344,3 +344,136 @@ def moe(x: torch.Tensor, logits: torch.Tensor, k: int, gate: PackedExperts, up: 
                      ctypes.byref(gate.desc), ctypes.byref(up.desc), ctypes.byref(down.desc), _ptr(y), _ptr(ws),
                      ws.numel(), _stream()))
     return y
+
+
+# -- the Splash MoE block: Q8 router and shared expert (MoE.hpp:15-44) ----------
+
+class Q8Projection:
+    """Splash's Q8Projection (docs/splash/runtime/ops/Linear.hpp:27-33): 8-bit
+    affine weights in StorageN = 256 order -- the byte of output n and input
+    k at ((k/64)*256 + n)*64 + k%64, the bf16 scale and bias at (k/64)*256 +
+    n -- on the device.  Used as the MoE router and the shared expert's
+    scalar gate (row 0)."""
+
+    def __init__(self, q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, inp: int, out: int = 256):
+        self.q = q.contiguous().view(torch.uint8)
+        self.scales = scales.contiguous()
+        self.biases = biases.contiguous()
+        self.out, self.inp = out, inp
+        self.desc = _lib.thq4_q8_weight(out, inp, self.q.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr())
+
+    @classmethod
+    def from_section(cls, packed: torch.Tensor, inp: int, out: int = 256) -> "Q8Projection":
+        """One package section (out*inp weight bytes, then the bf16 scales,
+        then the bf16 biases: WeightStore.cpp:264-282) on the device."""
+        elements = out * inp
+        pb = elements // 32
+        packed = packed.contiguous().view(torch.uint8)
+        return cls(packed[:elements], packed[elements:elements + pb].view(torch.bfloat16),
+                   packed[elements + pb:elements + 2 * pb].view(torch.bfloat16), inp, out)
+
+
+class MoeWeights:
+    """All weights of one sparse MoE block, the host mirror of Splash's
+    MoeWeights (MoE.hpp:35-44): the router, the routed experts and,
+    optionally, the shared expert (one-expert gate / up / down) with its
+    scalar gate.  For an expert shard, gate / up / down hold the shard's
+    experts and the shared projections are given on the rank that runs the
+    shared expert (the shared expert gate on every rank)."""
+
+    def __init__(self, router: Q8Projection, gate: PackedExperts, up: PackedExperts, down: PackedExperts,
+                 shared_gate: Optional[PackedExperts] = None, shared_up: Optional[PackedExperts] = None,
+                 shared_down: Optional[PackedExperts] = None, shared_expert_gate: Optional[Q8Projection] = None):
+        self.router, self.gate, self.up, self.down = router, gate, up, down
+        self.shared_gate, self.shared_up, self.shared_down = shared_gate, shared_up, shared_down
+        self.shared_expert_gate = shared_expert_gate
+        d = _lib.thq4_moe_weights()
+        d.router = router.desc
+        d.gate, d.up, d.down = gate.desc, up.desc, down.desc
+        if shared_gate is not None:
+            d.shared_gate, d.shared_up, d.shared_down = shared_gate.desc, shared_up.desc, shared_down.desc
+        if shared_expert_gate is not None:
+            d.shared_expert_gate = shared_expert_gate.desc
+        self.desc = d
+
+    @property
+    def has_shared(self) -> bool:
+        return self.shared_expert_gate is not None
+
+    @property
+    def runs_shared(self) -> bool:
+        return self.shared_gate is not None
+
+
+def _moe_ws(key, need: int, device) -> torch.Tensor:
+    ws = _MOE_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _MOE_WS[key] = ws
+    return ws
+
+
+def moe_scores_q8(x: torch.Tensor, router: Q8Projection, ncols: int = 256) -> torch.Tensor:
+    """Router scores bf16 [T, ncols] (moe_route_scores_q8, moe.metal:34-262)."""
+    T = x.shape[0]
+    L = _lib.lib()
+    ws = _moe_ws(("scores", x.device.index, torch.cuda.current_stream(x.device).cuda_stream),
+                 L.thq4_moe_scores_workspace_bytes(T, ncols), x.device)
+    s = torch.empty((T, ncols), dtype=torch.bfloat16, device=x.device)
+    check(L.thq4_moe_scores_q8(_ptr(x.contiguous()), T, ctypes.byref(router.desc), ncols, _ptr(s), ncols, _ptr(ws),
+                               ws.numel(), _stream()))
+    return s
+
+
+def moe_route_q8(x: torch.Tensor, router: Q8Projection, E: int, k: int,
+                 shared_expert_gate: Optional[Q8Projection] = None):
+    """The routing of MoE::add on the device: ids [T, rpr] u32, weights
+    [T, rpr] bf16 (rpr = k, + 1 with a shared expert), tiles [n, 2],
+    grouped_routes [n*32], route_rows [T*rpr]."""
+    T = x.shape[0]
+    L = _lib.lib()
+    sh = shared_expert_gate is not None
+    rpr = k + int(sh)
+    mt = L.thq4_moe_add_max_tiles(T, E, k, int(sh))
+    dev = x.device
+    ids = torch.empty((T, rpr), dtype=torch.int32, device=dev)
+    w = torch.empty((T, rpr), dtype=torch.bfloat16, device=dev)
+    tiles = torch.empty((mt, 2), dtype=torch.int32, device=dev)
+    grouped = torch.empty(mt * 32, dtype=torch.int32, device=dev)
+    rows = torch.empty(T * rpr, dtype=torch.int32, device=dev)
+    n = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _moe_ws(("scores", dev.index, torch.cuda.current_stream(dev).cuda_stream),
+                 L.thq4_moe_scores_workspace_bytes(T, E), dev)
+    check(L.thq4_moe_route_q8(_ptr(x.contiguous()), T, E, k, ctypes.byref(router.desc),
+                              ctypes.byref(shared_expert_gate.desc) if sh else None, _ptr(ids), _ptr(w), _ptr(tiles),
+                              _ptr(grouped), _ptr(rows), _ptr(n), mt, _ptr(ws), ws.numel(), _stream()))
+    nt = int(n.item())
+    return ids, w, tiles[:nt], grouped[:nt * 32], rows
+
+
+def moe_add(x: torch.Tensor, weights: MoeWeights, k: int, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One MoE block (MoE::add, MoE.cpp:119-231): bf16 [T, H]."""
+    T, H = x.shape
+    E, I = weights.gate.experts, weights.gate.rows
+    L = _lib.lib()
+    need = L.thq4_moe_add_workspace_bytes(T, H, I, E, k, int(weights.runs_shared))
+    ws = _moe_ws(("add", x.device.index, torch.cuda.current_stream(x.device).cuda_stream), need, x.device)
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    check(L.thq4_moe_add(_ptr(x.contiguous()), _ptr(residual), T, H, I, E, k, ctypes.byref(weights.desc), _ptr(y),
+                         _ptr(ws), ws.numel(), _stream()))
+    return y
+
+
+def moe_add_partial(x: torch.Tensor, weights: MoeWeights, k: int, e0: int, E: int,
+                    residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """An expert shard's part of one MoE block: the shard holds routed
+    experts [e0, e0 + weights.gate.experts) of E; f32 [T, H]."""
+    T, H = x.shape
+    El, I = weights.gate.experts, weights.gate.rows
+    L = _lib.lib()
+    need = L.thq4_moe_add_workspace_bytes(T, H, I, El, k, int(weights.runs_shared))
+    ws = _moe_ws(("add_partial", x.device.index, torch.cuda.current_stream(x.device).cuda_stream), need, x.device)
+    y = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    check(L.thq4_moe_add_partial(_ptr(x.contiguous()), _ptr(residual), T, H, I, E, k, e0, e0 + El,
+                                 ctypes.byref(weights.desc), _ptr(y), _ptr(ws), ws.numel(), _stream()))
+    return y
