@@ -502,11 +502,24 @@ def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
     return out
 
 
+def synthetic_router(torch, H, dev, seed):
+    """A random Q8 router (StorageN = 256 order) for the MoE block."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    G = H // 64
+    q = torch.randint(0, 256, (G * 256 * 64,), dtype=torch.uint8, device=dev, generator=g)
+    sc = (torch.rand((G * 256,), device=dev, generator=g) * 0.0035 + 0.0005).to(torch.bfloat16)
+    bi = (torch.randn((G * 256,), device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    return q, sc, bi
+
+
 def bench_moe(torch, thq4, synth, dev, hbm_peak):
     """T = 256 tokens, H = 2048, E = 128 experts, top-8,
-    I = 768, Q4 f16 scale/bias -> expert-weight GB/s (339,738,624 algorithmic
-    bytes, every expert touched) and us per layer (routing, gather, grouped
-    gate/up and down products, combine).  Two expert sets (680 MB) rotate."""
+    I = 768, Q4 f16 scale/bias, through thq4_moe_add (MoE::add: the Q8
+    router, routing, gather, grouped gate/up and down products, combine; no
+    shared expert, as the config has none) -> expert-weight GB/s (339,738,624
+    algorithmic bytes, every expert touched) and us per layer.  Two expert
+    sets (680 MB) rotate."""
     T, H, I, E, k = 256, 2048, 768, 128, 8
     sets = []
     for s in range(2):
@@ -521,29 +534,31 @@ def bench_moe(torch, thq4, synth, dev, hbm_peak):
                      thq4.PackedExperts.from_mlx(dn_wq, dn_sb, thq4.F16)))
         del gu_wq, gu_sb, dn_wq, dn_sb
     x = torch.randn((T, H), device=dev).to(torch.bfloat16)
-    logits = torch.randn((T, E), device=dev).to(torch.bfloat16)
+    blocks = [thq4.MoeWeights(thq4.Q8Projection(*synthetic_router(torch, H, dev, 77 + i), H), g, u, d)
+              for i, (g, u, d) in enumerate(sets)]
 
     def call():
-        for g, u, d in sets:
-            thq4.moe(x, logits, k, g, u, d)
+        for w in blocks:
+            thq4.moe_add(x, w, k)
 
     ms = _time_ms(torch, call, 10) / len(sets)
     nbytes = E * (2 * I * H + H * I) * Q4_BYTES_PER_WEIGHT
     gbs = nbytes / (ms * 1e-3) / 1e9
-    return {"config": "T 256, H 2048, E 128, k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
+    return {"config": "T 256, H 2048, E 128, k 8, I 768, Q4 f16 scale/bias, Q8 router", "us": round(ms * 1e3, 2),
             "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
-            "kernel": "moe_gemv_kernel (grouped small-tile mma.sync experts) + routing / gather / combine"}
+            "kernel": "thq4_moe_add: route_scores_kernel (Q8 router) + select / group / gather + moe_gemv_kernel "
+                      "(grouped small-tile mma.sync experts) + combine"}
 
 
 def bench_moe_sharded(torch, thq4, synth, dev, hbm_peak, world, rank, local):
     """BASELINE configs[4] with the experts split E/N per GPU: every rank
-    routes all 256 tokens (bit-identically), runs its experts' routes
-    (thq4_moe_partial, f32 partial) and one NCCL all-reduce sums the
-    partials; whole-job expert-weight GB/s and us per layer, max over ranks.
-    Two expert sets rotate."""
+    routes all 256 tokens through the same Q8 router (bit-identically), runs
+    its experts' routes (thq4_moe_add_partial, f32 partial) and one NCCL
+    all-reduce sums the partials; whole-job expert-weight GB/s and us per
+    layer, max over ranks.  Two expert sets rotate."""
     import torch.distributed as dist
 
-    from thq4.shard import expert_range, moe_sharded
+    from thq4.shard import expert_range, moe_add_sharded
 
     T, H, I, E, k = 256, 2048, 768, 128, 8
     e0, n = expert_range(E, world, rank)
@@ -562,11 +577,12 @@ def bench_moe_sharded(torch, thq4, synth, dev, hbm_peak, world, rank, local):
     g = torch.Generator(device=dev)
     g.manual_seed(1234)  # the same activations and logits on every rank
     x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
-    logits = torch.randn((T, E), device=dev, generator=g).to(torch.bfloat16)
+    blocks = [thq4.MoeWeights(thq4.Q8Projection(*synthetic_router(torch, H, dev, 77 + i), H), gt, up, dn)
+              for i, (gt, up, dn) in enumerate(sets)]
 
     def call():
-        for gt, up, dn in sets:
-            moe_sharded(x, logits, k, e0, gt, up, dn)
+        for w in blocks:
+            moe_add_sharded(x, w, k, e0, E)
 
     for _ in range(3):
         call()
@@ -585,7 +601,7 @@ def bench_moe_sharded(torch, thq4, synth, dev, hbm_peak, world, rank, local):
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"config": f"T 256, H 2048, E 128 ({n} per GPU), k 8, I 768, Q4 f16 scale/bias", "us": round(ms * 1e3, 2),
             "weight_gbs": round(gbs, 1), "frac": round(gbs / (hbm_peak * world), 4), "bytes": int(nbytes),
-            "kernel": "moe_gemv_kernel per expert shard + NCCL all-reduce of the f32 partials"}
+            "kernel": "thq4_moe_add_partial per expert shard + NCCL all-reduce of the f32 partials"}
 
 
 # ---------------------------------------------------------------------------

@@ -285,8 +285,7 @@ thq4_status thq4_moe_route_q8(const void *x, int T, int E, int k, const thq4_q8_
                               const thq4_q8_weight *shared_expert_gate, uint32_t *ids, void *weights, uint32_t *tiles,
                               uint32_t *grouped_routes, uint32_t *route_rows, uint32_t *ntiles, int max_tiles,
                               void *workspace, size_t workspace_bytes, void *stream);
-/* Workspace bytes of thq4_moe_add / thq4_moe_add_partial (E = the experts
- * this call holds; shared: it runs the shared expert). */
+/* Workspace bytes of thq4_moe_add (shared: the block has a shared expert). */
 size_t thq4_moe_add_workspace_bytes(int T, int H, int I, int E, int k, int shared);
 /* One MoE block (replaces MoE::add, MoE.cpp:119-231): routing as
  * thq4_moe_route_q8, then y bf16 [T][H] = residual (optional) + the sum over
@@ -347,12 +346,17 @@ thq4_status thq4_moe_partial(const void *x, const void *residual, const void *lo
                              const thq4_experts *down, float *y_part, void *workspace, size_t workspace_bytes,
                              void *stream);
 
+/* Workspace bytes of thq4_moe_add_partial for a shard holding experts
+ * [e0, e1) of E; shared_route: the layer has a shared expert (every token k +
+ * 1 routes); runs_shared: this shard runs it. */
+size_t thq4_moe_add_partial_workspace_bytes(int T, int H, int I, int E, int k, int e0, int e1, int shared_route,
+                                            int runs_shared);
 /* thq4_moe_add for an expert shard: w holds routed experts [e0, e1) of E
  * (gate, up, down: e1 - e0 experts), the full router and, when
  * shared_expert_gate.q is not NULL, the layer's shared expert gate (every
  * token then has k + 1 routes); the shard runs the shared expert when
  * w->shared_gate.qw is not NULL (one rank of the group).  y_part f32 [T][H]
- * as thq4_moe_partial. */
+ * as thq4_moe_partial.  Workspace: thq4_moe_add_partial_workspace_bytes. */
 thq4_status thq4_moe_add_partial(const void *x, const void *residual, int T, int H, int I, int E, int k, int e0,
                                  int e1, const thq4_moe_weights *w, float *y_part, void *workspace,
                                  size_t workspace_bytes, void *stream);

@@ -631,7 +631,7 @@ thq4_status moe_add_common(const void *x, const void *residual, int T, int H, in
   if (!workspace || workspace_bytes < need.bytes || !aligned(workspace, 256))
     return set_error(THQ4_ERR_WORKSPACE, std::string(who) + ": MoE grouped scratch is smaller than its bound (needs a "
                                                             "256-byte aligned workspace of " +
-                                             std::to_string(need.bytes) + " bytes, thq4_moe_add_workspace_bytes; got " +
+                                             std::to_string(need.bytes) + " bytes; got " +
                                              std::to_string(workspace_bytes) + ")");
   const MoeWorkspace ws = moe_workspace(T, H, I, El, k, workspace, rpr, runs_shared(w), E);
   MoeRouting rt{};
@@ -723,6 +723,12 @@ thq4_status thq4_moe_route_q8(const void *x, int T, int E, int k, const thq4_q8_
 size_t thq4_moe_add_workspace_bytes(int T, int H, int I, int E, int k, int shared) {
   if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return 0;
   return moe_workspace(T, H, I, E, k, nullptr, k + (shared ? 1 : 0), shared != 0, E).bytes;
+}
+
+size_t thq4_moe_add_partial_workspace_bytes(int T, int H, int I, int E, int k, int e0, int e1, int shared_route,
+                                            int runs_shared) {
+  if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0 || e0 < 0 || e1 <= e0 || e1 > E) return 0;
+  return moe_workspace(T, H, I, e1 - e0, k, nullptr, k + (shared_route ? 1 : 0), runs_shared != 0, E).bytes;
 }
 
 thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int I, int E, int k,

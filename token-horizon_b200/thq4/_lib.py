@@ -106,6 +106,8 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                                   c_size_t, c_void_p]),
     "thq4_moe_add_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "thq4_moe_add_partial_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                                        c_int]),
     "thq4_moe_add": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(thq4_moe_weights),
                              c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_moe_add_partial": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -471,7 +471,8 @@ def moe_add_partial(x: torch.Tensor, weights: MoeWeights, k: int, e0: int, E: in
     T, H = x.shape
     El, I = weights.gate.experts, weights.gate.rows
     L = _lib.lib()
-    need = L.thq4_moe_add_workspace_bytes(T, H, I, El, k, int(weights.runs_shared))
+    need = L.thq4_moe_add_partial_workspace_bytes(T, H, I, E, k, e0, e0 + El, int(weights.has_shared),
+                                                  int(weights.runs_shared))
     ws = _moe_ws(("add_partial", x.device.index, torch.cuda.current_stream(x.device).cuda_stream), need, x.device)
     y = torch.empty((T, H), dtype=torch.float32, device=x.device)
     check(L.thq4_moe_add_partial(_ptr(x.contiguous()), _ptr(residual), T, H, I, E, k, e0, e0 + El,

@@ -76,6 +76,24 @@ def moe_sharded(x: torch.Tensor, logits: torch.Tensor, k: int, e0: int, gate, up
     return part.to(torch.bfloat16)
 
 
+def moe_add_sharded(x: torch.Tensor, weights, k: int, e0: int, E: int, residual: Optional[torch.Tensor] = None,
+                    group=None) -> torch.Tensor:
+    """One MoE block (MoE::add) with the routed experts sharded over the
+    ranks: `weights` (a MoeWeights) holds this rank's experts [e0, e0 +
+    weights.gate.experts) of E, the full router and, on the rank that runs
+    it, the shared expert; each rank writes its f32 partial (the residual on
+    rank 0 only), one all-reduce sums them, one rounding to bf16."""
+    import torch.distributed as dist
+
+    from .qlin import moe_add_partial
+
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    part = moe_add_partial(x, weights, k, e0, E, residual if rank == 0 else None)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(part, group=group)
+    return part.to(torch.bfloat16)
+
+
 class PeerGroup:
     """One IPC-mapped region per rank: [0, 256) control words (flags[world]
     u32 at 0, the gather count at 64, the CTA arrival counter at 128), then
