@@ -70,3 +70,24 @@ def test_malformed_files_are_rejected(tmp_path, case, msg):
             f.section(16, "late")
         elif case == "empty":
             f.section(0, "nothing")
+
+
+def test_q8_section_round_trip(tmp_path):
+    # readQ8Projection (WeightStore.cpp:264-282): weights, scales, biases in one section
+    out, inp = 256, 512
+    rng = np.random.default_rng(2)
+    q = rng.integers(0, 256, out * inp, dtype=np.uint8)
+    sc = rng.integers(0, 1 << 16, out * inp // 64, dtype=np.uint16)
+    bi = rng.integers(0, 1 << 16, out * inp // 64, dtype=np.uint16)
+    sec = np.concatenate([q, sc.view(np.uint8), bi.view(np.uint8)])
+    assert sec.size == pk.q8_packed_bytes(out, inp) == out * inp + out * inp // 32 * 2
+    _, _, slab = _proj(256, 64, 5)
+    path = os.path.join(tmp_path, "moe.bin")
+    pk.write_weight_file(path, MAGIC, 3, 4, [sec.tobytes(), slab.tobytes()])
+    with pk.WeightFile(path, MAGIC, 3, 4) as f:
+        got = f.q8_projection(out, inp, "router")
+        assert np.array_equal(got, sec)
+        f.q4_projection(256, 64, "next")
+        f.finish()
+    with pytest.raises(pk.WeightFileError, match="input-aligned"):
+        pk.q8_packed_bytes(256, 100)

@@ -45,3 +45,22 @@ def test_package_projection_and_experts(tmp_path):
                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     want = O.linear_group(wq, sb, O.SB_BF16, O.bf16_to_f32(x).reshape(1, inp))[0]
     assert_close_ref("package projection", y.cpu().numpy().ravel(), want)
+
+
+def test_package_q8_router_scores(tmp_path):
+    """A Q8 section loaded from a package is the router the library reads
+    as stored: its scores equal the oracle's bit for bit."""
+    out, inp, T = 256, 1024, 12
+    rng = np.random.default_rng(3)
+    q = rng.integers(0, 256, out * inp, dtype=np.uint8)
+    sc = O.f32_to_bf16(rng.uniform(0.0005, 0.004, out * inp // 64).astype(np.float32))
+    bi = O.f32_to_bf16((rng.standard_normal(out * inp // 64) * 0.05).astype(np.float32))
+    path = os.path.join(tmp_path, "router.bin")
+    pk.write_weight_file(path, MAGIC, 0, 5, [np.concatenate([q, sc.view(np.uint8), bi.view(np.uint8)]).tobytes()])
+    with pk.WeightFile(path, MAGIC, 0, 5) as f:
+        r = pk.load_q8_projection(f.q8_projection(out, inp, "router"), out, inp, torch.device("cuda"))
+        f.finish()
+    x = O.f32_to_bf16(rng.standard_normal((T, inp)).astype(np.float32))
+    got = thq4.moe_scores_q8(dev(x).view(torch.bfloat16), r, 256)
+    want = O.moe_scores_q8(x, q, sc, bi, 256)
+    assert np.array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16), want)

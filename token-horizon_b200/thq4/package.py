@@ -16,7 +16,11 @@ The format follows docs/splash/runtime/model/WeightStore.{hpp,cpp}:
   256 (WeightStore.cpp:57-67, 229-249) -- the Splash slab layout that
   thq4_repack reads as THQ4_SRC_SLAB;
 - an expert projection is one section of `experts` such slabs back to back
-  (WeightStore.cpp:284-299).
+  (WeightStore.cpp:284-299);
+- a Q8 projection (the MoE router, the shared expert's gate) is one section
+  of out*inp + 2 * out*inp/32 bytes: the weight bytes, then the bf16 scales,
+  then the bf16 biases, in StorageN = 256 order (WeightStore.cpp:47-53,
+  264-282), read by the library as stored.
 
 Error messages follow the reference's WeightStoreError texts.  This module
 only moves bytes; the arithmetic runs in libthq4.so.
@@ -48,6 +52,13 @@ def q4_elements(out: int, inp: int) -> int:
 def q4_packed_bytes(out: int, inp: int) -> int:
     """Bytes of one Q4 projection section: 9/16 of a byte per element."""
     return q4_elements(out, inp) // 16 * 9
+
+
+def q8_packed_bytes(out: int, inp: int) -> int:
+    """Bytes of one Q8 projection section: the elements plus a bf16 scale and
+    bias per 64 elements (q8PackedBytes, WeightStore.cpp:47-53)."""
+    elements = q4_elements(out, inp)
+    return elements + elements // 32 * 2
 
 
 def validate_q4_layout(out: int, inp: int) -> None:
@@ -116,6 +127,12 @@ class WeightFile:
         raw = np.frombuffer(self.section(experts * stride, label), dtype=np.uint8)
         return raw.reshape(experts, stride)
 
+    def q8_projection(self, out: int, inp: int, label: str) -> np.ndarray:
+        """The bytes (u8) of one Q8 projection section (readQ8Projection,
+        WeightStore.cpp:264-282)."""
+        validate_q4_layout(out, inp)
+        return np.frombuffer(self.section(q8_packed_bytes(out, inp), label), dtype=np.uint8)
+
     def close(self) -> None:
         try:
             self._map.close()
@@ -170,3 +187,16 @@ def load_expert_q4_projection(slabs: np.ndarray, out: int, inp: int, device, sb_
     validate_q4_layout(out, inp)
     src = torch.from_numpy(np.ascontiguousarray(slabs)).to(device)
     return PackedExperts.from_slabs(src, out, inp, BF16 if sb_dtype is None else sb_dtype)
+
+
+def load_q8_projection(section: np.ndarray, out: int, inp: int, device):
+    """A Q8Projection from one section's bytes, uploaded as stored (the
+    library reads the StorageN = 256 order directly)."""
+    import torch
+
+    from .qlin import Q8Projection
+
+    validate_q4_layout(out, inp)
+    if section.size != q8_packed_bytes(out, inp):
+        raise WeightFileError("Q8 projection section has the wrong size")
+    return Q8Projection.from_section(torch.from_numpy(np.ascontiguousarray(section)).to(device), inp, out)
