@@ -69,6 +69,10 @@ def parse():
     p.add_argument("--nccl-gather", action="store_true",
                    help="N > 1: gather each projection's output with NCCL all-gather (the baseline) instead of "
                         "the GEMV epilogue's NVLink stores")
+    p.add_argument("--tp", default="col", choices=["col", "row"],
+                   help="N > 1: col = every projection column-sharded with a fused all-gather; row = o and down "
+                        "row-sharded with a fused all-reduce (partials stored to every rank, summed as the next "
+                        "projection stages them), q/k/v and gate/up column-sharded with local outputs")
     return p.parse_args()
 
 
@@ -158,7 +162,7 @@ def run_thq4(args):
     import torch.distributed as dist
     import thq4
     from thq4 import synth
-    from thq4.shard import shard_rows
+    from thq4.shard import shard_rows, slice_cols_mlx
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -175,9 +179,19 @@ def run_thq4(args):
         del wq, sb
         return p
 
-    q0, qn = shard_rows(HIDDEN, world, rank)
+    row_tp = world > 1 and args.tp == "row" and not args.nccl_gather
+    align = 64 if row_tp else 16  # row shards split o's and down's inputs into whole groups
+    q0, qn = shard_rows(HIDDEN, world, rank, align)
     k0, kn = shard_rows(KV, world, rank)
-    i0, inn = shard_rows(INTER, world, rank)
+    i0, inn = shard_rows(INTER, world, rank, align)
+
+    def packed_cols(out_rows, inp, seed, c0, cols):
+        """A row-parallel shard: input columns [c0, c0 + cols), every output row."""
+        wq, sb = synth.normal_weight(out_rows, inp, seed, dev)
+        wq_r, sb_r = slice_cols_mlx(wq, sb, c0, cols)
+        del wq, sb
+        return thq4.PackedWeight.repack(thq4.SRC_MLX, wq_r, sb_r, out_rows, cols, thq4.F16)
+
     layers = []
     for l in range(L):
         s = 1000 * (l + 1)
@@ -190,10 +204,10 @@ def run_thq4(args):
         del wq_q, wq_k, wq_v, sb_q, sb_k, sb_v
         qkv = thq4.PackedWeight.repack(thq4.SRC_MLX, wq_qkv, sb_qkv, qn + 2 * kn, HIDDEN, thq4.F16)
         del wq_qkv, sb_qkv
-        o = packed(HIDDEN, HIDDEN, s + 4, q0, qn)
+        o = packed_cols(HIDDEN, HIDDEN, s + 4, q0, qn) if row_tp else packed(HIDDEN, HIDDEN, s + 4, q0, qn)
         gate = packed(INTER, HIDDEN, s + 5, i0, inn)
         up = packed(INTER, HIDDEN, s + 6, i0, inn)
-        down = packed(HIDDEN, INTER, s + 7, q0, qn)
+        down = packed_cols(HIDDEN, INTER, s + 7, i0, inn) if row_tp else packed(HIDDEN, INTER, s + 7, q0, qn)
         layers.append((qkv, o, gate, up, down))
     torch.cuda.synchronize()
     rank_bytes = sum(p.nbytes for lay in layers for p in lay)
@@ -225,7 +239,23 @@ def run_thq4(args):
     # every peer; the next projection waits for the peers' flags before it
     # reads x.  No collective runs in the step.
     peer = None
-    if world > 1 and not args.nccl_gather:
+    if row_tp:
+        # o and down row-sharded: each writes its f32 partial of the whole
+        # output into its slot of every rank's reduction buffer; q/k/v and
+        # gate/up read x as the sum of the partials (after the peers' flags)
+        # and keep their column-sharded outputs local.  Two exchanges per
+        # layer instead of four.
+        from thq4.shard import PeerGroup
+
+        peer = PeerGroup(2 * world * HIDDEN * 4 + 4 * 256, dev)
+        red_o, red_d = peer.buffer(peer.reduction_bytes(HIDDEN, 1)), peer.buffer(peer.reduction_bytes(HIDDEN, 1))
+        g_qkv = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN)
+        g_o = peer.reduce(red_o, HIDDEN, 1, wait=False)
+        g_gu = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN)
+        g_dn = peer.reduce(red_d, HIDDEN, 1, wait=False)
+        V = lambda off: ctypes.c_void_p(peer.ptr(off))  # noqa: E731
+        F32 = thq4.F32
+    elif world > 1 and not args.nccl_gather:
         from thq4.shard import PeerGroup
 
         peer = PeerGroup((3 * HIDDEN + INTER) * 2 + 4 * 256, dev)
@@ -249,7 +279,24 @@ def run_thq4(args):
             thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, V(off_h), BF, 1, P(t_d), P(ws), ws_bytes,
                                             ctypes.byref(g_dn), s))
 
+    def step_row():
+        s = stream()
+        for li, (qkv, o, gate, up, down) in enumerate(layers):
+            if li == 0:  # the step's input
+                thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
+            else:  # the previous layer's down, all-reduced as it is staged
+                thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, V(red_d), F32, 1, P(t_qkv), P(ws),
+                                                ws_bytes, ctypes.byref(g_qkv), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, P(t_qkv), BF, 1, None, P(ws), ws_bytes,
+                                            ctypes.byref(g_o), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(red_o), F32, 1, P(t_h),
+                                            P(ws), ws_bytes, ctypes.byref(g_gu), s))
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, P(t_h), BF, 1, None, P(ws), ws_bytes,
+                                            ctypes.byref(g_dn), s))
+
     def step():
+        if row_tp:
+            return step_row()
         if peer is not None:
             return step_peer()
         s = stream()
@@ -332,10 +379,16 @@ def run_thq4(args):
     x_host.copy_(x_in.cpu())
     y_host = torch.empty((1, HIDDEN), dtype=torch.bfloat16).pin_memory()
 
+    if row_tp:  # the step's result is the last down's partials, one per rank
+        y_host = torch.empty((world, HIDDEN), dtype=torch.float32).pin_memory()
+
     def e2e_body():
         x_in.copy_(x_host, non_blocking=True)
         run()
-        if peer is not None:
+        if row_tp:
+            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_gu), stream()))
+            thq4.check(lib.thq4_copy(P(y_host), V(red_d), world * HIDDEN * 4, stream()))
+        elif peer is not None:
             thq4.check(lib.thq4_copy(P(y_host), V(off_y), HIDDEN * 2, stream()))
         else:
             y_host.copy_(y_out, non_blocking=True)
@@ -433,9 +486,12 @@ def run_thq4(args):
                 "intermediate": INTER, "group": 64, "scale_dtype": "f16",
                 "l2": f"inputs larger than L2: {total_bytes / 1e9:.2f} GB of weights per step "
                       f"({rank_bytes / 1e9:.2f} GB per GPU), no flush",
-                "parallelism": f"column-shard x{world}" + (
-                    "" if world == 1 else " + NCCL all-gather per projection" if args.nccl_gather else
-                    ", outputs gathered by the GEMV epilogue (NVLink stores to IPC-mapped buffers + flags)"),
+                "parallelism": (f"tensor-parallel x{world}: q/k/v and gate/up column-sharded, o and down row-sharded "
+                                "with the all-reduce fused (f32 partials stored over NVLink into every rank's buffer "
+                                "+ flags, summed by the next projection's staging)") if row_tp else (
+                    f"column-shard x{world}" + (
+                        "" if world == 1 else " + NCCL all-gather per projection" if args.nccl_gather else
+                        ", outputs gathered by the GEMV epilogue (NVLink stores to IPC-mapped buffers + flags)")),
                 "cuda_graph": cuda_graph_used,
             },
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue)",
@@ -445,7 +501,8 @@ def run_thq4(args):
                          "step_frac": round(value / world / hbm_peak, 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * HIDDEN * world,
-                    "d2h_bytes_per_step": 2 * HIDDEN * world, "ms_per_step": round(ms_e2e, 5)},
+                    "d2h_bytes_per_step": (4 * HIDDEN * world * world) if row_tp else 2 * HIDDEN * world,
+                    "ms_per_step": round(ms_e2e, 5)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "prefill": prefill,

@@ -298,39 +298,56 @@ size_t thq4_moe_add_workspace_bytes(int T, int H, int I, int E, int k, int share
 thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int I, int E, int k,
                          const thq4_moe_weights *w, void *y, void *workspace, size_t workspace_bytes, void *stream);
 
-/* ---- multi-GPU column shards --------------------------------------------
+/* ---- multi-GPU shards ------------------------------------------------------
  * The reference engine is single-device; these entry points are the sharded
- * extension.  Each rank (one process per GPU) holds a contiguous range of a
+ * extension, one process per GPU.
+ *
+ * Column shards (out_mode 0, gather): each rank holds a contiguous range of a
  * projection's output rows; instead of an all-gather after the projection,
  * the GEMV's epilogue stores its rows straight into every rank's copy of the
- * full vector (NVLink stores through IPC mappings), and the grid's last CTA
- * then writes this rank's completed-gather count into its slot of every
- * peer's flag words (system-scope release).  A projection whose x is such a
- * full vector waits (wait = 1, before it reads x; bounded, kStatusTimeout
- * bit 2 of thq4_device_status) until every peer's flag has reached this
- * rank's own count.  Every rank must make the same sequence of gathered
- * calls.  The flag and count words live in memory every rank maps
- * (thq4_ipc_alloc / thq4_ipc_open) and start at 0. */
+ * full vector (NVLink stores through IPC mappings).
+ *
+ * Row shards (out_mode 1, reduce): each rank holds a contiguous range of a
+ * projection's input columns and computes an f32 partial of every output;
+ * the epilogue stores it into slot `rank` of every rank's reduction buffer
+ * (dst[r] + rank * slot floats, [t][stride]).  The all-reduce finishes on
+ * read: a projection with x_parts = world reads x as the sum of the partials
+ * in rank order, rounded once to bf16 -- a column-then-row-sharded pair (an
+ * MLP's gate/up then down) exchanges one vector instead of two.
+ *
+ * After its stores the grid's last CTA writes this rank's completed-exchange
+ * count into its slot of every peer's flag words (system-scope release).  A
+ * projection whose x comes from such an exchange waits (wait = 1, before it
+ * reads x; bounded, kStatusTimeout bit 2 of thq4_device_status) until every
+ * peer's flag has reached this rank's own count.  out_mode 2 (local) neither
+ * exchanges nor signals (a column shard whose output stays local).  Every
+ * rank must make the same sequence of calls.  The flag and count words live
+ * in memory every rank maps (thq4_ipc_alloc / thq4_ipc_open) and start at 0. */
 typedef struct thq4_peer_gather {
   int32_t world;           /* ranks, 1 .. 8 */
   int32_t rank;
-  int32_t rows;            /* the first `rows` outputs of the call are gathered ... */
+  int32_t rows;            /* gather: the first `rows` outputs of the call are gathered ... */
   int32_t offset;          /* ... to full[t * stride + offset + row] on every rank */
-  int32_t stride;          /* full-vector length per token */
-  int32_t wait;            /* 1: wait for the peers' gathers before reading x */
-  void *const *dst;        /* device array [world]: rank r's full vector (bf16), as mapped here */
+  int32_t stride;          /* full-vector length per token (reduce: >= out) */
+  int32_t wait;            /* 1: wait for the peers' exchanges before reading x */
+  void *const *dst;        /* device array [world]: rank r's full vector (bf16) or reduction buffer (f32) */
   uint32_t *const *flags;  /* device array [world]: rank r's flag words (u32 [world]), as mapped here */
-  uint32_t *count;         /* this rank's completed-gather count (one device word) */
+  uint32_t *count;         /* this rank's completed-exchange count (one device word) */
   uint32_t *arrive;        /* this rank's CTA arrival counter (one device word, left at 0) */
+  int32_t out_mode;        /* 0 gather, 1 reduce, 2 local */
+  int32_t x_parts;         /* > 0: x (THQ4_F32) is x_parts partials, x + p * x_slot floats, each [m][in] */
+  int64_t slot;            /* reduce: floats between the ranks' partials in a reduction buffer (>= m * stride) */
+  int64_t x_slot;          /* floats between the partials of x (>= m * in) */
 } thq4_peer_gather;
 
-/* thq4_linear (up == NULL) or thq4_gate_up with the all-gather fused in; y is
- * bf16 [m][out] (the local rows), m <= 8 for bf16 x (4 for f32 x). */
+/* thq4_linear (up == NULL) or thq4_gate_up with the exchange fused in; y is
+ * bf16 [m][out] (the local rows; ignored, may be NULL, in reduce mode), m <= 8
+ * for bf16 x or x partials (4 for f32 x). */
 thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const void *x, int x_dtype, int m,
                              void *y, void *workspace, size_t workspace_bytes, const thq4_peer_gather *g,
                              void *stream);
-/* On `stream`, waits until every peer has completed as many gathers as this
- * rank (for a gathered vector read by something other than thq4_linear_peer). */
+/* On `stream`, waits until every peer has completed as many exchanges as this
+ * rank (for an exchanged vector read by something other than thq4_linear_peer). */
 thq4_status thq4_peer_wait(const thq4_peer_gather *g, void *stream);
 
 /* Expert-sharded MoE: this rank holds experts [e0, e1) of E (gate, up and

@@ -178,3 +178,137 @@ def test_peer_call_validation():
     g.offset = 300
     st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.BF16, 1, P(y), P(x), 1 << 20, ctypes.byref(g), S())
     assert st == _lib.ERR_INVALID_ARGUMENT and "stride" in thq4.last_error()
+
+
+# ---- row-parallel shards: the reduce epilogue and partials read back --------------
+
+def _f32_out(q, x, m=1):
+    ws = _workspace(q.packed.desc)
+    y = torch.empty((m, q.packed.desc.out), dtype=torch.float32, device="cuda")
+    thq4.check(thq4.lib().thq4_linear(ctypes.byref(q.packed.desc), P(x), thq4.BF16, m, P(y), thq4.F32, P(ws),
+                                      ws.numel(), S()))
+    return y
+
+
+def test_world1_reduce_then_partials_equal_the_plain_chain():
+    """World 1: a projection in reduce mode writes its f32 output into slot 0;
+    the next projection reads it as one partial (rounded to bf16 as staged):
+    the pair equals the plain chain bit for bit."""
+    n1, k1, n2, m = 512, 768, 256, 2
+    _, _, q1 = _weight(n1, k1, 71)
+    _, _, q2 = _weight(n2, n1, 72)
+    L = thq4.lib()
+    x = dev(np.stack([O.rand_x(k1, 80 + t) for t in range(m)]))
+    ws1, ws2 = _workspace(q1.packed.desc), _workspace(q2.packed.desc)
+    y1 = torch.empty((m, n1), dtype=torch.bfloat16, device="cuda")
+    y2 = torch.empty((m, n2), dtype=torch.bfloat16, device="cuda")
+    thq4.check(L.thq4_linear(ctypes.byref(q1.packed.desc), P(x), thq4.BF16, m, P(y1), thq4.BF16, P(ws1), ws1.numel(),
+                             S()))
+    thq4.check(L.thq4_linear(ctypes.byref(q2.packed.desc), P(y1), thq4.BF16, m, P(y2), thq4.BF16, P(ws2), ws2.numel(),
+                             S()))
+    grp = PeerGroup(4 * m * n1 + 256, torch.device("cuda"))
+    try:
+        off = grp.buffer(grp.reduction_bytes(n1, m))
+        g1 = grp.reduce(off, n1, m, wait=False)
+        g2 = grp.local_out(wait=True, x_parts=1, x_slot=m * n1)
+        z2 = torch.empty_like(y2)
+        for _ in range(2):
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q1.packed.desc), None, P(x), thq4.BF16, m, None, P(ws1),
+                                          ws1.numel(), ctypes.byref(g1), S()))
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q2.packed.desc), None, ctypes.c_void_p(grp.ptr(off)),
+                                          thq4.F32, m, P(z2), P(ws2), ws2.numel(), ctypes.byref(g2), S()))
+            torch.cuda.synchronize()
+            assert torch.equal(z2.view(torch.int16), y2.view(torch.int16)), "reduce + partials differ from the chain"
+        part = torch.empty((m, n1), dtype=torch.float32, device="cuda")
+        thq4.check(L.thq4_copy(P(part), ctypes.c_void_p(grp.ptr(off)), part.numel() * 4, S()))
+        torch.cuda.synchronize()
+        assert torch.equal(part, _f32_out(q1, x, m)), "slot 0 holds the f32 output"
+        assert _status() & TIMEOUT_BIT == 0
+    finally:
+        grp.close()
+
+
+def test_world2_reduce_epilogue_on_one_gpu():
+    """Rank 0 of 2 (the peer's region also on this GPU, the peer never runs):
+    its f32 partial lands in slot 0 of both ranks' reduction buffers, slot 1
+    stays untouched, and rank 0's flag on the peer counts the exchange."""
+    out, inp, m = 384, 512, 1
+    _, _, q = _weight(out, inp, 73)
+    L = thq4.lib()
+    x = dev(O.rand_x(inp, 74).reshape(1, inp))
+    ws = _workspace(q.packed.desc)
+    nbytes = 256 + 2 * m * out * 4
+    ra = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    rb = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    g, keep = _emulated_rank0(ra, rb, out, out, wait=False)
+    g.out_mode, g.slot = 1, m * out
+    thq4.check(L.thq4_linear_peer(ctypes.byref(q.packed.desc), None, P(x), thq4.BF16, m, None, P(ws), ws.numel(),
+                                  ctypes.byref(g), S()))
+    torch.cuda.synchronize()
+    want = _f32_out(q, x).cpu()
+    for region in (ra, rb):
+        slots = region[256:].view(torch.float32).cpu().reshape(2, out)
+        assert torch.equal(slots[0], want[0]), "rank 0's partial missing from a rank's buffer"
+        assert not slots[1].any(), "rank 1's slot was written"
+    assert int(rb[:4].view(torch.int32).item()) == 1 and not ra[:8].any()
+
+
+@pytest.mark.parametrize("parts,gate_up", [(2, False), (3, True), (8, False)])
+def test_partials_are_summed_in_rank_order(parts, gate_up):
+    """x given as `parts` f32 partials is staged as bf16(p0 + p1 + ...): the
+    call equals the plain call on that x, bit for bit."""
+    n, inp, m = 256, 1024, 3
+    wq, sb = O.rand_qlin(2 * n if gate_up else n, inp, 75)
+    q = thq4.QLin(dev(wq), dev(sb), 2 * n if gate_up else n, inp, 64).tiled(n if gate_up else 0)
+    first = q.packed_gate if gate_up else q.packed
+    L = thq4.lib()
+    rng = np.random.default_rng(parts)
+    p = torch.from_numpy(rng.standard_normal((parts, m, inp)).astype(np.float32)).cuda()
+    total = torch.zeros((m, inp), dtype=torch.float32, device="cuda")
+    for r in range(parts):
+        total += p[r]
+    xb = total.to(torch.bfloat16)  # round to nearest even, as the staging does
+    ws = _workspace(first.desc)
+    ud = ctypes.byref(q.packed_up.desc) if gate_up else None
+    y_ref = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    if gate_up:
+        thq4.check(L.thq4_gate_up(ctypes.byref(first.desc), ud, P(xb), thq4.BF16, m, P(y_ref), thq4.BF16, P(ws),
+                                  ws.numel(), S()))
+    else:
+        thq4.check(L.thq4_linear(ctypes.byref(first.desc), P(xb), thq4.BF16, m, P(y_ref), thq4.BF16, P(ws),
+                                 ws.numel(), S()))
+    flags = torch.zeros(64, dtype=torch.int32, device="cuda")
+    g = _lib.thq4_peer_gather()
+    g.world, g.rank, g.wait, g.out_mode = 1, 0, 0, 2
+    keep = torch.tensor([flags.data_ptr()], dtype=torch.int64, device="cuda")
+    g.flags, g.count = keep.data_ptr(), flags.data_ptr() + 64
+    g.x_parts, g.x_slot = parts, m * inp
+    y = torch.empty_like(y_ref)
+    thq4.check(L.thq4_linear_peer(ctypes.byref(first.desc), ud, P(p), thq4.F32, m, P(y), P(ws), ws.numel(),
+                                  ctypes.byref(g), S()))
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+
+
+def test_reduce_validation():
+    L = thq4.lib()
+    w = _lib.thq4_weight()
+    w.out, w.in_, w.gs, w.sb_dtype = 256, 512, 64, thq4.BF16
+    x = torch.zeros((16, 512), dtype=torch.float32, device="cuda")
+    w.qw = w.sb = ctypes.c_void_p(x.data_ptr())
+    g = _lib.thq4_peer_gather()
+    g.world, g.rank, g.rows, g.offset, g.stride, g.out_mode, g.slot = 2, 0, 256, 0, 256, 1, 256
+    g.dst = g.flags = g.count = g.arrive = x.data_ptr()
+    g.rows = 128
+    st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.BF16, 1, None, P(x), 1 << 20, ctypes.byref(g), S())
+    assert st == _lib.ERR_INVALID_ARGUMENT and "reduce needs rows == out" in thq4.last_error()
+    g.rows = 256
+    st = L.thq4_linear_peer(ctypes.byref(w), ctypes.byref(w), P(x), thq4.BF16, 1, None, P(x), 1 << 20,
+                            ctypes.byref(g), S())
+    assert st == _lib.ERR_UNSUPPORTED
+    g.out_mode, g.x_parts, g.x_slot = 2, 2, 512
+    st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.BF16, 1, P(x), P(x), 1 << 20, ctypes.byref(g), S())
+    assert st == _lib.ERR_INVALID_ARGUMENT and "partials are f32" in thq4.last_error()
+    g.out_mode = 3
+    st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.F32, 1, P(x), P(x), 1 << 20, ctypes.byref(g), S())
+    assert st == _lib.ERR_INVALID_ARGUMENT and "out_mode" in thq4.last_error()

@@ -184,3 +184,101 @@ def test_two_gpu_expert_shards_match_oracle():
     assert np.array_equal(got[0], got[1]), "ranks disagree after the all-reduce"
     y = O.bf16_to_f32(got[0]).astype(np.float64)
     assert np.all(np.abs(y - want) <= 0.02 + 0.01 * np.abs(want)), "sharded MoE differs from the oracle"
+
+
+def _row_rank(rank, world, port, ret):
+    """y1 = W1 x on this rank's rows (kept local), y2 = W2 y1 row-parallel
+    (this rank's input columns = its y1 rows; f32 partial into slot `rank`
+    of every rank's reduction buffer), y3 = W3 bf16(sum of the partials)
+    column-sharded and gathered."""
+    import ctypes
+    import datetime
+
+    import torch.distributed as dist
+
+    import q4oracle as O
+    import thq4
+    from helpers import dev
+    from thq4.shard import PeerGroup, shard_cols, shard_rows, slice_cols_mlx
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    d = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=d,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        n1, k1, n2, n3 = 1024, 768, 768, 512
+        w1q, w1s = O.rand_qlin(n1, k1, 41)
+        w2q, w2s = O.rand_qlin(n2, n1, 42)
+        w3q, w3s = O.rand_qlin(n3, n2, 43)
+        x = O.rand_x(k1, 44)
+        b1, r1 = shard_rows(n1, world, rank, align=64)
+        k0, kk = shard_cols(n1, world, rank)
+        b3, r3 = shard_rows(n3, world, rank)
+        q1 = thq4.QLin(dev(w1q[b1:b1 + r1]).to(d), dev(w1s[b1:b1 + r1]).to(d), r1, k1, 64).tiled()
+        w2r, s2r = slice_cols_mlx(dev(w2q).to(d), dev(w2s).to(d), k0, kk)
+        q2 = thq4.QLin(w2r, s2r, n2, kk, 64).tiled()
+        q3 = thq4.QLin(dev(w3q[b3:b3 + r3]).to(d), dev(w3s[b3:b3 + r3]).to(d), r3, n2, 64).tiled()
+        L = thq4.lib()
+        grp = PeerGroup(world * n2 * 4 + n3 * 2 + 1024, d)
+        red = grp.buffer(grp.reduction_bytes(n2, 1))
+        full3 = grp.buffer(n3 * 2)
+        g2 = grp.reduce(red, n2, 1, wait=False)
+        g3 = grp.gather(full3, r3, b3, n3, wait=True, x_parts=world, x_slot=n2)
+        ws = [thq4.qlin.workspace(q.packed.desc, d) for q in (q1, q2, q3)]
+        xt = dev(x.reshape(1, k1)).to(d)
+        y1 = torch.empty((1, r1), dtype=torch.bfloat16, device=d)
+        y3 = torch.empty((1, r3), dtype=torch.bfloat16, device=d)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            thq4.check(L.thq4_linear(ctypes.byref(q1.packed.desc), P(xt), thq4.BF16, 1, P(y1), thq4.BF16, P(ws[0]),
+                                     ws[0].numel(), s))
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q2.packed.desc), None, P(y1), thq4.BF16, 1, None, P(ws[1]),
+                                          ws[1].numel(), ctypes.byref(g2), s))
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q3.packed.desc), None, ctypes.c_void_p(grp.ptr(red)), thq4.F32,
+                                          1, P(y3), P(ws[2]), ws[2].numel(), ctypes.byref(g3), s))
+        thq4.check(L.thq4_peer_wait(ctypes.byref(g3), s))
+        out = torch.empty((1, n3), dtype=torch.bfloat16, device=d)
+        thq4.check(L.thq4_copy(P(out), ctypes.c_void_p(grp.ptr(full3)), n3 * 2, s))
+        torch.cuda.synchronize()
+        st = ctypes.c_uint32()
+        thq4.check(L.thq4_device_status(ctypes.byref(st), None))
+        ret.put((rank, (out.float().cpu().numpy().ravel(), int(st.value))))
+        grp.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_row_parallel_reduce_matches_oracle():
+    import torch.multiprocessing as mp
+
+    import q4oracle as O
+    from helpers import assert_close_ref
+
+    paths = [HERE, ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "token-horizon_b200")]
+    os.environ["PYTHONPATH"] = os.pathsep.join(paths + [os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_rank, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(ret.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    n1, k1, n2, n3 = 1024, 768, 768, 512
+    w1q, w1s = O.rand_qlin(n1, k1, 41)
+    w2q, w2s = O.rand_qlin(n2, n1, 42)
+    w3q, w3s = O.rand_qlin(n3, n2, 43)
+    x = O.bf16_to_f32(O.rand_x(k1, 44)).reshape(1, k1)
+    y1 = O.bf16_round(O.linear_group(w1q, w1s, O.SB_BF16, x))
+    y2 = O.bf16_round(O.linear_group(w2q, w2s, O.SB_BF16, y1))
+    y3 = O.linear_group(w3q, w3s, O.SB_BF16, y2)
+    for rank in range(2):
+        f3, status = got[rank]
+        assert status == 0, f"rank {rank}: device status {status:#x}"
+        assert_close_ref(f"rank {rank} row-parallel chain", f3, y3[0])
+    assert np.array_equal(got[0][0], got[1][0]), "ranks disagree"

@@ -333,10 +333,24 @@ thq4_status check_peer(const thq4_peer_gather *g, const char *who) {
   if (g->world < 1 || g->world > 8 || g->rank < 0 || g->rank >= g->world)
     return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "need 1 <= world <= 8 and 0 <= rank < world (world " +
                                                     std::to_string(g->world) + ", rank " + std::to_string(g->rank) + ")");
-  if (!g->dst || !g->flags || !g->count || !g->arrive)
-    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "dst, flags, count and arrive must be device pointers");
+  if (g->out_mode < 0 || g->out_mode > 2)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "out_mode must be 0 (gather), 1 (reduce) or 2 (local)");
   if (g->wait != 0 && g->wait != 1) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "wait must be 0 or 1");
+  if (!g->flags || !g->count || (g->out_mode != 2 && (!g->dst || !g->arrive)))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "dst, flags, count and arrive must be device pointers");
+  if (g->x_parts < 0 || g->x_parts > 8)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "x_parts must be 0 .. 8");
   return THQ4_OK;
+}
+
+PeerGather peer_of(const thq4_peer_gather *g) {
+  PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
+                g->rows, g->offset, g->stride, g->wait};
+  pg.mode = g->out_mode == 0 ? 1 : g->out_mode == 1 ? 2 : 0;
+  pg.slot = g->slot;
+  pg.x_parts = g->x_parts;
+  pg.x_slot = g->x_slot;
+  return pg;
 }
 }  // namespace
 
@@ -350,19 +364,31 @@ thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const 
     if (w->out != up->out || w->in != up->in || w->sb_dtype != up->sb_dtype)
       return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: gate and up halves differ in shape or dtype");
   }
-  if ((s = check_io(x, x_dtype, m, y, THQ4_BF16, who)) != THQ4_OK) return s;
   if ((s = check_peer(g, who)) != THQ4_OK) return s;
-  const int per = x_dtype == THQ4_F32 ? 4 : 8;
+  const bool reduce = g->out_mode == 1;
+  // reduce mode stores no y: check the rest of the I/O against x alone
+  if ((s = check_io(x, x_dtype, m, reduce ? x : y, THQ4_BF16, who)) != THQ4_OK) return s;
+  const bool parts = g->x_parts > 0;
+  if (parts && x_dtype != THQ4_F32)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: x partials are f32 (x_dtype THQ4_F32)");
+  const int per = x_dtype == THQ4_F32 && !parts ? 4 : 8;
   if (m > per)
     return set_error(THQ4_ERR_UNSUPPORTED, "thq4_linear_peer: m " + std::to_string(m) + " > " + std::to_string(per) +
-                                               " (one decode/verify launch per gathered call)");
-  if (g->rows < 0 || g->rows > w->out || g->offset < 0 || g->stride < 1 || (long long)g->offset + g->rows > g->stride)
+                                               " (one decode/verify launch per exchanged call)");
+  if (parts && (g->x_slot < (long long)m * w->in || g->x_slot % 4))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: x_slot must be >= m * in and a multiple of 4");
+  if (g->out_mode == 0 &&
+      (g->rows < 0 || g->rows > w->out || g->offset < 0 || g->stride < 1 || (long long)g->offset + g->rows > g->stride))
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: need 0 <= rows <= out and offset + rows <= stride");
+  if (reduce && (g->rows != w->out || g->offset != 0 || g->stride < w->out || g->slot < (long long)m * g->stride))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_linear_peer: reduce needs rows == out, offset 0, stride >= out and slot >= m * stride");
+  if (reduce && up)
+    return set_error(THQ4_ERR_UNSUPPORTED, "thq4_linear_peer: a gate/up pair is column-sharded (no reduce)");
   if ((s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(w->out), who)) != THQ4_OK) return s;
-  PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
-                g->rows, g->offset, g->stride, g->wait};
-  const cudaError_t e = gemv_launch(*w, up, x, x_dtype == THQ4_F32, m, y, false, workspace,
-                                    static_cast<cudaStream_t>(stream), &pg);
+  const PeerGather pg = peer_of(g);
+  const cudaError_t e = gemv_launch(*w, up, x, x_dtype == THQ4_F32 && !parts, m, reduce ? nullptr : y, false,
+                                    workspace, static_cast<cudaStream_t>(stream), &pg);
   if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
 }
@@ -370,8 +396,7 @@ thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const 
 thq4_status thq4_peer_wait(const thq4_peer_gather *g, void *stream) {
   thq4_status s = check_peer(g, "thq4_peer_wait");
   if (s != THQ4_OK) return s;
-  PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
-                g->rows, g->offset, g->stride, g->wait};
+  const PeerGather pg = peer_of(g);
   const cudaError_t e = peer_wait_launch(pg, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, "thq4_peer_wait");
   return THQ4_OK;

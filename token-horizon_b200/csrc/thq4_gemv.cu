@@ -97,13 +97,21 @@ struct GemvArgs {
   int xcap;            // activation groups staged per CTA
   int pre;             // stages requested before x is staged (0: all)
   int cl_j;            // > 1: slab-split mode, j CTAs per slab in one cluster
-  // fused all-gather of column shards (g_dst null: none): the first g_rows
-  // outputs also go to full[t * g_stride + g_off + row] on every rank, and
-  // the grid's last CTA raises this rank's flag on every peer
+  // fused exchange of shards (g_mode 0: none).  g_mode 1 (gather): the
+  // first g_rows outputs also go to full[t * g_stride + g_off + row] on
+  // every rank; g_mode 2 (reduce): every output, in f32, goes to slot g_rank
+  // of every rank's reduction buffer instead of y.  Then the grid's last CTA
+  // raises this rank's flag on every peer.  g_wait: wait for the peers'
+  // flags before reading x.
   uint16_t *const *g_dst;
   uint32_t *const *g_flags;
   uint32_t *g_count, *g_arrive;
-  int g_world, g_rank, g_rows, g_off, g_stride, g_wait;
+  int g_mode, g_world, g_rank, g_rows, g_off, g_stride, g_wait;
+  long long g_slot;
+  // xparts > 0: x is xparts f32 partials (x + p * xslot floats, [m][in]),
+  // summed in order and rounded to bf16 as they are staged
+  int xparts;
+  long long xslot;
 };
 
 // columns with per-group metadata: P rounded up to even (lanes own pairs)
@@ -146,7 +154,8 @@ __device__ __forceinline__ void consumer_sync() {
 // adjacent lanes, which reduce the group's max |x| and sum with a fixed
 // shuffle tree (deterministic).  Up to four items per thread are requested
 // before any is used.
-__device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
+template <bool PARTS>
+__device__ __forceinline__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
   const int tid = threadIdx.x, nthr = kConsumers * 32;
   const int P = a.P, P8 = meta_cols(P);
   constexpr int kU = 4;
@@ -169,7 +178,18 @@ __device__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *z
       if (g >= a.ng) g -= a.ng;
       const int t = a.xf32 ? q >> 1 : q;
       const size_t at = (size_t)t * a.in + (size_t)g * kGroup + 8 * h8;
-      if (a.xf32) {
+      if (PARTS) {  // the all-reduce's last step: sum the ranks' partials in order, one bf16 rounding
+#pragma unroll 1
+        for (int pp = 0; pp < a.xparts; ++pp) {
+          const float4 *p4 =
+              reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + (size_t)pp * a.xslot + at);
+          const float4 u0 = p4[0], u1 = p4[1];
+          v[it][0] += u0.x, v[it][1] += u0.y, v[it][2] += u0.z, v[it][3] += u0.w;
+          v[it][4] += u1.x, v[it][5] += u1.y, v[it][6] += u1.z, v[it][7] += u1.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[it][e] = __uint_as_float((uint32_t)f32_to_bf16_bits(v[it][e]) << 16);
+      } else if (a.xf32) {
         const float4 *p4 = reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + at);
         const float4 u0 = p4[0], u1 = p4[1];
         v[it][0] = u0.x, v[it][1] = u0.y, v[it][2] = u0.z, v[it][3] = u0.w;
@@ -261,12 +281,15 @@ __device__ __forceinline__ void store_tile(const GemvArgs &a, int rt, int lane, 
       }
       if (t >= a.m) continue;
       if constexpr (GATE_UP) v = silu_mul(v, u);
-      if (a.yf32) {
+      if (a.g_mode == 2) {  // this rank's partial of the output, into its slot on every rank (NVLink stores)
+        for (int rk = 0; rk < a.g_world; ++rk)
+          reinterpret_cast<float *>(a.g_dst[rk])[(size_t)a.g_rank * a.g_slot + (size_t)t * a.g_stride + row] = v;
+      } else if (a.yf32) {
         static_cast<float *>(a.y)[(size_t)t * a.out + row] = v;
       } else {
         const uint16_t bits = f32_to_bf16_bits(v);
         static_cast<uint16_t *>(a.y)[(size_t)t * a.out + row] = bits;
-        if (a.g_dst && row < a.g_rows)  // the shard's slice of the full vector, on every rank (NVLink stores)
+        if (a.g_mode == 1 && row < a.g_rows)  // the shard's slice of the full vector, on every rank (NVLink stores)
           for (int rk = 0; rk < a.g_world; ++rk) a.g_dst[rk][(size_t)t * a.g_stride + a.g_off + row] = bits;
       }
     }
@@ -348,7 +371,7 @@ __device__ __forceinline__ void produce_run(const GemvArgs &a, int C0, int nch, 
   // the consumers wait for every chunk before they release it
 }
 
-template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
+template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr int NS = GATE_UP ? 2 : 1;
   constexpr int CPG = 8 / GW;  // B columns per window position
@@ -407,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
   const int tile = warp;
   pdl_wait();
-  if (a.g_dst && a.g_wait) {  // x holds the peers' slices: wait until they have landed
+  if (a.g_wait) {  // x holds the peers' slices or partials: wait until they have landed
     if (threadIdx.x == 0) peer_wait(a.g_flags, a.g_count, a.g_world, a.g_rank, a.status);
     consumer_sync();
   }
@@ -415,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   const int gs = cg0 * CB;
   const int xcnt =
       min(a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
-  stage_x(a, gs, xcnt, xf, zero, mx);
+  stage_x<PARTS>(a, gs, xcnt, xf, zero, mx);
   if (threadIdx.x == 0) mbar_arrive(xready);
 
   const int r = lane >> 2, c = lane & 3;
@@ -636,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         }
       if (!aborted) store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
     }
-    if (a.g_dst) peer_signal(a);
+    if (a.g_mode) peer_signal(a);
     return;
   }
 
@@ -673,12 +696,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     if (done & 1u) combine(first_slab);
     if (done & 2u) combine(last_slab);
   }
-  if (a.g_dst) peer_signal(a);  // every consumer warp gets here
+  if (a.g_mode) peer_signal(a);  // every consumer warp gets here
 }
 
-template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
+template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
 cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t stream) {
-  auto *k = &gemv_kernel<CB, GW, ONE, SF16, GATE_UP>;
+  auto *k = &gemv_kernel<CB, GW, ONE, SF16, GATE_UP, PARTS>;
   static DeviceOnce once;
   cudaError_t e = once.run([&] {
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
@@ -721,13 +744,25 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
   return cudaLaunchKernelEx(&cfg, k, a);
 }
 
+template <int CB, bool SF16, bool GATE_UP, bool PARTS>
+cudaError_t dispatch_gw_t(const GemvArgs &a, int gw, int grid, size_t smem, cudaStream_t s) {
+  if (gw == 4)
+    return a.P == 1 ? launch_one<CB, 4, true, SF16, GATE_UP, PARTS>(a, grid, smem, s)
+                    : launch_one<CB, 4, false, SF16, GATE_UP, PARTS>(a, grid, smem, s);
+  if (gw == 2) return launch_one<CB, 2, false, SF16, GATE_UP, PARTS>(a, grid, smem, s);
+  return launch_one<CB, 1, false, SF16, GATE_UP, PARTS>(a, grid, smem, s);
+}
+
+// x partials (the end of a fused all-reduce) have their own instances, only
+// for the default 8-group chunks: the extra staging code would otherwise
+// weigh on the register allocation of every kernel.
 template <int CB, bool SF16, bool GATE_UP>
 cudaError_t dispatch_gw(const GemvArgs &a, int gw, int grid, size_t smem, cudaStream_t s) {
-  if (gw == 4)
-    return a.P == 1 ? launch_one<CB, 4, true, SF16, GATE_UP>(a, grid, smem, s)
-                    : launch_one<CB, 4, false, SF16, GATE_UP>(a, grid, smem, s);
-  if (gw == 2) return launch_one<CB, 2, false, SF16, GATE_UP>(a, grid, smem, s);
-  return launch_one<CB, 1, false, SF16, GATE_UP>(a, grid, smem, s);
+  if (a.xparts) {
+    if constexpr (CB == 8) return dispatch_gw_t<CB, SF16, GATE_UP, true>(a, gw, grid, smem, s);
+    return cudaErrorInvalidValue;
+  }
+  return dispatch_gw_t<CB, SF16, GATE_UP, false>(a, gw, grid, smem, s);
 }
 
 template <bool SF16>
@@ -753,7 +788,7 @@ int cluster_capacity(int j) {
   if (j < 2 || j > 8 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   std::lock_guard<std::mutex> lock(mu);
   if (cache[dev][j]) return cache[dev][j] - 1;
-  auto *k = &gemv_kernel<8, 4, true, true, false>;
+  auto *k = &gemv_kernel<8, 4, true, true, false, false>;
   int n = 0;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -899,12 +934,16 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
       a.g_flags = peer->flags;
       a.g_count = peer->count;
       a.g_arrive = peer->arrive;
+      a.g_mode = peer->mode;
       a.g_world = peer->world;
       a.g_rank = peer->rank;
       a.g_rows = peer->rows;
       a.g_off = peer->offset;
       a.g_stride = peer->stride;
       a.g_wait = peer->wait;
+      a.g_slot = peer->slot;
+      a.xparts = peer->x_parts;
+      a.xslot = peer->x_slot;
     }
     // a last pass with fewer tokens fits in the footprint planned for more
     const size_t smem = gemv_smem(p.stages, p.ch, gate_up, p.xcap, a.P);

@@ -71,10 +71,14 @@ bool gemv_pdl_enabled();
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
 // The all-gather of column shards fused into the projection (thq4_peer_gather).
 struct PeerGather {
-  uint16_t *const *dst;     // device array [world]: each rank's full-vector buffer
+  uint16_t *const *dst;     // device array [world]: each rank's full-vector (bf16) or reduction (f32) buffer
   uint32_t *const *flags;   // device array [world]: each rank's flag words [world]
   uint32_t *count, *arrive;
   int world, rank, rows, offset, stride, wait;
+  int mode;                 // 0: no exchange, 1: gather, 2: reduce
+  long long slot;           // reduce: floats between the ranks' partials
+  int x_parts;              // > 0: x is this many f32 partials, summed as staged
+  long long x_slot;         // floats between the partials of x
 };
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
                         int m, void *y, bool y_f32, void *workspace, cudaStream_t stream,

@@ -66,7 +66,9 @@ class thq4_moe_weights(ctypes.Structure):
 class thq4_peer_gather(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("rows", ctypes.c_int32),
                 ("offset", ctypes.c_int32), ("stride", ctypes.c_int32), ("wait", ctypes.c_int32),
-                ("dst", c_void_p), ("flags", c_void_p), ("count", c_void_p), ("arrive", c_void_p)]
+                ("dst", c_void_p), ("flags", c_void_p), ("count", c_void_p), ("arrive", c_void_p),
+                ("out_mode", ctypes.c_int32), ("x_parts", ctypes.c_int32), ("slot", ctypes.c_int64),
+                ("x_slot", ctypes.c_int64)]
 
 
 IPC_HANDLE_BYTES = 64

@@ -33,6 +33,24 @@ def shard_rows(total: int, world: int, rank: int, align: int = 16):
     return rank * per, per
 
 
+def shard_cols(total: int, world: int, rank: int):
+    """(first input column, columns) of `rank`'s equal shard of a row-
+    parallel projection's `total` inputs: whole 64-wide quant groups."""
+    return shard_rows(total, world, rank, align=64)
+
+
+def slice_cols_mlx(wq: torch.Tensor, sb: torch.Tensor, k0: int, k: int):
+    """Input columns [k0, k0 + k) of an MLX weight (wq u32 [out][in/8], sb
+    [out][2 * in/64]: a row's scales, then its biases), as an MLX weight of
+    k inputs -- a row-parallel shard, before the repack."""
+    if k0 % 64 or k % 64:
+        raise ValueError("column shards must be whole 64-wide groups")
+    ng = sb.shape[1] // 2
+    g0, gk = k0 // 64, k // 64
+    return (wq[:, k0 // 8:(k0 + k) // 8].contiguous(),
+            torch.cat([sb[:, g0:g0 + gk], sb[:, ng + g0:ng + g0 + gk]], dim=1).contiguous())
+
+
 def gather_rows(local: torch.Tensor, full: Optional[torch.Tensor] = None, group=None) -> torch.Tensor:
     """All-gather the ranks' y slices [m, rows] into y [m, world * rows] in
     rank order.  The collective concatenates the ranks' [m, rows] blocks;
@@ -151,7 +169,8 @@ class PeerGroup:
         """This rank's address of the buffer at `offset`."""
         return self.local + offset
 
-    def gather(self, offset: int, rows: int, at: int, stride: int, wait: bool):
+    def gather(self, offset: int, rows: int, at: int, stride: int, wait: bool, x_parts: int = 0,
+               x_slot: int = 0):
         """A thq4_peer_gather for a projection whose first `rows` outputs go to
         full[t * stride + at + row] in the buffer at `offset` on every rank."""
         dst = self._ptr_array([b + offset for b in self.bases])
@@ -160,7 +179,31 @@ class PeerGroup:
         g.world, g.rank, g.rows, g.offset, g.stride, g.wait = self.world, self.rank, rows, at, stride, int(wait)
         g.dst, g.flags = dst.data_ptr(), self._flags.data_ptr()
         g.count, g.arrive = self.count, self.arrive
+        g.x_parts, g.x_slot = x_parts, x_slot
         return g
+
+    def reduce(self, offset: int, out: int, m: int, wait: bool, x_parts: int = 0, x_slot: int = 0):
+        """A thq4_peer_gather for a row-parallel projection of `out` outputs:
+        its f32 partial goes to slot `rank` of the reduction buffer at
+        `offset` on every rank (slots of m * out floats; the buffer holds
+        world slots, `reduction_bytes`).  Read back with x_parts = world,
+        x_slot = m * out."""
+        g = self.gather(offset, out, 0, out, wait, x_parts, x_slot)
+        g.out_mode, g.slot = 1, m * out
+        return g
+
+    def local_out(self, wait: bool, x_parts: int = 0, x_slot: int = 0):
+        """A thq4_peer_gather that only waits (for the exchange x comes from)
+        and reads x as partials; the projection's output stays local."""
+        g = self._L.thq4_peer_gather()
+        g.world, g.rank, g.wait = self.world, self.rank, int(wait)
+        g.flags, g.count = self._flags.data_ptr(), self.count
+        g.out_mode, g.x_parts, g.x_slot = 2, x_parts, x_slot
+        return g
+
+    def reduction_bytes(self, out: int, m: int) -> int:
+        """Bytes of a reduction buffer: world slots of m * out f32."""
+        return self.world * m * out * 4
 
     def close(self) -> None:
         """Unmap the peers' regions, then free this rank's (after every rank
