@@ -66,7 +66,8 @@ struct GemvPlan {
 // partial-sum slots for every warp plus one counter per 16-row tile.  It
 // must be zero-filled before first use; every call leaves it zeroed.
 size_t gemv_workspace_bytes(int rows);
-// Programmatic dependent launch for the GEMV (THQ4_PDL=0 disables; read once).
+// Programmatic dependent launch for the GEMV and the MoE chain (THQ4_PDL=0
+// disables; read once).
 bool gemv_pdl_enabled();
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
 // The all-gather of column shards fused into the projection (thq4_peer_gather).

@@ -53,6 +53,8 @@ __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uin
 // experts not yet taken whose score is not -inf; ties go to the lower id; a
 // token without a candidate takes expert 0 (the oracle's rule).
 __global__ void select_kernel(const uint16_t *logits, int T, int E, int k, uint32_t *ids, uint16_t *weights) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const uint16_t *row = logits + (size_t)warp * E;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_scores_kernel(const uint1
   __shared__ __align__(16) float xs[64][kRouteRows];
   __shared__ __align__(16) float qs[64][kRouteCols];
   __shared__ float sums[kRouteRows], ss[kRouteCols], bs[kRouteCols];
+  pdl_wait();
+  pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * kRouteRows, col0 = blockIdx.y * kRouteCols, sl = blockIdx.z;
   const int G = H / 64, g0 = sl * G / kRouteSlices, g1 = (sl + 1) * G / kRouteSlices;
@@ -203,6 +207,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_scores_kernel(const uint1
 
 // scores[t*ld + n] = bf16 of the slice sums added in slice order.
 __global__ void scores_kernel(const float *partial, int T, int ncols, uint16_t *scores, int ld) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)T * ncols) return;
   float total = 0.0f;
@@ -220,6 +226,8 @@ __global__ void scores_kernel(const float *partial, int T, int ncols, uint16_t *
 __global__ void select_q8_kernel(const float *partial, int T, int E, int k, int rpr, const uint16_t *x, int H,
                                  const uint8_t *sq, const uint16_t *ssc, const uint16_t *sbi, uint32_t *ids,
                                  uint16_t *weights) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   float sc[8];
@@ -307,6 +315,8 @@ __host__ __device__ inline int group_warps(int E) { return E <= 512 ? 32 : 16; }
 __global__ void group_kernel(const uint32_t *ids, int T, int k, int rpr, int E_all, int e0, int E, int shared_local,
                              int max_tiles, uint32_t *tiles, uint32_t *grouped, uint32_t *route_rows, uint32_t *ntiles,
                              uint32_t *status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int R = T * rpr;
   extern __shared__ uint32_t sm[];
   const int W = blockDim.x >> 5;
@@ -419,6 +429,8 @@ __global__ void group_kernel(const uint32_t *ids, int T, int k, int rpr, int E_a
 // shuffle tree (deterministic).
 __global__ void gather_kernel(const uint16_t *x, int H, int rpr, const uint32_t *grouped, const uint32_t *ntiles,
                               uint16_t *xg, float *xsum) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int pieces = H / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t row = i / pieces;
@@ -445,6 +457,8 @@ __global__ void gather_kernel(const uint16_t *x, int H, int rpr, const uint32_t 
 template <bool F32>
 __global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const uint32_t *route_rows,
                                const uint16_t *residual, int T, int H, int rpr, void *y) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int pieces = H / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)T * pieces) return;
@@ -459,14 +473,30 @@ __global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = 0.0f;
   }
-  for (int s = 0; s < rpr; ++s) {
-    const uint32_t row = route_rows[(size_t)t * rpr + s];
-    if (row == kPad) continue;
-    const float ws = bf16f(weights[(size_t)t * rpr + s]);
-    const uint4 dv = reinterpret_cast<const uint4 *>(d + (size_t)row * H)[p];
-    const uint32_t w[4] = {dv.x, dv.y, dv.z, dv.w};
+  // four slots at a time: their row indices, then their rows, are requested
+  // together; the sums still run in slot order
+  constexpr int kB = 4;
+  for (int s0 = 0; s0 < rpr; s0 += kB) {
+    uint32_t row[kB];
+    float ws[kB];
+    uint4 dv[kB];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __fmul_rn(ws, bf16f((uint16_t)(w[e >> 1] >> (16 * (e & 1))))));
+    for (int j = 0; j < kB; ++j) {
+      const int s = s0 + j;
+      row[j] = s < rpr ? route_rows[(size_t)t * rpr + s] : kPad;
+      ws[j] = s < rpr ? bf16f(weights[(size_t)t * rpr + s]) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kB; ++j)
+      dv[j] = row[j] != kPad ? reinterpret_cast<const uint4 *>(d + (size_t)row[j] * H)[p] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      if (row[j] == kPad) continue;
+      const uint32_t w[4] = {dv[j].x, dv[j].y, dv[j].z, dv[j].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[e] = __fadd_rn(v[e], __fmul_rn(ws[j], bf16f((uint16_t)(w[e >> 1] >> (16 * (e & 1))))));
+    }
   }
   if constexpr (F32) {
     float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(y) + (size_t)t * H) + 2 * p;
@@ -482,6 +512,24 @@ __global__ void combine_kernel(const uint16_t *d, const uint16_t *weights, const
 }
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+// Every kernel of the MoE chain starts with griddepcontrol.wait (before it
+// touches global memory) and launches with programmatic stream
+// serialization, so its launch and set-up overlap its predecessor's tail.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = gemv_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
 
 }  // namespace
 
@@ -501,14 +549,13 @@ size_t moe_scores_bytes(int T, int ncols) { return (size_t)kRouteSlices * T * nc
 cudaError_t moe_scores_launch(const void *x, int T, int H, const thq4_q8_weight &router, int ncols, float *partial,
                               uint16_t *scores, int ld, cudaStream_t stream) {
   const dim3 grid((T + kRouteRows - 1) / kRouteRows, (ncols + kRouteCols - 1) / kRouteCols, kRouteSlices);
-  route_scores_kernel<<<grid, kRouteThreads, 0, stream>>>(
-      static_cast<const uint16_t *>(x), T, H, static_cast<const uint8_t *>(router.q),
-      static_cast<const uint16_t *>(router.scales), static_cast<const uint16_t *>(router.biases), ncols, partial);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(route_scores_kernel, grid, dim3(kRouteThreads), 0, stream, static_cast<const uint16_t *>(x),
+                             T, H, static_cast<const uint8_t *>(router.q), static_cast<const uint16_t *>(router.scales),
+                             static_cast<const uint16_t *>(router.biases), ncols, partial);
   if (e != cudaSuccess || !scores) return e;
   const size_t n = (size_t)T * ncols;
-  scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(partial, T, ncols, scores, ld);
-  return cudaGetLastError();
+  return launch_pdl(scores_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream, partial, T, ncols, scores,
+                    ld);
 }
 
 cudaError_t moe_route_launch(const MoeRouting &rt, int T, int E, int k, uint32_t *ids, uint16_t *weights,
@@ -518,27 +565,28 @@ cudaError_t moe_route_launch(const MoeRouting &rt, int T, int E, int k, uint32_t
   const int threads = 256, warps = threads / 32;
   const int rpr = k + (rt.shared_gate ? 1 : 0);
   cudaError_t e;
+  const dim3 sgrid((T + warps - 1) / warps);
   if (rt.logits) {
-    select_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(rt.logits, T, E, k, ids, weights);
+    e = launch_pdl(select_kernel, sgrid, dim3(threads), 0, stream, rt.logits, T, E, k, ids, weights);
   } else {
     if ((e = moe_scores_launch(rt.x, T, rt.H, *rt.router, E, rt.partial, nullptr, 0, stream)) != cudaSuccess) return e;
     const thq4_q8_weight *sg = rt.shared_gate;
-    select_q8_kernel<<<(T + warps - 1) / warps, threads, 0, stream>>>(
-        rt.partial, T, E, k, rpr, static_cast<const uint16_t *>(rt.x), rt.H,
-        sg ? static_cast<const uint8_t *>(sg->q) : nullptr, sg ? static_cast<const uint16_t *>(sg->scales) : nullptr,
-        sg ? static_cast<const uint16_t *>(sg->biases) : nullptr, ids, weights);
+    e = launch_pdl(select_q8_kernel, sgrid, dim3(threads), 0, stream, static_cast<const float *>(rt.partial), T, E, k,
+                   rpr, static_cast<const uint16_t *>(rt.x), rt.H,
+                   sg ? static_cast<const uint8_t *>(sg->q) : nullptr,
+                   sg ? static_cast<const uint16_t *>(sg->scales) : nullptr,
+                   sg ? static_cast<const uint16_t *>(sg->biases) : nullptr, ids, weights);
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int E_loc = e1 - e0;
   const size_t smem = moe_group_smem(T * rpr, E_loc);
   static DeviceOnce once;
   e = once.run([] { return cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
   if (e != cudaSuccess) return e;
-  group_kernel<<<1, group_warps(E_loc) * 32, smem, stream>>>(ids, T, k, rpr, E, e0, E_loc,
-                                                               rt.shared_gate && rt.shared_local ? 1 : 0, max_tiles,
-                                                               tiles, grouped, route_rows, ntiles, status_word());
-  return cudaGetLastError();
+  return launch_pdl(group_kernel, dim3(1), dim3(group_warps(E_loc) * 32), smem, stream,
+                    static_cast<const uint32_t *>(ids), T, k, rpr, E, e0, E_loc,
+                    rt.shared_gate && rt.shared_local ? 1 : 0, max_tiles, tiles, grouped, route_rows, ntiles,
+                    status_word());
 }
 
 MoeWorkspace moe_workspace(int T, int H, int I, int E, int k, void *base, int rpr, bool shared_local,
@@ -580,9 +628,10 @@ cudaError_t moe_launch(const void *x, const void *residual, const MoeRouting &rt
   const size_t rows = (size_t)w.max_tiles * kMoeTileRows;
   {
     const size_t n = rows * (H / 8);
-    gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const uint16_t *>(x), H, rpr,
-                                                                    w.grouped, w.ntiles, w.xg, w.xsum);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = launch_pdl(gather_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream,
+                   static_cast<const uint16_t *>(x), H, rpr, static_cast<const uint32_t *>(w.grouped),
+                   static_cast<const uint32_t *>(w.ntiles), w.xg, w.xsum);
+    if (e != cudaSuccess) return e;
   }
   const bool sh = rt.shared_gate && rt.shared_local;
   MoeExperts g{};
@@ -611,11 +660,10 @@ cudaError_t moe_launch(const void *x, const void *residual, const MoeRouting &rt
   const size_t n = (size_t)T * (H / 8);
   const unsigned blocks = (unsigned)((n + 255) / 256);
   const uint16_t *res = static_cast<const uint16_t *>(residual);
-  if (y_f32)
-    combine_kernel<true><<<blocks, 256, 0, stream>>>(w.d, w.weights, w.route_rows, res, T, H, rpr, y);
-  else
-    combine_kernel<false><<<blocks, 256, 0, stream>>>(w.d, w.weights, w.route_rows, res, T, H, rpr, y);
-  return cudaGetLastError();
+  const uint16_t *dd = w.d, *wts = w.weights;
+  const uint32_t *rr = w.route_rows;
+  return launch_pdl(y_f32 ? combine_kernel<true> : combine_kernel<false>, dim3(blocks), dim3(256), 0, stream, dd, wts,
+                    rr, res, T, H, rpr, y);
 }
 
 }  // namespace thq4

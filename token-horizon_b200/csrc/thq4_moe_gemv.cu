@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
   }
   fence_mbar_init();
   __syncthreads();
+  pdl_wait();  // the tiles, rows and sums come from the preceding kernels
+  pdl_launch_dependents();
   const int units = min(a.max_units, (int)(*a.ntiles) * a.n_slabs);
   const int cpu = (a.ng + kMgCB - 1) / kMgCB;  // stages per unit
 
@@ -362,8 +364,17 @@ cudaError_t mg_launch_t(const CUtensorMap &map, const MgArgs &a, int grid, size_
   static DeviceOnce once;
   cudaError_t e = once.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem); });
   if (e != cudaSuccess) return e;
-  k<<<grid, kMgThreads, smem, stream>>>(map, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMgThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = gemv_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, map, a);
 }
 
 }  // namespace
