@@ -127,3 +127,103 @@ def test_error_messages_are_per_thread():
     t.start()
     t.join()
     assert seen["msg"] == "" and "multiple of 64" in thq4.last_error()
+
+
+# ---- the MoE block and the multi-GPU exchange: host-side validation ---------------
+
+def _experts(E, out, inp, qw=0x10000, sb=0x20000, sbd=thq4.BF16):
+    q, s = ctypes.c_size_t(), ctypes.c_size_t()
+    thq4.lib().thq4_weight_bytes(out, inp, 64, ctypes.byref(q), ctypes.byref(s))
+    return _lib.thq4_experts(E, out, inp, 64, sbd, 0, qw, sb, q.value, s.value)
+
+
+def _moe_weights(H=1024, I=512, E=8, shared=True):
+    w = _lib.thq4_moe_weights()
+    w.router = _lib.thq4_q8_weight(256, H, 0x30000, 0x40000, 0x50000)
+    w.gate, w.up, w.down = _experts(E, I, H), _experts(E, I, H), _experts(E, H, I)
+    if shared:
+        w.shared_gate, w.shared_up, w.shared_down = _experts(1, I, H), _experts(1, I, H), _experts(1, H, I)
+        w.shared_expert_gate = _lib.thq4_q8_weight(256, H, 0x60000, 0x70000, 0x80000)
+    return w
+
+
+def _moe_add(w, T=16, H=1024, I=512, E=8, k=2, ws_bytes=1 << 30):
+    return thq4.lib().thq4_moe_add(ctypes.c_void_p(0x90000), None, T, H, I, E, k, ctypes.byref(w),
+                                   ctypes.c_void_p(0xA0000), ctypes.c_void_p(0x100000), ws_bytes, None)
+
+
+def test_moe_add_tile_bound_pinned_to_reference():
+    from test_oracle import ref
+    for T, E, k in [(256, 128, 8), (520, 8, 2), (1, 256, 8), (33, 64, 4)]:
+        with_shared = thq4.lib().thq4_moe_add_max_tiles(T, E, k, 1)
+        without = thq4.lib().thq4_moe_add_max_tiles(T, E, k, 0)
+        assert with_shared == without + (T + 31) // 32
+        if ref is not None:  # moeMaximumTiles (MoE.hpp:72-77) with 32-row tiles
+            assert with_shared == ref.ref_moe_maximum_tiles(T, 2048, E, k, 768, 32)
+
+
+def test_moe_add_workspace_sizes():
+    L = thq4.lib()
+    full = L.thq4_moe_add_workspace_bytes(256, 2048, 768, 128, 8, 1)
+    assert full > L.thq4_moe_add_workspace_bytes(256, 2048, 768, 128, 8, 0) > 0
+    # a shard holds fewer experts' tiles; without the shared expert it needs less still
+    half = L.thq4_moe_add_partial_workspace_bytes(256, 2048, 768, 128, 8, 0, 64, 1, 1)
+    assert 0 < L.thq4_moe_add_partial_workspace_bytes(256, 2048, 768, 128, 8, 64, 128, 1, 0) < half < full
+    assert L.thq4_moe_add_partial_workspace_bytes(256, 2048, 768, 128, 8, 64, 200, 1, 0) == 0
+    assert L.thq4_moe_scores_workspace_bytes(256, 128) == 8 * 256 * 128 * 4
+
+
+@pytest.mark.parametrize("change,msg", [
+    (dict(I=320), "execution shape"),
+    (dict(H=1000), "execution shape"),
+    (dict(E=300), "execution shape"),
+    (dict(k=9, E=8), "execution shape"),
+])
+def test_moe_add_rejects_bad_shapes(change, msg):
+    args = dict(T=16, H=1024, I=512, E=8, k=2)
+    args.update(change)
+    st = _moe_add(_moe_weights(), **args)
+    assert st == _lib.ERR_INVALID_ARGUMENT and msg in thq4.last_error()
+
+
+def test_moe_add_rejects_bad_weights():
+    w = _moe_weights()
+    w.router.in_ = 512
+    assert _moe_add(w) == _lib.ERR_INVALID_ARGUMENT and "router" in thq4.last_error()
+    w = _moe_weights()
+    w.down = _experts(8, 512, 512)
+    assert _moe_add(w) == _lib.ERR_INVALID_ARGUMENT and "down" in thq4.last_error()
+    w = _moe_weights()
+    w.shared_expert_gate.q = None  # a shared expert without its gate
+    assert _moe_add(w) == _lib.ERR_INVALID_ARGUMENT
+    w = _moe_weights()
+    w.up = _experts(8, 512, 1024, sbd=thq4.F16)
+    assert _moe_add(w) == _lib.ERR_INVALID_ARGUMENT and "dtype" in thq4.last_error()
+    w = _moe_weights()
+    w.router.q = 0x30008  # the router's bytes are read as 16-byte vectors
+    assert _moe_add(w) == _lib.ERR_INVALID_ARGUMENT and "16-byte" in thq4.last_error()
+    assert _moe_add(_moe_weights(), ws_bytes=1024) == _lib.ERR_WORKSPACE
+    assert "smaller than its bound" in thq4.last_error()
+
+
+def test_peer_exchange_rejects_bad_descriptors():
+    L = thq4.lib()
+    w = _w(out=256, inp=512)
+    g = _lib.thq4_peer_gather()
+    g.world, g.rank, g.rows, g.stride = 2, 0, 256, 512
+    g.dst = g.flags = g.count = g.arrive = 0x5000
+    call = lambda y=0x4000, xd=thq4.BF16: L.thq4_linear_peer(  # noqa: E731
+        ctypes.byref(w), None, ctypes.c_void_p(0x3000), xd, 1, ctypes.c_void_p(y) if y else None,
+        ctypes.c_void_p(0x100000), 1 << 20, ctypes.byref(g), None)
+    g.world = 9
+    assert call() == _lib.ERR_INVALID_ARGUMENT and "world" in thq4.last_error()
+    g.world, g.out_mode = 2, 4
+    assert call() == _lib.ERR_INVALID_ARGUMENT and "out_mode" in thq4.last_error()
+    g.out_mode, g.x_parts = 1, 9
+    assert call() == _lib.ERR_INVALID_ARGUMENT and "x_parts" in thq4.last_error()
+    g.x_parts, g.slot = 0, 100  # reduce slots hold m * stride floats
+    assert call(y=0) == _lib.ERR_INVALID_ARGUMENT and "slot" in thq4.last_error()
+    g.out_mode, g.x_parts, g.x_slot = 2, 2, 512
+    assert call(xd=thq4.BF16) == _lib.ERR_INVALID_ARGUMENT and "partials are f32" in thq4.last_error()
+    g.x_slot = 100
+    assert call(xd=thq4.F32) == _lib.ERR_INVALID_ARGUMENT and "x_slot" in thq4.last_error()
