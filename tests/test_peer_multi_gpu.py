@@ -282,3 +282,77 @@ def test_two_gpu_row_parallel_reduce_matches_oracle():
         assert status == 0, f"rank {rank}: device status {status:#x}"
         assert_close_ref(f"rank {rank} row-parallel chain", f3, y3[0])
     assert np.array_equal(got[0][0], got[1][0]), "ranks disagree"
+
+
+def _block_rank(rank, world, port, ret):
+    """The Splash MoE block (Q8 router, shared expert) with the routed experts
+    split over two ranks and the shared expert on the last rank
+    (thq4.shard.moe_add_sharded: partials, one NCCL all-reduce)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    import q4oracle as O
+    import thq4
+    from test_moe_q8_cpu import E, H, I, K, configure_routing, fixture_router, fixture_shared_gate
+    from thq4.shard import expert_range, moe_add_sharded
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    d = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=d,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        rows = 48
+        fx = O.splash_moe_fixture(H, I, E, rows)
+        x = configure_routing(fx["x"], "dispersed")
+        e0, n = expert_range(E, world, rank)
+        sl = lambda name, lo=0, hi=None: torch.from_numpy(fx[name][lo:hi]).to(d)  # noqa: E731
+        bf = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(d).view(torch.bfloat16)  # noqa
+        q8 = lambda p: thq4.Q8Projection(torch.from_numpy(p[0]).to(d), bf(p[1]), bf(p[2]), H)  # noqa: E731
+        last = rank == world - 1
+        w = thq4.MoeWeights(q8(fixture_router(H, E)),
+                            thq4.PackedExperts.from_slabs(sl("gate", e0, e0 + n), I, H, thq4.BF16),
+                            thq4.PackedExperts.from_slabs(sl("up", e0, e0 + n), I, H, thq4.BF16),
+                            thq4.PackedExperts.from_slabs(sl("down", e0, e0 + n), H, I, thq4.BF16),
+                            thq4.PackedExperts.from_slabs(sl("shared_gate"), I, H, thq4.BF16) if last else None,
+                            thq4.PackedExperts.from_slabs(sl("shared_up"), I, H, thq4.BF16) if last else None,
+                            thq4.PackedExperts.from_slabs(sl("shared_down"), H, I, thq4.BF16) if last else None,
+                            q8(fixture_shared_gate(H)))
+        y = moe_add_sharded(bf(x), w, K, e0, E, residual=bf(fx["residual"]))
+        torch.cuda.synchronize()
+        ret.put((rank, y.cpu().view(torch.int16).numpy().view(np.uint16)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_moe_block_with_shared_expert():
+    import torch.multiprocessing as mp
+
+    import q4oracle as O
+    from test_moe_q8_cpu import E, H, I, K, configure_routing, fixture_router, fixture_shared_gate, mlx_experts
+
+    paths = [HERE, ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "token-horizon_b200")]
+    os.environ["PYTHONPATH"] = os.pathsep.join(paths + [os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_block_rank, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(ret.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.array_equal(got[0], got[1]), "ranks disagree after the all-reduce"
+    rows = 48
+    fx = O.splash_moe_fixture(H, I, E, rows)
+    x = configure_routing(fx["x"], "dispersed")
+    ids, w, _ = O.moe_route_q8(x, E, K, fixture_router(H, E), fixture_shared_gate(H))
+    gu_q, gu_s, dq, ds, shared = mlx_experts(fx)
+    want, _, dd = O.moe_forward(x, fx["residual"], ids, w, gu_q, gu_s, dq, ds, O.SB_BF16, I, shared=shared)
+    mag = np.abs(O.bf16_to_f32(fx["residual"])).astype(np.float64) + (
+        np.abs(O.bf16_to_f32(w)[:, :, None] * O.bf16_to_f32(dd).reshape(rows, K + 1, H))).sum(axis=1)
+    diff = np.abs(O.bf16_to_f32(got[0]).astype(np.float64) - O.bf16_to_f32(want))
+    assert np.all(diff <= 0.02 + 0.01 * mag), "sharded MoE block differs from the oracle"
