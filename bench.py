@@ -69,7 +69,7 @@ def parse():
     p.add_argument("--nccl-gather", action="store_true",
                    help="N > 1: gather each projection's output with NCCL all-gather (the baseline) instead of "
                         "the GEMV epilogue's NVLink stores")
-    p.add_argument("--tp", default="col", choices=["col", "row"],
+    p.add_argument("--tp", default="row", choices=["col", "row"],
                    help="N > 1: col = every projection column-sharded with a fused all-gather; row = o and down "
                         "row-sharded with a fused all-reduce (partials stored to every rank, summed as the next "
                         "projection stages them), q/k/v and gate/up column-sharded with local outputs")
