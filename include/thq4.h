@@ -397,6 +397,16 @@ thq4_status thq4_copy(void *dst, const void *src, size_t bytes, void *stream);
  * run every instantiated tile config the same way (qwen35.rs:6963-6989).
  * Returns THQ4_ERR_INVALID_ARGUMENT for other values; `reserved` must be 0. */
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved);
+/* The decode/verify launch plan for an out x in weight and m tokens (x_f32,
+ * gate_up as thq4_linear / thq4_gate_up would pass them) on a GPU with `sms`
+ * SMs on which cluster_fit[j] clusters of j one-CTA-per-SM CTAs can be
+ * resident at once (j = 2..8; cluster_fit may be NULL: no clusters).  Fills
+ * plan[8] = {planned (0/1), CTAs, cluster size (1: none), ring stages,
+ * tokens per launch, chunks per 128-row slab, slab-groups per chunk,
+ * dynamic shared memory bytes}.  Host only; the reference's tests pin their
+ * dispatch tables the same way (quant_kernel.rs:5914-5973). */
+thq4_status thq4_debug_gemv_plan(int out, int in, int m, int x_f32, int gate_up, int sms, const int *cluster_fit,
+                                 int64_t *plan);
 
 #ifdef __cplusplus
 }

@@ -227,3 +227,58 @@ def test_peer_exchange_rejects_bad_descriptors():
     assert call(xd=thq4.BF16) == _lib.ERR_INVALID_ARGUMENT and "partials are f32" in thq4.last_error()
     g.x_slot = 100
     assert call(xd=thq4.F32) == _lib.ERR_INVALID_ARGUMENT and "x_slot" in thq4.last_error()
+
+
+# ---- the decode/verify planner's policy table (host only) ------------------------
+# The reference pins its dispatch tables per decode shape (plain_tile_table,
+# qmvt_policy_table, quant_kernel.rs:5914-5973); this is the same check of
+# this library's planner for the BASELINE shapes on a 148-SM B200.  Cluster
+# capacity depends on how the SMs group into GPCs; the table below stands for
+# eight GPCs of 18 SMs (clusters of j: 8 * floor(18 / j)).
+GPC_FIT = [0, 0] + [8 * (18 // j) for j in range(2, 9)]
+
+
+def _plan(out, inp, m=1, x_f32=0, gate_up=0, sms=148, fit=GPC_FIT):
+    p = (ctypes.c_int64 * 8)()
+    f = (ctypes.c_int * 9)(*fit) if fit is not None else None
+    assert thq4.lib().thq4_debug_gemv_plan(out, inp, m, x_f32, gate_up, sms, f, p) == 0, thq4.last_error()
+    return tuple(p)[:7]  # planned, CTAs, cluster size, stages, tokens per launch, chunks per slab, groups per chunk
+
+
+@pytest.mark.parametrize("shape,want", [
+    # hidden-5120 decode layer, m = 1
+    ((17408, 5120, 1, 0, 1), (1, 136, 1, 2, 1, 10, 8)),  # fused gate/up: one whole slab per CTA, no split
+    ((7168, 5120), (1, 112, 2, 5, 1, 10, 8)),  # q/k/v: 56 slabs x clusters of 2
+    ((5120, 5120), (1, 120, 3, 5, 1, 10, 8)),  # o: 40 slabs x 3
+    ((5120, 17408), (1, 120, 3, 5, 1, 34, 8)),  # down: 40 slabs x 3
+    # 6144 x 2048, f32 x and y
+    ((6144, 2048, 1, 1, 0), (1, 144, 3, 5, 1, 4, 8)),
+    # configs[1] verify: gate/up 2 x 9728 x 2560 (76 slabs: split-K over every SM), down 2560 x 9728
+    ((9728, 2560, 8, 0, 1), (1, 148, 1, 2, 8, 5, 8)),
+    ((2560, 9728, 4), (1, 120, 6, 5, 4, 19, 8)),  # 20 slabs: clusters of 6
+    ((9728, 2560, 8, 1, 1), (1, 148, 1, 2, 4, 5, 8)),  # f32 x: 4 tokens per launch (hi + lo columns)
+    # column shards at two and eight GPUs
+    ((2560, 5120), (1, 120, 6, 5, 1, 10, 8)),  # o at N = 2: clusters of 7 do not all fit, 6 do
+    ((896, 5120), (1, 70, 1, 5, 1, 10, 8)),  # q/k/v at N = 8: 7 slabs, too few to fill with clusters
+])
+def test_planner_policy_table(shape, want):
+    assert _plan(*shape) == want
+
+
+def test_planner_without_clusters_and_on_fewer_sms():
+    # no cluster fits: split-K over every SM
+    assert _plan(7168, 5120, fit=None) == (1, 148, 1, 5, 1, 10, 8)
+    # a 132-SM part: the 136-slab gate/up no longer fits one slab per SM
+    assert _plan(17408, 5120, 1, 0, 1, sms=132)[:3] == (1, 132, 1)
+
+
+def test_planner_follows_the_testing_hook():
+    L = thq4.lib()
+    try:
+        assert L.thq4_debug_set_gemv(4, 3, 64, 0) == 0
+        planned, ctas, cl, stages, _, cps, ch = _plan(5120, 5120)
+        assert (planned, ctas, cl, ch, cps) == (1, 64, 1, 4, 20) and stages <= 3
+    finally:
+        assert L.thq4_debug_set_gemv(0, 0, 0, 0) == 0
+    assert _plan(5120, 5120) == (1, 120, 3, 5, 1, 10, 8)
+    assert L.thq4_debug_gemv_plan(5120, 100, 1, 0, 0, 148, None, (ctypes.c_int64 * 8)()) == _lib.ERR_INVALID_ARGUMENT

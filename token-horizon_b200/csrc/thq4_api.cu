@@ -783,4 +783,19 @@ thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
   return THQ4_OK;
 }
 
+thq4_status thq4_debug_gemv_plan(int out, int in, int m, int x_f32, int gate_up, int sms, const int *cluster_fit,
+                                 int64_t *plan) {
+  if (out < 1 || in < kGroup || in % kGroup || m < 1 || sms < 1 || sms > 1024 || !plan)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_debug_gemv_plan: need out >= 1, in a positive multiple of 64, m >= 1, 1 <= sms <= 1024, "
+                     "plan non-NULL");
+  const GemvPlan p = gemv_plan_for(out, in, m, x_f32 != 0, gate_up != 0, sms, [cluster_fit](int j) {
+    return cluster_fit && j >= 2 && j <= 8 ? cluster_fit[j] : 0;
+  });
+  const int64_t v[8] = {p.ok ? 1 : 0, p.grid, p.cl_j > 1 ? p.cl_j : 1, p.stages, p.tokens_per_pass, p.cps, p.ch,
+                        (int64_t)p.smem};
+  for (int i = 0; i < 8; ++i) plan[i] = p.ok || i == 0 ? v[i] : 0;
+  return THQ4_OK;
+}
+
 }  // extern "C"

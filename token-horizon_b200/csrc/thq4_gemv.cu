@@ -777,7 +777,6 @@ int window_groups(int P) { return P <= 2 ? 4 : (P <= 4 ? 2 : 1); }
 
 }  // namespace
 
-namespace {
 // Clusters of j CTAs (one CTA per SM, the GEMV's footprint) that can be
 // resident at once: it depends on how the SMs group into GPCs.  Asked once
 // per device and j.
@@ -808,7 +807,6 @@ int cluster_capacity(int j) {
   cache[dev][j] = n + 1;
   return n;
 }
-}  // namespace
 
 size_t gemv_workspace_bytes(int rows) {
   // one partial per CTA side, sized for gate and up (room for two CTAs per
@@ -819,10 +817,13 @@ size_t gemv_workspace_bytes(int rows) {
 }
 
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
+  return gemv_plan_for(out, in, m, x_f32, gate_up, device_sm_count(), cluster_capacity);
+}
+
+GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms, const ClusterCapacity &capacity) {
   GemvPlan p{};
   p.ok = false;
   const int ng = in / kGroup;
-  const int sms = device_sm_count();
   const GemvCfg cfg = gemv_cfg_override();
   const int cb = cfg.warps > 0 ? cfg.warps : 8;
   const int cps = (ng + cb - 1) / cb;
@@ -855,7 +856,7 @@ GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up) {
           // the largest j whose clusters all fit at once and fill >= 75%
           for (int jc = std::min(std::min(8, sms / slabs), cps); jc >= 2; --jc) {
             if ((long long)slabs * jc * 100 < (long long)sms * 75) break;
-            if (cluster_capacity(jc) >= slabs) {
+            if (capacity(jc) >= slabs) {
               grid = (long long)slabs * jc;
               p.cl_j = jc;
               break;

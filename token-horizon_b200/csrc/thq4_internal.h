@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <functional>
 #include <string>
 
 #include "../../include/thq4.h"
@@ -70,6 +71,11 @@ size_t gemv_workspace_bytes(int rows);
 // disables; read once).
 bool gemv_pdl_enabled();
 GemvPlan gemv_plan(int out, int in, int m, bool x_f32, bool gate_up);
+// The same plan for a given SM count and cluster capacity (clusters of j
+// one-CTA-per-SM CTAs resident at once); gemv_plan passes the device's.
+using ClusterCapacity = std::function<int(int)>;
+GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms, const ClusterCapacity &capacity);
+int cluster_capacity(int j);
 // The all-gather of column shards fused into the projection (thq4_peer_gather).
 struct PeerGather {
   uint16_t *const *dst;     // device array [world]: each rank's full-vector (bf16) or reduction (f32) buffer

@@ -123,6 +123,7 @@ SIGNATURES = {
     "thq4_ipc_free": (c_int, [c_void_p]),
     "thq4_copy": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
+    "thq4_debug_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
 }
 
 
