@@ -282,3 +282,29 @@ def test_planner_follows_the_testing_hook():
         assert L.thq4_debug_set_gemv(0, 0, 0, 0) == 0
     assert _plan(5120, 5120) == (1, 120, 3, 5, 1, 10, 8)
     assert L.thq4_debug_gemv_plan(5120, 100, 1, 0, 0, 148, None, (ctypes.c_int64 * 8)()) == _lib.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("env,want", [
+    ("4,3,64", (1, 64, 1, None, 1, 20, 4)),   # every field taken
+    ("8,0,0", (1, 120, 3, 5, 1, 10, 8)),      # zeros leave the policy
+    ("5,9,-1", (1, 120, 3, 5, 1, 10, 8)),     # out-of-range fields are ignored one by one
+    ("r2s4", (1, 120, 3, 5, 1, 10, 8)),       # not a THQ4_GEMV value: ignored
+    ("", (1, 120, 3, 5, 1, 10, 8)),
+])
+def test_environment_override_is_parsed_once_and_validated(env, want):
+    """THQ4_GEMV="chunk,stages,grid,pre" is read once per process (as the
+    reference reads its TH_QMVT / TH_Q4_POLICY switches, quant_kernel.rs:
+    41-78, 367-432, and rejects values that name no instantiated config)."""
+    import json
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = (
+        "import ctypes, json, sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+        "from test_abi import _plan\n"
+        "print(json.dumps(_plan(5120, 5120)))\n" % (os.path.join(here, "..", "token-horizon_b200"), here))
+    out = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, THQ4_GEMV=env), capture_output=True,
+                         text=True, timeout=120, check=True).stdout
+    got = tuple(json.loads(out.strip().splitlines()[-1]))
+    assert got[:3] == want[:3] and got[4:] == want[4:]
+    assert (got[3] <= 3) if want[3] is None else got[3] == want[3]
