@@ -191,3 +191,32 @@ def moe_shared_gate(x_bf16, q, scales, biases):
     for w in range(8):
         total = (total + warps[:, w]).astype(np.float32)
     return f32_to_bf16((np.float32(1) / (np.float32(1) + np.exp(-total))).astype(np.float32)), total
+
+
+def moe_group_shared(ids: np.ndarray, k: int, E: int, tile_rows: int):
+    """Grouping with a shared slot last in each token's routes: the routed
+    slots sorted stably by expert, then the shared routes in token order as
+    expert E.  Returns (tiles list, grouped, route_rows)."""
+    ids = np.asarray(ids, dtype=np.int64)
+    T, rpr = ids.shape
+    routed = [(int(ids[t, s]), t * rpr + s) for t in range(T) for s in range(min(k, rpr))]
+    tiles, grouped = [], []
+    route_rows = np.full(T * rpr, 0xFFFFFFFF, dtype=np.uint32)
+    for e in range(E):
+        mine = [r for (ee, r) in routed if ee == e]  # routes ascend: stable
+        for t0 in range(0, len(mine), tile_rows):
+            chunk = mine[t0:t0 + tile_rows]
+            tiles.append((e, len(chunk)))
+            for i, r in enumerate(chunk):
+                route_rows[r] = len(grouped) + i
+            grouped.extend(chunk)
+            grouped.extend([0xFFFFFFFF] * (tile_rows - len(chunk)))
+    if rpr > k:
+        for t0 in range(0, T, tile_rows):
+            chunk = [t * rpr + k for t in range(t0, min(T, t0 + tile_rows))]
+            tiles.append((E, len(chunk)))
+            for i, r in enumerate(chunk):
+                route_rows[r] = len(grouped) + i
+            grouped.extend(chunk)
+            grouped.extend([0xFFFFFFFF] * (tile_rows - len(chunk)))
+    return tiles, np.array(grouped, dtype=np.uint32), route_rows

@@ -199,3 +199,16 @@ def test_reference_fixture_layer_matches_project(fixture):
             magnitude += np.abs(wf[row, slot] * down)
         yf = O.bf16_to_f32(y[row]).astype(np.float64)
         assert np.all(np.abs(yf - expected) <= 0.02 + 0.01 * magnitude), f"row {row}"
+
+
+@pytest.mark.parametrize("T,E_,k,shared,tile_rows", [(37, 16, 4, True, 32), (100, 8, 2, True, 8),
+                                                      (64, 32, 8, False, 32), (1, 4, 2, True, 32)])
+def test_group_shared_c_matches_numpy(T, E_, k, shared, tile_rows):
+    rng = np.random.default_rng(T * E_ + k)
+    ids = np.stack([rng.permutation(E_)[:k] for _ in range(T)]).astype(np.uint32)
+    if shared:
+        ids = np.concatenate([ids, np.full((T, 1), E_, np.uint32)], axis=1)
+    tiles, n, grouped, rr = O.moe_group_shared(ids, k, E_, tile_rows)
+    t2, g2, rr2 = N.moe_group_shared(ids, k, E_, tile_rows)
+    assert n == len(t2) and [tuple(t) for t in tiles[:n]] == t2
+    assert np.array_equal(grouped[:n * tile_rows], g2) and np.array_equal(rr, rr2)
