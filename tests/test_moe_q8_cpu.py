@@ -212,3 +212,61 @@ def test_group_shared_c_matches_numpy(T, E_, k, shared, tile_rows):
     t2, g2, rr2 = N.moe_group_shared(ids, k, E_, tile_rows)
     assert n == len(t2) and [tuple(t) for t in tiles[:n]] == t2
     assert np.array_equal(grouped[:n * tile_rows], g2) and np.array_equal(rr, rr2)
+
+
+def _py_fixture(H_, I_, E_, rows, seed=0x0E5):
+    """moe_metal_test.mm's Random and makeFixture (:69-75, :108-145, :217-271)
+    restated in plain Python, as an independent check of the C generator:
+    nibbles n-major, then per parameter a scale and a bias, slabs packed in
+    StorageN = 256 order; then per row and column an input and a residual."""
+    state = [seed]
+    M = (1 << 64) - 1
+
+    def nxt():
+        state[0] = (state[0] * 6364136223846793005 + 1442695040888963407) & M
+        return state[0] >> 33
+
+    def unit():
+        return np.float32(np.float32(nxt() & 0xFFFFFF) / np.float32(8388608.0)) - np.float32(1.0)
+
+    def fma32(a, b, c):  # the contracted multiply-add of the reference build, rounded once
+        return np.float32(np.float64(np.float32(a)) * np.float64(np.float32(b)) + np.float64(np.float32(c)))
+
+    def slab(out, inp):
+        n_el = out * inp
+        nib = np.array([nxt() & 15 for _ in range(n_el)], dtype=np.uint8).reshape(out, inp)
+        sc, bi = np.empty(n_el // 64, np.uint16), np.empty(n_el // 64, np.uint16)
+        for i in range(n_el // 64):
+            sc[i] = O.f32_to_bf16(np.float32([fma32(0.01, unit() + np.float32(1.0), 0.01)]))[0]
+            bi[i] = O.f32_to_bf16(np.float32([fma32(0.05, unit(), -0.2)]))[0]
+        groups = inp // 64
+        packed = np.zeros(n_el // 2, np.uint8)
+        for n in range(out):
+            prm = ((n // 256) * groups + np.arange(groups)) * 256 + n % 256
+            idx = (prm[:, None] * 64 + np.arange(64)[None, :]).ravel()
+            vals = nib[n].reshape(groups, 64).ravel()
+            lo, hi = idx[idx % 2 == 0], idx[idx % 2 == 1]
+            packed[lo // 2] |= vals[idx % 2 == 0]
+            packed[hi // 2] |= (vals[idx % 2 == 1] << 4).astype(np.uint8)
+        return np.concatenate([packed, sc.view(np.uint8), bi.view(np.uint8)])
+
+    f = {}
+    for name, (o, i_, cnt) in [("gate", (I_, H_, E_)), ("up", (I_, H_, E_)), ("down", (H_, I_, E_)),
+                               ("shared_gate", (I_, H_, 1)), ("shared_up", (I_, H_, 1)),
+                               ("shared_down", (H_, I_, 1))]:
+        f[name] = np.stack([slab(o, i_) for _ in range(cnt)])
+    x, res = np.empty((rows, H_), np.uint16), np.empty((rows, H_), np.uint16)
+    for r in range(rows):
+        sign = np.float32(-1.0 if r % 3 == 0 else 1.0)
+        for c in range(H_):
+            x[r, c] = O.f32_to_bf16(np.float32([sign * fma32(0.45, unit(), 0.55)]))[0]
+            res[r, c] = O.f32_to_bf16(np.float32([np.float32(0.1) * unit()]))[0]
+    f["x"], f["residual"] = x, res
+    return f
+
+
+def test_fixture_generator_matches_a_python_restatement():
+    got = O.splash_moe_fixture(256, 256, 1, 3)
+    want = _py_fixture(256, 256, 1, 3)
+    for name in want:
+        assert np.array_equal(got[name], want[name]), name
