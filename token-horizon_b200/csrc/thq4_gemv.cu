@@ -725,19 +725,20 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
     cfg.numAttrs = 2;
     // all clusters must be resident at once (one wave): how many fit depends
     // on how the SMs group into GPCs; asked once per (instance, size, smem)
-    static std::atomic<uint64_t> key{0};
-    static std::atomic<int> fits{0};
-    const uint64_t want = ((uint64_t)smem << 8) | (uint64_t)a.cl_j;
+    // one word holds the question and its answer, so concurrent callers
+    // never pair one footprint's answer with another's key
+    static std::atomic<uint64_t> cached{0};
+    const uint64_t want = ((uint64_t)smem << 8) | (uint64_t)a.cl_j;  // < 2^40
     int n = 0;
-    if (key.load(std::memory_order_acquire) == want) {
-      n = fits.load(std::memory_order_relaxed);
+    const uint64_t c = cached.load(std::memory_order_relaxed);
+    if (c != 0 && (c >> 20) == want) {
+      n = (int)(c & 0xFFFFFu);
     } else {
       if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
       }
-      fits.store(n, std::memory_order_relaxed);
-      key.store(want, std::memory_order_release);
+      cached.store((want << 20) | (uint64_t)std::min(std::max(n, 0), 0xFFFFF), std::memory_order_relaxed);
     }
     if (n * a.cl_j < grid) return cudaErrorCooperativeLaunchTooLarge;  // the caller re-plans without clusters
   }
