@@ -158,10 +158,13 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
  * that may overlap on the GPU need separate workspaces. */
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
 /* thq4_linear without a workspace argument.  No reference counterpart: the
- * reference's ops take scratch from candle's buffer pool.  The decode/verify
- * kernel's split-K scratch (partial sums and arrival counters) comes from one
- * 6 MiB buffer the library keeps in device memory per device, so the call
- * allocates nothing and needs only the weight, x and y.
+ * reference's ops take scratch from candle's buffer pool.  It routes by row
+ * count exactly as thq4_linear does (the prefill kernel for m > 8 bf16 rows,
+ * which needs no scratch; the decode/verify kernel otherwise), so both entry
+ * points give the same numbers.  The decode/verify kernel's split-K scratch
+ * (partial sums and arrival counters) comes from one 6 MiB buffer the library
+ * keeps in device memory per device, so the call allocates nothing and needs
+ * only the weight, x and y.
  *
  * For callers that cannot allocate or own device memory where they run a
  * projection: a binding that only receives tensors from its host and has no
@@ -179,8 +182,10 @@ size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
  *   - Must start at zero: the arrival counters.  The buffer is zero when the
  *     library's module loads on a device, and every completed call leaves the
  *     counters zero again.  A call whose kernel reported kStatusTimeout
- *     (thq4_device_status) may leave them set; later calls of this entry
- *     point in that process are then unreliable.
+ *     (thq4_device_status) may leave them set, and nothing in this ABI clears
+ *     the buffer: after a timeout, restart the process before calling this
+ *     entry point again (thq4_linear's caller can re-zero its own
+ *     workspace instead).
  *   - Every call on a device shares the one buffer: calls that can overlap on
  *     the GPU (streams not ordered with each other) race and produce wrong
  *     results.  Order them on one stream, or use thq4_linear with a workspace

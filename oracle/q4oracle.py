@@ -28,12 +28,28 @@ SB_BF16 = 0
 SB_F16 = 1
 
 
+def reference_root():
+    """The reference checkout whose headers the pins compile: $REF_ROOT, else
+    BASELINE.json's reference_path; None when neither names a directory (the
+    GPU box has no reference)."""
+    root = os.environ.get("REF_ROOT")
+    if not root:
+        try:
+            import json
+            with open(os.path.join(_HERE, "..", "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(root) else None
+
+
 def build(force: bool = False) -> None:
     """Compile the oracle (and the reference pins when the reference exists)."""
     if force or not os.path.exists(_LIB):
         subprocess.check_call(["make", "-s", "-C", _HERE, "oracle"])
-    if os.path.isdir("/root/reference") and (force or not os.path.exists(_REF)):
-        subprocess.check_call(["make", "-s", "-C", _HERE, "ref"])
+    root = reference_root()
+    if root and (force or not os.path.exists(_REF)):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "ref", "REF_ROOT=" + root])
 
 
 def lib():

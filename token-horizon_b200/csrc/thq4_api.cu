@@ -288,6 +288,13 @@ thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype
   if (s != THQ4_OK) return s;
   s = check_io(x, x_dtype, m, y, y_dtype, who);
   if (s != THQ4_OK) return s;
+  // the same row-count routing as thq4_linear: the prefill kernel needs no
+  // scratch at all
+  if (prefill_supported(m, x_dtype == THQ4_F32)) {
+    const cudaError_t e = prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "thq4_linear_noalloc (prefill)");
+    return THQ4_OK;
+  }
   const size_t need = gemv_workspace_bytes(w->out);
   if (need > kNoAllocScratchBytes)
     return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": a " + std::to_string(w->out) +

@@ -140,6 +140,11 @@ __device__ __forceinline__ void st_cluster_f4(uint32_t addr, float4 v) {
                "f"(v.w)
                : "memory");
 }
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 // System-scope ordering for flags that other GPUs read over NVLink.
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;\n" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {

@@ -335,7 +335,7 @@ __global__ void peer_wait_kernel(uint32_t *const *flags, const uint32_t *count, 
 // The producer lane: streams the run's nch chunks from chunk C0 into the
 // ring.  On a timeout it waits (bounded) for the copies it issued and stops.
 template <int CB, bool GATE_UP>
-__device__ __forceinline__ void produce_run(const GemvArgs &a, int C0, int nch, int R, uint64_t *full, uint64_t *empty,
+__device__ __forceinline__ bool produce_run(const GemvArgs &a, int C0, int nch, int R, uint64_t *full, uint64_t *empty,
                                             uint64_t *xready, unsigned char *ring) {
   constexpr int NS = GATE_UP ? 2 : 1;
   constexpr size_t SB = (size_t)NS * CB * kSgBytes;
@@ -354,7 +354,7 @@ __device__ __forceinline__ void produce_run(const GemvArgs &a, int C0, int nch, 
       raise_status(a.status, kStatusTimeout);
       // copies already issued must land before the CTA's memory is reused
       for (int k = n - R; k < n; ++k) (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
-      return;
+      return false;
     }
     const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
     const long long sg = (long long)sl * a.ng + g0c;
@@ -369,6 +369,7 @@ __device__ __forceinline__ void produce_run(const GemvArgs &a, int C0, int nch, 
     if (++s == R) s = 0, par ^= 1u;
   }
   // the consumers wait for every chunk before they release it
+  return true;
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
@@ -383,6 +384,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + kMaxStages;
   uint64_t *xready = empty + kMaxStages;  // the consumers have staged x
+  // set by any warp of this CTA that gave up on a wait (read by the other
+  // CTAs of a cluster before they exchange tile sums)
+  volatile uint32_t *abort_word = reinterpret_cast<volatile uint32_t *>(smem + 240);
   unsigned char *ring = smem + 256;
   unsigned char *xt = ring + (size_t)R * SB;
   const int P = a.P, P8 = meta_cols(P);
@@ -411,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       mbar_init(&empty[s], kConsumers);
     }
     mbar_init(xready, 1);
+    *abort_word = 0u;
   }
   fence_mbar_init();
   __syncthreads();
@@ -419,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   if (warp == kConsumers) {
     // ---- producer: one elected lane streams the run -------------------------
     // (in slab-split mode the whole warp stays for the final cluster barrier)
-    if (lane == 0) produce_run<CB, GATE_UP>(a, C0, nch, R, full, empty, xready, ring);
+    if (lane == 0 && !produce_run<CB, GATE_UP>(a, C0, nch, R, full, empty, xready, ring)) *abort_word = 1u;
     __syncwarp();
     if (clustered) {  // the consumers' two cluster barriers (below)
       cluster_sync_all();
@@ -592,6 +597,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     if (!aborted && !mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
       raise_status(a.status, kStatusTimeout);
       aborted = true;
+      *abort_word = 1u;
     }
     const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
     const unsigned char *nib = ring + (size_t)s * SB;
@@ -639,10 +645,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     // CTA of the cluster is past its stream (barrier 1) the leader's ring is
     // free; the other parts go there through DSMEM (barrier 2), and the
     // leader adds them in part order and stores the tile.
+    // If any CTA of the cluster gave up on a wait (its copies may still be
+    // landing in its ring), nobody writes into the leader's ring and nothing
+    // is stored; every CTA still passes both barriers.
     reduce_y();
     float4 *xb = reinterpret_cast<float4 *>(ring);
     cluster_sync_all();
-    if (part > 0) {
+    uint32_t gave_up = 0;
+    if (lane == 0)
+      for (int pp = 0; pp < a.cl_j; ++pp)
+        gave_up |= ld_cluster_u32(cluster_map(smem_addr(const_cast<uint32_t *>(abort_word)), (uint32_t)pp));
+    gave_up = __shfl_sync(0xffffffffu, gave_up, 0);
+    if (part > 0 && !gave_up) {
 #pragma unroll
       for (int si = 0; si < NS; ++si) {
         const uint32_t at = smem_addr(xb + (((size_t)part * kSlabTiles + tile) * NS + si) * 32 + lane);
@@ -650,14 +664,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       }
     }
     cluster_sync_all();
-    if (part == 0) {
+    if (part == 0 && !gave_up) {
       for (int pp = 1; pp < a.cl_j; ++pp)
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
           const float4 v = xb[(((size_t)pp * kSlabTiles + tile) * NS + si) * 32 + lane];
           y[si][0] += v.x, y[si][1] += v.y, y[si][2] += v.z, y[si][3] += v.w;
         }
-      if (!aborted) store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
+      store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
     }
     if (a.g_mode) peer_signal(a);
     return;
@@ -724,21 +738,23 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
     // all clusters must be resident at once (one wave): how many fit depends
-    // on how the SMs group into GPCs; asked once per (instance, size, smem)
-    // one word holds the question and its answer, so concurrent callers
-    // never pair one footprint's answer with another's key
-    static std::atomic<uint64_t> cached{0};
+    // on how the SMs group into GPCs; asked once per (device, instance,
+    // size, smem).  One word per device holds the question and its answer,
+    // so concurrent callers never pair one footprint's answer with another's
+    // key; a failed query is not remembered.
+    static std::atomic<uint64_t> cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     const uint64_t want = ((uint64_t)smem << 8) | (uint64_t)a.cl_j;  // < 2^40
     int n = 0;
-    const uint64_t c = cached.load(std::memory_order_relaxed);
+    const uint64_t c = cached[dev].load(std::memory_order_relaxed);
     if (c != 0 && (c >> 20) == want) {
       n = (int)(c & 0xFFFFFu);
+    } else if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess) {
+      cached[dev].store((want << 20) | (uint64_t)std::min(std::max(n, 0), 0xFFFFF), std::memory_order_relaxed);
     } else {
-      if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
-        (void)cudaGetLastError();
-        n = 0;
-      }
-      cached.store((want << 20) | (uint64_t)std::min(std::max(n, 0), 0xFFFFF), std::memory_order_relaxed);
+      (void)cudaGetLastError();
+      n = 0;
     }
     if (n * a.cl_j < grid) return cudaErrorCooperativeLaunchTooLarge;  // the caller re-plans without clusters
   }
@@ -790,6 +806,7 @@ int cluster_capacity(int j) {
   if (cache[dev][j]) return cache[dev][j] - 1;
   auto *k = &gemv_kernel<8, 4, true, true, false, false>;
   int n = 0;
+  bool ok = false;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(j * 64);
@@ -802,9 +819,10 @@ int cluster_capacity(int j) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+    ok = cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess;
   }
   (void)cudaGetLastError();
+  if (!ok) return 0;  // not remembered: asked again next time
   cache[dev][j] = n + 1;
   return n;
 }
