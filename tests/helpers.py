@@ -80,3 +80,58 @@ def assert_gate_up_close(tag: str, got: np.ndarray, gate: np.ndarray, up: np.nda
         tol = split_tolerance(2, want[i], 0.0, gate[i], up[i], slack)
         assert abs(got[i] - want[i]) <= tol, (f"{tag}: element {i}: got {got[i]} want {want[i]} "
                                               f"(g {gate[i]}, u {up[i]}, tol {tol})")
+
+
+def moe_combine_f32(residual_bf16, weights_bf16, d_bf16, T: int, H: int) -> np.ndarray:
+    """The MoE combine before its bf16 rounding (moe.metal:642-664): per
+    token, the residual (or 0) then + w * d over the route slots in order,
+    each product and each sum rounded to f32 (no fused multiply-add), from
+    the oracle's per-route bf16 expert outputs d [T * slots][H]."""
+    w = O.bf16_to_f32(np.asarray(weights_bf16)).astype(np.float32).reshape(T, -1)
+    slots = w.shape[1]
+    d = O.bf16_to_f32(np.asarray(d_bf16)).astype(np.float32).reshape(T, slots, H)
+    acc = np.zeros((T, H), dtype=np.float32) if residual_bf16 is None else \
+        O.bf16_to_f32(np.asarray(residual_bf16)).astype(np.float32).reshape(T, H)
+    for s in range(slots):
+        prod = (w[:, s:s + 1] * d[:, s, :]).astype(np.float32)
+        acc = (acc + prod).astype(np.float32)
+    return acc
+
+
+def ulp_bf16_array(v) -> np.ndarray:
+    """One bf16 step at each |v| (LinearNumerics.hpp ulpBf16, restated in
+    tests/helpers_tol.py and pinned there): 2^(e - 8) for |v| in [2^(e-1), 2^e),
+    2^-133 below the normal range."""
+    a = np.abs(np.asarray(v, dtype=np.float64))
+    out = np.full(a.shape, 2.0 ** -133)
+    ok = a >= 2.0 ** -126
+    _, e = np.frexp(a[ok])
+    out[ok] = np.ldexp(1.0, e - 8)
+    return out
+
+
+def assert_moe_close(tag: str, got32, want32, weights_bf16, d_bf16, T: int, H: int, rel: float = 1e-2,
+                     max_beyond: float = 1e-3) -> dict:
+    """The MoE layer's f32 output (the combine before its bf16 rounding)
+    against the oracle's.  The reference stores every route's expert output d
+    in bf16 (moe.metal:642-664 reads expert_output as bfloat), so two correct
+    implementations whose f32 sums differ in order round a few d elements to
+    neighbouring bf16 values; one such step at |d| ~ 0.5 alone moves an output
+    by ~2e-3, above 1e-2 RMS of this layer.  The bar is therefore, per
+    element: |got - want| <= rel * RMS(want) + sum over the token's routes of
+    |w| * one bf16 step of d (one rounding flip per route), and at most
+    `max_beyond` of the elements may exceed rel * RMS at all (flips are rare)."""
+    got = np.asarray(got32, dtype=np.float64).reshape(T, H)
+    want = np.asarray(want32, dtype=np.float64).reshape(T, H)
+    w = np.abs(O.bf16_to_f32(np.asarray(weights_bf16)).astype(np.float64)).reshape(T, -1)
+    slots = w.shape[1]
+    d = O.bf16_to_f32(np.asarray(d_bf16)).astype(np.float64).reshape(T, slots, H)
+    flip = (w[:, :, None] * ulp_bf16_array(d)).sum(axis=1)
+    rms = float(np.sqrt(np.mean(want ** 2)))
+    err = np.abs(got - want)
+    bad = err > rel * rms + flip
+    assert not bad.any(), (f"{tag}: {int(bad.sum())} outputs beyond 1e-2 RMS + one bf16 step per route; "
+                           f"worst {float(err[bad].max()):.3e} (RMS {rms:.3e})")
+    beyond = float((err > rel * rms).mean())
+    assert beyond <= max_beyond, f"{tag}: {beyond:.2e} of the outputs exceed {rel} RMS (flips should be rare)"
+    return {"max_err_over_rms": float(err.max()) / rms, "beyond_rel": beyond}

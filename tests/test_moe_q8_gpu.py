@@ -13,6 +13,7 @@ import torch
 
 import q4oracle as O
 import thq4
+from helpers import assert_moe_close, moe_combine_f32
 from thq4 import _lib
 from test_moe_q8_cpu import (E, H, I, K, configure_routing, fixture_router, fixture_shared_gate, mlx_experts,
                              rand_q8)
@@ -121,6 +122,35 @@ def test_reference_fixture_moe_add(fixture, distribution, rows):
     assert np.all(np.isfinite(got))
     bad = np.abs(got - ref) > 0.02 + 0.01 * mag
     assert not bad.any(), f"{bad.sum()} outputs differ from the oracle's layer"
+
+
+@pytest.mark.parametrize("distribution", ["dispersed", "concentrated", "skewed"])
+def test_reference_fixture_f32_at_north_star_bar(fixture, distribution):
+    """The whole block (all 520 rows, shared expert included) in f32: the
+    f32 output of thq4_moe_add_partial over every expert, with the residual,
+    is the combine before its one bf16 rounding; against the oracle's f32
+    combine of its own per-route expert outputs, max|err| <= 1e-2 * RMS plus
+    one bf16 step of each route's bf16 expert output (assert_moe_close; the
+    reference test's 0.02 + 0.01 magnitude above is the weaker check)."""
+    rows = 520
+    x = configure_routing(fixture["x"], distribution)[:rows]
+    res = fixture["residual"][:rows]
+    w = _weights(fixture)
+    y32 = thq4.moe_add_partial(dev_bf16(x), w, K, 0, E, residual=dev_bf16(res))
+    y = thq4.moe_add(dev_bf16(x), w, K, residual=dev_bf16(res))
+    torch.cuda.synchronize()
+    assert status() == 0
+    want_ids, want_w, _ = O.moe_route_q8(x, E, K, fixture_router(H, E), fixture_shared_gate(H))
+    gu_q, gu_s, dq, ds, shared = mlx_experts(fixture)
+    _, _, d = O.moe_forward(x, res, want_ids, want_w, gu_q, gu_s, dq, ds, O.SB_BF16, I, shared=shared)
+    # the device's routing weights may differ from the host's by one bf16 step
+    # (exp); the oracle's combine uses the device's weights
+    _, wt, _, _, _ = thq4.moe_route_q8(dev_bf16(x), w.router, E, K, w.shared_expert_gate)
+    want = moe_combine_f32(res, bits(wt), d, rows, H)
+    got = y32.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    assert_moe_close(f"block f32 {distribution}", got, want, bits(wt), d, rows, H)
+    assert torch.equal(y32.to(torch.bfloat16).view(torch.int16), y.view(torch.int16)), "bf16 block != rounded f32"
 
 
 def test_without_shared_expert_equals_logits_path(fixture):
