@@ -13,18 +13,30 @@ times over and no flush is needed.  Per layer: the fused qkv GEMV, o, the
 fused gate/up GEMV with the SwiGLU epilogue, and down; each layer starts from
 the same input activation (no norms or attention exist on this path, and
 chaining raw projections would overflow bf16), while every projection still
-consumes the previous one's output.  With N GPUs every projection is
-column-sharded (rows split in multiples of 16) and its output is
-all-gathered over NVLink with NCCL before the next projection reads it.
+consumes the previous one's output.  On one GPU the step's 96 projections
+run by default as one persistent chain launch (thq4_linear_chain;
+`--launch chain-layer` runs one chain per layer, `--launch calls` one
+thq4_linear / thq4_gate_up call per projection; the line reports all
+three).  With N GPUs (the default `--tp row`) q/k/v and gate/up are
+column-sharded with local outputs and o and down are row-sharded: their f32
+partials go over NVLink into every rank's reduction buffer from the GEMV's
+epilogue and the next projection sums them as it stages its input (no
+collective inside the step); each layer then reads the previous layer's
+all-reduced output.  `--tp col` column-shards every projection with the
+all-gather fused into the epilogue, `--nccl-gather` uses NCCL all-gathers.
 
 One JSON line on rank 0: `value` is algorithmic weight bytes of the whole job
 per step / max-over-ranks step time (GB/s), the step captured in a CUDA graph
 and timed with CUDA events; `e2e` is the same metric with the input copied
-from pinned host memory and the result read back inside the timed region;
-`roofline` times the dominant kernel (the fused gate/up GEMV) alone;
-`cpu_baseline` times the CPU restatement of the reference's CPU path on a
-bounded sample (N=1 only); `prefill` reports the prefill GEMM (BASELINE
-configs[2], M=512) in TFLOP/s.
+from pinned host memory and the layer output read back inside the timed
+region; `roofline` is the dominant kernel; `cpu_baseline` times the CPU
+restatement of the reference's CPU path on a bounded sample (N=1 only,
+before any CUDA work); `prefill` reports the prefill GEMM (BASELINE
+configs[2], M=512 and 2048) in TFLOP/s, `moe` the MoE layer,
+`c1` the single GEMV of configs[0] and `verify` the spec-verify products of
+configs[1] (N=1).  With N > 1 the line also carries `kernel_only` (the same
+shards without any exchange) and `parity` (the sharded layer's output
+against one GPU's unsharded recomputation).
 
 `--impl reference` times the reference's CPU semantics (the oracle port, all
 host threads) on the same workload and metric; under torchrun only rank 0
@@ -65,7 +77,14 @@ def parse():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--skip-prefill", action="store_true")
+    p.add_argument("--skip-prefill", action="store_true", help="N=1: skip the prefill and MoE lines")
+    p.add_argument("--skip-extras", action="store_true", help="N=1: skip the configs[0] and configs[1] lines")
+    p.add_argument("--launch", default="chain-step", choices=["chain-step", "chain-layer", "calls"],
+                   help="N=1: the step as one persistent chain launch (thq4_linear_chain), one chain per layer, or "
+                        "one thq4_linear / thq4_gate_up call per projection (N > 1 always uses calls)")
+    p.add_argument("--trace", default=None,
+                   help="write the GEMV's per-phase %%globaltimer trace of one step made of separate calls (after "
+                        "the timed runs) to this JSON file (one file per rank: .rankR appended for N > 1)")
     p.add_argument("--nccl-gather", action="store_true",
                    help="N > 1: gather each projection's output with NCCL all-gather (the baseline) instead of "
                         "the GEMV epilogue's NVLink stores")
@@ -165,6 +184,9 @@ def run_thq4(args):
     from thq4.shard import shard_rows, slice_cols_mlx
 
     world, rank, local = dist_env()
+    # the CPU baseline runs first, before this process has touched CUDA, as
+    # the reference arm does
+    cpu = cpu_baseline(args.cpu_seconds) if rank == 0 and world == 1 else None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -192,8 +214,10 @@ def run_thq4(args):
         del wq, sb
         return thq4.PackedWeight.repack(thq4.SRC_MLX, wq_r, sb_r, out_rows, cols, thq4.F16)
 
-    layers = []
-    for l in range(L):
+    def build_layer(l, q0, qn, k0, kn, i0, inn, rows_of_o_down):
+        """Layer l's weights (seeds 1000 (l + 1) + 1..7): this rank's shards, or
+        the whole layer with full ranges.  rows_of_o_down: o and down hold
+        input-column shards (row-parallel) instead of output rows."""
         s = 1000 * (l + 1)
         # fused qkv shard = [q rows | k rows | v rows] of this rank, repacked as three weights then joined
         wq_q, sb_q = synth.normal_weight(HIDDEN, HIDDEN, s + 1, dev)
@@ -204,11 +228,13 @@ def run_thq4(args):
         del wq_q, wq_k, wq_v, sb_q, sb_k, sb_v
         qkv = thq4.PackedWeight.repack(thq4.SRC_MLX, wq_qkv, sb_qkv, qn + 2 * kn, HIDDEN, thq4.F16)
         del wq_qkv, sb_qkv
-        o = packed_cols(HIDDEN, HIDDEN, s + 4, q0, qn) if row_tp else packed(HIDDEN, HIDDEN, s + 4, q0, qn)
+        o = packed_cols(HIDDEN, HIDDEN, s + 4, q0, qn) if rows_of_o_down else packed(HIDDEN, HIDDEN, s + 4, q0, qn)
         gate = packed(INTER, HIDDEN, s + 5, i0, inn)
         up = packed(INTER, HIDDEN, s + 6, i0, inn)
-        down = packed_cols(HIDDEN, INTER, s + 7, i0, inn) if row_tp else packed(HIDDEN, INTER, s + 7, q0, qn)
-        layers.append((qkv, o, gate, up, down))
+        down = packed_cols(HIDDEN, INTER, s + 7, i0, inn) if rows_of_o_down else packed(HIDDEN, INTER, s + 7, q0, qn)
+        return qkv, o, gate, up, down
+
+    layers = [build_layer(l, q0, qn, k0, kn, i0, inn, row_tp) for l in range(L)]
     torch.cuda.synchronize()
     rank_bytes = sum(p.nbytes for lay in layers for p in lay)
 
@@ -267,58 +293,87 @@ def run_thq4(args):
         g_dn = peer.gather(off_y, qn, q0, HIDDEN, wait=True)
         V = lambda off: ctypes.c_void_p(peer.ptr(off))  # noqa: E731
 
-    def step_peer():
+    def layer_peer(lay):
+        qkv, o, gate, up, down = lay
         s = stream()
-        for (qkv, o, gate, up, down) in layers:
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, P(x_in), BF, 1, P(t_qkv), P(ws), ws_bytes,
-                                            ctypes.byref(g_qkv), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, V(off_q), BF, 1, P(t_o), P(ws), ws_bytes,
-                                            ctypes.byref(g_o), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(off_o), BF, 1, P(t_h),
-                                            P(ws), ws_bytes, ctypes.byref(g_gu), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, V(off_h), BF, 1, P(t_d), P(ws), ws_bytes,
-                                            ctypes.byref(g_dn), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, P(x_in), BF, 1, P(t_qkv), P(ws), ws_bytes,
+                                        ctypes.byref(g_qkv), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, V(off_q), BF, 1, P(t_o), P(ws), ws_bytes,
+                                        ctypes.byref(g_o), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(off_o), BF, 1, P(t_h),
+                                        P(ws), ws_bytes, ctypes.byref(g_gu), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, V(off_h), BF, 1, P(t_d), P(ws), ws_bytes,
+                                        ctypes.byref(g_dn), s))
 
-    def step_row():
+    def layer_row(li, lay):
+        qkv, o, gate, up, down = lay
         s = stream()
-        for li, (qkv, o, gate, up, down) in enumerate(layers):
-            if li == 0:  # the step's input
-                thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
-            else:  # the previous layer's down, all-reduced as it is staged
-                thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, V(red_d), F32, 1, P(t_qkv), P(ws),
-                                                ws_bytes, ctypes.byref(g_qkv), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, P(t_qkv), BF, 1, None, P(ws), ws_bytes,
-                                            ctypes.byref(g_o), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(red_o), F32, 1, P(t_h),
-                                            P(ws), ws_bytes, ctypes.byref(g_gu), s))
-            thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, P(t_h), BF, 1, None, P(ws), ws_bytes,
-                                            ctypes.byref(g_dn), s))
-
-    def step():
-        if row_tp:
-            return step_row()
-        if peer is not None:
-            return step_peer()
-        s = stream()
-        for (qkv, o, gate, up, down) in layers:
+        if li == 0:  # the step's input
             thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
-            if world > 1:
-                dist.all_gather_into_tensor(full_q, t_qkv[:, :qn])
-                src_o = full_q
-            else:
-                src_o = t_qkv  # the first 5120 outputs are q; o reads in = 5120 of them
-            thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(src_o), BF, 1, P(t_o), BF, P(ws), ws_bytes, s))
-            if world > 1:
-                dist.all_gather_into_tensor(full_o, t_o)
-            thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h),
-                                        BF, P(ws), ws_bytes, s))
-            if world > 1:
-                dist.all_gather_into_tensor(full_h, t_h)
-            thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(full_h), BF, 1, P(t_d), BF, P(ws), ws_bytes, s))
-            if world > 1:
-                dist.all_gather_into_tensor(y_out, t_d)
+        else:  # the previous layer's down, all-reduced as it is staged
+            thq4.check(lib.thq4_linear_peer(ctypes.byref(qkv.desc), None, V(red_d), F32, 1, P(t_qkv), P(ws),
+                                            ws_bytes, ctypes.byref(g_qkv), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(o.desc), None, P(t_qkv), BF, 1, None, P(ws), ws_bytes,
+                                        ctypes.byref(g_o), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(red_o), F32, 1, P(t_h),
+                                        P(ws), ws_bytes, ctypes.byref(g_gu), s))
+        thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, P(t_h), BF, 1, None, P(ws), ws_bytes,
+                                        ctypes.byref(g_dn), s))
 
-    launches_per_step = 4 * L
+    def layer_plain(lay):
+        qkv, o, gate, up, down = lay
+        s = stream()
+        thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
+        if world > 1:
+            dist.all_gather_into_tensor(full_q, t_qkv[:, :qn])
+            src_o = full_q
+        else:
+            src_o = t_qkv  # the first 5120 outputs are q; o reads in = 5120 of them
+        thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(src_o), BF, 1, P(t_o), BF, P(ws), ws_bytes, s))
+        if world > 1:
+            dist.all_gather_into_tensor(full_o, t_o)
+        thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(full_o), BF, 1, P(t_h),
+                                    BF, P(ws), ws_bytes, s))
+        if world > 1:
+            dist.all_gather_into_tensor(full_h, t_h)
+        thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(full_h), BF, 1, P(t_d), BF, P(ws), ws_bytes, s))
+        if world > 1:
+            dist.all_gather_into_tensor(y_out, t_d)
+
+    def layer(li, lay):
+        if row_tp:
+            layer_row(li, lay)
+        elif peer is not None:
+            layer_peer(lay)
+        else:
+            layer_plain(lay)
+
+    def step_calls():
+        for li, lay in enumerate(layers):
+            layer(li, lay)
+
+    # N = 1: the step's projections can also run as persistent chains
+    # (thq4_linear_chain): one launch per layer or one for the whole step
+    chains_layer = chain_step = None
+    if world == 1:
+        chains_layer = [thq4.LinearChain([(qkv, None, x_in, t_qkv), (o, None, t_qkv, t_o), (gate, up, t_o, t_h),
+                                          (down, None, t_h, t_d)], device=dev)
+                        for (qkv, o, gate, up, down) in layers]
+        chain_step = thq4.LinearChain([op for c in chains_layer for op in c._keep], device=dev)
+
+    def step_chain_layer():
+        for c in chains_layer:
+            c()
+
+    def step_chain_step():
+        chain_step()
+
+    modes = {"calls": (step_calls, 4 * L)}
+    if world == 1:
+        modes["chain-layer"] = (step_chain_layer, L)
+        modes["chain-step"] = (step_chain_step, 1)
+    launch_mode = args.launch if world == 1 else "calls"
+    step, launches_per_step = modes[launch_mode]
 
     def barrier():
         if world > 1:
@@ -374,20 +429,44 @@ def run_thq4(args):
     total_bytes = LAYER_BYTES * L
     value = total_bytes / (ms_step * 1e-3) / 1e9
 
+    # the other launch modes of the same step, for comparison (N = 1)
+    mode_results = {launch_mode: {"ms_per_step": round(ms_step, 5), "value": round(value, 2),
+                                  "launches_per_step": launches_per_step}}
+    for name, (fn, nl) in modes.items():
+        if name == launch_mode:
+            continue
+        fn()
+        gm = None
+        if not args.no_graph:
+            gm = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gm):
+                fn()
+        rm = gm.replay if gm is not None else fn
+        for _ in range(3):
+            rm()
+        msm = timed(rm, args.steps) / args.steps
+        mode_results[name] = {"ms_per_step": round(msm, 5), "value": round(total_bytes / (msm * 1e-3) / 1e9, 2),
+                              "launches_per_step": nl}
+        if gm is not None:
+            gm.reset()
+        rm = gm = None
+
     # e2e: pinned host input -> device, step, result -> pinned host
     x_host = torch.empty((1, HIDDEN), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(x_in.cpu())
     y_host = torch.empty((1, HIDDEN), dtype=torch.bfloat16).pin_memory()
 
-    if row_tp:  # the step's result is the last down's partials, one per rank
-        y_host = torch.empty((world, HIDDEN), dtype=torch.float32).pin_memory()
+    if row_tp:  # the step's result: the last down's partials, summed on the device
+        y_host = torch.empty((1, HIDDEN), dtype=torch.float32).pin_memory()
+        red_dev = torch.empty((world, HIDDEN), dtype=torch.float32, device=dev)
 
     def e2e_body():
         x_in.copy_(x_host, non_blocking=True)
         run()
         if row_tp:
             thq4.check(lib.thq4_peer_wait(ctypes.byref(g_gu), stream()))
-            thq4.check(lib.thq4_copy(P(y_host), V(red_d), world * HIDDEN * 4, stream()))
+            thq4.check(lib.thq4_copy(P(red_dev), V(red_d), world * HIDDEN * 4, stream()))
+            y_host.copy_(red_dev.sum(0, keepdim=True), non_blocking=True)
         elif peer is not None:
             thq4.check(lib.thq4_copy(P(y_host), V(off_y), HIDDEN * 2, stream()))
         else:
@@ -397,6 +476,134 @@ def run_thq4(args):
         e2e_body()
     ms_e2e = timed(e2e_body, args.steps) / args.steps
     e2e_value = total_bytes / (ms_e2e * 1e-3) / 1e9
+
+    if args.trace:
+        path = args.trace + (f".rank{rank}" if world > 1 else "")
+        trace_step(torch, lib, step_calls, dev, path, barrier, world, rank)
+
+    kernel_only = parity = projections = None
+    if world > 1:
+        # the same shards and launches with no exchange and no waits: what the
+        # step costs without its collectives
+        k_o = torch.empty((1, layers[0][1].desc.out), dtype=torch.bfloat16, device=dev)
+        k_d = torch.empty((1, layers[0][4].desc.out), dtype=torch.bfloat16, device=dev)
+        o_in = t_qkv if row_tp else x_in
+        d_in = t_h if row_tp else full_h
+
+        def step_local():
+            s = stream()
+            for (qkv, o, gate, up, down) in layers:
+                thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(t_qkv), BF, P(ws), ws_bytes, s))
+                thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(o_in), BF, 1, P(k_o), BF, P(ws), ws_bytes, s))
+                thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(x_in), BF, 1, P(t_h),
+                                            BF, P(ws), ws_bytes, s))
+                thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(d_in), BF, 1, P(k_d), BF, P(ws), ws_bytes, s))
+
+        step_local()
+        g_loc = None
+        if not args.no_graph:
+            g_loc = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_loc):
+                step_local()
+        run_loc = g_loc.replay if g_loc is not None else step_local
+        for _ in range(3):
+            run_loc()
+        ms_loc = timed(run_loc, args.steps) / args.steps
+        kernel_only = {"value": round(total_bytes / (ms_loc * 1e-3) / 1e9, 2), "unit": "GB/s",
+                       "ms_per_step": round(ms_loc, 5),
+                       "what": "the same per-rank shards and launches with no exchange (no NVLink stores, flags or "
+                               "waits): whole-job weight bytes / max-over-ranks step time"}
+        if g_loc is not None:
+            g_loc.reset()
+        run_loc = g_loc = None
+
+        # parity: layer 0 through the sharded chain (the step's own calls),
+        # against the same layer recomputed unsharded on one GPU (rank 0)
+        torch.cuda.synchronize()
+        barrier()
+        layer(0, layers[0])
+        if row_tp:
+            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_gu), stream()))
+            parts = torch.empty((world, HIDDEN), dtype=torch.float32, device=dev)
+            thq4.check(lib.thq4_copy(P(parts), V(red_d), world * HIDDEN * 4, stream()))
+            ph = parts.cpu().numpy()
+            y_sh = ph[0].copy()
+            for r in range(1, world):  # the rank-order sum the next projection would form
+                y_sh = (y_sh + ph[r]).astype(ph.dtype)
+        else:
+            if peer is not None:
+                thq4.check(lib.thq4_peer_wait(ctypes.byref(g_dn), stream()))
+                y_dev = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=dev)
+                thq4.check(lib.thq4_copy(P(y_dev), V(off_y), HIDDEN * 2, stream()))
+            else:
+                y_dev = y_out
+            y_sh = y_dev.float().cpu().numpy()[0]
+        torch.cuda.synchronize()
+        if rank == 0:
+            import numpy as np
+            full = build_layer(0, 0, HIDDEN, 0, KV, 0, INTER, False)
+            f_ws = torch.zeros(max(lib.thq4_linear_workspace_bytes(ctypes.byref(p.desc), 1) for p in full),
+                               dtype=torch.uint8, device=dev)
+            fb = f_ws.numel()
+            f_qkv = torch.empty((1, HIDDEN + 2 * KV), dtype=torch.bfloat16, device=dev)
+            f_o = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=dev)
+            f_h = torch.empty((1, INTER), dtype=torch.bfloat16, device=dev)
+            f_y = torch.empty((1, HIDDEN), dtype=torch.float32 if row_tp else torch.bfloat16, device=dev)
+            s = stream()
+            qkv, o, gate, up, down = full
+            thq4.check(lib.thq4_linear(ctypes.byref(qkv.desc), P(x_in), BF, 1, P(f_qkv), BF, P(f_ws), fb, s))
+            thq4.check(lib.thq4_linear(ctypes.byref(o.desc), P(f_qkv), BF, 1, P(f_o), BF, P(f_ws), fb, s))
+            thq4.check(lib.thq4_gate_up(ctypes.byref(gate.desc), ctypes.byref(up.desc), P(f_o), BF, 1, P(f_h), BF,
+                                        P(f_ws), fb, s))
+            thq4.check(lib.thq4_linear(ctypes.byref(down.desc), P(f_h), BF, 1, P(f_y),
+                                       thq4.F32 if row_tp else BF, P(f_ws), fb, s))
+            y_ref = f_y.float().cpu().numpy()[0].astype(np.float64)
+            rms = float(np.sqrt(np.mean(y_ref ** 2)))
+            err = float(np.abs(y_sh.astype(np.float64) - y_ref).max())
+            parity = {"max_err_over_rms": round(err / rms, 6), "rms": round(rms, 6), "bar": 1e-2,
+                      "ok": bool(err <= 1e-2 * rms),
+                      "vs": "layer 0 of the step through the sharded chain (its exchanges included) against the "
+                            "same layer unsharded on one GPU (rank 0), " +
+                            ("f32 outputs" if row_tp else "bf16 outputs")}
+            del full, f_ws
+        barrier()
+    else:
+        # each projection kind alone: 24 launches on the 24 layers' weights
+        def kind(i):
+            def body():
+                s = stream()
+                for lay in layers:
+                    w = lay[i]
+                    if i == 2:
+                        thq4.check(lib.thq4_gate_up(ctypes.byref(w.desc), ctypes.byref(lay[3].desc), P(x_in), BF, 1,
+                                                    P(t_h), BF, P(ws), ws_bytes, s))
+                    else:
+                        src = t_h if i == 4 else x_in
+                        thq4.check(lib.thq4_linear(ctypes.byref(w.desc), P(src), BF, 1,
+                                                   P(t_qkv if i == 0 else t_o), BF, P(ws), ws_bytes, s))
+            return body
+
+        projections = {}
+        reps_k = max(5, min(100, args.steps))
+        for i, name in ((0, "qkv 7168x5120"), (1, "o 5120x5120"), (2, "gate_up 2x17408x5120"),
+                        (4, "down 5120x17408")):
+            body = kind(i)
+            body()
+            gk = None
+            if not args.no_graph:
+                gk = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gk):
+                    body()
+            rk = gk.replay if gk is not None else body
+            for _ in range(3):
+                rk()
+            us = timed(rk, reps_k) / (reps_k * L) * 1e3
+            nb = layers[0][i].nbytes + (layers[0][3].nbytes if i == 2 else 0)
+            projections[name] = {"us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                                 "frac": round(nb / (us * 1e-6) / 1e9 / hbm_peak, 4)}
+            if gk is not None:
+                gk.reset()
+            rk = gk = None
 
     # roofline: the fused gate/up GEMV (dominant kernel) alone, one launch per layer
     g2 = None
@@ -445,6 +652,14 @@ def run_thq4(args):
         prefill = bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind)
         torch.cuda.empty_cache()
         moe = bench_moe(torch, thq4, synth, dev, hbm_peak)
+        torch.cuda.empty_cache()
+    c1 = verify = None
+    if rank == 0 and world == 1 and not args.skip_extras:
+        layers = chains_layer = chain_step = None
+        torch.cuda.empty_cache()
+        c1 = bench_c1(torch, thq4, synth, dev, hbm_peak, not args.no_graph)
+        torch.cuda.empty_cache()
+        verify = bench_verify(torch, thq4, synth, dev, hbm_peak, not args.no_graph)
 
     # Release the graphs (they hold NCCL work) before the process group goes
     # away, or its teardown waits for good: reset them and drop every
@@ -461,10 +676,28 @@ def run_thq4(args):
     if peer is not None:
         peer.close()
 
-    cpu = None
-    if rank == 0 and world == 1:
-        cpu = cpu_baseline(args.cpu_seconds)
-
+    gate_up_alone = {"kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue), one launch per layer",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "bytes_per_launch": int(gu_bytes),
+                     "us_per_launch": round(ms_gu * 1e3, 3)}
+    if launch_mode == "chain-step":
+        # the step is one launch of the chain kernel: it is the dominant (only) kernel
+        chain_traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+                tr = json.load(f).get("chain_bytes_per_weight")
+            if tr:
+                chain_traffic = tr * LAYER_WEIGHTS * L
+        except Exception:
+            pass
+        roofline = {"bound": "hbm", "kernel": "chain_kernel (the step's 96 projections in one persistent launch)",
+                    "achieved": round(value, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(value / hbm_peak, 4), "peak_kind": peak_kind, "traffic": chain_traffic,
+                    "bytes_per_launch": int(total_bytes), "us_per_launch": round(ms_step * 1e3, 3),
+                    "gate_up_alone": gate_up_alone}
+    else:
+        roofline = dict(bound="hbm", peak_kind=peak_kind, traffic=traffic, **gate_up_alone,
+                        step_frac=round(value / world / hbm_peak, 4))
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -494,24 +727,205 @@ def run_thq4(args):
                         ", outputs gathered by the GEMV epilogue (NVLink stores to IPC-mapped buffers + flags)")),
                 "cuda_graph": cuda_graph_used,
             },
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel (fused gate/up, SwiGLU epilogue)",
-                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "bytes_per_launch": int(gu_bytes), "us_per_launch": round(ms_gu * 1e3, 3),
-                         "step_frac": round(value / world / hbm_peak, 4)},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * HIDDEN * world,
-                    "d2h_bytes_per_step": (4 * HIDDEN * world * world) if row_tp else 2 * HIDDEN * world,
+                    "d2h_bytes_per_step": (4 * HIDDEN * world) if row_tp else 2 * HIDDEN * world,
                     "ms_per_step": round(ms_e2e, 5)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
+            "launch_mode": launch_mode,
+            "launch_modes": mode_results,
+            "kernel_only": kernel_only,
+            "parity": parity,
+            "projections": projections,
             "prefill": prefill,
             "moe": moe,
+            "c1": c1,
+            "verify": verify,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+TRACE_PHASES = ("running", "predecessor complete", "peers' flags seen", "activation staged",
+                "first stage landed", "stream consumed", "outputs stored", "exchange signalled")
+
+
+def trace_step(torch, lib, step, dev, path, barrier, world, rank):
+    """One step with the GEMV's phase trace on (thq4_debug_set_trace), captured
+    in its own CUDA graph and replayed (the last replay's stamps are kept).
+    Writes, per launch, the CTA-median time of each phase after the launch's
+    first CTA started, its span (first start to last exit) and the gap from the
+    previous launch's last exit; and the same averaged per projection shape."""
+    import numpy as np
+    import thq4
+
+    words = 1 << 22  # 32 MB of records
+    buf = torch.zeros(words, dtype=torch.int64, device=dev)
+    thq4.check(lib.thq4_debug_set_trace(ctypes.c_void_p(buf.data_ptr()), words * 8))
+    g = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(g):
+            step()
+    finally:
+        thq4.check(lib.thq4_debug_set_trace(None, 0))
+    for _ in range(3):
+        torch.cuda.synchronize()
+        barrier()
+        g.replay()
+    torch.cuda.synchronize()
+    g.reset()
+    del g
+    h = buf.cpu().numpy().view(np.uint64)
+    recs, off = [], 0
+    while off + 8 <= h.size and h[off] == 0x7468713474726163:
+        grid = int(h[off + 1])
+        st = h[off + 8: off + 8 + 8 * grid].reshape(grid, 8).astype(np.int64)
+        flags = int(h[off + 4])
+        recs.append({"out": int(h[off + 2]), "in": int(h[off + 3]), "gate_up": flags & 1,
+                     "cluster": (flags >> 8) & 0xFF, "mode": (flags >> 16) & 0xFF, "wait": (flags >> 24) & 0xFF,
+                     "m": int(h[off + 5]), "chunk": int(h[off + 6]) & 0xFF, "stages": int(h[off + 6]) >> 8,
+                     "ctas": grid, "st": st})
+        off += 8 + 8 * grid
+    launches, prev_end = [], None
+    for r in recs:
+        st = r.pop("st")
+        t0 = int(st[:, 0].min())
+        end = int(st[:, 7].max())
+        med = [round(float(np.median(st[:, i] - t0)) / 1e3, 3) for i in range(8)]
+        r.update({"span_us": round((end - t0) / 1e3, 3),
+                  "gap_from_previous_exit_us": None if prev_end is None else round((t0 - prev_end) / 1e3, 3),
+                  "phase_median_us": dict(zip(TRACE_PHASES, med)),
+                  "stream_max_us": round(float((st[:, 5] - t0).max()) / 1e3, 3), "start_ns": t0})
+        prev_end = end
+        launches.append(r)
+    base = launches[0]["start_ns"] if launches else 0
+    for r in launches:
+        r["start_us"] = round((r.pop("start_ns") - base) / 1e3, 3)
+    kinds = {}
+    for r in launches:
+        key = f"{'gate_up 2x' if r['gate_up'] else ''}{r['out']}x{r['in']} m{r['m']}"
+        kinds.setdefault(key, []).append(r)
+    summary = {}
+    for key, rs in kinds.items():
+        gaps = [r["gap_from_previous_exit_us"] for r in rs if r["gap_from_previous_exit_us"] is not None]
+        summary[key] = {
+            "launches": len(rs), "ctas": rs[0]["ctas"], "cluster": rs[0]["cluster"], "chunk": rs[0]["chunk"],
+            "stages": rs[0]["stages"], "mode": rs[0]["mode"], "wait": rs[0]["wait"],
+            "span_us": round(float(np.mean([r["span_us"] for r in rs])), 3),
+            "gap_us": round(float(np.mean(gaps)) if gaps else 0.0, 3),
+            "phase_median_us": {p: round(float(np.mean([r["phase_median_us"][p] for r in rs])), 3)
+                                for p in TRACE_PHASES}}
+    step_us = max((r["start_us"] + r["span_us"] for r in launches), default=0.0)
+    with open(path, "w") as f:
+        json.dump({"world": world, "rank": rank, "launches": len(launches), "step_us": round(step_us, 3),
+                   "per_shape": summary, "per_launch": launches}, f, indent=1)
+
+
+def bench_c1(torch, thq4, synth, dev, hbm_peak, graph):
+    """the single GEMV, x [1 x 2048] f32 ~ N(0, 1), W
+    [6144 x 2048] Q4 ~ N(0, 0.02) with f16 scale/bias, y f32.  72 distinct
+    weight copies (510 MB, > 4x L2) rotate inside one CUDA graph; GB/s =
+    7,077,888 algorithmic bytes per launch / mean launch time."""
+    out, inp, copies = 6144, 2048, 72
+    ws = []
+    for i in range(copies):
+        wq, sb = synth.normal_weight(out, inp, 60_000 + i, dev)
+        ws.append(thq4.PackedWeight.repack(thq4.SRC_MLX, wq, sb, out, inp, thq4.F16))
+        del wq, sb
+    lib = thq4.lib()
+    wsb = lib.thq4_linear_workspace_bytes(ctypes.byref(ws[0].desc), 1)
+    scratch = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    x = torch.randn((1, inp), device=dev, dtype=torch.float32)
+    y = torch.empty((1, out), dtype=torch.float32, device=dev)
+
+    def call():
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for w in ws:
+            thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.F32, 1,
+                                       ctypes.c_void_p(y.data_ptr()), thq4.F32, ctypes.c_void_p(scratch.data_ptr()),
+                                       wsb, s))
+
+    call()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            call()
+    run = g.replay if g is not None else call
+    ms = _time_ms(torch, run, 20) / copies
+    nbytes = out * inp * Q4_BYTES_PER_WEIGHT
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    if g is not None:
+        g.reset()
+    return {"config": "x 1x2048 f32, W 6144x2048 Q4 (f16 scale/bias), y f32", "us": round(ms * 1e3, 3),
+            "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
+            "l2": f"{copies} weight copies ({copies * nbytes / 1e6:.0f} MB) rotate in one CUDA graph",
+            "kernel": "gemv_kernel (f32 x split into fp16 hi/lo columns)"}
+
+
+def bench_verify(torch, thq4, synth, dev, hbm_peak, graph):
+    """spec-decode verify, x [M x 2560] bf16 ~ N(0, 1),
+    M in {1, 2, 4, 8}; the fused gate/up 2 x 9728 x 2560 (SwiGLU epilogue)
+    then down 2560 x 9728, Q4 f16 scale/bias.  12 distinct weight sets
+    (504 MB, > 4x L2) rotate inside one CUDA graph per M; GB/s per kernel =
+    its algorithmic bytes (28,016,640 and 14,008,320) / its mean launch time,
+    each kernel timed in its own graph of 12 launches."""
+    H, I, sets_n = 2560, 9728, 12
+    sets = []
+    for i in range(sets_n):
+        g_wq, g_sb = synth.normal_weight(I, H, 70_000 + 3 * i, dev)
+        u_wq, u_sb = synth.normal_weight(I, H, 70_001 + 3 * i, dev)
+        d_wq, d_sb = synth.normal_weight(H, I, 70_002 + 3 * i, dev)
+        sets.append((thq4.PackedWeight.repack(thq4.SRC_MLX, g_wq, g_sb, I, H, thq4.F16),
+                     thq4.PackedWeight.repack(thq4.SRC_MLX, u_wq, u_sb, I, H, thq4.F16),
+                     thq4.PackedWeight.repack(thq4.SRC_MLX, d_wq, d_sb, H, I, thq4.F16)))
+        del g_wq, g_sb, u_wq, u_sb, d_wq, d_sb
+    lib = thq4.lib()
+    wsb = max(lib.thq4_linear_workspace_bytes(ctypes.byref(p.desc), 8) for st in sets for p in st)
+    scratch = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    gu_bytes, dn_bytes = 2 * I * H * Q4_BYTES_PER_WEIGHT, H * I * Q4_BYTES_PER_WEIGHT
+    out = {"config": "x Mx2560 bf16; gate/up 2x9728x2560 then down 2560x9728, Q4 f16 scale/bias",
+           "l2": f"{sets_n} weight sets ({sets_n * (gu_bytes + dn_bytes) / 1e6:.0f} MB) rotate in one CUDA graph",
+           "kernel": "gemv_kernel with M token columns",
+           "reference_m5max": "m=8 on an Apple M5 Max (other shapes): gate_up 34816x5120 530 GB/s, down 5120x17408 "
+                              "400 GB/s (engine/reports/perf-2026-09/impl-th-wp2-matmul-roofline.md:142-143)"}
+    for M in (1, 2, 4, 8):
+        x = torch.randn((M, H), device=dev).to(torch.bfloat16)
+        h = torch.empty((M, I), dtype=torch.bfloat16, device=dev)
+        y = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+
+        def gu_call():
+            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for g_, u_, _ in sets:
+                thq4.check(lib.thq4_gate_up(ctypes.byref(g_.desc), ctypes.byref(u_.desc), P(x), thq4.BF16, M, P(h),
+                                            thq4.BF16, P(scratch), wsb, s))
+
+        def dn_call():
+            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for _, _, d_ in sets:
+                thq4.check(lib.thq4_linear(ctypes.byref(d_.desc), P(h), thq4.BF16, M, P(y), thq4.BF16, P(scratch),
+                                           wsb, s))
+
+        res = {}
+        for name, fn, nb in (("gate_up", gu_call, gu_bytes), ("down", dn_call, dn_bytes)):
+            fn()
+            g = None
+            if graph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+            ms = _time_ms(torch, g.replay if g is not None else fn, 20) / sets_n
+            gbs = nb / (ms * 1e-3) / 1e9
+            res[name] = {"us": round(ms * 1e3, 3), "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)}
+            if g is not None:
+                g.reset()
+        out[f"m{M}"] = res
+    return out
 
 
 def _time_ms(torch, fn, reps):

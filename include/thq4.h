@@ -157,6 +157,31 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
  * call returns it zeroed, so one allocation serves every later call.  Calls
  * that may overlap on the GPU need separate workspaces. */
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
+/* A chain of dependent projections in one persistent launch.  No single
+ * reference counterpart: it runs what consecutive QLin::linear_ps /
+ * gate_up_act_ps calls (qwen35.rs:398, 711) would, e.g. an MLP's gate/up and
+ * then its down projection (lin_apply_ps, :918), or a decode layer's
+ * projections, with op i seeing every output of ops 0 .. i-1.  Each op is
+ * thq4_linear (up == NULL) or thq4_gate_up (w = gate half, up = up half) on
+ * x [m][w->in] -> y [m][w->out] with the arithmetic of that call.  One
+ * cooperative launch with one CTA per SM streams the weights of op after op
+ * without pausing at op boundaries; a grid-wide barrier orders each op's
+ * outputs before the next op reads them. */
+typedef struct thq4_chain_op {
+  const thq4_weight *w;  /* the projection (the gate half of a gate/up op) */
+  const thq4_weight *up; /* the up half, or NULL */
+  const void *x;         /* device, [m][w->in] of the chain's x_dtype (may be an earlier op's y) */
+  void *y;               /* device, [m][w->out], y_dtype; never this op's x */
+  int32_t y_dtype;       /* THQ4_BF16 or THQ4_F32 */
+  int32_t reserved;      /* 0 */
+} thq4_chain_op;
+/* Workspace bytes of thq4_linear_chain (256-byte aligned, zero-filled before
+ * the first call; every call leaves it zeroed unless it timed out). */
+size_t thq4_linear_chain_workspace_bytes(const thq4_chain_op *ops, int n);
+/* 1 <= n <= 112 ops, one scale dtype, m <= 8 tokens of bf16 x (4 of f32 x).
+ * Calls that may overlap on the GPU need separate workspaces. */
+thq4_status thq4_linear_chain(const thq4_chain_op *ops, int n, int x_dtype, int m, void *workspace,
+                              size_t workspace_bytes, void *stream);
 /* thq4_linear without a workspace argument.  No reference counterpart: the
  * reference's ops take scratch from candle's buffer pool.  It routes by row
  * count exactly as thq4_linear does (the prefill kernel for m > 8 bf16 rows,
@@ -402,6 +427,17 @@ thq4_status thq4_copy(void *dst, const void *src, size_t bytes, void *stream);
  * run every instantiated tile config the same way (qwen35.rs:6963-6989).
  * Returns THQ4_ERR_INVALID_ARGUMENT for other values; `reserved` must be 0. */
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved);
+/* Phase trace of the decode/verify kernel for every later launch in this
+ * process (NULL turns it off; each call starts over at the buffer's start).
+ * `buf` is zero-filled device memory.  Each launch that fits appends a record:
+ * 8 header words {0x7468713474726163, CTAs, out, in, gate_up | cluster size
+ * << 8 | exchange mode << 16 | waits << 24, tokens, chunk | stages << 8, 0}
+ * then, per CTA, 8 %globaltimer stamps (ns): running, predecessor complete,
+ * peers' flags seen, activation staged, first weight stage landed, stream
+ * consumed, outputs stored, exchange signalled.  A launch captured in a CUDA
+ * graph keeps its record; replays overwrite it.  No reference counterpart
+ * (the reference times its kernels with Metal's GPU counters). */
+thq4_status thq4_debug_set_trace(void *buf, size_t bytes);
 /* The decode/verify launch plan for an out x in weight and m tokens (x_f32,
  * gate_up as thq4_linear / thq4_gate_up would pass them) on a GPU with `sms`
  * SMs on which cluster_fit[j] clusters of j one-CTA-per-SM CTAs can be

@@ -4,6 +4,7 @@
 // row-count routing (engine/src/qwen35.rs:398-617), gate_up_act_ps
 // (:711-884) and the candle op checks that bail before anything is encoded
 // (check3, quant_kernel.rs:2671-2684; presum length check :3642-3657).
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -306,6 +307,52 @@ thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype
   if (!scratch) return cuda_error(e, "thq4_linear_noalloc: cudaGetSymbolAddress");
   e = gemv_launch(*w, nullptr, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32, scratch,
                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+size_t thq4_linear_chain_workspace_bytes(const thq4_chain_op *ops, int n) {
+  if (!ops || n < 1) return 0;
+  int rows = 0;
+  for (int i = 0; i < n; ++i)
+    if (ops[i].w && ops[i].w->out > rows) rows = ops[i].w->out;
+  return rows > 0 ? chain_workspace_bytes(rows) : 0;
+}
+
+thq4_status thq4_linear_chain(const thq4_chain_op *ops, int n, int x_dtype, int m, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  const char *who = "thq4_linear_chain";
+  if (!ops || n < 1 || n > chain_max_ops())
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": need 1 <= n <= " +
+                                                    std::to_string(chain_max_ops()) + " ops");
+  const int per = x_dtype == THQ4_F32 ? 4 : 8;
+  if (m < 1 || m > per)
+    return set_error(THQ4_ERR_UNSUPPORTED, std::string(who) + ": m " + std::to_string(m) + " outside 1.." +
+                                               std::to_string(per) + " (one decode/verify pass per op)");
+  ChainSpec spec[128];
+  int rows = 0;
+  for (int i = 0; i < n; ++i) {
+    const thq4_chain_op &o = ops[i];
+    const std::string at = std::string(who) + " op " + std::to_string(i);
+    thq4_status s = check_weight(o.w, at.c_str());
+    if (s != THQ4_OK) return s;
+    if (o.up) {
+      if ((s = check_weight(o.up, at.c_str())) != THQ4_OK) return s;
+      if (o.w->out != o.up->out || o.w->in != o.up->in || o.w->sb_dtype != o.up->sb_dtype)
+        return set_error(THQ4_ERR_INVALID_ARGUMENT, at + ": gate and up halves differ in shape or dtype");
+    }
+    if (o.w->sb_dtype != ops[0].w->sb_dtype)
+      return set_error(THQ4_ERR_INVALID_ARGUMENT, at + ": every op of a chain has the same scale dtype");
+    if (o.reserved != 0) return set_error(THQ4_ERR_INVALID_ARGUMENT, at + ": reserved must be 0");
+    if ((s = check_io(o.x, x_dtype, m, o.y, o.y_dtype, at.c_str())) != THQ4_OK) return s;
+    if (o.x == o.y) return set_error(THQ4_ERR_INVALID_ARGUMENT, at + ": y aliases x");
+    spec[i] = ChainSpec{o.w, o.up, o.x, o.y, o.y_dtype == THQ4_F32};
+    rows = std::max(rows, (int)o.w->out);
+  }
+  thq4_status s = check_workspace(workspace, workspace_bytes, chain_workspace_bytes(rows), who);
+  if (s != THQ4_OK) return s;
+  const cudaError_t e =
+      chain_launch(spec, n, x_dtype == THQ4_F32, m, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, who);
   return THQ4_OK;
 }
@@ -787,6 +834,13 @@ thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {
   g_force_warps.store(chunk, std::memory_order_relaxed);
   g_force_depth.store(stages, std::memory_order_relaxed);
   g_force_grid.store(grid, std::memory_order_relaxed);
+  return THQ4_OK;
+}
+
+thq4_status thq4_debug_set_trace(void *buf, size_t bytes) {
+  if (buf && (bytes < 256 || reinterpret_cast<uintptr_t>(buf) % 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_debug_set_trace: a 16-byte aligned buffer of >= 256 bytes");
+  gemv_set_trace(buf, bytes);
   return THQ4_OK;
 }
 

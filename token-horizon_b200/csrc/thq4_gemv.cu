@@ -112,7 +112,25 @@ struct GemvArgs {
   // summed in order and rounded to bf16 as they are staged
   int xparts;
   long long xslot;
+  // phase trace (testing hook; nullptr = off): a record of 8 header words
+  // then 8 %globaltimer stamps per CTA (thq4_debug_set_trace)
+  unsigned long long *trace;
 };
+
+// Phase stamps of the trace, taken by thread 0 (consumer warp 0).
+enum : int {
+  kTrEntry = 0,    // CTA running, barriers initialised
+  kTrPdl = 1,      // griddepcontrol.wait returned: the predecessor completed
+  kTrPeer = 2,     // the peers' exchange flags seen (= kTrPdl without a wait)
+  kTrStaged = 3,   // activation staged in shared memory
+  kTrFirst = 4,    // the first weight stage has landed
+  kTrStreamed = 5, // every stage consumed
+  kTrStored = 6,   // outputs stored (after any split-K or cluster combine)
+  kTrDone = 7,     // exchange signalled; the CTA exits
+};
+__device__ __forceinline__ void trace_stamp(const GemvArgs &a, int i) {
+  if (a.trace && threadIdx.x == 0) a.trace[8 + (size_t)blockIdx.x * 8 + i] = global_timer_ns();
+}
 
 // columns with per-group metadata: P rounded up to even (lanes own pairs)
 __host__ __device__ inline int meta_cols(int P) { return (P + 1) & ~1; }
@@ -129,9 +147,11 @@ __host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, in
 // floats of one CTA side's partial: 8 tiles x NS x 32 lanes x 4
 __host__ __device__ inline int side_floats(bool gate_up) { return kSlabTiles * (gate_up ? 2 : 1) * 32 * 4; }
 // First chunk of run i: runs hold base + 1 chunks for i < rem, base after.
-__device__ __forceinline__ int run_begin(const GemvArgs &a, int i) { return i * a.run_base + min(i, a.run_rem); }
+template <class A>
+__device__ __forceinline__ int run_begin(const A &a, int i) { return i * a.run_base + min(i, a.run_rem); }
 // The run holding chunk o (every run is non-empty: base >= 1).
-__device__ __forceinline__ int run_of(const GemvArgs &a, int o) {
+template <class A>
+__device__ __forceinline__ int run_of(const A &a, int o) {
   const int big = a.run_rem * (a.run_base + 1);
   return o < big ? o / (a.run_base + 1) : a.run_rem + (o - big) / a.run_base;
 }
@@ -154,8 +174,8 @@ __device__ __forceinline__ void consumer_sync() {
 // adjacent lanes, which reduce the group's max |x| and sum with a fixed
 // shuffle tree (deterministic).  Up to four items per thread are requested
 // before any is used.
-template <bool PARTS>
-__device__ __forceinline__ void stage_x(const GemvArgs &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
+template <bool PARTS, class A>
+__device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
   const int tid = threadIdx.x, nthr = kConsumers * 32;
   const int P = a.P, P8 = meta_cols(P);
   constexpr int kU = 4;
@@ -256,8 +276,8 @@ __device__ __forceinline__ void stage_x(const GemvArgs &a, int gs, int xcnt, uin
 
 // Final values of one 16-row tile from lanes holding reduced column pairs;
 // gate/up combines streams 0 and 1.
-template <int GW, bool GATE_UP>
-__device__ __forceinline__ void store_tile(const GemvArgs &a, int rt, int lane, const float *y0, const float *y1) {
+template <int GW, bool GATE_UP, class A>
+__device__ __forceinline__ void store_tile(const A &a, int rt, int lane, const float *y0, const float *y1) {
   constexpr int LPJ = 4 / GW;
   const int r = lane >> 2, c = lane & 3;
   if (c >= LPJ) return;
@@ -420,6 +440,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   fence_mbar_init();
   __syncthreads();
   pdl_launch_dependents();
+  trace_stamp(a, kTrEntry);
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+    a.trace[0] = 0x7468713474726163ull;  // record magic
+    a.trace[1] = gridDim.x;
+    a.trace[2] = (unsigned long long)a.out;
+    a.trace[3] = (unsigned long long)a.in;
+    a.trace[4] = (unsigned long long)(GATE_UP ? 1 : 0) | ((unsigned long long)a.cl_j << 8) |
+                 ((unsigned long long)a.g_mode << 16) | ((unsigned long long)a.g_wait << 24);
+    a.trace[5] = (unsigned long long)a.m;
+    a.trace[6] = (unsigned long long)CB | ((unsigned long long)a.stages << 8);
+    a.trace[7] = 0;
+  }
 
   if (warp == kConsumers) {
     // ---- producer: one elected lane streams the run -------------------------
@@ -435,16 +467,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
   const int tile = warp;
   pdl_wait();
+  trace_stamp(a, kTrPdl);
   if (a.g_wait) {  // x holds the peers' slices or partials: wait until they have landed
     if (threadIdx.x == 0) peer_wait(a.g_flags, a.g_count, a.g_world, a.g_rank, a.status);
     consumer_sync();
   }
+  trace_stamp(a, kTrPeer);
   const int sl0 = C0 / a.cps, cg0 = C0 - sl0 * a.cps;
   const int gs = cg0 * CB;
   const int xcnt =
       min(a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
   stage_x<PARTS>(a, gs, xcnt, xf, zero, mx);
   if (threadIdx.x == 0) mbar_arrive(xready);
+  trace_stamp(a, kTrStaged);
 
   const int r = lane >> 2, c = lane & 3;
   const int jr = r / CPG, qr = r % CPG;  // this lane's B column: window position jr, column qr
@@ -599,6 +634,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       aborted = true;
       *abort_word = 1u;
     }
+    if (n == 0) trace_stamp(a, kTrFirst);
     const int g0c = cg * CB, cnt = min(CB, a.ng - g0c);
     const unsigned char *nib = ring + (size_t)s * SB;
     const unsigned char *scl = nib + (size_t)NS * CB * 4096;
@@ -640,6 +676,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     }
   }
 
+  trace_stamp(a, kTrStreamed);
   if (clustered) {
     // Slab-split mode: this CTA holds part `part` of one slab.  Once every
     // CTA of the cluster is past its stream (barrier 1) the leader's ring is
@@ -673,7 +710,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         }
       store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
     }
+    trace_stamp(a, kTrStored);
     if (a.g_mode) peer_signal(a);
+    trace_stamp(a, kTrDone);
     return;
   }
 
@@ -710,7 +749,462 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     if (done & 1u) combine(first_slab);
     if (done & 2u) combine(last_slab);
   }
+  trace_stamp(a, kTrStored);
   if (a.g_mode) peer_signal(a);  // every consumer warp gets here
+  trace_stamp(a, kTrDone);
+}
+
+// ---------------------------------------------------------------------------
+// Chains: dependent projections in one persistent launch (thq4_linear_chain)
+// ---------------------------------------------------------------------------
+// Within one launch of a single projection the weight stream stops at every
+// launch boundary: a launch's CTAs start only as the predecessor's leave the
+// SMs, then wait for the predecessor's output before staging x.  A chain
+// runs ops 0..n-1 in one cooperative launch (one CTA per SM): the producer
+// warp streams the weights of op after op into the ring without ever
+// waiting for activations (weights do not depend on them), while the
+// consumer warps finish op p, meet the other CTAs at a grid barrier (op p's
+// outputs complete and visible), stage op p + 1's x and go on with stages
+// that are already in shared memory.  Every stage holds 8 slab-groups of
+// one weight or 4 of gate and 4 of up (the same 36,864 bytes), so ops of
+// either kind share one ring.  Each op's slab-groups are split over the CTAs
+// as in the single launch (whole slabs per CTA where they fill >= 85% of
+// the SMs, else equal runs of chunks whose split slabs finish by the last
+// arriver); CTAs without a run in an op only pass its barrier, while their
+// producer already streams the next op.
+constexpr int kMaxChainOps = 112;
+constexpr int kChainStageBytes = 8 * kSgBytes;
+
+struct ChainOp {
+  const uint8_t *qw0, *sb0, *qw1, *sb1;
+  const void *x;
+  void *y;
+  int out, in, ng, cps;
+  int chunks, run_base, run_rem, active;  // CTAs 0 .. active-1 hold a run of the op
+  int gate_up, yf32;
+};
+
+struct ChainArgs {
+  uint32_t *status;
+  float *part;     // split-K partials, as GemvArgs::part
+  uint32_t *count; // arrivals per (slab, tile), as GemvArgs::count
+  uint32_t *bar;   // [0] barrier arrivals, [1] exits (zero between launches)
+  int n, m, P, xf32, stages, xcap;
+  ChainOp ops[kMaxChainOps];
+};
+
+// One op of a chain through the members the GEMV helpers read (no exchange).
+// The consumers keep the current op's view in shared memory: held in
+// registers across the chunk loop it would crowd out the loop's own.
+struct OpView {
+  const void *x;
+  void *y;
+  int m, in, ng, out, P, xf32, yf32;
+  int run_base, run_rem, cps, active, gate_up;
+  int g_mode, g_world, g_rank, g_rows, g_off, g_stride;
+  long long g_slot;
+  uint16_t *const *g_dst;
+  int xparts;
+  long long xslot;
+};
+constexpr int kViewOffset = 256;  // the view's place in shared memory, after the barriers
+static_assert(sizeof(OpView) <= 256, "the op view fits its slot");
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Thread 0 writes op p's view; the consumers see it after their barrier.
+__device__ __forceinline__ void chain_set_view(const ChainArgs &a, int p, OpView *vs) {
+  if (threadIdx.x == 0) {
+    const ChainOp &op = a.ops[p];
+    OpView v;
+    v.x = op.x;
+    v.y = op.y;
+    v.m = a.m;
+    v.in = op.in;
+    v.ng = op.ng;
+    v.out = op.out;
+    v.P = a.P;
+    v.xf32 = a.xf32;
+    v.yf32 = op.yf32;
+    v.run_base = op.run_base;
+    v.run_rem = op.run_rem;
+    v.cps = op.cps;
+    v.active = op.active;
+    v.gate_up = op.gate_up;
+    v.g_mode = v.g_world = v.g_rank = v.g_rows = v.g_off = v.g_stride = 0;
+    v.g_slot = 0;
+    v.g_dst = nullptr;
+    v.xparts = 0;
+    v.xslot = 0;
+    *vs = v;
+  }
+  consumer_sync();
+}
+
+// The producer lane's stream of one op: its run's chunks into the ring, whose
+// cursor (stage s, parity par, chunks issued so far) carries over between
+// ops.  False after a timeout (the copies in flight have been waited for).
+template <int CB, bool GATE_UP>
+__device__ __forceinline__ bool chain_produce_op(const ChainOp &op, int C0, int nch, int R, uint64_t *full,
+                                                uint64_t *empty, unsigned char *ring, uint32_t *status, int &s,
+                                                uint32_t &par, long long &issued, uint64_t pol) {
+  constexpr int NS = GATE_UP ? 2 : 1;
+  static_assert(NS * CB * kSgBytes == kChainStageBytes, "chain stages are uniform");
+  int sl = C0 / op.cps, cg = C0 - sl * op.cps;
+  for (int n = 0; n < nch; ++n, ++cg) {
+    if (cg == op.cps) cg = 0, ++sl;
+    if (issued >= R && !mbar_wait_bounded(&empty[s], par ^ 1u, kWaitLimitNs)) {
+      raise_status(status, kStatusTimeout);
+      for (long long k = issued - R; k < issued; ++k)
+        (void)mbar_wait_bounded(&full[k % R], (uint32_t)((k / R) & 1), kWaitLimitNs);
+      return false;
+    }
+    const int g0c = cg * CB, cnt = min(CB, op.ng - g0c);
+    const long long sg = (long long)sl * op.ng + g0c;
+    unsigned char *dst = ring + (size_t)s * kChainStageBytes;
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(NS * cnt * kSgBytes));
+    bulk_g2s(dst, op.qw0 + sg * 4096, cnt * 4096, &full[s], pol);
+    bulk_g2s(dst + (size_t)NS * CB * 4096, op.sb0 + sg * 512, cnt * 512, &full[s], pol);
+    if constexpr (GATE_UP) {
+      bulk_g2s(dst + (size_t)CB * 4096, op.qw1 + sg * 4096, cnt * 4096, &full[s], pol);
+      bulk_g2s(dst + (size_t)NS * CB * 4096 + CB * 512, op.sb1 + sg * 512, cnt * 512, &full[s], pol);
+    }
+    ++issued;
+    if (++s == R) s = 0, par ^= 1u;
+  }
+  return true;
+}
+
+// Every CTA's consumers are done with op p - 1 (outputs stored, split slabs
+// finished): one arrival per CTA on the launch's counter, then a bounded wait
+// for all of them.  A timeout marks the CTA aborted (status kStatusTimeout).
+__device__ __forceinline__ void chain_barrier(const ChainArgs &a, int p, volatile uint32_t *abort_word) {
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();  // this CTA's outputs (ordered before by the bar.sync) before its arrival
+    atom_add_relaxed(a.bar, 1u);
+    const uint32_t target = (uint32_t)p * gridDim.x;
+    const uint64_t t0 = global_timer_ns();
+    while ((int32_t)(ld_acquire_gpu(a.bar) - target) < 0) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        raise_status(a.status, kStatusTimeout);
+        *abort_word = 1u;
+        break;
+      }
+    }
+  }
+  consumer_sync();
+}
+
+// The consumers' place in the ring (the stage of the last chunk taken and its
+// parity) and whether this warp gave up on a wait, carried from op to op.
+struct RingCursor {
+  int s;
+  uint32_t par;
+  int aborted;
+};
+
+// The consumers' share of one op: stage its x, consume the run's chunks from
+// the ring, store whole slabs and finish split ones by the last arriver --
+// the same arithmetic as gemv_kernel.  Not inlined: each kind of op (one
+// weight, gate/up) gets the kernel's register budget for its own loop.
+template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP>
+__device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const OpView &v, int R, uint64_t *full,
+                                                    uint64_t *empty, unsigned char *ring, uint4 *xf, uint4 *zero,
+                                                    float4 *mx, volatile uint32_t *abort_word, RingCursor cur) {
+  constexpr int NS = GATE_UP ? 2 : 1;
+  constexpr int CPG = 8 / GW;
+  constexpr int LPJ = 4 / GW;
+  const int lane = threadIdx.x & 31, tile = threadIdx.x >> 5;
+  if ((int)blockIdx.x >= v.active) return cur;  // no run in this op (every consumer warp alike)
+  int s = cur.s;
+  uint32_t par = cur.par;
+  bool aborted = cur.aborted != 0;
+  const int C0 = run_begin(v, blockIdx.x), C1 = run_begin(v, blockIdx.x + 1);
+  const int nch = C1 - C0;
+  const int P = a.P, P8 = meta_cols(P);
+  const int sl0 = C0 / v.cps, cg0 = C0 - sl0 * v.cps;
+  const int gs = cg0 * CB;
+  const int xcnt = min(v.ng, sgs_before(C1, v.cps, v.ng, CB) - sgs_before(C0, v.cps, v.ng, CB));
+  stage_x<false>(v, gs, xcnt, xf, zero, mx);
+
+  const int r = lane >> 2, c = lane & 3;
+  const int jr = r / CPG, qr = r % CPG;
+  const int jc = c / LPJ, cp = c % LPJ;
+  const bool colv = 2 * cp < P;
+  const int xoff = qr * 8 + c;
+  bool bsel[GW];
+#pragma unroll
+  for (int j = 0; j < GW; ++j) bsel[j] = jr == j && qr < P;
+  auto slot_of = [&](int g) { return g >= gs ? g - gs : g + v.ng - gs; };
+
+  float lo[NS][4], hi[NS][4], y[NS][4];
+#pragma unroll
+  for (int si = 0; si < NS; ++si)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) lo[si][e] = hi[si][e] = y[si][e] = 0.0f;
+  bool seg_whole = cg0 == 0;
+  bool finished_any = false;
+
+  auto group = [&](const unsigned char *nib, const uint4 *xc, int u, bool live, bool first) {
+    const uint4 *bp = live ? xc + u * P * 8 : zero + c;
+    const uint4 xa = bp[0], xb = bp[4];
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(si * CB + u) * 4096 + tile * 512 + lane * 16);
+      const uint32_t a00 = nib_f16x2<kNibMask>(w.x << 4), a01 = nib_f16x2<kNibMask>(w.x >> 4);
+      const uint32_t a02 = nib_f16x2<kNibMask>(w.y << 4), a03 = nib_f16x2<kNibMask>(w.y >> 4);
+      const uint32_t a10 = nib_f16x2<kNibMask>(w.x), a11 = nib_f16x2<kNibMask>(w.x >> 8);
+      const uint32_t a12 = nib_f16x2<kNibMask>(w.y), a13 = nib_f16x2<kNibMask>(w.y >> 8);
+      const uint32_t a20 = nib_f16x2<kNibMask>(w.z << 4), a21 = nib_f16x2<kNibMask>(w.z >> 4);
+      const uint32_t a22 = nib_f16x2<kNibMask>(w.w << 4), a23 = nib_f16x2<kNibMask>(w.w >> 4);
+      const uint32_t a30 = nib_f16x2<kNibMask>(w.z), a31 = nib_f16x2<kNibMask>(w.z >> 8);
+      const uint32_t a32 = nib_f16x2<kNibMask>(w.w), a33 = nib_f16x2<kNibMask>(w.w >> 8);
+      if (first) {
+        mma_f16_16816_z(lo[si], a00, a01, a02, a03, xa.x, xa.y);
+        mma_f16_16816_z(hi[si], a10, a11, a12, a13, xa.z, xa.w);
+      } else {
+        mma_f16_16816(lo[si], a00, a01, a02, a03, xa.x, xa.y);
+        mma_f16_16816(hi[si], a10, a11, a12, a13, xa.z, xa.w);
+      }
+      mma_f16_16816(lo[si], a20, a21, a22, a23, xb.x, xb.y);
+      mma_f16_16816(hi[si], a30, a31, a32, a33, xb.z, xb.w);
+    }
+  };
+  auto close_window = [&](const unsigned char *scl, const float4 *mc, int w0, bool valid) {
+    if (!valid) return;
+    const int gu = w0 + jc;
+    const float4 m0 = mc[gu * P8];
+    const float4 m1 = ONE ? m0 : mc[gu * P8 + 1];
+#pragma unroll
+    for (int si = 0; si < NS; ++si) {
+      const uint2 q = *reinterpret_cast<const uint2 *>(scl + (size_t)(si * CB + gu) * 512 + tile * 64 + r * 8);
+      const float sr = sb_to_f32<SF16>(q.x & 0xffffu), br = sb_to_f32<SF16>(q.x >> 16);
+      const float s8 = sb_to_f32<SF16>(q.y & 0xffffu), b8 = sb_to_f32<SF16>(q.y >> 16);
+      y[si][0] = fmaf(sr * m0.y, (lo[si][0] + hi[si][0]) - m0.z, fmaf(br, m0.x, y[si][0]));
+      y[si][2] = fmaf(s8 * m0.y, (lo[si][2] + hi[si][2]) - m0.z, fmaf(b8, m0.x, y[si][2]));
+      if constexpr (!ONE) {
+        y[si][1] = fmaf(sr * m1.y, (lo[si][1] + hi[si][1]) - m1.z, fmaf(br, m1.x, y[si][1]));
+        y[si][3] = fmaf(s8 * m1.y, (lo[si][3] + hi[si][3]) - m1.z, fmaf(b8, m1.x, y[si][3]));
+      }
+    }
+  };
+  auto reduce_y = [&]() {
+#pragma unroll
+    for (int si = 0; si < NS; ++si)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float t = y[si][e];
+        if constexpr (GW == 4) {
+          t += __shfl_xor_sync(0xffffffffu, t, 1);
+          t += __shfl_xor_sync(0xffffffffu, t, 2);
+        } else if constexpr (GW == 2) {
+          t += __shfl_xor_sync(0xffffffffu, t, 2);
+        }
+        y[si][e] = t;
+      }
+  };
+  auto publish = [&](int side, const float (&pv)[NS][4]) {
+    float *gslot = a.part + (((size_t)blockIdx.x * 2 + side) * kSlabTiles + tile) * (NS * 128) + lane * 4;
+#pragma unroll
+    for (int si = 0; si < NS; ++si)
+      *reinterpret_cast<float4 *>(gslot + si * 128) = make_float4(pv[si][0], pv[si][1], pv[si][2], pv[si][3]);
+  };
+  auto contributors = [&](int sl, int &clo, int &chi) {
+    const int t0 = sl * v.cps;
+    clo = run_of(v, t0);
+    chi = run_of(v, t0 + v.cps - 1);
+  };
+  auto combine = [&](int sl) {
+    int clo, chi;
+    contributors(sl, clo, chi);
+    const int t0 = sl * v.cps;
+    float acc[NS][4];
+#pragma unroll
+    for (int si = 0; si < NS; ++si)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[si][e] = 0.0f;
+    constexpr int kBatch = 8 / NS;
+    for (int q0 = clo; q0 <= chi; q0 += kBatch) {
+      float4 pv[kBatch][NS];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int q = q0 + i;
+        if (q > chi) break;
+        const int qs = (q == clo && run_begin(v, q) < t0) ? 1 : 0;
+        const float *src = a.part + (((size_t)q * 2 + qs) * kSlabTiles + tile) * (NS * 128) + lane * 4;
+#pragma unroll
+        for (int si = 0; si < NS; ++si) pv[i][si] = ld_relaxed_f4(src + si * 128);
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i > chi) break;
+#pragma unroll
+        for (int si = 0; si < NS; ++si)
+          acc[si][0] += pv[i][si].x, acc[si][1] += pv[i][si].y, acc[si][2] += pv[i][si].z, acc[si][3] += pv[i][si].w;
+      }
+    }
+    if (lane == 0) a.count[(size_t)sl * kSlabTiles + tile] = 0;
+    store_tile<GW, GATE_UP>(v, sl * kSlabTiles + tile, lane, acc[0], acc[NS - 1]);
+  };
+
+  int first_slab = -1;
+  int sl = sl0, cg = cg0 - 1;
+  for (int n = 0; n < nch; ++n) {
+    if (++cg == v.cps) cg = 0, ++sl;
+    if (++s == R) s = 0, par ^= 1u;
+    if (!aborted && !mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
+      raise_status(a.status, kStatusTimeout);
+      aborted = true;
+      *abort_word = 1u;
+    }
+    const int g0c = cg * CB, cnt = min(CB, v.ng - g0c);
+    const unsigned char *nib = ring + (size_t)s * kChainStageBytes;
+    const unsigned char *scl = nib + (size_t)NS * CB * 4096;
+    const int slot0 = slot_of(g0c);
+    const uint4 *xc = xf + (size_t)slot0 * P * 8 + xoff;
+    const float4 *mc = mx + (size_t)slot0 * P8 + 2 * cp;
+    if (aborted) {
+    } else if (cnt == CB) {
+#pragma unroll
+      for (int u = 0; u < CB; ++u) {
+        group(nib, xc, u, bsel[u % GW], u % GW == 0);
+        if (u % GW == GW - 1) close_window(scl, mc, u - (GW - 1), colv);
+      }
+    } else {
+      for (int u = 0; u < cnt; ++u) {
+        const int j = u % GW;
+        group(nib, xc, u, jr == j && qr < P, j == 0);
+        if (j == GW - 1 || u == cnt - 1) close_window(scl, mc, u - j, colv && u - j + jc < cnt);
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && !aborted) mbar_arrive(&empty[s]);
+    if (cg == v.cps - 1) {
+      reduce_y();
+      if (aborted) {
+      } else if (seg_whole) {
+        store_tile<GW, GATE_UP>(v, sl * kSlabTiles + tile, lane, y[0], y[NS - 1]);
+      } else {
+        publish(0, y);
+      }
+      if (!seg_whole) first_slab = sl;
+#pragma unroll
+      for (int si = 0; si < NS; ++si)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[si][e] = 0.0f;
+      seg_whole = true;
+      finished_any = true;
+    }
+  }
+  int last_slab = -1;
+  if (nch > 0 && cg != v.cps - 1) {
+    reduce_y();
+    if (!aborted) publish(finished_any ? 1 : 0, y);
+    last_slab = sl;
+  }
+  if (!aborted && (first_slab >= 0 || last_slab >= 0)) {
+    __syncwarp();
+    uint32_t done = 0;
+    if (lane == 0) {
+      uint32_t o0 = 0, o1 = 0;
+      int clo, chi;
+      fence_acq_rel_gpu();
+      if (first_slab >= 0) o0 = atom_add_relaxed(&a.count[(size_t)first_slab * kSlabTiles + tile], 1u);
+      if (last_slab >= 0) o1 = atom_add_relaxed(&a.count[(size_t)last_slab * kSlabTiles + tile], 1u);
+      if (first_slab >= 0) {
+        contributors(first_slab, clo, chi);
+        if (o0 + 1 == (uint32_t)(chi - clo + 1)) done |= 1u;
+      }
+      if (last_slab >= 0) {
+        contributors(last_slab, clo, chi);
+        if (o1 + 1 == (uint32_t)(chi - clo + 1)) done |= 2u;
+      }
+      if (done) fence_acq_rel_gpu();
+    }
+    done = __shfl_sync(0xffffffffu, done, 0);
+    __syncwarp();
+    if (done & 1u) combine(first_slab);
+    if (done & 2u) combine(last_slab);
+  }
+  return RingCursor{s, par, aborted ? 1 : 0};
+}
+
+template <int GW, bool ONE, bool SF16>
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ ChainArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int R = a.stages;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kMaxStages;
+  volatile uint32_t *abort_word = reinterpret_cast<volatile uint32_t *>(smem + 240);
+  OpView *view = reinterpret_cast<OpView *>(smem + kViewOffset);
+  unsigned char *ring = smem + 512;
+  unsigned char *xt = ring + (size_t)R * kChainStageBytes;
+  uint4 *xf = reinterpret_cast<uint4 *>(xt);
+  uint4 *zero = reinterpret_cast<uint4 *>(xt + (size_t)a.xcap * a.P * 128);
+  float4 *mx = reinterpret_cast<float4 *>(xt + (size_t)a.xcap * a.P * 128 + 128);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    *abort_word = 0u;
+  }
+  fence_mbar_init();
+  __syncthreads();
+
+  if (warp == kConsumers) {
+    // ---- producer: every op's run, back to back ----------------------------
+    if (lane == 0) {
+      const uint64_t pol = evict_first_policy();
+      int s = 0;
+      uint32_t par = 0;
+      long long issued = 0;
+      for (int p = 0; p < a.n; ++p) {
+        const ChainOp &op = a.ops[p];
+        if ((int)blockIdx.x >= op.active) continue;
+        const int C0 = blockIdx.x * op.run_base + min((int)blockIdx.x, op.run_rem);
+        const int C1 = C0 + op.run_base + ((int)blockIdx.x < op.run_rem ? 1 : 0);
+        const bool ok = op.gate_up
+                            ? chain_produce_op<4, true>(op, C0, C1 - C0, R, full, empty, ring, a.status, s, par,
+                                                        issued, pol)
+                            : chain_produce_op<8, false>(op, C0, C1 - C0, R, full, empty, ring, a.status, s, par,
+                                                         issued, pol);
+        if (!ok) {
+          *abort_word = 1u;
+          break;
+        }
+      }
+    }
+    return;
+  }
+  // ---- consumers ------------------------------------------------------------
+  RingCursor cur{R - 1, 1u, 0};
+  for (int p = 0; p < a.n; ++p) {
+    if (p > 0) {
+      chain_barrier(a, p, abort_word);
+      if (*abort_word != 0u) cur.aborted = 1;
+    }
+    chain_set_view(a, p, view);
+    cur = view->gate_up
+              ? chain_consume_op<4, GW, ONE, SF16, true>(a, *view, R, full, empty, ring, xf, zero, mx, abort_word, cur)
+              : chain_consume_op<8, GW, ONE, SF16, false>(a, *view, R, full, empty, ring, xf, zero, mx, abort_word,
+                                                         cur);
+  }
+  // the last CTA out leaves the barrier words zero for the next launch
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();
+    if (atom_add_acq_rel(a.bar + 1, 1u) + 1u == gridDim.x) {
+      a.bar[0] = 0u;
+      a.bar[1] = 0u;
+    }
+  }
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
@@ -912,6 +1406,31 @@ GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms
   return p;
 }
 
+namespace {
+// The phase trace buffer (thq4_debug_set_trace): records are reserved in
+// launch order on the host.
+std::mutex g_trace_mu;
+unsigned long long *g_trace = nullptr;
+size_t g_trace_words = 0, g_trace_next = 0;
+
+unsigned long long *trace_record(int grid) {
+  std::lock_guard<std::mutex> lock(g_trace_mu);
+  if (!g_trace) return nullptr;
+  const size_t need = 8 + (size_t)grid * 8;
+  if (g_trace_next + need + 8 > g_trace_words) return nullptr;  // keep room for the end marker
+  unsigned long long *r = g_trace + g_trace_next;
+  g_trace_next += need;
+  return r;
+}
+}  // namespace
+
+void gemv_set_trace(void *buf, size_t bytes) {
+  std::lock_guard<std::mutex> lock(g_trace_mu);
+  g_trace = static_cast<unsigned long long *>(buf);
+  g_trace_words = buf ? bytes / 8 : 0;
+  g_trace_next = 0;
+}
+
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32, int m, void *y,
                         bool y_f32, void *workspace, cudaStream_t stream, const PeerGather *peer) {
   const bool gate_up = w1 != nullptr;
@@ -965,6 +1484,7 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
       a.xparts = peer->x_parts;
       a.xslot = peer->x_slot;
     }
+    a.trace = trace_record(p.grid);
     // a last pass with fewer tokens fits in the footprint planned for more
     const size_t smem = gemv_smem(p.stages, p.ch, gate_up, p.xcap, a.P);
     const int gw = window_groups(a.P);
@@ -974,6 +1494,7 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
       // the clusters do not fit in one wave: one CTA per SM with split-K
       const int grid = (int)std::min<long long>(p.chunks, device_sm_count());
       a.cl_j = 1;
+      if (a.trace && grid > p.grid) a.trace = nullptr;  // the record holds p.grid CTAs
       a.run_base = (int)(p.chunks / grid);
       a.run_rem = (int)(p.chunks % grid);
       e = w0.sb_dtype == THQ4_F16 ? dispatch<true>(a, gate_up, p.ch, gw, grid, smem, stream)
@@ -982,6 +1503,109 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+size_t chain_workspace_bytes(int max_rows) { return gemv_workspace_bytes(max_rows) + 256; }
+
+int chain_max_ops() { return kMaxChainOps; }
+
+namespace {
+template <int GW, bool ONE, bool SF16>
+cudaError_t chain_launch_t(const ChainArgs &a, int grid, size_t smem, cudaStream_t stream) {
+  auto *k = &chain_kernel<GW, ONE, SF16>;
+  static DeviceOnce once;
+  cudaError_t e = once.run([&] {
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
+  });
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  // every CTA is resident at once: the grid barrier between ops relies on it
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, a);
+}
+}  // namespace
+
+cudaError_t chain_launch(const ChainSpec *ops, int n, bool x_f32, int m, void *workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  if (n < 1 || n > kMaxChainOps) return cudaErrorInvalidValue;
+  const int grid = device_sm_count();
+  ChainArgs a{};
+  a.status = status_word();
+  a.n = n;
+  a.m = m;
+  a.P = x_f32 ? 2 * m : m;
+  a.xf32 = x_f32 ? 1 : 0;
+  int max_rows = 0, xcap = 1;
+  for (int i = 0; i < n; ++i) {
+    const ChainSpec &c = ops[i];
+    ChainOp &o = a.ops[i];
+    const bool gu = c.up != nullptr;
+    const int cb = gu ? 4 : 8;
+    o.qw0 = static_cast<const uint8_t *>(c.w->qw);
+    o.sb0 = static_cast<const uint8_t *>(c.w->sb);
+    o.qw1 = gu ? static_cast<const uint8_t *>(c.up->qw) : nullptr;
+    o.sb1 = gu ? static_cast<const uint8_t *>(c.up->sb) : nullptr;
+    o.x = c.x;
+    o.y = c.y;
+    o.out = c.w->out;
+    o.in = c.w->in;
+    o.ng = c.w->in / kGroup;
+    o.cps = (o.ng + cb - 1) / cb;
+    const int slabs = row_slabs(o.out);
+    if ((long long)slabs * o.ng >= (1ll << 31)) return cudaErrorInvalidValue;
+    o.chunks = slabs * o.cps;
+    // whole slabs per CTA where that fills >= 85% of the SMs, else equal runs
+    const int j = (slabs + grid - 1) / grid;
+    if (slabs % j == 0 && (long long)(slabs / j) * 100 >= (long long)grid * 85) {
+      o.active = slabs / j;
+      o.run_base = j * o.cps;
+      o.run_rem = 0;
+    } else {
+      o.active = std::min(o.chunks, grid);
+      o.run_base = o.chunks / o.active;
+      o.run_rem = o.chunks % o.active;
+    }
+    o.gate_up = gu ? 1 : 0;
+    o.yf32 = c.y_f32 ? 1 : 0;
+    const int max_run = o.run_base + (o.run_rem ? 1 : 0);
+    xcap = std::max(xcap, std::min(o.ng, max_run * cb));
+    max_rows = std::max(max_rows, o.out);
+  }
+  if (workspace_bytes < chain_workspace_bytes(max_rows)) return cudaErrorInvalidValue;
+  const size_t part_bytes =
+      gemv_workspace_bytes(max_rows) - ((size_t)row_slabs(max_rows) * kSlabTiles * 4 + 255) / 256 * 256;
+  a.part = static_cast<float *>(workspace);
+  a.count = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + part_bytes);
+  a.bar = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + gemv_workspace_bytes(max_rows));
+  a.xcap = xcap;
+  int st = 0;
+  for (int t = 5; t >= 2 && !st; --t)
+    if (512 + (size_t)t * kChainStageBytes + xstage_bytes(xcap, a.P) <= (size_t)kGemvMaxSmem) st = t;
+  if (!st) return cudaErrorInvalidConfiguration;
+  a.stages = st;
+  const size_t smem = 512 + (size_t)st * kChainStageBytes + xstage_bytes(xcap, a.P);
+  const int gw = window_groups(a.P);
+  const bool f16 = ops[0].w->sb_dtype == THQ4_F16;
+  if (gw == 4)
+    return a.P == 1 ? (f16 ? chain_launch_t<4, true, true>(a, grid, smem, stream)
+                           : chain_launch_t<4, true, false>(a, grid, smem, stream))
+                    : (f16 ? chain_launch_t<4, false, true>(a, grid, smem, stream)
+                           : chain_launch_t<4, false, false>(a, grid, smem, stream));
+  if (gw == 2)
+    return f16 ? chain_launch_t<2, false, true>(a, grid, smem, stream) : chain_launch_t<2, false, false>(a, grid, smem, stream);
+  return f16 ? chain_launch_t<1, false, true>(a, grid, smem, stream) : chain_launch_t<1, false, false>(a, grid, smem, stream);
 }
 
 cudaError_t peer_wait_launch(const PeerGather &g, cudaStream_t stream) {

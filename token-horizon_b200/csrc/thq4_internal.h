@@ -90,6 +90,20 @@ struct PeerGather {
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
                         int m, void *y, bool y_f32, void *workspace, cudaStream_t stream,
                         const PeerGather *peer = nullptr);
+// A chain of dependent projections in one persistent launch (thq4_linear_chain).
+struct ChainSpec {
+  const thq4_weight *w, *up;  // up: the second half of a gate/up op, or nullptr
+  const void *x;
+  void *y;
+  bool y_f32;
+};
+int chain_max_ops();
+size_t chain_workspace_bytes(int max_rows);
+cudaError_t chain_launch(const ChainSpec *ops, int n, bool x_f32, int m, void *workspace, size_t workspace_bytes,
+                         cudaStream_t stream);
+// The GEMV's phase trace buffer (device memory, nullptr = off); records are
+// taken from the start of the buffer again after every call.
+void gemv_set_trace(void *buf, size_t bytes);
 // Waits (one thread, bounded) until every peer has completed as many gathers
 // as this rank, then returns; used where a gathered vector is consumed by
 // something other than the next projection.

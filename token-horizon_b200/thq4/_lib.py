@@ -71,6 +71,11 @@ class thq4_peer_gather(ctypes.Structure):
                 ("x_slot", ctypes.c_int64)]
 
 
+class thq4_chain_op(ctypes.Structure):
+    _fields_ = [("w", c_void_p), ("up", c_void_p), ("x", c_void_p), ("y", c_void_p), ("y_dtype", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
 IPC_HANDLE_BYTES = 64
 
 _lib = None
@@ -122,7 +127,10 @@ SIGNATURES = {
     "thq4_ipc_close": (c_int, [c_void_p]),
     "thq4_ipc_free": (c_int, [c_void_p]),
     "thq4_copy": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "thq4_linear_chain_workspace_bytes": (c_size_t, [c_void_p, c_int]),
+    "thq4_linear_chain": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
+    "thq4_debug_set_trace": (c_int, [c_void_p, c_size_t]),
     "thq4_debug_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
 }
 

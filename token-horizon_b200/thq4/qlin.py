@@ -231,6 +231,39 @@ def lin_apply(x: torch.Tensor, l: QLin) -> torch.Tensor:
 
 # -- MoE (Splash MoE::add, docs/splash/runtime/ops/MoE.cpp:119-231) ------------
 
+class LinearChain:
+    """Dependent projections in one persistent launch (thq4_linear_chain).
+
+    ``ops`` is a list of (w, up, x, y): a PackedWeight (the gate half of a
+    gate/up op), the up half or None, and the op's input and output tensors
+    ([m, w.in] of the chain's x dtype, [m, w.out] bf16 or f32).  An op may
+    read any earlier op's output.  The descriptors and the workspace are built
+    once, so calling the chain again (or capturing it in a CUDA graph) reuses
+    them."""
+
+    def __init__(self, ops, m: int = 1, x_dtype: int = _lib.BF16, device: Optional[torch.device] = None):
+        self.n = len(ops)
+        self.m = m
+        self.x_dtype = x_dtype
+        self._keep = list(ops)
+        self._arr = (_lib.thq4_chain_op * max(self.n, 1))()
+        for i, (w, up, x, y) in enumerate(ops):
+            o = self._arr[i]
+            o.w = ctypes.addressof(w.desc)
+            o.up = ctypes.addressof(up.desc) if up is not None else None
+            o.x = x.data_ptr()
+            o.y = y.data_ptr()
+            o.y_dtype = _lib.F32 if y.dtype == torch.float32 else _lib.BF16
+            o.reserved = 0
+        need = _lib.lib().thq4_linear_chain_workspace_bytes(self._arr, self.n)
+        dev = device if device is not None else ops[0][2].device
+        self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+
+    def __call__(self) -> None:
+        check(_lib.lib().thq4_linear_chain(self._arr, self.n, self.x_dtype, self.m, _ptr(self.ws), self.ws.numel(),
+                                           _stream()))
+
+
 class PackedExperts:
     """E experts of one shape (rows x inp), packed back to back in the frag
     layout; the host mirror of Splash's ExpertQ4Projection
