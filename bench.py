@@ -13,11 +13,11 @@ times over and no flush is needed.  Per layer: the fused qkv GEMV, o, the
 fused gate/up GEMV with the SwiGLU epilogue, and down; each layer starts from
 the same input activation (no norms or attention exist on this path, and
 chaining raw projections would overflow bf16), while every projection still
-consumes the previous one's output.  On one GPU the step's 96 projections
-run by default as one persistent chain launch (thq4_linear_chain;
-`--launch chain-layer` runs one chain per layer, `--launch calls` one
-thq4_linear / thq4_gate_up call per projection; the line reports all
-three).  With N GPUs (the default `--tp row`) q/k/v and gate/up are
+consumes the previous one's output.  On one GPU the step runs by default
+as one thq4_linear / thq4_gate_up call per projection (`--launch
+chain-step` runs the step's 96 projections as one persistent chain launch,
+thq4_linear_chain, `--launch chain-layer` one chain per layer; the line
+reports all three).  With N GPUs (the default `--tp row`) q/k/v and gate/up are
 column-sharded with local outputs and o and down are row-sharded: their f32
 partials go over NVLink into every rank's reduction buffer from the GEMV's
 epilogue and the next projection sums them as it stages its input (no
@@ -79,7 +79,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--skip-prefill", action="store_true", help="N=1: skip the prefill and MoE lines")
     p.add_argument("--skip-extras", action="store_true", help="N=1: skip the configs[0] and configs[1] lines")
-    p.add_argument("--launch", default="chain-step", choices=["chain-step", "chain-layer", "calls"],
+    p.add_argument("--launch", default="calls", choices=["chain-step", "chain-layer", "calls"],
                    help="N=1: the step as one persistent chain launch (thq4_linear_chain), one chain per layer, or "
                         "one thq4_linear / thq4_gate_up call per projection (N > 1 always uses calls)")
     p.add_argument("--trace", default=None,
@@ -480,6 +480,8 @@ def run_thq4(args):
     if args.trace:
         path = args.trace + (f".rank{rank}" if world > 1 else "")
         trace_step(torch, lib, step_calls, dev, path, barrier, world, rank)
+        if launch_mode == "chain-step":
+            trace_step(torch, lib, step, dev, path + ".chain", barrier, world, rank)
 
     kernel_only = parity = projections = None
     if world > 1:
@@ -780,6 +782,8 @@ def trace_step(torch, lib, step, dev, path, barrier, world, rank):
     g.reset()
     del g
     h = buf.cpu().numpy().view(np.uint64)
+    if h.size and h[0] == 0x7468713463686e21:  # a chain launch: per (op, CTA) stamps
+        return _trace_chain(h, path, world, rank)
     recs, off = [], 0
     while off + 8 <= h.size and h[off] == 0x7468713474726163:
         grid = int(h[off + 1])
@@ -823,6 +827,47 @@ def trace_step(torch, lib, step, dev, path, barrier, world, rank):
     with open(path, "w") as f:
         json.dump({"world": world, "rank": rank, "launches": len(launches), "step_us": round(step_us, 3),
                    "per_shape": summary, "per_launch": launches}, f, indent=1)
+
+
+CHAIN_PHASES = ("op begun", "activation staged", "stream consumed", "outputs stored")
+
+
+def _trace_chain(h, path, world, rank):
+    """The chain kernel's record: per op, the CTA medians of each phase after
+    the op's first CTA began it, the longest stream, and the op's span from
+    the previous op's last store to its own."""
+    import numpy as np
+    grid, n = int(h[1]), int(h[2])
+    st = h[8: 8 + n * grid * 4].reshape(n, grid, 4).astype(np.int64)
+    ops, prev_end = [], int(st[0, :, 0].min())
+    base = prev_end
+    for p in range(n):
+        begun = st[p, :, 0]
+        t0 = int(begun.min())
+        act = st[p, :, 3] > 0  # CTAs with a run in this op
+        end = int(st[p, act, 3].max()) if act.any() else t0
+        med = {CHAIN_PHASES[i]: round(float(np.median(st[p, act, i] - t0)) / 1e3, 3) if act.any() else None
+               for i in range(4)}
+        ops.append({"op": p, "active": int(act.sum()), "begin_us": round((t0 - base) / 1e3, 3),
+                    "span_us": round((end - prev_end) / 1e3, 3), "phase_median_us": med,
+                    "stream_max_us": round(float((st[p, act, 2] - t0).max()) / 1e3, 3) if act.any() else None,
+                    "store_max_us": round(float((st[p, act, 3] - t0).max()) / 1e3, 3) if act.any() else None})
+        prev_end = end
+    by_kind = {}
+    for o in ops:
+        by_kind.setdefault(o["op"] % 4, []).append(o)
+    names = {0: "qkv", 1: "o", 2: "gate_up", 3: "down"}
+    summary = {names[k]: {"span_us": round(float(np.mean([o["span_us"] for o in v])), 3),
+                          "phase_median_us": {ph: round(float(np.mean([o["phase_median_us"][ph] for o in v
+                                                                        if o["phase_median_us"][ph] is not None])), 3)
+                                              for ph in CHAIN_PHASES},
+                          "stream_max_us": round(float(np.mean([o["stream_max_us"] for o in v if o["stream_max_us"]])), 3),
+                          "store_max_us": round(float(np.mean([o["store_max_us"] for o in v if o["store_max_us"]])), 3)}
+               for k, v in by_kind.items()} if n % 4 == 0 else {}
+    with open(path, "w") as f:
+        json.dump({"world": world, "rank": rank, "kernel": "chain_kernel", "ops": n, "ctas": grid,
+                   "stages": int(h[3]), "step_us": round((prev_end - base) / 1e3, 3), "per_kind": summary,
+                   "per_op": ops}, f, indent=1)
 
 
 def bench_c1(torch, thq4, synth, dev, hbm_peak, graph):

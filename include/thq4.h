@@ -175,8 +175,10 @@ typedef struct thq4_chain_op {
   int32_t y_dtype;       /* THQ4_BF16 or THQ4_F32 */
   int32_t reserved;      /* 0 */
 } thq4_chain_op;
-/* Workspace bytes of thq4_linear_chain (256-byte aligned, zero-filled before
- * the first call; every call leaves it zeroed unless it timed out). */
+/* Workspace bytes of thq4_linear_chain: split-K partials, arrival counters
+ * and the grid barrier's words.  256-byte aligned and zero-filled before its
+ * first use; every completed call leaves the counters and barrier words at
+ * zero again (unless it timed out), so one allocation serves later calls. */
 size_t thq4_linear_chain_workspace_bytes(const thq4_chain_op *ops, int n);
 /* 1 <= n <= 112 ops, one scale dtype, m <= 8 tokens of bf16 x (4 of f32 x).
  * Calls that may overlap on the GPU need separate workspaces. */

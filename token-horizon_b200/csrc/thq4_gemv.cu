@@ -790,6 +790,10 @@ struct ChainArgs {
   uint32_t *count; // arrivals per (slab, tile), as GemvArgs::count
   uint32_t *bar;   // [0] barrier arrivals, [1] exits (zero between launches)
   int n, m, P, xf32, stages, xcap;
+  // phase trace (thq4_debug_set_trace; nullptr = off): 8 header words, then
+  // per (op, CTA) 4 %globaltimer stamps: op begun (barrier passed), x
+  // staged, stream consumed, outputs stored
+  unsigned long long *trace;
   ChainOp ops[kMaxChainOps];
 };
 
@@ -800,7 +804,7 @@ struct OpView {
   const void *x;
   void *y;
   int m, in, ng, out, P, xf32, yf32;
-  int run_base, run_rem, cps, active, gate_up;
+  int run_base, run_rem, cps, active, gate_up, index;
   int g_mode, g_world, g_rank, g_rows, g_off, g_stride;
   long long g_slot;
   uint16_t *const *g_dst;
@@ -814,6 +818,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void chain_stamp(const ChainArgs &a, int p, int i) {
+  if (a.trace && threadIdx.x == 0) a.trace[8 + ((size_t)p * gridDim.x + blockIdx.x) * 4 + i] = global_timer_ns();
 }
 
 // Thread 0 writes op p's view; the consumers see it after their barrier.
@@ -835,6 +843,7 @@ __device__ __forceinline__ void chain_set_view(const ChainArgs &a, int p, OpView
     v.cps = op.cps;
     v.active = op.active;
     v.gate_up = op.gate_up;
+    v.index = p;
     v.g_mode = v.g_world = v.g_rank = v.g_rows = v.g_off = v.g_stride = 0;
     v.g_slot = 0;
     v.g_dst = nullptr;
@@ -920,6 +929,7 @@ __device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const Op
   constexpr int CPG = 8 / GW;
   constexpr int LPJ = 4 / GW;
   const int lane = threadIdx.x & 31, tile = threadIdx.x >> 5;
+  chain_stamp(a, v.index, 0);
   if ((int)blockIdx.x >= v.active) return cur;  // no run in this op (every consumer warp alike)
   int s = cur.s;
   uint32_t par = cur.par;
@@ -931,6 +941,7 @@ __device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const Op
   const int gs = cg0 * CB;
   const int xcnt = min(v.ng, sgs_before(C1, v.cps, v.ng, CB) - sgs_before(C0, v.cps, v.ng, CB));
   stage_x<false>(v, gs, xcnt, xf, zero, mx);
+  chain_stamp(a, v.index, 1);
 
   const int r = lane >> 2, c = lane & 3;
   const int jr = r / CPG, qr = r % CPG;
@@ -1101,6 +1112,7 @@ __device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const Op
       finished_any = true;
     }
   }
+  chain_stamp(a, v.index, 2);
   int last_slab = -1;
   if (nch > 0 && cg != v.cps - 1) {
     reduce_y();
@@ -1131,6 +1143,7 @@ __device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const Op
     if (done & 1u) combine(first_slab);
     if (done & 2u) combine(last_slab);
   }
+  chain_stamp(a, v.index, 3);
   return RingCursor{s, par, aborted ? 1 : 0};
 }
 
@@ -1184,6 +1197,13 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     return;
   }
   // ---- consumers ------------------------------------------------------------
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+    a.trace[0] = 0x7468713463686e21ull;  // chain record magic
+    a.trace[1] = gridDim.x;
+    a.trace[2] = (unsigned long long)a.n;
+    a.trace[3] = (unsigned long long)a.stages;
+    for (int i = 4; i < 8; ++i) a.trace[i] = 0;
+  }
   RingCursor cur{R - 1, 1u, 0};
   for (int p = 0; p < a.n; ++p) {
     if (p > 0) {
@@ -1413,15 +1433,15 @@ std::mutex g_trace_mu;
 unsigned long long *g_trace = nullptr;
 size_t g_trace_words = 0, g_trace_next = 0;
 
-unsigned long long *trace_record(int grid) {
+unsigned long long *trace_record_words(size_t need) {
   std::lock_guard<std::mutex> lock(g_trace_mu);
   if (!g_trace) return nullptr;
-  const size_t need = 8 + (size_t)grid * 8;
   if (g_trace_next + need + 8 > g_trace_words) return nullptr;  // keep room for the end marker
   unsigned long long *r = g_trace + g_trace_next;
   g_trace_next += need;
   return r;
 }
+unsigned long long *trace_record(int grid) { return trace_record_words(8 + (size_t)grid * 8); }
 }  // namespace
 
 void gemv_set_trace(void *buf, size_t bytes) {
@@ -1590,6 +1610,7 @@ cudaError_t chain_launch(const ChainSpec *ops, int n, bool x_f32, int m, void *w
   a.count = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + part_bytes);
   a.bar = reinterpret_cast<uint32_t *>(static_cast<char *>(workspace) + gemv_workspace_bytes(max_rows));
   a.xcap = xcap;
+  a.trace = trace_record_words(8 + (size_t)n * grid * 4);
   int st = 0;
   for (int t = 5; t >= 2 && !st; --t)
     if (512 + (size_t)t * kChainStageBytes + xstage_bytes(xcap, a.P) <= (size_t)kGemvMaxSmem) st = t;
