@@ -753,7 +753,14 @@ def run_thq4(args):
 
 
 TRACE_PHASES = ("running", "predecessor complete", "peers' flags seen", "activation staged",
-                "first stage landed", "stream consumed", "outputs stored", "exchange signalled")
+                "first stage landed", "stream consumed", "outputs stored", "exchange signalled",
+                "stores fenced (exchange)", "flags written (exchange, last CTA)")
+TRACE_STAMPS = len(TRACE_PHASES)
+
+
+def _mean_or_none(v):
+    v = [x for x in v if x is not None]
+    return round(sum(v) / len(v), 3) if v else None
 
 
 def trace_step(torch, lib, step, dev, path, barrier, world, rank):
@@ -787,23 +794,27 @@ def trace_step(torch, lib, step, dev, path, barrier, world, rank):
     recs, off = [], 0
     while off + 8 <= h.size and h[off] == 0x7468713474726163:
         grid = int(h[off + 1])
-        st = h[off + 8: off + 8 + 8 * grid].reshape(grid, 8).astype(np.int64)
+        st = h[off + 8: off + 8 + TRACE_STAMPS * grid].reshape(grid, TRACE_STAMPS).astype(np.int64)
         flags = int(h[off + 4])
         recs.append({"out": int(h[off + 2]), "in": int(h[off + 3]), "gate_up": flags & 1,
                      "cluster": (flags >> 8) & 0xFF, "mode": (flags >> 16) & 0xFF, "wait": (flags >> 24) & 0xFF,
                      "m": int(h[off + 5]), "chunk": int(h[off + 6]) & 0xFF, "stages": int(h[off + 6]) >> 8,
                      "ctas": grid, "st": st})
-        off += 8 + 8 * grid
+        off += 8 + TRACE_STAMPS * grid
     launches, prev_end = [], None
     for r in recs:
         st = r.pop("st")
         t0 = int(st[:, 0].min())
         end = int(st[:, 7].max())
-        med = [round(float(np.median(st[:, i] - t0)) / 1e3, 3) for i in range(8)]
+        med, mx = [], []
+        for i in range(TRACE_STAMPS):
+            col = st[:, i][st[:, i] > 0]  # stamps a CTA did not take stay 0
+            med.append(round(float(np.median(col - t0)) / 1e3, 3) if col.size else None)
+            mx.append(round(float((col - t0).max()) / 1e3, 3) if col.size else None)
         r.update({"span_us": round((end - t0) / 1e3, 3),
                   "gap_from_previous_exit_us": None if prev_end is None else round((t0 - prev_end) / 1e3, 3),
-                  "phase_median_us": dict(zip(TRACE_PHASES, med)),
-                  "stream_max_us": round(float((st[:, 5] - t0).max()) / 1e3, 3), "start_ns": t0})
+                  "phase_median_us": dict(zip(TRACE_PHASES, med)), "phase_max_us": dict(zip(TRACE_PHASES, mx)),
+                  "stream_max_us": mx[5], "start_ns": t0})
         prev_end = end
         launches.append(r)
     base = launches[0]["start_ns"] if launches else 0
@@ -821,8 +832,8 @@ def trace_step(torch, lib, step, dev, path, barrier, world, rank):
             "stages": rs[0]["stages"], "mode": rs[0]["mode"], "wait": rs[0]["wait"],
             "span_us": round(float(np.mean([r["span_us"] for r in rs])), 3),
             "gap_us": round(float(np.mean(gaps)) if gaps else 0.0, 3),
-            "phase_median_us": {p: round(float(np.mean([r["phase_median_us"][p] for r in rs])), 3)
-                                for p in TRACE_PHASES}}
+            "phase_median_us": {p: _mean_or_none([r["phase_median_us"][p] for r in rs]) for p in TRACE_PHASES},
+            "phase_max_us": {p: _mean_or_none([r["phase_max_us"][p] for r in rs]) for p in TRACE_PHASES}}
     step_us = max((r["start_us"] + r["span_us"] for r in launches), default=0.0)
     with open(path, "w") as f:
         json.dump({"world": world, "rank": rank, "launches": len(launches), "step_us": round(step_us, 3),

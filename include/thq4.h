@@ -434,9 +434,14 @@ thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved);
  * `buf` is zero-filled device memory.  Each launch that fits appends a record:
  * 8 header words {0x7468713474726163, CTAs, out, in, gate_up | cluster size
  * << 8 | exchange mode << 16 | waits << 24, tokens, chunk | stages << 8, 0}
- * then, per CTA, 8 %globaltimer stamps (ns): running, predecessor complete,
+ * then, per CTA, 10 %globaltimer stamps (ns): running, predecessor complete,
  * peers' flags seen, activation staged, first weight stage landed, stream
- * consumed, outputs stored, exchange signalled.  A launch captured in a CUDA
+ * consumed, outputs stored, exchange signalled, and for an exchanging launch
+ * its stores fenced at system scope (every CTA) and the peers' flags written
+ * (the last CTA; 0 elsewhere).  A chain launch (thq4_linear_chain) appends
+ * 8 header words {0x7468713463686e21, CTAs, ops, stages, 0...} then, per
+ * (op, CTA), 4 stamps: op begun, x staged, stream consumed, outputs
+ * stored.  A launch captured in a CUDA
  * graph keeps its record; replays overwrite it.  No reference counterpart
  * (the reference times its kernels with Metal's GPU counters). */
 thq4_status thq4_debug_set_trace(void *buf, size_t bytes);

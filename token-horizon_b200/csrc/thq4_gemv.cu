@@ -127,9 +127,12 @@ enum : int {
   kTrStreamed = 5, // every stage consumed
   kTrStored = 6,   // outputs stored (after any split-K or cluster combine)
   kTrDone = 7,     // exchange signalled; the CTA exits
+  kTrFenced = 8,   // exchange: this CTA's stores fenced at system scope, arrival counted
+  kTrFlagged = 9,  // exchange: the peers' flags written (the grid's last CTA only)
 };
+constexpr int kTrStamps = 10;
 __device__ __forceinline__ void trace_stamp(const GemvArgs &a, int i) {
-  if (a.trace && threadIdx.x == 0) a.trace[8 + (size_t)blockIdx.x * 8 + i] = global_timer_ns();
+  if (a.trace && threadIdx.x == 0) a.trace[8 + (size_t)blockIdx.x * kTrStamps + i] = global_timer_ns();
 }
 
 // columns with per-group metadata: P rounded up to even (lanes own pairs)
@@ -339,13 +342,16 @@ __device__ void peer_signal(const GemvArgs &a) {
   consumer_sync();
   if (threadIdx.x != 0) return;
   fence_acq_rel_sys();  // this CTA's stores, local and remote, before its arrival
-  if (atom_add_acq_rel(a.g_arrive, 1u) + 1u != gridDim.x) return;
+  const bool last = atom_add_acq_rel(a.g_arrive, 1u) + 1u == gridDim.x;
+  trace_stamp(a, kTrFenced);
+  if (!last) return;
   *a.g_arrive = 0;
   const uint32_t c = *a.g_count + 1u;  // only the last CTA of each launch touches it
   *a.g_count = c;
   fence_acq_rel_sys();  // every CTA's stores (acquired through the counter) before the flags
   for (int rk = 0; rk < a.g_world; ++rk)
     if (rk != a.g_rank) st_release_sys(a.g_flags[rk] + a.g_rank, c);
+  trace_stamp(a, kTrFlagged);
 }
 
 __global__ void peer_wait_kernel(uint32_t *const *flags, const uint32_t *count, int world, int rank, uint32_t *status) {
@@ -1441,7 +1447,7 @@ unsigned long long *trace_record_words(size_t need) {
   g_trace_next += need;
   return r;
 }
-unsigned long long *trace_record(int grid) { return trace_record_words(8 + (size_t)grid * 8); }
+unsigned long long *trace_record(int grid) { return trace_record_words(8 + (size_t)grid * kTrStamps); }
 }  // namespace
 
 void gemv_set_trace(void *buf, size_t bytes) {
