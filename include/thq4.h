@@ -48,7 +48,10 @@ typedef enum thq4_status {
 typedef enum thq4_dtype {
   THQ4_BF16 = 0,
   THQ4_F16 = 1,
-  THQ4_F32 = 2
+  THQ4_F32 = 2,
+  /* x of thq4_linear / thq4_gate_up given as a presum block (m <= 8): see
+   * thq4_presum_block_bytes */
+  THQ4_PRESUM = 3
 } thq4_dtype;
 
 /* Source layouts thq4_repack accepts (the reference's formats, plus ours). */
@@ -219,6 +222,33 @@ thq4_status thq4_linear_chain(const thq4_chain_op *ops, int n, int x_dtype, int 
  *     per stream. */
 thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype,
                                 int m, void *y, int y_dtype, void *stream);
+/* ---- presum blocks (replaces the K45 presum machinery, quant_kernel.rs:
+ * 265-318, 2544-2568, 3355-3440, 3642-3657) ------------------------------
+ * A presum block of width `in` is a decode / verify activation of m <= 8
+ * rows laid out as 8 bf16 rows [8][in] (rows >= m zero) followed by the f32
+ * sums [in/64][8]: sums[g * 8 + t] is row t's group g summed in the
+ * reference's lane pattern (lane l adds x[64g + l] + x[64g + 32 + l] in f32,
+ * the 32 lanes combine by xor butterfly 16, 8, 4, 2, 1).  Passed as x with
+ * x_dtype THQ4_PRESUM, thq4_linear and thq4_gate_up use the block's sums for
+ * each group's bias term b * sum(x) instead of computing them; the block must
+ * be thq4_presum_block_bytes(in) bytes long and 16-byte aligned (the
+ * reference's "presum block missing" check, quant_kernel.rs:3642-3657). */
+/* 8 * in * 2 + (in / 64) * 8 * 4 (presum_block_bytes, quant_kernel.rs:
+ * 265-273); 0 when in is not a positive multiple of 64. */
+size_t thq4_presum_block_bytes(int in);
+/* Q4AttachSums (quant_kernel.rs:3355-3440): block = x [m][in] bf16 as a
+ * presum block (rows m..7 zero) with its sums.  1 <= m <= 8. */
+thq4_status thq4_presum_attach(const void *x, int m, int in, void *block, void *stream);
+/* AddRmsNorm { sums } (engine/src/gdn_kernel.rs:1851-1866, 1919-1962):
+ * res bf16 [T][C] = bf16(x + r) and block = the presum block of
+ * bf16(bf16(res) * inv * w) (rows T..7 zero), inv = 1 / sqrt(ss / C + eps),
+ * ss = sum of (x + r)^2 in f32, lane l accumulating columns l, l + 32, ...
+ * in order, the 32 lanes combined by the butterfly; 1 / sqrt is correctly
+ * rounded here where the reference's Metal rsqrt is approximate.  x, r, w
+ * bf16; 1 <= T <= 8; C a multiple of 64, at most 32768. */
+thq4_status thq4_add_rms_norm(const void *x, const void *r, const void *w, int T, int C, float eps, void *res,
+                              void *block, void *stream);
+
 /* Replaces AffineDequant (quant_kernel.rs:1743-1782, 5836-5899): y bf16
  * [out][in] = bf16(q * s + b). */
 thq4_status thq4_dequant(const thq4_weight *w, void *y, void *stream);

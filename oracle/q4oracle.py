@@ -479,3 +479,61 @@ def cpu_linear(wq, sb, sb_dtype: int, x, nthreads: int | None = None):
     if n < 0:
         raise ValueError("unsupported shape for the CPU baseline")
     return y, n
+
+
+# ---- presum blocks (engine/src/quant_kernel.rs:265-318, 1864-1884;
+#      engine/src/gdn_kernel.rs:1851-1866, 1919-1962) --------------------------
+
+def _lane_butterfly(v: np.ndarray) -> np.ndarray:
+    """32 lanes on the last axis combined by xor butterfly (partners 16, 8, 4,
+    2, 1), each step an f32 add; returns lane 0's value."""
+    lanes = np.arange(32)
+    v = np.asarray(v, dtype=np.float32)
+    for o in (16, 8, 4, 2, 1):
+        v = (v + v[..., lanes ^ o]).astype(np.float32)
+    return v[..., 0]
+
+
+def presum_sums(rows_bf16) -> np.ndarray:
+    """f32 sums [in/64][8] of a presum block's 8 bf16 rows [8][in]: lane l of
+    group g adds x[64g + l] + x[64g + 32 + l] (q4_store_input_sums,
+    quant_kernel.rs:1864-1884), the lanes combine by the butterfly."""
+    x = bf16_to_f32(np.asarray(rows_bf16, dtype=np.uint16)).astype(np.float32)
+    rows, inp = x.shape
+    g = x.reshape(rows, inp // 64, 64)
+    v = (g[:, :, :32] + g[:, :, 32:]).astype(np.float32)
+    return np.ascontiguousarray(_lane_butterfly(v).T)
+
+
+def presum_block(x_bf16) -> tuple:
+    """Q4AttachSums: (rows [8][in] bf16 with rows >= m zero, sums [in/64][8])."""
+    x = np.asarray(x_bf16, dtype=np.uint16)
+    m, inp = x.shape
+    rows = np.zeros((8, inp), dtype=np.uint16)
+    rows[:m] = x
+    return rows, presum_sums(rows)
+
+
+def add_rms_norm(x_bf16, r_bf16, w_bf16, eps: float) -> tuple:
+    """AddRmsNorm { sums } (gdn_kernel.rs:1919-1962, per-row form :1964-2004):
+    v = x + r in f32, res = bf16(v); lane l accumulates ss += v * v over
+    columns l, l + 32, ... in order (f32 multiply, then f32 add), the lanes
+    combine by the butterfly; inv = 1 / sqrt(ss / C + eps), each step f32 and
+    correctly rounded; nrm = bf16((bf16(v) * inv) * w).  Returns (res [T][C],
+    block rows [8][C] with rows >= T zero, sums [C/64][8])."""
+    xf = bf16_to_f32(np.asarray(x_bf16, dtype=np.uint16)).astype(np.float32)
+    rf = bf16_to_f32(np.asarray(r_bf16, dtype=np.uint16)).astype(np.float32)
+    wf = bf16_to_f32(np.asarray(w_bf16, dtype=np.uint16)).astype(np.float32)
+    T, C = xf.shape
+    v = (xf + rf).astype(np.float32)
+    res = f32_to_bf16(v)
+    ss = np.zeros((T, 32), dtype=np.float32)
+    for j in range(C // 32):
+        c = v[:, j * 32:(j + 1) * 32]
+        ss = (ss + (c * c).astype(np.float32)).astype(np.float32)
+    tot = _lane_butterfly(ss)
+    inv = (np.float32(1.0) / np.sqrt((tot / np.float32(C)).astype(np.float32) + np.float32(eps))).astype(np.float32)
+    nrm = f32_to_bf16(((bf16_to_f32(res).astype(np.float32) * inv[:, None]).astype(np.float32) * wf).astype(np.float32))
+    rows = np.zeros((8, C), dtype=np.uint16)
+    rows[:T] = nrm
+    return res, rows, presum_sums(rows)

@@ -198,3 +198,36 @@ def test_golden_fixtures_reproduce():
     assert set(got) == set(want.files)
     for k in want.files:
         assert np.array_equal(np.asarray(got[k]), want[k]), k
+
+
+def test_presum_sums_follow_the_lane_pattern():
+    """The presum sums (q4_store_input_sums, quant_kernel.rs:1864-1884) against
+    a plain-Python restatement: lane l adds x[64g + l] + x[64g + 32 + l], then
+    xor butterfly over the 32 lanes, every add in f32."""
+    rng = np.random.default_rng(3)
+    rows = O.f32_to_bf16(rng.standard_normal((8, 192)).astype(np.float32))
+    got = O.presum_sums(rows)
+    xf = O.bf16_to_f32(rows).astype(np.float32)
+    for t in range(8):
+        for g in range(3):
+            v = [np.float32(xf[t, 64 * g + l] + xf[t, 64 * g + 32 + l]) for l in range(32)]
+            for o in (16, 8, 4, 2, 1):
+                v = [np.float32(v[l] + v[l ^ o]) for l in range(32)]
+            assert got[g, t] == v[0]
+    assert abs(float(got.sum()) - float(xf.astype(np.float64).sum())) < 1e-3
+
+
+def test_add_rms_norm_oracle_is_rms_norm():
+    rng = np.random.default_rng(4)
+    T, C = 3, 512
+    x = O.f32_to_bf16(rng.standard_normal((T, C)).astype(np.float32))
+    r = O.f32_to_bf16(rng.standard_normal((T, C)).astype(np.float32))
+    w = O.f32_to_bf16((1 + 0.1 * rng.standard_normal(C)).astype(np.float32))
+    res, rows, sums = O.add_rms_norm(x, r, w, 1e-6)
+    v = O.bf16_to_f32(x).astype(np.float64) + O.bf16_to_f32(r).astype(np.float64)
+    want = O.bf16_to_f32(O.f32_to_bf16(v.astype(np.float32))).astype(np.float64)
+    want = want / np.sqrt((v ** 2).mean(axis=1, keepdims=True) + 1e-6) * O.bf16_to_f32(w).astype(np.float64)
+    got = O.bf16_to_f32(rows[:T]).astype(np.float64)
+    assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max()
+    assert not rows[T:].any() and not sums[:, T:].any()
+    assert np.array_equal(sums, O.presum_sums(rows))

@@ -263,10 +263,34 @@ size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m) {
   return gemv_workspace_bytes(w->out);
 }
 
+namespace {
+// x given as a presum block (x_dtype THQ4_PRESUM): m <= 8 rows of bf16 in an
+// [8][in] block followed by its sums; the checks of quant_kernel.rs:3642-3657
+// that the host can make (the block's length is the caller's to provide:
+// thq4_presum_block_bytes).
+thq4_status check_presum_x(const void *x, int m, const void *y, int y_dtype, const char *who) {
+  thq4_status s = check_io(x, THQ4_BF16, m, y, y_dtype, who);
+  if (s != THQ4_OK) return s;
+  if (m > 8)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": a presum block holds at most 8 rows (m " +
+                                                    std::to_string(m) + ")");
+  return THQ4_OK;
+}
+}  // namespace
+
 thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
                         void *workspace, size_t workspace_bytes, void *stream) {
   thq4_status s = check_weight(w, "thq4_linear");
   if (s != THQ4_OK) return s;
+  if (x_dtype == THQ4_PRESUM) {
+    if ((s = check_presum_x(x, m, y, y_dtype, "thq4_linear")) != THQ4_OK) return s;
+    if ((s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(w->out), "thq4_linear")) != THQ4_OK)
+      return s;
+    const cudaError_t e = gemv_launch(*w, nullptr, x, false, m, y, y_dtype == THQ4_F32, workspace,
+                                      static_cast<cudaStream_t>(stream), nullptr, true);
+    if (e != cudaSuccess) return cuda_error(e, "thq4_linear (presum)");
+    return THQ4_OK;
+  }
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_linear");
   if (s != THQ4_OK) return s;
   if (prefill_supported(m, x_dtype == THQ4_F32)) {
@@ -365,6 +389,15 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const v
   if (s != THQ4_OK) return s;
   if (gate->out != up->out || gate->in != up->in || gate->sb_dtype != up->sb_dtype)
     return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_gate_up: gate and up halves differ in shape or dtype");
+  if (x_dtype == THQ4_PRESUM) {
+    if ((s = check_presum_x(x, m, y, y_dtype, "thq4_gate_up")) != THQ4_OK) return s;
+    if ((s = check_workspace(workspace, workspace_bytes, gemv_workspace_bytes(gate->out), "thq4_gate_up")) != THQ4_OK)
+      return s;
+    const cudaError_t e = gemv_launch(*gate, up, x, false, m, y, y_dtype == THQ4_F32, workspace,
+                                      static_cast<cudaStream_t>(stream), nullptr, true);
+    if (e != cudaSuccess) return cuda_error(e, "thq4_gate_up (presum)");
+    return THQ4_OK;
+  }
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_gate_up");
   if (s != THQ4_OK) return s;
   if (prefill_supported(m, x_dtype == THQ4_F32)) {
@@ -824,6 +857,40 @@ thq4_status thq4_moe_add_partial(const void *x, const void *residual, int T, int
                                  size_t workspace_bytes, void *stream) {
   return moe_add_common(x, residual, T, H, I, E, k, e0, e1, w, y_part, true, workspace, workspace_bytes, stream,
                         "thq4_moe_add_partial");
+}
+
+size_t thq4_presum_block_bytes(int in) {
+  if (in <= 0 || in % kGroup) return 0;
+  return presum_block_bytes(in);
+}
+
+thq4_status thq4_presum_attach(const void *x, int m, int in, void *block, void *stream) {
+  const char *who = "thq4_presum_attach";
+  if (m < 1 || m > 8 || in <= 0 || in % kGroup)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": need 1 <= m <= 8 and in a positive multiple "
+                                                                   "of 64 (m " + std::to_string(m) + ", in " +
+                                                    std::to_string(in) + ")");
+  if (!x || !block || !aligned(x, 16) || !aligned(block, 16))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": x and block must be 16-byte aligned");
+  const cudaError_t e = presum_attach_launch(x, m, in, block, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
+thq4_status thq4_add_rms_norm(const void *x, const void *r, const void *w, int T, int C, float eps, void *res,
+                              void *block, void *stream) {
+  const char *who = "thq4_add_rms_norm";
+  if (T < 1 || T > 8 || C <= 0 || C % kGroup || C > kAddRmsNormMaxC)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": need 1 <= T <= 8 and C a multiple of 64 up "
+                                                                   "to " + std::to_string(kAddRmsNormMaxC) +
+                                                    " (T " + std::to_string(T) + ", C " + std::to_string(C) + ")");
+  if (!x || !r || !w || !res || !block || !aligned(block, 16) || !aligned(x, 2) || !aligned(r, 2) ||
+      !aligned(w, 2) || !aligned(res, 2))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL or misaligned buffer (block 16-byte aligned)");
+  if (!(eps >= 0.0f)) return set_error(THQ4_ERR_INVALID_ARGUMENT, std::string(who) + ": eps must be >= 0");
+  const cudaError_t e = add_rms_norm_launch(x, r, w, T, C, eps, res, block, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
 }
 
 thq4_status thq4_debug_set_gemv(int chunk, int stages, int grid, int reserved) {

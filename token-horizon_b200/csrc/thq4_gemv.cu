@@ -112,6 +112,9 @@ struct GemvArgs {
   // summed in order and rounded to bf16 as they are staged
   int xparts;
   long long xslot;
+  // x is a presum block: its f32 sums [ng][8] (the bias term's sum(x) of
+  // group g, token t at xsum[g * 8 + t]); nullptr otherwise
+  const float *xsum;
   // phase trace (testing hook; nullptr = off): a record of 8 header words
   // then 8 %globaltimer stamps per CTA (thq4_debug_set_trace)
   unsigned long long *trace;
@@ -271,7 +274,14 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      if (live && h8 == 0) mx[slot * P8 + q] = make_float4(f * sum, f, 64.0f * sum, 0.0f);
+      if (live && h8 == 0) {
+        // the bias term's sum(x): the producer's (presum block) or this one;
+        // the offset term always uses the sum of the fp16 values multiplied
+        int g = gs + slot;
+        if (g >= a.ng) g -= a.ng;
+        const float bsum = a.xsum ? a.xsum[g * 8 + q] : f * sum;
+        mx[slot * P8 + q] = make_float4(bsum, f, 64.0f * sum, 0.0f);
+      }
     }
   }
   consumer_sync();
@@ -348,7 +358,10 @@ __device__ void peer_signal(const GemvArgs &a) {
   *a.g_arrive = 0;
   const uint32_t c = *a.g_count + 1u;  // only the last CTA of each launch touches it
   *a.g_count = c;
-  fence_acq_rel_sys();  // every CTA's stores (acquired through the counter) before the flags
+  // Each flag store is a system-scope release: it orders before the flag
+  // everything this thread has observed, including every other CTA's stores,
+  // which each CTA fenced at system scope before its arrival that the
+  // counter's acquire read (release is cumulative), so no second fence.
   for (int rk = 0; rk < a.g_world; ++rk)
     if (rk != a.g_rank) st_release_sys(a.g_flags[rk] + a.g_rank, c);
   trace_stamp(a, kTrFlagged);
@@ -816,6 +829,7 @@ struct OpView {
   uint16_t *const *g_dst;
   int xparts;
   long long xslot;
+  const float *xsum;
 };
 constexpr int kViewOffset = 256;  // the view's place in shared memory, after the barriers
 static_assert(sizeof(OpView) <= 256, "the op view fits its slot");
@@ -855,6 +869,7 @@ __device__ __forceinline__ void chain_set_view(const ChainArgs &a, int p, OpView
     v.g_dst = nullptr;
     v.xparts = 0;
     v.xslot = 0;
+    v.xsum = nullptr;
     *vs = v;
   }
   consumer_sync();
@@ -1458,7 +1473,7 @@ void gemv_set_trace(void *buf, size_t bytes) {
 }
 
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32, int m, void *y,
-                        bool y_f32, void *workspace, cudaStream_t stream, const PeerGather *peer) {
+                        bool y_f32, void *workspace, cudaStream_t stream, const PeerGather *peer, bool x_presum) {
   const bool gate_up = w1 != nullptr;
   const GemvPlan p = gemv_plan(w0.out, w0.in, m, x_f32, gate_up);
   if (!p.ok) return cudaErrorInvalidConfiguration;
@@ -1490,6 +1505,9 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
     a.P = x_f32 ? 2 * mt : mt;
     a.xf32 = x_f32 ? 1 : 0;
     a.yf32 = y_f32 ? 1 : 0;
+    // a presum block is one pass (m <= 8): its sums follow the 8 rows
+    a.xsum = x_presum ? reinterpret_cast<const float *>(static_cast<const uint16_t *>(x) + (size_t)8 * w0.in) + t0
+                      : nullptr;
     a.stages = p.stages;
     a.xcap = p.xcap;
     a.pre = gemv_cfg_override().pre;

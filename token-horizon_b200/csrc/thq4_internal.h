@@ -89,7 +89,7 @@ struct PeerGather {
 };
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
                         int m, void *y, bool y_f32, void *workspace, cudaStream_t stream,
-                        const PeerGather *peer = nullptr);
+                        const PeerGather *peer = nullptr, bool x_presum = false);
 // A chain of dependent projections in one persistent launch (thq4_linear_chain).
 struct ChainSpec {
   const thq4_weight *w, *up;  // up: the second half of a gate/up op, or nullptr
@@ -197,6 +197,15 @@ struct MoeSets {
 cudaError_t moe_launch(const void *x, const void *residual, const MoeRouting &r, int T, int H, int I, int E, int k,
                        const MoeSets &sets, void *y, const MoeWorkspace &w, cudaStream_t stream, int e0 = 0,
                        int e1 = -1, bool y_f32 = false);
+
+// ---- presum blocks ----------------------------------------------------------
+// [8][in] bf16 rows then f32 sums [in/64][8] (thq4_presum.cu).
+size_t presum_block_bytes(int in);
+// add_rms_norm keeps a row of f32 x + r in shared memory
+constexpr int kAddRmsNormMaxC = 32768;
+cudaError_t add_rms_norm_launch(const void *x, const void *r, const void *w, int T, int C, float eps, void *res,
+                                void *block, cudaStream_t stream);
+cudaError_t presum_attach_launch(const void *x, int m, int in, void *block, cudaStream_t stream);
 
 // ---- repack / dequant ------------------------------------------------------
 cudaError_t repack_launch(int src_layout, const void *src_w, const void *src_sb, int src_out, int in,

@@ -24,6 +24,7 @@ ERR_NCCL = 5
 BF16 = 0
 F16 = 1
 F32 = 2
+PRESUM = 3
 
 # thq4_src_layout
 SRC_MLX = 0
@@ -129,6 +130,10 @@ SIGNATURES = {
     "thq4_copy": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_chain_workspace_bytes": (c_size_t, [c_void_p, c_int]),
     "thq4_linear_chain": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "thq4_presum_block_bytes": (c_size_t, [c_int]),
+    "thq4_presum_attach": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "thq4_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p, c_void_p,
+                                  c_void_p]),
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
     "thq4_debug_set_trace": (c_int, [c_void_p, c_size_t]),
     "thq4_debug_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -137,10 +137,11 @@ class QLin:
 
     def linear_ps(self, x: torch.Tensor, presum: bool = False, out_dtype: Optional[torch.dtype] = None,
                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """x [..., in] -> y [..., out].  ``presum`` is accepted for interface
-        parity: this library computes the per-group input sums inside the
-        kernel's prologue, so a producer's presum block is an ordinary x."""
-        del presum
+        """x [..., in] -> y [..., out].  With ``presum`` x is the live [m, in]
+        view of a presum block (presum_block / add_rms_norm, m <= 8): the
+        kernel takes each group's sum for the bias term from the block."""
+        if presum:
+            _check_presum_view(x, self.inp, "affine-qmpp")
         dims = list(x.shape)
         in_d = dims[-1]
         rows = 1
@@ -151,10 +152,10 @@ class QLin:
                             f"QLin::linear: x last dim {in_d} != weight inp {self.inp} (x {dims})")
         if not self.tiled_flag:
             self.tiled()
-        x_dtype = _X_DTYPE.get(x.dtype)
+        x_dtype = _lib.PRESUM if presum else _X_DTYPE.get(x.dtype)
         if x_dtype is None:
             raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin::linear: x dtype {x.dtype} is not bf16 or f32")
-        xv = x.reshape(rows, in_d).contiguous()
+        xv = x if presum else x.reshape(rows, in_d).contiguous()
         ydt = out_dtype or (torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         y = out if out is not None else torch.empty((rows, self.out), dtype=ydt, device=x.device)
         ws = workspace(self.packed.desc, x.device)
@@ -171,8 +172,10 @@ class QLin:
                        out: Optional[torch.Tensor] = None):
         """Fused [gate | up] -> silu(bf16 g) * bf16 u, [..., half].  Returns
         (tensor, emitted_presum) like the reference; the flag is always False
-        (no presum blocks are needed downstream)."""
-        del presum
+        (the down projection's block comes from presum_block when wanted).
+        With ``presum`` x is the live view of a presum block."""
+        if presum:
+            _check_presum_view(x, self.inp, "affine-qmpp gate_up")
         if self.out % 2 != 0 and up_row is None:
             return None
         half = self.out // 2 if up_row is None else self.out - up_row
@@ -189,10 +192,10 @@ class QLin:
                 raise Thq4Error(_lib.ERR_UNSUPPORTED, "QLin::gate_up_act: weight was not built from MLX tensors")
             self.tiled_flag = False
             self.tiled(up_row)
-        x_dtype = _X_DTYPE.get(x.dtype)
+        x_dtype = _lib.PRESUM if presum else _X_DTYPE.get(x.dtype)
         if x_dtype is None:
             raise Thq4Error(_lib.ERR_INVALID_ARGUMENT, f"QLin::gate_up_act: x dtype {x.dtype}")
-        xv = x.reshape(rows, dims[-1]).contiguous()
+        xv = x if presum else x.reshape(rows, dims[-1]).contiguous()
         y = out if out is not None else torch.empty((rows, half), dtype=torch.bfloat16, device=x.device)
         ws = workspace(self.packed_gate.desc, x.device)
         check(_lib.lib().thq4_gate_up(ctypes.byref(self.packed_gate.desc), ctypes.byref(self.packed_up.desc),
@@ -207,6 +210,47 @@ class QLin:
         y = torch.empty((self.out, self.inp), dtype=torch.bfloat16, device=self.packed.qw.device)
         check(_lib.lib().thq4_dequant(ctypes.byref(self.packed.desc), _ptr(y), _stream()))
         return y
+
+
+# -- presum blocks (quant_kernel.rs:265-318, 3642-3657) ---------------------------
+
+def presum_block_bytes(inp: int) -> int:
+    return int(_lib.lib().thq4_presum_block_bytes(inp))
+
+
+def _check_presum_view(x: torch.Tensor, inp: int, who: str) -> None:
+    """The reference's check that x is the live [m, in] view of a whole presum
+    block (quant_kernel.rs:3642-3657)."""
+    need = x.storage_offset() * 2 + presum_block_bytes(inp)
+    have = x.untyped_storage().nbytes()
+    m = x.numel() // inp if inp else 0
+    if (x.dtype != torch.bfloat16 or not x.is_contiguous() or (x.storage_offset() * 2) % 16 != 0 or have < need
+            or x.numel() != m * inp or not 1 <= m <= 8):
+        raise Thq4Error(_lib.ERR_INVALID_ARGUMENT,
+                        f"{who}: presum block missing (x_off {x.storage_offset() * 2}, buffer {have} < {need}, "
+                        f"x {list(x.shape)}, m {m})")
+
+
+def presum_block(x: torch.Tensor):
+    """Q4AttachSums: x [m, in] bf16 (m <= 8) as a presum block.  Returns the
+    block (uint8, presum_block_bytes(in)) and the [m, in] view of its rows."""
+    m, inp = x.shape
+    block = torch.empty(presum_block_bytes(inp), dtype=torch.uint8, device=x.device)
+    xc = x.contiguous()
+    check(_lib.lib().thq4_presum_attach(_ptr(xc), m, inp, _ptr(block), _stream()))
+    return block, block[:m * inp * 2].view(torch.bfloat16).view(m, inp)
+
+
+def add_rms_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float):
+    """AddRmsNorm { sums } (gdn_kernel.rs:1851-1866): res = bf16(x + r) and the
+    normed rows as a presum block.  Returns (res [T, C], block, the [T, C]
+    view of the block's normed rows)."""
+    T, C = x.shape
+    res = torch.empty_like(x)
+    block = torch.empty(presum_block_bytes(C), dtype=torch.uint8, device=x.device)
+    check(_lib.lib().thq4_add_rms_norm(_ptr(x.contiguous()), _ptr(r.contiguous()), _ptr(w.contiguous()), T, C,
+                                       ctypes.c_float(eps), _ptr(res), _ptr(block), _stream()))
+    return res, block, block[:T * C * 2].view(torch.bfloat16).view(T, C)
 
 
 def fuse_lins(lins: Sequence[QLin]) -> QLin:
