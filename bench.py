@@ -88,6 +88,9 @@ def parse():
     p.add_argument("--nccl-gather", action="store_true",
                    help="N > 1: gather each projection's output with NCCL all-gather (the baseline) instead of "
                         "the GEMV epilogue's NVLink stores")
+    p.add_argument("--exchange", default="ll", choices=["ll", "flags"],
+                   help="--tp row: the reduce's partials as low-latency words the reader polls (ll) or as f32 values "
+                        "behind a system-scope fence and per-rank flags (flags)")
     p.add_argument("--tp", default="row", choices=["col", "row"],
                    help="N > 1: col = every projection column-sharded with a fused all-gather; row = o and down "
                         "row-sharded with a fused all-reduce (partials stored to every rank, summed as the next "
@@ -271,14 +274,23 @@ def run_thq4(args):
         # gate/up read x as the sum of the partials (after the peers' flags)
         # and keep their column-sharded outputs local.  Two exchanges per
         # layer instead of four.
+        # With --exchange ll (the default) the partials are low-latency words
+        # {value, exchange number} that the readers poll (no fence, no flag);
+        # the step's last down uses the flagged form into its own buffer, so
+        # the result can be waited for and read back.
         from thq4.shard import PeerGroup
 
-        peer = PeerGroup(2 * world * HIDDEN * 4 + 4 * 256, dev)
-        red_o, red_d = peer.buffer(peer.reduction_bytes(HIDDEN, 1)), peer.buffer(peer.reduction_bytes(HIDDEN, 1))
-        g_qkv = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN)
-        g_o = peer.reduce(red_o, HIDDEN, 1, wait=False)
-        g_gu = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN)
-        g_dn = peer.reduce(red_d, HIDDEN, 1, wait=False)
+        ll = args.exchange == "ll"
+        peer = PeerGroup(3 * world * HIDDEN * 8 + 4 * 256, dev)
+        red_o = peer.buffer(peer.reduction_bytes(HIDDEN, 1, ll=ll))
+        red_d = peer.buffer(peer.reduction_bytes(HIDDEN, 1, ll=ll))
+        red_f = peer.buffer(peer.reduction_bytes(HIDDEN, 1))
+        g_qkv = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN, x_ll=ll)
+        g_o = peer.reduce(red_o, HIDDEN, 1, wait=False, ll=ll)
+        g_gu = peer.local_out(wait=True, x_parts=world, x_slot=HIDDEN, x_ll=ll)
+        g_dn = peer.reduce(red_d, HIDDEN, 1, wait=False, ll=ll)
+        g_dn_last = peer.reduce(red_f, HIDDEN, 1, wait=False)
+        g_fin = peer.local_out(wait=True)  # waits for the peers' last flagged exchange
         V = lambda off: ctypes.c_void_p(peer.ptr(off))  # noqa: E731
         F32 = thq4.F32
     elif world > 1 and not args.nccl_gather:
@@ -305,7 +317,8 @@ def run_thq4(args):
         thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, V(off_h), BF, 1, P(t_d), P(ws), ws_bytes,
                                         ctypes.byref(g_dn), s))
 
-    def layer_row(li, lay):
+    def layer_row(li, lay, last=False):
+        """last: the step's final down, in the flagged form into red_f."""
         qkv, o, gate, up, down = lay
         s = stream()
         if li == 0:  # the step's input
@@ -318,7 +331,7 @@ def run_thq4(args):
         thq4.check(lib.thq4_linear_peer(ctypes.byref(gate.desc), ctypes.byref(up.desc), V(red_o), F32, 1, P(t_h),
                                         P(ws), ws_bytes, ctypes.byref(g_gu), s))
         thq4.check(lib.thq4_linear_peer(ctypes.byref(down.desc), None, P(t_h), BF, 1, None, P(ws), ws_bytes,
-                                        ctypes.byref(g_dn), s))
+                                        ctypes.byref(g_dn_last if last else g_dn), s))
 
     def layer_plain(lay):
         qkv, o, gate, up, down = lay
@@ -340,9 +353,9 @@ def run_thq4(args):
         if world > 1:
             dist.all_gather_into_tensor(y_out, t_d)
 
-    def layer(li, lay):
+    def layer(li, lay, last=None):
         if row_tp:
-            layer_row(li, lay)
+            layer_row(li, lay, li == len(layers) - 1 if last is None else last)
         elif peer is not None:
             layer_peer(lay)
         else:
@@ -464,8 +477,8 @@ def run_thq4(args):
         x_in.copy_(x_host, non_blocking=True)
         run()
         if row_tp:
-            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_gu), stream()))
-            thq4.check(lib.thq4_copy(P(red_dev), V(red_d), world * HIDDEN * 4, stream()))
+            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_fin), stream()))
+            thq4.check(lib.thq4_copy(P(red_dev), V(red_f), world * HIDDEN * 4, stream()))
             y_host.copy_(red_dev.sum(0, keepdim=True), non_blocking=True)
         elif peer is not None:
             thq4.check(lib.thq4_copy(P(y_host), V(off_y), HIDDEN * 2, stream()))
@@ -523,11 +536,11 @@ def run_thq4(args):
         # against the same layer recomputed unsharded on one GPU (rank 0)
         torch.cuda.synchronize()
         barrier()
-        layer(0, layers[0])
+        layer(0, layers[0], last=True)
         if row_tp:
-            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_gu), stream()))
+            thq4.check(lib.thq4_peer_wait(ctypes.byref(g_fin), stream()))
             parts = torch.empty((world, HIDDEN), dtype=torch.float32, device=dev)
-            thq4.check(lib.thq4_copy(P(parts), V(red_d), world * HIDDEN * 4, stream()))
+            thq4.check(lib.thq4_copy(P(parts), V(red_f), world * HIDDEN * 4, stream()))
             ph = parts.cpu().numpy()
             y_sh = ph[0].copy()
             for r in range(1, world):  # the rank-order sum the next projection would form
@@ -723,7 +736,8 @@ def run_thq4(args):
                       f"({rank_bytes / 1e9:.2f} GB per GPU), no flush",
                 "parallelism": (f"tensor-parallel x{world}: q/k/v and gate/up column-sharded, o and down row-sharded "
                                 "with the all-reduce fused (f32 partials stored over NVLink into every rank's buffer "
-                                "+ flags, summed by the next projection's staging)") if row_tp else (
+                                + ("as low-latency words {value, exchange number} polled by" if args.exchange == "ll"
+                                   else "+ flags, summed by") + " the next projection's staging)") if row_tp else (
                     f"column-shard x{world}" + (
                         "" if world == 1 else " + NCCL all-gather per projection" if args.nccl_gather else
                         ", outputs gathered by the GEMV epilogue (NVLink stores to IPC-mapped buffers + flags)")),

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define THQ4_ABI_VERSION 1
+#define THQ4_ABI_VERSION 2
 
 typedef enum thq4_status {
   THQ4_OK = 0,
@@ -377,6 +377,15 @@ thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int 
  * in rank order, rounded once to bf16 -- a column-then-row-sharded pair (an
  * MLP's gate/up then down) exchanges one vector instead of two.
  *
+ * Low-latency reduce (out_mode 3): as reduce, but every output is one
+ * aligned 8-byte word {f32 value, exchange number} in the reduction buffer
+ * (slot and x_slot then count words); the exchange number is this rank's
+ * completed-exchange count + 1, the same on every rank.  The writer neither
+ * fences nor raises flags; a projection reading such partials (x_parts with
+ * x_ll = 1, wait = 0) polls each word in its own memory until it carries the
+ * exchange number (bounded; kStatusTimeout).  No NVLink round trip is on the
+ * writer's path: the values themselves are the signal.
+ *
  * After its stores the grid's last CTA writes this rank's completed-exchange
  * count into its slot of every peer's flag words (system-scope release).  A
  * projection whose x comes from such an exchange waits (wait = 1, before it
@@ -396,10 +405,12 @@ typedef struct thq4_peer_gather {
   uint32_t *const *flags;  /* device array [world]: rank r's flag words (u32 [world]), as mapped here */
   uint32_t *count;         /* this rank's completed-exchange count (one device word) */
   uint32_t *arrive;        /* this rank's CTA arrival counter (one device word, left at 0) */
-  int32_t out_mode;        /* 0 gather, 1 reduce, 2 local */
+  int32_t out_mode;        /* 0 gather, 1 reduce, 2 local, 3 low-latency reduce */
   int32_t x_parts;         /* > 0: x (THQ4_F32) is x_parts partials, x + p * x_slot floats, each [m][in] */
-  int64_t slot;            /* reduce: floats between the ranks' partials in a reduction buffer (>= m * stride) */
-  int64_t x_slot;          /* floats between the partials of x (>= m * in) */
+  int64_t slot;            /* reduce: floats (3: words) between the ranks' partials in a reduction buffer (>= m * stride) */
+  int64_t x_slot;          /* floats (x_ll: words) between the partials of x (>= m * in) */
+  int32_t x_ll;            /* 1: the partials of x are low-latency words (written by out_mode 3) */
+  int32_t reserved;        /* 0 */
 } thq4_peer_gather;
 
 /* thq4_linear (up == NULL) or thq4_gate_up with the exchange fused in; y is

@@ -309,6 +309,131 @@ def test_reduce_validation():
     g.out_mode, g.x_parts, g.x_slot = 2, 2, 512
     st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.BF16, 1, P(x), P(x), 1 << 20, ctypes.byref(g), S())
     assert st == _lib.ERR_INVALID_ARGUMENT and "partials are f32" in thq4.last_error()
-    g.out_mode = 3
+    g.out_mode = 4
     st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.F32, 1, P(x), P(x), 1 << 20, ctypes.byref(g), S())
     assert st == _lib.ERR_INVALID_ARGUMENT and "out_mode" in thq4.last_error()
+    g.out_mode, g.x_ll, g.wait = 2, 1, 1  # the low-latency words are polled: no flag wait with them
+    st = L.thq4_linear_peer(ctypes.byref(w), None, P(x), thq4.F32, 1, P(x), P(x), 1 << 20, ctypes.byref(g), S())
+    assert st == _lib.ERR_INVALID_ARGUMENT and "x_ll" in thq4.last_error()
+
+
+# ---- the low-latency reduce: 8-byte words {value, exchange number}, polled ----------
+
+def test_world1_low_latency_reduce_equals_the_plain_chain():
+    """World 1, out_mode 3: the projection's f32 output lands in slot 0 as
+    words {value, exchange number}; the next projection polls them (x_ll)
+    and equals the plain chain bit for bit, call after call (the exchange
+    number goes up by one per exchange)."""
+    n1, k1, n2, m = 512, 768, 256, 2
+    _, _, q1 = _weight(n1, k1, 91)
+    _, _, q2 = _weight(n2, n1, 92)
+    L = thq4.lib()
+    x = dev(np.stack([O.rand_x(k1, 93 + t) for t in range(m)]))
+    ws1, ws2 = _workspace(q1.packed.desc), _workspace(q2.packed.desc)
+    y1 = torch.empty((m, n1), dtype=torch.bfloat16, device="cuda")
+    y2 = torch.empty((m, n2), dtype=torch.bfloat16, device="cuda")
+    thq4.check(L.thq4_linear(ctypes.byref(q1.packed.desc), P(x), thq4.BF16, m, P(y1), thq4.BF16, P(ws1), ws1.numel(),
+                             S()))
+    thq4.check(L.thq4_linear(ctypes.byref(q2.packed.desc), P(y1), thq4.BF16, m, P(y2), thq4.BF16, P(ws2), ws2.numel(),
+                             S()))
+    grp = PeerGroup(8 * m * n1 + 256, torch.device("cuda"))
+    try:
+        off = grp.buffer(grp.reduction_bytes(n1, m, ll=True))
+        g1 = grp.reduce(off, n1, m, wait=False, ll=True)
+        g2 = grp.local_out(wait=True, x_parts=1, x_slot=m * n1, x_ll=True)
+        assert g2.wait == 0
+        z2 = torch.empty_like(y2)
+        for call in range(1, 4):
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q1.packed.desc), None, P(x), thq4.BF16, m, None, P(ws1),
+                                          ws1.numel(), ctypes.byref(g1), S()))
+            thq4.check(L.thq4_linear_peer(ctypes.byref(q2.packed.desc), None, ctypes.c_void_p(grp.ptr(off)),
+                                          thq4.F32, m, P(z2), P(ws2), ws2.numel(), ctypes.byref(g2), S()))
+            torch.cuda.synchronize()
+            assert torch.equal(z2.view(torch.int16), y2.view(torch.int16)), "low-latency reduce differs from the chain"
+            words = torch.empty((m, n1, 2), dtype=torch.int32, device="cuda")
+            thq4.check(L.thq4_copy(P(words), ctypes.c_void_p(grp.ptr(off)), words.numel() * 4, S()))
+            torch.cuda.synchronize()
+            assert torch.equal(words[..., 0].view(torch.float32), _f32_out(q1, x, m)), "slot 0 holds the f32 output"
+            assert bool((words[..., 1] == call).all()), "every word carries this exchange's number"
+        assert _status() & TIMEOUT_BIT == 0
+    finally:
+        grp.close()
+
+
+def _ll_regions(out, m, parts):
+    ra = torch.zeros(256 + parts * m * out * 8, dtype=torch.uint8, device="cuda")
+    rb = torch.zeros_like(ra)
+    return ra, rb
+
+
+def test_world2_low_latency_writer_and_reader_on_one_gpu():
+    """Rank 0 of 2 on one GPU (the peer never runs): its out_mode 3 words land
+    in slot 0 of both ranks' buffers with exchange number count + 1, no flag is
+    raised and the count goes up; a reader whose slot 1 words the test has
+    written (the peer's share) equals the plain call on bf16(p0 + p1)."""
+    out, inp, m = 384, 512, 1
+    _, _, q = _weight(out, inp, 94)
+    _, _, q2 = _weight(256, out, 95)
+    L = thq4.lib()
+    x = dev(O.rand_x(inp, 96).reshape(1, inp))
+    ws, ws2 = _workspace(q.packed.desc), _workspace(q2.packed.desc)
+    ra, rb = _ll_regions(out, m, 2)
+    ra[64:68].view(torch.int32).fill_(6)  # this rank has completed 6 exchanges
+    g, keep = _emulated_rank0(ra, rb, out, out, wait=False)
+    g.out_mode, g.slot = 3, m * out
+    thq4.check(L.thq4_linear_peer(ctypes.byref(q.packed.desc), None, P(x), thq4.BF16, m, None, P(ws), ws.numel(),
+                                  ctypes.byref(g), S()))
+    torch.cuda.synchronize()
+    want = _f32_out(q, x).cpu()
+    for region in (ra, rb):
+        words = region[256:].view(torch.int32).cpu().reshape(2, out, 2)
+        assert torch.equal(words[0, :, 0].view(torch.float32), want[0])
+        assert bool((words[0, :, 1] == 7).all()), "words carry exchange number count + 1"
+        assert not words[1].any(), "rank 1's slot was written"
+    assert not ra[:8].any() and not rb[:8].any(), "no flags for low-latency words"
+    assert int(ra[64:68].view(torch.int32).item()) == 7 and int(ra[128:132].view(torch.int32).item()) == 0
+    # the peer's share arrives in slot 1 of this rank's buffer; the reader sums both
+    peer = torch.from_numpy(np.random.default_rng(3).standard_normal(out).astype(np.float32)).cuda()
+    w1 = ra[256 + m * out * 8:].view(torch.int32).view(out, 2)
+    w1[:, 0] = peer.view(torch.int32)
+    w1[:, 1] = 7
+    g2, keep2 = _emulated_rank0(ra, rb, out, out, wait=False)
+    g2.out_mode, g2.x_parts, g2.x_slot, g2.x_ll = 2, 2, m * out, 1
+    y = torch.empty((1, 256), dtype=torch.bfloat16, device="cuda")
+    _status()
+    thq4.check(L.thq4_linear_peer(ctypes.byref(q2.packed.desc), None, ctypes.c_void_p(ra.data_ptr() + 256), thq4.F32,
+                                  1, P(y), P(ws2), ws2.numel(), ctypes.byref(g2), S()))
+    xb = (want[0].cuda() + peer).to(torch.bfloat16).reshape(1, out)
+    y_ref = torch.empty_like(y)
+    thq4.check(L.thq4_linear(ctypes.byref(q2.packed.desc), P(xb), thq4.BF16, 1, P(y_ref), thq4.BF16, P(ws2),
+                             ws2.numel(), S()))
+    torch.cuda.synchronize()
+    assert _status() & TIMEOUT_BIT == 0
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+
+
+def test_low_latency_words_that_never_arrive_time_out():
+    """Failure detection for the low-latency exchange: the peer's words never
+    carry this exchange's number.  Every poll shares one 2 s deadline, the
+    call returns with the timeout bit set and the context stays usable."""
+    out, inp, m = 256, 512, 1
+    _, _, q = _weight(out, inp, 97)
+    L = thq4.lib()
+    ws = _workspace(q.packed.desc)
+    ra, rb = _ll_regions(inp, m, 2)
+    ra[64:68].view(torch.int32).fill_(5)  # expects exchange 5; the words say 4
+    ra[256:].view(torch.int32).view(-1, 2)[:, 1] = 4
+    g, keep = _emulated_rank0(ra, rb, inp, inp, wait=False)
+    g.out_mode, g.x_parts, g.x_slot, g.x_ll = 2, 2, m * inp, 1
+    y = torch.empty((1, out), dtype=torch.bfloat16, device="cuda")
+    _status()
+    t0 = time.time()
+    thq4.check(L.thq4_linear_peer(ctypes.byref(q.packed.desc), None, ctypes.c_void_p(ra.data_ptr() + 256), thq4.F32, 1,
+                                  P(y), P(ws), ws.numel(), ctypes.byref(g), S()))
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 30
+    assert _status() & TIMEOUT_BIT, "the bounded poll reports its timeout"
+    x = dev(O.rand_x(inp, 5).reshape(1, inp))
+    thq4.check(L.thq4_linear(ctypes.byref(q.packed.desc), P(x), thq4.BF16, 1, P(y), thq4.BF16, P(ws), ws.numel(), S()))
+    torch.cuda.synchronize()
+    assert _status() == 0

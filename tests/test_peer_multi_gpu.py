@@ -186,7 +186,7 @@ def test_two_gpu_expert_shards_match_oracle():
     assert np.all(np.abs(y - want) <= 0.02 + 0.01 * np.abs(want)), "sharded MoE differs from the oracle"
 
 
-def _row_rank(rank, world, port, ret):
+def _row_rank(rank, world, port, ret, ll=False):
     """y1 = W1 x on this rank's rows (kept local), y2 = W2 y1 row-parallel
     (this rank's input columns = its y1 rows; f32 partial into slot `rank`
     of every rank's reduction buffer), y3 = W3 bf16(sum of the partials)
@@ -220,11 +220,11 @@ def _row_rank(rank, world, port, ret):
         q2 = thq4.QLin(w2r, s2r, n2, kk, 64).tiled()
         q3 = thq4.QLin(dev(w3q[b3:b3 + r3]).to(d), dev(w3s[b3:b3 + r3]).to(d), r3, n2, 64).tiled()
         L = thq4.lib()
-        grp = PeerGroup(world * n2 * 4 + n3 * 2 + 1024, d)
-        red = grp.buffer(grp.reduction_bytes(n2, 1))
+        grp = PeerGroup(world * n2 * 8 + n3 * 2 + 1024, d)
+        red = grp.buffer(grp.reduction_bytes(n2, 1, ll=ll))
         full3 = grp.buffer(n3 * 2)
-        g2 = grp.reduce(red, n2, 1, wait=False)
-        g3 = grp.gather(full3, r3, b3, n3, wait=True, x_parts=world, x_slot=n2)
+        g2 = grp.reduce(red, n2, 1, wait=False, ll=ll)
+        g3 = grp.gather(full3, r3, b3, n3, wait=True, x_parts=world, x_slot=n2, x_ll=ll)
         ws = [thq4.qlin.workspace(q.packed.desc, d) for q in (q1, q2, q3)]
         xt = dev(x.reshape(1, k1)).to(d)
         y1 = torch.empty((1, r1), dtype=torch.bfloat16, device=d)
@@ -251,7 +251,8 @@ def _row_rank(rank, world, port, ret):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_row_parallel_reduce_matches_oracle():
+@pytest.mark.parametrize("ll", [False, True], ids=["flags", "low-latency"])
+def test_two_gpu_row_parallel_reduce_matches_oracle(ll):
     import torch.multiprocessing as mp
 
     import q4oracle as O
@@ -262,7 +263,7 @@ def test_two_gpu_row_parallel_reduce_matches_oracle():
     ctx = mp.get_context("spawn")
     ret = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_row_rank, args=(r, 2, port, ret)) for r in range(2)]
+    procs = [ctx.Process(target=_row_rank, args=(r, 2, port, ret, ll)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(ret.get(timeout=300) for _ in range(2))

@@ -420,8 +420,13 @@ thq4_status check_peer(const thq4_peer_gather *g, const char *who) {
   if (g->world < 1 || g->world > 8 || g->rank < 0 || g->rank >= g->world)
     return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "need 1 <= world <= 8 and 0 <= rank < world (world " +
                                                     std::to_string(g->world) + ", rank " + std::to_string(g->rank) + ")");
-  if (g->out_mode < 0 || g->out_mode > 2)
-    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "out_mode must be 0 (gather), 1 (reduce) or 2 (local)");
+  if (g->out_mode < 0 || g->out_mode > 3)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     pre + "out_mode must be 0 (gather), 1 (reduce), 2 (local) or 3 (low-latency reduce)");
+  if (g->x_ll != 0 && g->x_ll != 1) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "x_ll must be 0 or 1");
+  if (g->x_ll && (g->x_parts < 1 || g->wait))
+    return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "x_ll needs x_parts > 0 and wait 0 (the words are the signal)");
+  if (g->reserved != 0) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "reserved must be 0");
   if (g->wait != 0 && g->wait != 1) return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "wait must be 0 or 1");
   if (!g->flags || !g->count || (g->out_mode != 2 && (!g->dst || !g->arrive)))
     return set_error(THQ4_ERR_INVALID_ARGUMENT, pre + "dst, flags, count and arrive must be device pointers");
@@ -433,10 +438,11 @@ thq4_status check_peer(const thq4_peer_gather *g, const char *who) {
 PeerGather peer_of(const thq4_peer_gather *g) {
   PeerGather pg{reinterpret_cast<uint16_t *const *>(g->dst), g->flags, g->count, g->arrive, g->world, g->rank,
                 g->rows, g->offset, g->stride, g->wait};
-  pg.mode = g->out_mode == 0 ? 1 : g->out_mode == 1 ? 2 : 0;
+  pg.mode = g->out_mode == 0 ? 1 : g->out_mode == 1 ? 2 : g->out_mode == 3 ? 3 : 0;
   pg.slot = g->slot;
   pg.x_parts = g->x_parts;
   pg.x_slot = g->x_slot;
+  pg.x_ll = g->x_ll;
   return pg;
 }
 }  // namespace
@@ -452,7 +458,7 @@ thq4_status thq4_linear_peer(const thq4_weight *w, const thq4_weight *up, const 
       return set_error(THQ4_ERR_INVALID_ARGUMENT, "thq4_linear_peer: gate and up halves differ in shape or dtype");
   }
   if ((s = check_peer(g, who)) != THQ4_OK) return s;
-  const bool reduce = g->out_mode == 1;
+  const bool reduce = g->out_mode == 1 || g->out_mode == 3;
   // reduce mode stores no y: check the rest of the I/O against x alone
   if ((s = check_io(x, x_dtype, m, reduce ? x : y, THQ4_BF16, who)) != THQ4_OK) return s;
   const bool parts = g->x_parts > 0;

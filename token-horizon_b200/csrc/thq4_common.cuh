@@ -145,6 +145,19 @@ __device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
   asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
   return v;
 }
+// Volatile (relaxed, system scope) 16-byte load / 8-byte store: each aligned
+// 8-byte word is read or written whole, the low-latency exchange's unit.
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
 // System-scope ordering for flags that other GPUs read over NVLink.
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;\n" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {

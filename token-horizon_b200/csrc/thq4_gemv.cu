@@ -102,7 +102,9 @@ struct GemvArgs {
   // every rank; g_mode 2 (reduce): every output, in f32, goes to slot g_rank
   // of every rank's reduction buffer instead of y.  Then the grid's last CTA
   // raises this rank's flag on every peer.  g_wait: wait for the peers'
-  // flags before reading x.
+  // flags before reading x.  g_mode 3 (low-latency reduce): as 2, but every
+  // output is one 8-byte word {f32 bits, this exchange's number} that the
+  // reader polls for; no fence and no flag.
   uint16_t *const *g_dst;
   uint32_t *const *g_flags;
   uint32_t *g_count, *g_arrive;
@@ -112,6 +114,10 @@ struct GemvArgs {
   // summed in order and rounded to bf16 as they are staged
   int xparts;
   long long xslot;
+  // x_ll: the partials are low-latency words (g_mode 3's layout: 8 bytes
+  // {f32 bits, exchange number}, x + p * xslot words); each is waited for
+  // until it carries this exchange's number
+  int x_ll;
   // x is a presum block: its f32 sums [ng][8] (the bias term's sum(x) of
   // group g, token t at xsum[g * 8 + t]); nullptr otherwise
   const float *xsum;
@@ -170,6 +176,34 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumers * 32) : "memory");
 }
 
+// Eight consecutive low-latency words (four 16-byte loads, each 8-byte word
+// read whole): their f32 values once every word carries `seq`.  Words that
+// do not yet are read again until the deadline, after which `late` is set and
+// the values read last are used (the status word then says kStatusTimeout).
+__device__ __forceinline__ void ll_wait8(const uint4 *w4, uint32_t seq, uint64_t deadline, bool &late, float (&d)[8]) {
+  uint4 q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = ld_volatile_v4(w4 + i);
+  for (;;) {
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ok = ok && q[i].y == seq && q[i].w == seq;
+    if (ok || late) break;
+    if (global_timer_ns() > deadline) {
+      late = true;
+      break;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (q[i].y != seq || q[i].w != seq) q[i] = ld_volatile_v4(w4 + i);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    d[2 * i] = __uint_as_float(q[i].x);
+    d[2 * i + 1] = __uint_as_float(q[i].z);
+  }
+}
+
 // Stage the activation groups [gs, gs + xcnt) (mod ng) of the m tokens into
 // shared memory (consumer warps only).  Fragment entry ((slot*P + q)*2 + h)*4
 // + c (16 bytes) holds, for k-steps 2h and 2h+1 of the group, the fp16 pairs
@@ -190,6 +224,17 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
     for (int i = tid; i < xcnt; i += nthr) mx[i * P8 + P] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   uint32_t *xw = reinterpret_cast<uint32_t *>(xf);
   const int items = xcnt * P * 8;
+  // low-latency partials: this exchange's number (this rank's count, final
+  // once the previous launch completed) and one deadline for every wait
+  uint32_t ll_seq = 0;
+  uint64_t ll_deadline = 0;
+  bool ll_late = false;
+  if constexpr (PARTS) {
+    if (a.x_ll) {
+      ll_seq = *reinterpret_cast<const volatile uint32_t *>(a.g_count);
+      ll_deadline = global_timer_ns() + kWaitLimitNs;
+    }
+  }
   const int span = (items + 31) / 32 * 32;  // whole warps: every lane takes part in the shuffles
   for (int base = tid; base < span; base += kU * nthr) {
     float v[kU][8];
@@ -204,14 +249,26 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
       if (g >= a.ng) g -= a.ng;
       const int t = a.xf32 ? q >> 1 : q;
       const size_t at = (size_t)t * a.in + (size_t)g * kGroup + 8 * h8;
-      if (PARTS) {  // the all-reduce's last step: sum the ranks' partials in order, one bf16 rounding
+      if constexpr (PARTS) {  // the all-reduce's last step: sum the ranks' partials in order, one bf16 rounding
+        if (a.x_ll) {
 #pragma unroll 1
-        for (int pp = 0; pp < a.xparts; ++pp) {
-          const float4 *p4 =
-              reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + (size_t)pp * a.xslot + at);
-          const float4 u0 = p4[0], u1 = p4[1];
-          v[it][0] += u0.x, v[it][1] += u0.y, v[it][2] += u0.z, v[it][3] += u0.w;
-          v[it][4] += u1.x, v[it][5] += u1.y, v[it][6] += u1.z, v[it][7] += u1.w;
+          for (int pp = 0; pp < a.xparts; ++pp) {
+            const uint4 *w4 =
+                reinterpret_cast<const uint4 *>(static_cast<const unsigned long long *>(a.x) + (size_t)pp * a.xslot + at);
+            float d[8];
+            ll_wait8(w4, ll_seq, ll_deadline, ll_late, d);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[it][e] += d[e];
+          }
+        } else {
+#pragma unroll 1
+          for (int pp = 0; pp < a.xparts; ++pp) {
+            const float4 *p4 =
+                reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) + (size_t)pp * a.xslot + at);
+            const float4 u0 = p4[0], u1 = p4[1];
+            v[it][0] += u0.x, v[it][1] += u0.y, v[it][2] += u0.z, v[it][3] += u0.w;
+            v[it][4] += u1.x, v[it][5] += u1.y, v[it][6] += u1.z, v[it][7] += u1.w;
+          }
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[it][e] = __uint_as_float((uint32_t)f32_to_bf16_bits(v[it][e]) << 16);
@@ -284,13 +341,17 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
       }
     }
   }
+  if constexpr (PARTS) {
+    if (ll_late) raise_status(a.status, kStatusTimeout);
+  }
   consumer_sync();
 }
 
 // Final values of one 16-row tile from lanes holding reduced column pairs;
 // gate/up combines streams 0 and 1.
 template <int GW, bool GATE_UP, class A>
-__device__ __forceinline__ void store_tile(const A &a, int rt, int lane, const float *y0, const float *y1) {
+__device__ __forceinline__ void store_tile(const A &a, int rt, int lane, const float *y0, const float *y1,
+                                           uint32_t seq = 0) {
   constexpr int LPJ = 4 / GW;
   const int r = lane >> 2, c = lane & 3;
   if (c >= LPJ) return;
@@ -317,6 +378,12 @@ __device__ __forceinline__ void store_tile(const A &a, int rt, int lane, const f
       if (a.g_mode == 2) {  // this rank's partial of the output, into its slot on every rank (NVLink stores)
         for (int rk = 0; rk < a.g_world; ++rk)
           reinterpret_cast<float *>(a.g_dst[rk])[(size_t)a.g_rank * a.g_slot + (size_t)t * a.g_stride + row] = v;
+      } else if (a.g_mode == 3) {  // the same as one 8-byte word {value, exchange number} the reader polls for
+        const unsigned long long word = ((unsigned long long)seq << 32) | __float_as_uint(v);
+        for (int rk = 0; rk < a.g_world; ++rk)
+          st_volatile_u64(reinterpret_cast<unsigned long long *>(a.g_dst[rk]) + (size_t)a.g_rank * a.g_slot +
+                              (size_t)t * a.g_stride + row,
+                          word);
       } else if (a.yf32) {
         static_cast<float *>(a.y)[(size_t)t * a.out + row] = v;
       } else {
@@ -351,6 +418,16 @@ __device__ void peer_wait(uint32_t *const *flags, const uint32_t *count, int wor
 __device__ void peer_signal(const GemvArgs &a) {
   consumer_sync();
   if (threadIdx.x != 0) return;
+  if (a.g_mode == 3) {
+    // low-latency words need no fence or flag: the grid's last CTA only
+    // counts the exchange (every CTA read the count before its stores)
+    if (atom_add_acq_rel(a.g_arrive, 1u) + 1u == gridDim.x) {
+      *a.g_arrive = 0;
+      *a.g_count = *a.g_count + 1u;
+    }
+    trace_stamp(a, kTrFenced);
+    return;
+  }
   fence_acq_rel_sys();  // this CTA's stores, local and remote, before its arrival
   const bool last = atom_add_acq_rel(a.g_arrive, 1u) + 1u == gridDim.x;
   trace_stamp(a, kTrFenced);
@@ -487,6 +564,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   const int tile = warp;
   pdl_wait();
   trace_stamp(a, kTrPdl);
+  // a low-latency exchange's number: this rank's count + 1 (final once the
+  // previous launch completed; the grid's last CTA raises the count)
+  const uint32_t wseq = a.g_mode == 3 ? *reinterpret_cast<const volatile uint32_t *>(a.g_count) + 1u : 0u;
   if (a.g_wait) {  // x holds the peers' slices or partials: wait until they have landed
     if (threadIdx.x == 0) peer_wait(a.g_flags, a.g_count, a.g_world, a.g_rank, a.status);
     consumer_sync();
@@ -636,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       }
     }
     if (lane == 0) a.count[(size_t)sl * kSlabTiles + tile] = 0;  // ready for the next call
-    store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, acc[0], acc[NS - 1]);
+    store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, acc[0], acc[NS - 1], wseq);
   };
   int first_slab = -1;
   int sl = sl0, cg = cg0 - 1, s = R - 1;
@@ -681,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       reduce_y();
       if (aborted) {
       } else if (seg_whole) {
-        store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, y[0], y[NS - 1]);
+        store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, y[0], y[NS - 1], wseq);
       } else {  // the run's first segment, partial
         publish(0, y);
       }
@@ -727,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
           const float4 v = xb[(((size_t)pp * kSlabTiles + tile) * NS + si) * 32 + lane];
           y[si][0] += v.x, y[si][1] += v.y, y[si][2] += v.z, y[si][3] += v.w;
         }
-      store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1]);
+      store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1], wseq);
     }
     trace_stamp(a, kTrStored);
     if (a.g_mode) peer_signal(a);
@@ -1527,6 +1607,7 @@ cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void
       a.g_slot = peer->slot;
       a.xparts = peer->x_parts;
       a.xslot = peer->x_slot;
+      a.x_ll = peer->x_ll;
     }
     a.trace = trace_record(p.grid);
     // a last pass with fewer tokens fits in the footprint planned for more

@@ -82,10 +82,11 @@ struct PeerGather {
   uint32_t *const *flags;   // device array [world]: each rank's flag words [world]
   uint32_t *count, *arrive;
   int world, rank, rows, offset, stride, wait;
-  int mode;                 // 0: no exchange, 1: gather, 2: reduce
-  long long slot;           // reduce: floats between the ranks' partials
+  int mode;                 // 0: no exchange, 1: gather, 2: reduce, 3: low-latency reduce
+  long long slot;           // reduce: floats (mode 3: 8-byte words) between the ranks' partials
   int x_parts;              // > 0: x is this many f32 partials, summed as staged
-  long long x_slot;         // floats between the partials of x
+  long long x_slot;         // floats (x_ll: 8-byte words) between the partials of x
+  int x_ll = 0;             // the partials of x are low-latency words
 };
 cudaError_t gemv_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, bool x_f32,
                         int m, void *y, bool y_f32, void *workspace, cudaStream_t stream,

@@ -69,7 +69,7 @@ class thq4_peer_gather(ctypes.Structure):
                 ("offset", ctypes.c_int32), ("stride", ctypes.c_int32), ("wait", ctypes.c_int32),
                 ("dst", c_void_p), ("flags", c_void_p), ("count", c_void_p), ("arrive", c_void_p),
                 ("out_mode", ctypes.c_int32), ("x_parts", ctypes.c_int32), ("slot", ctypes.c_int64),
-                ("x_slot", ctypes.c_int64)]
+                ("x_slot", ctypes.c_int64), ("x_ll", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class thq4_chain_op(ctypes.Structure):

@@ -170,7 +170,7 @@ class PeerGroup:
         return self.local + offset
 
     def gather(self, offset: int, rows: int, at: int, stride: int, wait: bool, x_parts: int = 0,
-               x_slot: int = 0):
+               x_slot: int = 0, x_ll: bool = False):
         """A thq4_peer_gather for a projection whose first `rows` outputs go to
         full[t * stride + at + row] in the buffer at `offset` on every rank."""
         dst = self._ptr_array([b + offset for b in self.bases])
@@ -179,31 +179,38 @@ class PeerGroup:
         g.world, g.rank, g.rows, g.offset, g.stride, g.wait = self.world, self.rank, rows, at, stride, int(wait)
         g.dst, g.flags = dst.data_ptr(), self._flags.data_ptr()
         g.count, g.arrive = self.count, self.arrive
-        g.x_parts, g.x_slot = x_parts, x_slot
+        g.x_parts, g.x_slot, g.x_ll = x_parts, x_slot, int(x_ll)
+        if x_ll:
+            g.wait = 0  # the low-latency words are polled, not waited for
         return g
 
-    def reduce(self, offset: int, out: int, m: int, wait: bool, x_parts: int = 0, x_slot: int = 0):
+    def reduce(self, offset: int, out: int, m: int, wait: bool, x_parts: int = 0, x_slot: int = 0,
+               ll: bool = False, x_ll: bool = False):
         """A thq4_peer_gather for a row-parallel projection of `out` outputs:
         its f32 partial goes to slot `rank` of the reduction buffer at
-        `offset` on every rank (slots of m * out floats; the buffer holds
+        `offset` on every rank (slots of m * out values; the buffer holds
         world slots, `reduction_bytes`).  Read back with x_parts = world,
-        x_slot = m * out."""
+        x_slot = m * out.  ll: low-latency words (out_mode 3; the reader sets
+        x_ll and does not wait)."""
         g = self.gather(offset, out, 0, out, wait, x_parts, x_slot)
-        g.out_mode, g.slot = 1, m * out
+        g.out_mode, g.slot = (3 if ll else 1), m * out
+        g.x_ll = int(x_ll)
         return g
 
-    def local_out(self, wait: bool, x_parts: int = 0, x_slot: int = 0):
+    def local_out(self, wait: bool, x_parts: int = 0, x_slot: int = 0, x_ll: bool = False):
         """A thq4_peer_gather that only waits (for the exchange x comes from)
-        and reads x as partials; the projection's output stays local."""
+        and reads x as partials; the projection's output stays local.  x_ll:
+        the partials are low-latency words, polled instead of waited for."""
         g = self._L.thq4_peer_gather()
-        g.world, g.rank, g.wait = self.world, self.rank, int(wait)
+        g.world, g.rank, g.wait = self.world, self.rank, int(wait and not x_ll)
         g.flags, g.count = self._flags.data_ptr(), self.count
-        g.out_mode, g.x_parts, g.x_slot = 2, x_parts, x_slot
+        g.out_mode, g.x_parts, g.x_slot, g.x_ll = 2, x_parts, x_slot, int(x_ll)
         return g
 
-    def reduction_bytes(self, out: int, m: int) -> int:
-        """Bytes of a reduction buffer: world slots of m * out f32."""
-        return self.world * m * out * 4
+    def reduction_bytes(self, out: int, m: int, ll: bool = False) -> int:
+        """Bytes of a reduction buffer: world slots of m * out f32 values
+        (8-byte words for the low-latency form)."""
+        return self.world * m * out * (8 if ll else 4)
 
     def close(self) -> None:
         """Unmap the peers' regions, then free this rank's (after every rank
