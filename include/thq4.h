@@ -386,6 +386,13 @@ thq4_status thq4_moe_add(const void *x, const void *residual, int T, int H, int 
  * exchange number (bounded; kStatusTimeout).  No NVLink round trip is on the
  * writer's path: the values themselves are the signal.
  *
+ * Reuse: a rank may write a reduction or gather buffer of a peer again only
+ * after that peer's reader of its previous contents has completed, which the
+ * writer must have observed: e.g. o and down writing two buffers in turn,
+ * where a rank's next o follows its q/k/v that read the peers' down words,
+ * written after each peer's gate/up had read the previous o's; or a host
+ * barrier between uses.
+ *
  * After its stores the grid's last CTA writes this rank's completed-exchange
  * count into its slot of every peer's flag words (system-scope release).  A
  * projection whose x comes from such an exchange waits (wait = 1, before it

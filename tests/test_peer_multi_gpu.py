@@ -238,6 +238,10 @@ def _row_rank(rank, world, port, ret, ll=False):
                                           ws[1].numel(), ctypes.byref(g2), s))
             thq4.check(L.thq4_linear_peer(ctypes.byref(q3.packed.desc), None, ctypes.c_void_p(grp.ptr(red)), thq4.F32,
                                           1, P(y3), P(ws[2]), ws[2].numel(), ctypes.byref(g3), s))
+            # one reduction buffer serves every iteration: a rank may write it
+            # again only once every peer's reader of it is done
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[rank])
         thq4.check(L.thq4_peer_wait(ctypes.byref(g3), s))
         out = torch.empty((1, n3), dtype=torch.bfloat16, device=d)
         thq4.check(L.thq4_copy(P(out), ctypes.c_void_p(grp.ptr(full3)), n3 * 2, s))
