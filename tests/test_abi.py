@@ -259,7 +259,9 @@ def _plan(out, inp, m=1, x_f32=0, gate_up=0, sms=148, fit=GPC_FIT):
     ((9728, 2560, 8, 1, 1), (1, 148, 1, 2, 4, 5, 8)),  # f32 x: 4 tokens per launch (hi + lo columns)
     # column shards at two and eight GPUs
     ((2560, 5120), (1, 120, 6, 5, 1, 10, 8)),  # o at N = 2: clusters of 7 do not all fit, 6 do
-    ((896, 5120), (1, 70, 1, 5, 1, 10, 8)),  # q/k/v at N = 8: 7 slabs, too few to fill with clusters
+    ((896, 5120), (1, 56, 8, 5, 1, 10, 8)),  # q/k/v at N = 8: 7 slabs; a flat split cannot fill the SMs either,
+                                              # so clusters of 8 combine in DSMEM
+    ((5120, 640), (1, 80, 2, 5, 1, 2, 8)),    # o at N = 8 (row shard): 40 slabs of 2 chunks, clusters of 2
 ])
 def test_planner_policy_table(shape, want):
     assert _plan(*shape) == want

@@ -1496,6 +1496,17 @@ GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms
               break;
             }
           }
+          // When even the flat split cannot fill the SMs (at most one chunk
+          // per CTA, every slab split anyway), clusters combine the parts in
+          // DSMEM instead of the workspace fix-up, whatever their fill (the
+          // small shards of a tensor-parallel layer).
+          if (p.cl_j == 1 && chunks <= sms)
+            for (int jc = std::min(std::min(8, sms / slabs), cps); jc >= 2; --jc)
+              if (capacity(jc) >= slabs) {
+                grid = (long long)slabs * jc;
+                p.cl_j = jc;
+                break;
+              }
         }
       }
       if (chunks < grid) grid = chunks;  // every CTA run holds at least one chunk
