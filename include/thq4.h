@@ -152,6 +152,17 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
                          const void *x, int x_dtype, int m, void *y,
                          int y_dtype, void *workspace, size_t workspace_bytes,
                          void *stream);
+/* Replaces the scalar reference kernels AffineQmv / AffineQmm
+ * (quant_kernel.rs:1026-1147, 1634-1740; ops :2686-2766, 5766-5834), which the
+ * reference's tests use to check the tuned kernels on the device (scalar_ref,
+ * qwen35.rs:6928-6938).  y [m][out] = x [m][in] . W^T with every weight
+ * dequantised in f32 as fma(q, s, b) and the products accumulated in f32:
+ * one warp per output row, lane l adding the 8 consecutive k at 8l, 8l + 256,
+ * ... in k order, the lanes combined by xor butterfly (16, 8, 4, 2, 1); any
+ * m >= 1 (passes of 8 tokens), x and y as thq4_linear.  Deterministic, not
+ * tuned; no workspace. */
+thq4_status thq4_linear_scalar(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
+                               void *stream);
 /* Workspace bytes thq4_linear / thq4_gate_up need for this weight (for
  * thq4_gate_up pass the gate half).  The decode/verify kernel splits tiles
  * over warps and finishes each split tile in the warp that arrives last: the
@@ -472,7 +483,7 @@ thq4_status thq4_copy(void *dst, const void *src, size_t bytes, void *stream);
  * Forces the decode/verify kernel's launch shape for every later call in this
  * process: slab-groups per streamed stage (4 or 8), stages in the
  * shared-memory ring (2 .. 8; an upper bound, lowered to what fits) and CTAs
- * in the grid (1 .. 2x SM count, capped at one per SM); 0 leaves a field to
+ * in the grid (1 .. 2x SM count: up to two CTAs per SM); 0 leaves a field to
  * the policy, all zeros restore it.  The reference's tests
  * run every instantiated tile config the same way (qwen35.rs:6963-6989).
  * Returns THQ4_ERR_INVALID_ARGUMENT for other values; `reserved` must be 0. */

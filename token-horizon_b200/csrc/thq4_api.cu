@@ -335,6 +335,18 @@ thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype
   return THQ4_OK;
 }
 
+thq4_status thq4_linear_scalar(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
+                               void *stream) {
+  const char *who = "thq4_linear_scalar";
+  thq4_status s = check_weight(w, who);
+  if (s != THQ4_OK) return s;
+  if ((s = check_io(x, x_dtype, m, y, y_dtype, who)) != THQ4_OK) return s;
+  const cudaError_t e = scalar_launch(*w, x, x_dtype == THQ4_F32, m, y, y_dtype == THQ4_F32,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, who);
+  return THQ4_OK;
+}
+
 size_t thq4_linear_chain_workspace_bytes(const thq4_chain_op *ops, int n) {
   if (!ops || n < 1) return 0;
   int rows = 0;

@@ -32,7 +32,8 @@
 //            the A-fragment registers of mma.m16n8k16 (words j = 2p and
 //            2p+1 give the k and k+8 halves).  OR-ing 0x54005400 makes each
 //            half the fp16 number 64 + q -- exact (the unit in the last place
-//            of [64, 128) is 1/16) -- seven ALU operations per word.
+//            of [64, 128) is 1/16).  The decode kernel takes the even
+//            k-steps' nibbles from bits 0..3 in place instead (unpack_word).
 //   scales:  64 bytes at byte offset ch * 64: eight quads
 //            {s_r, b_r, s_r+8, b_r+8} (16-bit, bf16 or f16), quad r at + 8 r.
 //
@@ -94,6 +95,25 @@ __device__ __forceinline__ uint32_t nib_f16x2(uint32_t w) {
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(w), "n"(MASK), "n"(0x54005400));
   return r;
+}
+
+// The four mma.m16n8k16 A registers one frag word holds (see the layout
+// above): k-step 2p rows r / r + 8 (nibbles at bits 0..3 / 8..11 of each
+// half) as the exact fp16 q -- (w & 0x000F000F) | 0x64006400 is 1024 + q
+// (unit in the last place 1), less 1024 on the fp16 pipe -- and k-step
+// 2p + 1 rows r / r + 8 (bits 4..7 / 12..15) as 64 + q.  One shift, four
+// LOP3 and two f16x2 subtractions: five operations on the integer pipe per
+// eight weights instead of seven with a shift per register.
+__device__ __forceinline__ void unpack_word(uint32_t w, uint32_t &e_r, uint32_t &e_r8, uint32_t &o_r,
+                                            uint32_t &o_r8) {
+  const uint32_t t = w >> 8;
+  uint32_t u0, u1;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(u0) : "r"(w), "n"(0x000F000F), "n"(0x64006400));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(u1) : "r"(t), "n"(0x000F000F), "n"(0x64006400));
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(e_r) : "r"(u0), "r"(0x64006400));
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(e_r8) : "r"(u1), "r"(0x64006400));
+  o_r = nib_f16x2<0x00F000F0u>(w);
+  o_r8 = nib_f16x2<0x00F000F0u>(t);
 }
 
 // D = A * B (C = 0), fp16 inputs, f32 accumulate, m16n8k16.

@@ -25,16 +25,18 @@
 //     per tile, measured no faster: the LOP3 work of the in-register dequant
 //     fills the ALU pipe either way).  Per SG a warp
 //     runs four mma.m16n8k16 (fp16 x fp16 -> f32) with the weight as the A
-//     operand (16 rows) and activation columns as N (8).  A shift and one
-//     LOP3 per register put a nibble pair in mantissa bits 4..7 of the fp16
-//     pair 64 + q (exact; frag layout, thq4_common.cuh).  Two independent
-//     chains (k-steps 0, 2 and 1, 3) meet in the epilogue as
-//     acc0 + acc1 - off, off = 64 sum(x) computed when x is staged.  The
-//     group's value is then the reference's per-group form
+//     operand (16 rows) and activation columns as N (8).  unpack_word
+//     (thq4_common.cuh) turns a frag word into the four A registers: the
+//     even k-steps' nibble pairs as the exact fp16 q (a LOP3 gives 1024 + q,
+//     an f16x2 subtraction removes the 1024), the odd k-steps' as 64 + q (a
+//     LOP3 on the nibbles in mantissa bits 4..7).  Two independent chains
+//     (k-steps 0, 2 and 1, 3) meet in the epilogue as acc0 + acc1 - off,
+//     off = 64 * (sum of x over the odd k-steps) computed when x is staged.
+//     The group's value is then the reference's per-group form
 //     (quant_kernel.rs:1994-2001, 2887-2890):  s * sum(q x) + b * sum(x).
-//     (The offset enters the fp32 accumulation at 64x the size of the q
-//     signal; with the nibble in mantissa bits 0..3 it would be 1024x and
-//     cost ten bits of the accumulator instead of six);
+//     (Offsets cost accumulator bits: 1024 + q would carry the offset at
+//     1024x the size of the q signal, so it is removed exactly before the
+//     MMA; 64 + q costs six bits on half the products);
 //   - with few tokens most of the 8 columns are free, so consecutive groups
 //     share one accumulator: in a "window" of GW groups (4 when a group
 //     needs <= 2 columns), group j's activation sits in columns
@@ -75,7 +77,6 @@ constexpr int kConsumers = kSlabTiles;  // one consumer warp per tile of a slab
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kSgBytes = kSlabTiles * (kChunkBytes + kQuadBytes);  // 4608
 constexpr int kMaxStages = 8;
-constexpr uint32_t kNibMask = 0x00F000F0u;  // mantissa bits 4..7 of both halves
 
 struct GemvArgs {
   const uint8_t *qw0;  // gate (or the only) weight: frag nibbles
@@ -148,7 +149,7 @@ __device__ __forceinline__ void trace_stamp(const GemvArgs &a, int i) {
 __host__ __device__ inline int meta_cols(int P) { return (P + 1) & ~1; }
 // fp16 B fragments [slot][P][2][4] x 16 B, a 128-byte zero block, then per
 // (slot, column) {xs, f, off, 0}: the column's sum(x), its scale 2^e and
-// the magic-number offset 64 sum(x')
+// the magic-number offset 64 sum(x') over the group's odd k-steps
 __host__ __device__ inline size_t xstage_bytes(int xcap, int P) {
   return (size_t)xcap * P * 128 + 128 + (size_t)xcap * meta_cols(P) * 16;
 }
@@ -328,16 +329,22 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) xw[(e0 + pr) * 4 + wd] = hv[pr];
       }
+      // the odd k-steps' values meet the weights as 64 + q (unpack_word):
+      // their sum is the offset the epilogue takes back out
+      float osum = (h8 & 2) ? sum : 0.0f;
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      osum += __shfl_xor_sync(0xffffffffu, osum, 1);
+      osum += __shfl_xor_sync(0xffffffffu, osum, 2);
+      osum += __shfl_xor_sync(0xffffffffu, osum, 4);
       if (live && h8 == 0) {
         // the bias term's sum(x): the producer's (presum block) or this one;
         // the offset term always uses the sum of the fp16 values multiplied
         int g = gs + slot;
         if (g >= a.ng) g -= a.ng;
         const float bsum = a.xsum ? a.xsum[g * 8 + q] : f * sum;
-        mx[slot * P8 + q] = make_float4(bsum, f, 64.0f * sum, 0.0f);
+        mx[slot * P8 + q] = make_float4(bsum, f, 64.0f * osum, 0.0f);
       }
     }
   }
@@ -606,16 +613,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
       const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(s * CB + u) * 4096 + tile * 512 + lane * 16);
-      // k-step 2p rows r / r+8: bits 0..3 / 8..11 of each half, moved up by
-      // 4 / down by 4; k-step 2p+1: bits 4..7 in place / 12..15 down by 8
-      const uint32_t a00 = nib_f16x2<kNibMask>(w.x << 4), a01 = nib_f16x2<kNibMask>(w.x >> 4);
-      const uint32_t a02 = nib_f16x2<kNibMask>(w.y << 4), a03 = nib_f16x2<kNibMask>(w.y >> 4);
-      const uint32_t a10 = nib_f16x2<kNibMask>(w.x), a11 = nib_f16x2<kNibMask>(w.x >> 8);
-      const uint32_t a12 = nib_f16x2<kNibMask>(w.y), a13 = nib_f16x2<kNibMask>(w.y >> 8);
-      const uint32_t a20 = nib_f16x2<kNibMask>(w.z << 4), a21 = nib_f16x2<kNibMask>(w.z >> 4);
-      const uint32_t a22 = nib_f16x2<kNibMask>(w.w << 4), a23 = nib_f16x2<kNibMask>(w.w >> 4);
-      const uint32_t a30 = nib_f16x2<kNibMask>(w.z), a31 = nib_f16x2<kNibMask>(w.z >> 8);
-      const uint32_t a32 = nib_f16x2<kNibMask>(w.w), a33 = nib_f16x2<kNibMask>(w.w >> 8);
+      // k-step 2p rows r / r+8: bits 0..3 / 8..11 of each half (exact q);
+      // k-step 2p+1: bits 4..7 / 12..15 (64 + q)
+      uint32_t a00, a01, a02, a03, a10, a11, a12, a13, a20, a21, a22, a23, a30, a31, a32, a33;
+      unpack_word(w.x, a00, a01, a10, a11);
+      unpack_word(w.y, a02, a03, a12, a13);
+      unpack_word(w.z, a20, a21, a30, a31);
+      unpack_word(w.w, a22, a23, a32, a33);
       if (first) {
         mma_f16_16816_z(lo[s], a00, a01, a02, a03, xa.x, xa.y);
         mma_f16_16816_z(hi[s], a10, a11, a12, a13, xa.z, xa.w);
@@ -1068,14 +1072,11 @@ __device__ __noinline__ RingCursor chain_consume_op(const ChainArgs &a, const Op
 #pragma unroll
     for (int si = 0; si < NS; ++si) {
       const uint4 w = *reinterpret_cast<const uint4 *>(nib + (size_t)(si * CB + u) * 4096 + tile * 512 + lane * 16);
-      const uint32_t a00 = nib_f16x2<kNibMask>(w.x << 4), a01 = nib_f16x2<kNibMask>(w.x >> 4);
-      const uint32_t a02 = nib_f16x2<kNibMask>(w.y << 4), a03 = nib_f16x2<kNibMask>(w.y >> 4);
-      const uint32_t a10 = nib_f16x2<kNibMask>(w.x), a11 = nib_f16x2<kNibMask>(w.x >> 8);
-      const uint32_t a12 = nib_f16x2<kNibMask>(w.y), a13 = nib_f16x2<kNibMask>(w.y >> 8);
-      const uint32_t a20 = nib_f16x2<kNibMask>(w.z << 4), a21 = nib_f16x2<kNibMask>(w.z >> 4);
-      const uint32_t a22 = nib_f16x2<kNibMask>(w.w << 4), a23 = nib_f16x2<kNibMask>(w.w >> 4);
-      const uint32_t a30 = nib_f16x2<kNibMask>(w.z), a31 = nib_f16x2<kNibMask>(w.z >> 8);
-      const uint32_t a32 = nib_f16x2<kNibMask>(w.w), a33 = nib_f16x2<kNibMask>(w.w >> 8);
+      uint32_t a00, a01, a02, a03, a10, a11, a12, a13, a20, a21, a22, a23, a30, a31, a32, a33;
+      unpack_word(w.x, a00, a01, a10, a11);
+      unpack_word(w.y, a02, a03, a12, a13);
+      unpack_word(w.z, a20, a21, a30, a31);
+      unpack_word(w.w, a22, a23, a32, a33);
       if (first) {
         mma_f16_16816_z(lo[si], a00, a01, a02, a03, xa.x, xa.y);
         mma_f16_16816_z(hi[si], a10, a11, a12, a13, xa.z, xa.w);
@@ -1472,7 +1473,7 @@ GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms
     // every decode shape
     {
       // one CTA per SM (a CTA holds 17 warps and most of the shared memory)
-      long long grid = cfg.grid > 0 ? std::min(cfg.grid, sms) : (long long)sms;
+      long long grid = cfg.grid > 0 ? std::min(cfg.grid, 2 * sms) : (long long)sms;
       // Whole slabs per CTA when that still fills >= 85% of the SMs: no
       // slab is split, so there is no split-K fix-up at the end of the run
       // (the fused gate/up of a 17408-wide MLP: 136 slabs on 148 SMs).

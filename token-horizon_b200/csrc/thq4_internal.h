@@ -110,6 +110,11 @@ void gemv_set_trace(void *buf, size_t bytes);
 // something other than the next projection.
 cudaError_t peer_wait_launch(const PeerGather &g, cudaStream_t stream);
 
+// The scalar reference product (thq4_linear_scalar): f32 dequant, f32
+// accumulate, one warp per row, any m in passes of 8 tokens.
+cudaError_t scalar_launch(const thq4_weight &w, const void *x, bool x_f32, int m, void *y, bool y_f32,
+                          cudaStream_t stream);
+
 // ---- prefill GEMM (tcgen05) -------------------------------------------------
 // The tensor-core path serves m > 8 tokens of bf16 x.
 bool prefill_supported(int m, bool x_f32);

@@ -96,6 +96,7 @@ SIGNATURES = {
     "thq4_gate_up": (c_int, [POINTER(thq4_weight), POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p,
                              c_int, c_void_p, c_size_t, c_void_p]),
     "thq4_linear_workspace_bytes": (c_size_t, [POINTER(thq4_weight), c_int]),
+    "thq4_linear_scalar": (c_int, [POINTER(thq4_weight), c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "thq4_dequant": (c_int, [POINTER(thq4_weight), c_void_p, c_void_p]),
     "thq4_moe_max_tiles": (c_uint32, [c_int, c_int, c_int]),
     "thq4_moe_route": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
