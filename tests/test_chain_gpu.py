@@ -95,12 +95,15 @@ def test_chain_of_two_layers_matches_oracle(m):
 def test_chain_matches_separate_calls_on_the_bench_layer():
     """The bench's layer (hidden 5120, intermediate 17408) as a 4-op chain
     against the same four projections as separate calls on the chain's own
-    inputs: within the per-element rule (their split-K orders may differ)."""
+    inputs: within the per-element rule (their summation orders differ).
+    The gate/up op's bf16(silu(bf16 g) * bf16 u) is held, in both forms, to
+    the reference's split tolerance around the oracle's g and u: a bf16
+    step of g can move a strongly negative g's output by several steps."""
     H, KV, I = 5120, 1024, 17408
     qkv, _ = _w(H + 2 * KV, H, 1001)
     o, _ = _w(H, H, 1004)
-    g, _ = _w(I, H, 1005)
-    u, _ = _w(I, H, 1006)
+    g, (gq, gsb) = _w(I, H, 1005)
+    u, (uq, usb) = _w(I, H, 1006)
     d, _ = _w(H, I, 1007)
     x = torch.randn((1, H), device="cuda").to(torch.bfloat16)
     outs = [_empty(1, n) for n in (H + 2 * KV, H, I, H)]
@@ -123,9 +126,12 @@ def test_chain_matches_separate_calls_on_the_bench_layer():
                              s))
     torch.cuda.synchronize()
     for i, name in enumerate(("qkv", "o", "gate_up", "down")):
-        if name == "gate_up":  # both round bf16(silu(bf16 g) bf16 u): at most a bf16 step or two apart
-            d16 = np.abs(host_bits(outs[2]).astype(np.int32) - host_bits(ref[2]).astype(np.int32))
-            assert d16.max() <= 2, f"{name}: chain and separate call differ by {d16.max()} bf16 steps"
+        if name == "gate_up":
+            xo = _bf(outs[1])
+            gate = O.linear_group(gq, gsb, O.SB_F16, xo)[0]
+            up = O.linear_group(uq, usb, O.SB_F16, xo)[0]
+            assert_gate_up_close("gate_up chain", _bf(outs[2])[0], gate, up, H)
+            assert_gate_up_close("gate_up call", _bf(ref[2])[0], gate, up, H)
         else:
             assert_close_ref(f"{name} chain vs call", _bf(outs[i])[0], _bf(ref[i])[0])
 

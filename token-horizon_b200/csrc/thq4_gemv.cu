@@ -73,8 +73,18 @@ namespace thq4 {
 
 namespace {
 
-constexpr int kConsumers = kSlabTiles;  // one consumer warp per tile of a slab
+constexpr int kConsumers = kSlabTiles;  // chain kernel: one consumer warp per tile of a slab
 constexpr int kThreads = (kConsumers + 1) * 32;
+// Consumer warps per 16-row tile in the decode/verify kernel.  A single
+// weight has two: warp t + 8h takes the run's chunks n with n % 2 == h for
+// tile t, and the pair adds its partial sums at every slab end -- twice the
+// warps to cover the latency of the in-register dequant and of the MMA
+// chains (one-weight launches measured 6-15% faster).  The fused gate/up
+// keeps one: its 73.7 KB stages fill the ring in two, and with both stages
+// being consumed at once nothing would be in flight (measured 23% slower).
+__host__ __device__ constexpr int gemv_wpt(bool gate_up) { return gate_up ? 1 : 2; }
+__host__ __device__ constexpr int gemv_consumers(bool gate_up) { return kSlabTiles * gemv_wpt(gate_up); }
+__host__ __device__ constexpr int gemv_threads(bool gate_up) { return (gemv_consumers(gate_up) + 1) * 32; }
 constexpr int kSgBytes = kSlabTiles * (kChunkBytes + kQuadBytes);  // 4608
 constexpr int kMaxStages = 8;
 
@@ -154,8 +164,13 @@ __host__ __device__ inline size_t xstage_bytes(int xcap, int P) {
   return (size_t)xcap * P * 128 + 128 + (size_t)xcap * meta_cols(P) * 16;
 }
 __host__ __device__ inline size_t stage_bytes(int cb, bool gate_up) { return (size_t)(gate_up ? 2 : 1) * cb * kSgBytes; }
+// two buffers of one warp's partial sums per (tile, stream) for the warp
+// pairs' slab-end exchange (two consumer warps per tile)
+__host__ __device__ inline size_t pair_bytes(bool gate_up) {
+  return gemv_wpt(gate_up) == 2 ? (size_t)2 * kSlabTiles * (gate_up ? 2 : 1) * 32 * 16 : 0;
+}
 __host__ __device__ inline size_t gemv_smem(int stages, int cb, bool gate_up, int xcap, int P) {
-  return 256 + (size_t)stages * stage_bytes(cb, gate_up) + xstage_bytes(xcap, P);
+  return 256 + (size_t)stages * stage_bytes(cb, gate_up) + xstage_bytes(xcap, P) + pair_bytes(gate_up);
 }
 // floats of one CTA side's partial: 8 tiles x NS x 32 lanes x 4
 __host__ __device__ inline int side_floats(bool gate_up) { return kSlabTiles * (gate_up ? 2 : 1) * 32 * 4; }
@@ -173,8 +188,9 @@ __device__ __forceinline__ int sgs_before(int C, int cps, int ng, int cb) {
   const int sl = C / cps;
   return sl * ng + min((C - sl * cps) * cb, ng);
 }
+template <int NC = kConsumers>
 __device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;\n" ::"r"(kConsumers * 32) : "memory");
+  asm volatile("bar.sync 1, %0;\n" ::"r"(NC * 32) : "memory");
 }
 
 // Eight consecutive low-latency words (four 16-byte loads, each 8-byte word
@@ -215,9 +231,9 @@ __device__ __forceinline__ void ll_wait8(const uint4 *w4, uint32_t seq, uint64_t
 // adjacent lanes, which reduce the group's max |x| and sum with a fixed
 // shuffle tree (deterministic).  Up to four items per thread are requested
 // before any is used.
-template <bool PARTS, class A>
+template <bool PARTS, int NC = kConsumers, class A>
 __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf, uint4 *zero, float4 *mx) {
-  const int tid = threadIdx.x, nthr = kConsumers * 32;
+  const int tid = threadIdx.x, nthr = NC * 32;
   const int P = a.P, P8 = meta_cols(P);
   constexpr int kU = 4;
   if (tid < 8) zero[tid] = make_uint4(0, 0, 0, 0);
@@ -351,7 +367,7 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
   if constexpr (PARTS) {
     if (ll_late) raise_status(a.status, kStatusTimeout);
   }
-  consumer_sync();
+  consumer_sync<NC>();
 }
 
 // Final values of one 16-row tile from lanes holding reduced column pairs;
@@ -422,8 +438,9 @@ __device__ void peer_wait(uint32_t *const *flags, const uint32_t *count, int wor
 }
 // After every consumer warp's stores: the grid's last CTA bumps this rank's
 // gather count and writes it into this rank's slot of every peer's flags.
+template <int NC>
 __device__ void peer_signal(const GemvArgs &a) {
-  consumer_sync();
+  consumer_sync<NC>();
   if (threadIdx.x != 0) return;
   if (a.g_mode == 3) {
     // low-latency words need no fence or flag: the grid's last CTA only
@@ -496,7 +513,8 @@ __device__ __forceinline__ bool produce_run(const GemvArgs &a, int C0, int nch, 
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(gemv_threads(GATE_UP), GATE_UP ? 2 : 1) gemv_kernel(const GemvArgs a) {
+  constexpr int WPT = gemv_wpt(GATE_UP), NC = gemv_consumers(GATE_UP);
   constexpr int NS = GATE_UP ? 2 : 1;
   constexpr int CPG = 8 / GW;  // B columns per window position
   constexpr int LPJ = 4 / GW;  // lanes (c) per window position
@@ -516,6 +534,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   uint4 *xf = reinterpret_cast<uint4 *>(xt);
   uint4 *zero = reinterpret_cast<uint4 *>(xt + (size_t)a.xcap * P * 128);
   float4 *mx = reinterpret_cast<float4 *>(xt + (size_t)a.xcap * P * 128 + 128);
+  // the warp pairs' slab-end exchange: [2 buffers][8 tiles][NS][32 lanes]
+  float4 *pairbuf = reinterpret_cast<float4 *>(xt + xstage_bytes(a.xcap, P));
 
   // this CTA's run of chunks: an equal share of the flattened chunk space,
   // or (slab-split mode) part `part` of the chunks of slab blockIdx / j
@@ -535,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumers);
+      mbar_init(&empty[s], kSlabTiles);  // one warp per tile consumes each stage
     }
     mbar_init(xready, 1);
     *abort_word = 0u;
@@ -556,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     a.trace[7] = 0;
   }
 
-  if (warp == kConsumers) {
+  if (warp == NC) {
     // ---- producer: one elected lane streams the run -------------------------
     // (in slab-split mode the whole warp stays for the final cluster barrier)
     if (lane == 0 && !produce_run<CB, GATE_UP>(a, C0, nch, R, full, empty, xready, ring)) *abort_word = 1u;
@@ -567,8 +587,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     }
     return;
   }
-  // ---- consumers: warp `tile` owns tile `tile` of every slab-group ---------
-  const int tile = warp;
+  // ---- consumers: warp tile + 8 half owns tile `tile` of the slab-groups
+  // of the run's chunks n with n % WPT == half
+  const int tile = warp % kSlabTiles, half = warp / kSlabTiles;
   pdl_wait();
   trace_stamp(a, kTrPdl);
   // a low-latency exchange's number: this rank's count + 1 (final once the
@@ -576,14 +597,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   const uint32_t wseq = a.g_mode == 3 ? *reinterpret_cast<const volatile uint32_t *>(a.g_count) + 1u : 0u;
   if (a.g_wait) {  // x holds the peers' slices or partials: wait until they have landed
     if (threadIdx.x == 0) peer_wait(a.g_flags, a.g_count, a.g_world, a.g_rank, a.status);
-    consumer_sync();
+    consumer_sync<NC>();
   }
   trace_stamp(a, kTrPeer);
   const int sl0 = C0 / a.cps, cg0 = C0 - sl0 * a.cps;
   const int gs = cg0 * CB;
   const int xcnt =
       min(a.ng, sgs_before(C1, a.cps, a.ng, CB) - sgs_before(C0, a.cps, a.ng, CB));
-  stage_x<PARTS>(a, gs, xcnt, xf, zero, mx);
+  stage_x<PARTS, NC>(a, gs, xcnt, xf, zero, mx);
   if (threadIdx.x == 0) mbar_arrive(xready);
   trace_stamp(a, kTrStaged);
 
@@ -649,6 +670,31 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
         y[s][1] = fmaf(sr * m1.y, (lo[s][1] + hi[s][1]) - m1.z, fmaf(br, m1.x, y[s][1]));
         y[s][3] = fmaf(s8 * m1.y, (lo[s][3] + hi[s][3]) - m1.z, fmaf(b8, m1.x, y[s][3]));
       }
+    }
+  };
+  // The two warps of a tile hold sums over different chunks of the same
+  // outputs: the second stores its sums to shared memory, the pair meets at
+  // the tile's named barrier, the first adds them (always in this order).
+  // Buffers alternate, so one barrier per exchange suffices: a warp writes
+  // a buffer again only after passing the next exchange's barrier, which
+  // the first warp reaches after reading it.
+  int pair_phase = 0;
+  auto pair_combine = [&]() {
+    if constexpr (WPT == 2) {
+      float4 *pb = pairbuf + (size_t)(pair_phase * kSlabTiles + tile) * NS * 32 + lane;
+      if (half == 1) {
+#pragma unroll
+        for (int si = 0; si < NS; ++si) pb[si * 32] = make_float4(y[si][0], y[si][1], y[si][2], y[si][3]);
+      }
+      asm volatile("bar.sync %0, 64;\n" ::"r"(2 + tile) : "memory");
+      if (half == 0) {
+#pragma unroll
+        for (int si = 0; si < NS; ++si) {
+          const float4 v = pb[si * 32];
+          y[si][0] += v.x, y[si][1] += v.y, y[si][2] += v.z, y[si][3] += v.w;
+        }
+      }
+      pair_phase ^= 1;
     }
   };
   // lanes of one column pair but different window positions hold disjoint
@@ -732,6 +778,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
   for (int n = 0; n < nch; ++n) {
     if (++cg == a.cps) cg = 0, ++sl;
     if (++s == R) s = 0, par ^= 1u;
+    if (WPT == 1 || (n & 1) == half) {  // this warp's chunk
     if (!aborted && !mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
       raise_status(a.status, kStatusTimeout);
       aborted = true;
@@ -761,9 +808,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     }
     __syncwarp();
     if (lane == 0 && !aborted) mbar_arrive(&empty[s]);
+    }  // this warp's chunk
     if (!clustered && cg == a.cps - 1) {  // slab end
+      pair_combine();
       reduce_y();
-      if (aborted) {
+      if (aborted || half != 0) {
       } else if (seg_whole) {
         store_tile<GW, GATE_UP>(a, sl * kSlabTiles + tile, lane, y[0], y[NS - 1], wseq);
       } else {  // the run's first segment, partial
@@ -788,6 +837,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     // If any CTA of the cluster gave up on a wait (its copies may still be
     // landing in its ring), nobody writes into the leader's ring and nothing
     // is stored; every CTA still passes both barriers.
+    pair_combine();
     reduce_y();
     float4 *xb = reinterpret_cast<float4 *>(ring);
     cluster_sync_all();
@@ -796,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       for (int pp = 0; pp < a.cl_j; ++pp)
         gave_up |= ld_cluster_u32(cluster_map(smem_addr(const_cast<uint32_t *>(abort_word)), (uint32_t)pp));
     gave_up = __shfl_sync(0xffffffffu, gave_up, 0);
-    if (part > 0 && !gave_up) {
+    if (part > 0 && !gave_up && half == 0) {
 #pragma unroll
       for (int si = 0; si < NS; ++si) {
         const uint32_t at = smem_addr(xb + (((size_t)part * kSlabTiles + tile) * NS + si) * 32 + lane);
@@ -804,7 +854,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       }
     }
     cluster_sync_all();
-    if (part == 0 && !gave_up) {
+    if (part == 0 && !gave_up && half == 0) {
       for (int pp = 1; pp < a.cl_j; ++pp)
 #pragma unroll
         for (int si = 0; si < NS; ++si) {
@@ -814,18 +864,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
       store_tile<GW, GATE_UP>(a, (C0 / a.cps) * kSlabTiles + tile, lane, y[0], y[NS - 1], wseq);
     }
     trace_stamp(a, kTrStored);
-    if (a.g_mode) peer_signal(a);
+    if (a.g_mode) peer_signal<NC>(a);
     trace_stamp(a, kTrDone);
     return;
   }
 
   int last_slab = -1;
   if (nch > 0 && cg != a.cps - 1) {  // the run ended inside a slab
+    pair_combine();
     reduce_y();
-    if (!aborted) publish(finished_any ? 1 : 0, y);
+    if (!aborted && half == 0) publish(finished_any ? 1 : 0, y);
     last_slab = sl;
   }
-  if (!aborted && (first_slab >= 0 || last_slab >= 0)) {
+  if (!aborted && half == 0 && (first_slab >= 0 || last_slab >= 0)) {
     // the lanes' stores above happen before lane 0's release fence; one
     // fence covers both increments, which are then in flight together
     __syncwarp();
@@ -853,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
     if (done & 2u) combine(last_slab);
   }
   trace_stamp(a, kTrStored);
-  if (a.g_mode) peer_signal(a);  // every consumer warp gets here
+  if (a.g_mode) peer_signal<NC>(a);  // every consumer warp gets here
   trace_stamp(a, kTrDone);
 }
 
@@ -1339,7 +1390,7 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(gemv_threads(GATE_UP));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1426,7 +1477,7 @@ int cluster_capacity(int j) {
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(j * 64);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(gemv_threads(false));
     cfg.dynamicSmemBytes = 150 * 1024;  // any footprint that allows one CTA per SM
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1530,7 +1581,7 @@ GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms
     if (per == 1) return p;
     per = (per + 1) / 2;
   }
-  p.threads = kThreads;
+  p.threads = gemv_threads(gate_up);
   p.pieces = p.grid;
   p.tokens_per_pass = per;
   p.ch = cb;
