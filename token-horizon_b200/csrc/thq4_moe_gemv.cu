@@ -120,12 +120,6 @@ __device__ __forceinline__ uint64_t pk2(float lo, float hi) {
 __device__ __forceinline__ void unpk2(uint64_t v, float &lo, float &hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
-// a + b on both f32 lanes, round to nearest (one instruction)
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 // a * b + c on both f32 lanes, round to nearest (one instruction)
 __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
@@ -180,12 +174,9 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
     bq[nb][4] = t[0], bq[nb][5] = t[1], bq[nb][6] = t[2], bq[nb][7] = t[3];
     sx[nb] = *reinterpret_cast<const float2 *>(xs + nb * 8 + 2 * c);
   }
-  // k-step by k-step over every (stream, block) accumulator; with at most
-  // two blocks, even and odd k-steps go to separate accumulators (KC = 2:
-  // 2 x NS x NL independent chains of two MMAs, added in the epilogue),
-  // which the register budget allows only there
-  constexpr int KC = NL <= 2 ? 2 : 1;
-  float acc[KC][NS][NL][4];
+  // k-step by k-step over every (stream, block) accumulator: NS x NL
+  // independent chains in flight
+  float acc[NS][NL][4];
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
@@ -193,10 +184,10 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
 #pragma unroll
       for (int nb = 0; nb < NL; ++nb) {
         const uint32_t *A = &av[si][4 * ks];
-        if (ks < KC)
-          mma_bf16_z(acc[ks][si][nb], A[0], A[1], A[2], A[3], bq[nb][2 * ks], bq[nb][2 * ks + 1]);
+        if (ks == 0)
+          mma_bf16_z(acc[si][nb], A[0], A[1], A[2], A[3], bq[nb][0], bq[nb][1]);
         else
-          mma_bf16(acc[ks % KC][si][nb], A[0], A[1], A[2], A[3], bq[nb][2 * ks], bq[nb][2 * ks + 1]);
+          mma_bf16(acc[si][nb], A[0], A[1], A[2], A[3], bq[nb][2 * ks], bq[nb][2 * ks + 1]);
       }
   // the same two FMAs per output, in packed f32x2 form: {y0, y1} (row r,
   // tokens 2c and 2c + 1) and {y2, y3} (row r + 8)
@@ -208,13 +199,8 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
     for (int nb = 0; nb < NL; ++nb) {
       const uint64_t xs2 = pk2(sx[nb].x, sx[nb].y);
       uint64_t lo = pk2(y[si][nb][0], y[si][nb][1]), hi = pk2(y[si][nb][2], y[si][nb][3]);
-      uint64_t alo = pk2(acc[0][si][nb][0], acc[0][si][nb][1]), ahi = pk2(acc[0][si][nb][2], acc[0][si][nb][3]);
-      if constexpr (KC == 2) {
-        alo = add2(alo, pk2(acc[KC - 1][si][nb][0], acc[KC - 1][si][nb][1]));
-        ahi = add2(ahi, pk2(acc[KC - 1][si][nb][2], acc[KC - 1][si][nb][3]));
-      }
-      lo = ffma2(srr, alo, ffma2(crr, xs2, lo));
-      hi = ffma2(s88, ahi, ffma2(c88, xs2, hi));
+      lo = ffma2(srr, pk2(acc[si][nb][0], acc[si][nb][1]), ffma2(crr, xs2, lo));
+      hi = ffma2(s88, pk2(acc[si][nb][2], acc[si][nb][3]), ffma2(c88, xs2, hi));
       unpk2(lo, y[si][nb][0], y[si][nb][1]);
       unpk2(hi, y[si][nb][2], y[si][nb][3]);
     }
