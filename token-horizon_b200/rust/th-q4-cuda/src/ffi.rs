@@ -125,6 +125,8 @@ extern "C" {
     pub fn thq4_linear_chain_workspace_bytes(ops: *const thq4_chain_op, n: i32) -> usize;
     pub fn thq4_linear_chain(ops: *const thq4_chain_op, n: i32, x_dtype: i32, m: i32, workspace: *mut c_void,
                              workspace_bytes: usize, stream: *mut c_void) -> thq4_status;
+    pub fn thq4_linear_scalar(w: *const thq4_weight, x: *const c_void, x_dtype: i32, m: i32, y: *mut c_void,
+                              y_dtype: i32, stream: *mut c_void) -> thq4_status;
     pub fn thq4_linear_noalloc(w: *const thq4_weight, x: *const c_void, x_dtype: i32, m: i32, y: *mut c_void,
                                y_dtype: i32, stream: *mut c_void) -> thq4_status;
     pub fn thq4_dequant(w: *const thq4_weight, y: *mut c_void, stream: *mut c_void) -> thq4_status;
