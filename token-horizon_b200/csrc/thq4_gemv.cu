@@ -253,6 +253,10 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
     }
   }
   const int span = (items + 31) / 32 * 32;  // whole warps: every lane takes part in the shuffles
+  // An item slot whose whole warp lies past `span` is skipped (the test is
+  // warp-uniform: nthr and span are multiples of 32), so a warp does the
+  // conversion work of the items it holds and no more.
+  const int wfirst = tid & ~31;
   for (int base = tid; base < span; base += kU * nthr) {
     float v[kU][8];
 #pragma unroll
@@ -261,7 +265,7 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[it][e] = 0.0f;
       if (idx >= items) continue;
-      const int h8 = idx & 7, sq = idx >> 3, q = sq % P, slot = sq / P;
+      const int h8 = idx & 7, sq = idx >> 3, q = P == 1 ? 0 : sq % P, slot = P == 1 ? sq : sq / P;
       int g = gs + slot;
       if (g >= a.ng) g -= a.ng;
       const int t = a.xf32 ? q >> 1 : q;
@@ -309,8 +313,9 @@ __device__ __forceinline__ void stage_x(const A &a, int gs, int xcnt, uint4 *xf,
 #pragma unroll
     for (int it = 0; it < kU; ++it) {
       const int idx = base + it * nthr;
+      if ((base - tid + wfirst) + it * nthr >= span) break;  // this warp holds no item here or later
       const bool live = idx < items;
-      const int h8 = idx & 7, sq = live ? idx >> 3 : 0, q = sq % P, slot = sq / P;
+      const int h8 = idx & 7, sq = live ? idx >> 3 : 0, q = P == 1 ? 0 : sq % P, slot = P == 1 ? sq : sq / P;
       const int part = a.xf32 ? q & 1 : 0;
       float amax = 0.0f;
 #pragma unroll
