@@ -75,16 +75,18 @@ namespace {
 
 constexpr int kConsumers = kSlabTiles;  // chain kernel: one consumer warp per tile of a slab
 constexpr int kThreads = (kConsumers + 1) * 32;
-// Consumer warps per 16-row tile in the decode/verify kernel.  A single
-// weight has two: warp t + 8h takes the run's chunks n with n % 2 == h for
-// tile t, and the pair adds its partial sums at every slab end -- twice the
-// warps to cover the latency of the in-register dequant and of the MMA
-// chains (one-weight launches measured 6-15% faster).  The fused gate/up
-// keeps one: its 73.7 KB stages fill the ring in two, and with both stages
-// being consumed at once nothing would be in flight (measured 23% slower).
+// The decode/verify kernel has two consumer warps per 16-row tile; all
+// sixteen stage the activation.  For a single weight both also stream:
+// warp t + 8h takes the run's chunks n with n % 2 == h for tile t, and the
+// pair adds its partial sums at every slab end -- twice the warps to cover
+// the latency of the in-register dequant and of the MMA chains (one-weight
+// launches measured 6-15% faster).  In the fused gate/up only warp t
+// streams (gemv_wpt = 1): its 73.7 KB stages fill the ring in two, and with
+// both stages being consumed at once nothing would be in flight (measured
+// 23% slower).
+constexpr int kGemvConsumers = 2 * kSlabTiles;
+constexpr int kGemvThreads = (kGemvConsumers + 1) * 32;
 __host__ __device__ constexpr int gemv_wpt(bool gate_up) { return gate_up ? 1 : 2; }
-__host__ __device__ constexpr int gemv_consumers(bool gate_up) { return kSlabTiles * gemv_wpt(gate_up); }
-__host__ __device__ constexpr int gemv_threads(bool gate_up) { return (gemv_consumers(gate_up) + 1) * 32; }
 constexpr int kSgBytes = kSlabTiles * (kChunkBytes + kQuadBytes);  // 4608
 constexpr int kMaxStages = 8;
 
@@ -518,8 +520,8 @@ __device__ __forceinline__ bool produce_run(const GemvArgs &a, int C0, int nch, 
 }
 
 template <int CB, int GW, bool ONE, bool SF16, bool GATE_UP, bool PARTS>
-__global__ void __launch_bounds__(gemv_threads(GATE_UP), GATE_UP ? 2 : 1) gemv_kernel(const GemvArgs a) {
-  constexpr int WPT = gemv_wpt(GATE_UP), NC = gemv_consumers(GATE_UP);
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+  constexpr int WPT = gemv_wpt(GATE_UP), NC = kGemvConsumers;
   constexpr int NS = GATE_UP ? 2 : 1;
   constexpr int CPG = 8 / GW;  // B columns per window position
   constexpr int LPJ = 4 / GW;  // lanes (c) per window position
@@ -593,7 +595,8 @@ __global__ void __launch_bounds__(gemv_threads(GATE_UP), GATE_UP ? 2 : 1) gemv_k
     return;
   }
   // ---- consumers: warp tile + 8 half owns tile `tile` of the slab-groups
-  // of the run's chunks n with n % WPT == half
+  // of the run's chunks n with n % 2 == half (one weight), or of every
+  // chunk when half == 0 (gate/up: warps 8..15 only stage x)
   const int tile = warp % kSlabTiles, half = warp / kSlabTiles;
   pdl_wait();
   trace_stamp(a, kTrPdl);
@@ -783,7 +786,7 @@ __global__ void __launch_bounds__(gemv_threads(GATE_UP), GATE_UP ? 2 : 1) gemv_k
   for (int n = 0; n < nch; ++n) {
     if (++cg == a.cps) cg = 0, ++sl;
     if (++s == R) s = 0, par ^= 1u;
-    if (WPT == 1 || (n & 1) == half) {  // this warp's chunk
+    if (WPT == 1 ? half == 0 : (n & 1) == half) {  // this warp's chunk
     if (!aborted && !mbar_wait_bounded(&full[s], par, kWaitLimitNs)) {
       raise_status(a.status, kStatusTimeout);
       aborted = true;
@@ -1395,7 +1398,7 @@ cudaError_t launch_one(const GemvArgs &a, int grid, size_t smem, cudaStream_t st
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(gemv_threads(GATE_UP));
+  cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1482,7 +1485,7 @@ int cluster_capacity(int j) {
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(j * 64);
-    cfg.blockDim = dim3(gemv_threads(false));
+    cfg.blockDim = dim3(kGemvThreads);
     cfg.dynamicSmemBytes = 150 * 1024;  // any footprint that allows one CTA per SM
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1586,7 +1589,7 @@ GemvPlan gemv_plan_for(int out, int in, int m, bool x_f32, bool gate_up, int sms
     if (per == 1) return p;
     per = (per + 1) / 2;
   }
-  p.threads = gemv_threads(gate_up);
+  p.threads = kGemvThreads;
   p.pieces = p.grid;
   p.tokens_per_pass = per;
   p.ch = cb;
