@@ -1029,12 +1029,17 @@ def bench_prefill(torch, thq4, synth, dev, tc_peak, peak_kind):
     for M in (512, 2048):
         x = torch.randn((M, K), device=dev).to(torch.bfloat16)
         y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        # the workspace thq4_linear asks for at M rows: room for the stream-K
+        # parts, so the k-stages are split evenly over the SMs
+        wsb = lib.thq4_linear_workspace_bytes(ctypes.byref(ws[0].desc), M)
+        wsp = torch.zeros(max(wsb, 256), dtype=torch.uint8, device=dev)
 
         def call():
             s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
             for w in ws:
                 thq4.check(lib.thq4_linear(ctypes.byref(w.desc), ctypes.c_void_p(x.data_ptr()), thq4.BF16, M,
-                                           ctypes.c_void_p(y.data_ptr()), thq4.BF16, None, 0, s))
+                                           ctypes.c_void_p(y.data_ptr()), thq4.BF16, ctypes.c_void_p(wsp.data_ptr()),
+                                           wsp.numel(), s))
 
         ms = _time_ms(torch, call, 10) / len(ws)
         tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12

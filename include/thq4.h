@@ -163,13 +163,20 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up,
  * tuned; no workspace. */
 thq4_status thq4_linear_scalar(const thq4_weight *w, const void *x, int x_dtype, int m, void *y, int y_dtype,
                                void *stream);
-/* Workspace bytes thq4_linear / thq4_gate_up need for this weight (for
- * thq4_gate_up pass the gate half).  The decode/verify kernel splits tiles
- * over warps and finishes each split tile in the warp that arrives last: the
- * workspace holds the partial sums and one arrival counter per 16-row tile.
- * It must be 256-byte aligned and zero-filled before its first use; every
- * call returns it zeroed, so one allocation serves every later call.  Calls
- * that may overlap on the GPU need separate workspaces. */
+/* Workspace bytes thq4_linear / thq4_gate_up need for this weight at m rows
+ * (for thq4_gate_up pass the gate half).  The decode/verify kernel splits
+ * tiles over warps and finishes each split tile in the warp that arrives
+ * last: the workspace holds the partial sums and one arrival counter per
+ * 16-row tile.  At m > 8 (bf16 x) the figure can be larger: thq4_linear's
+ * prefill then splits the k-stages of its 128-row x 256-token tiles evenly
+ * over the SMs (stream-K) and needs, after the decode region, one claim word
+ * pair and one f32 part tile (128 KB) per SM.  Given less (or no workspace)
+ * the prefill runs whole tiles instead, which is slower when the tiles do
+ * not fill whole waves.  The workspace must be 256-byte aligned and
+ * zero-filled before its first use; every call leaves its counters and
+ * claim words zeroed (the parts need no clearing), so one allocation serves
+ * every later call.  Calls that may overlap on the GPU need separate
+ * workspaces. */
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m);
 /* A chain of dependent projections in one persistent launch.  No single
  * reference counterpart: it runs what consecutive QLin::linear_ps /

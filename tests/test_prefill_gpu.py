@@ -80,3 +80,59 @@ def test_prefill_baseline_config(m):
     cols = np.unique(np.concatenate([np.arange(64), np.arange(out - 64, out), rng.choice(out, 64, replace=False)]))
     want = O.linear_dequant(wq[cols], sb[cols], O.SB_F16, O.bf16_to_f32(x))
     assert_rms_close(f"prefill C3 m{m}", got[:, cols], want, rel=1e-3)
+
+
+@pytest.mark.parametrize("out,inp,m", [(20000, 1024, 300), (4608, 2048, 1100)])
+@pytest.mark.parametrize("y_f32", [True, False])
+def test_prefill_stream_k_split(out, inp, m, y_f32):
+    """With a workspace of thq4_linear_workspace_bytes(w, m) bytes the
+    prefill splits the k-stages of the tiles evenly over the SMs (these
+    shapes have more 256-token tiles than SMs, not a whole number of waves,
+    ragged rows and a ragged last token tile); a tile cut between two CTAs
+    is finished by the one that claims it second.  Checked against the
+    oracle on every token of 192 columns, against the whole-tile kernel (no
+    workspace), for run-to-run equality, and for the claim words being zero
+    again after the call."""
+    import ctypes
+    L = thq4.lib()
+    wq, sb = O.synthetic_weight(out, inp, 31 + m, O.SB_F16)
+    rng = np.random.default_rng(m)
+    x = O.f32_to_bf16(rng.standard_normal((m, inp)).astype(np.float32))
+    q = thq4.QLin(dev(wq), dev_sb(sb, O.SB_F16), out, inp, 64).tiled()
+    desc = ctypes.byref(q.packed.desc)
+    need = L.thq4_linear_workspace_bytes(desc, m)
+    gemv_need = L.thq4_linear_workspace_bytes(desc, 1)
+    assert need > gemv_need, "these shapes take the split"
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    xd = dev(x)
+    ydt = torch.float32 if y_f32 else torch.bfloat16
+    code = thq4.F32 if y_f32 else thq4.BF16
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def run(workspace):
+        y = torch.full((m, out), float("nan"), dtype=ydt, device="cuda")
+        wp, wn = (ctypes.c_void_p(workspace.data_ptr()), workspace.numel()) if workspace is not None else (None, 0)
+        thq4.check(L.thq4_linear(desc, ctypes.c_void_p(xd.data_ptr()), thq4.BF16, m, ctypes.c_void_p(y.data_ptr()),
+                                 code, wp, wn, stream))
+        torch.cuda.synchronize()
+        return to_f32(y)
+
+    split = run(ws)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    sync0 = (gemv_need + 255) // 256 * 256
+    assert int(ws[sync0:sync0 + 8 * sms].count_nonzero()) == 0, "claim words not zeroed"
+    assert int(ws[:gemv_need].count_nonzero()) == 0, "decode region touched"
+    again = run(ws)
+    assert np.array_equal(split, again), "split prefill not deterministic"
+    whole = run(None)
+    assert not np.isnan(split).any() and not np.isnan(whole).any()
+    cols = np.unique(np.concatenate([np.arange(64), np.arange(out - 64, out), rng.choice(out, 64, replace=False)]))
+    want = O.linear_dequant(wq[cols], sb[cols], O.SB_F16, O.bf16_to_f32(x))
+    if y_f32:
+        assert_rms_close(f"split prefill {out}x{inp} m{m}", split[:, cols], want, rel=1e-3)
+        assert_rms_close(f"whole prefill {out}x{inp} m{m}", whole[:, cols], want, rel=1e-3)
+        assert_rms_close(f"split vs whole {out}x{inp} m{m}", split, whole, rel=1e-5)
+    else:  # bf16 outputs: the reference's per-element rule (qwen35.rs:6946-6961)
+        for t in range(m):
+            assert_close_ref(f"split prefill bf16 {out}x{inp} m{m} t{t}", split[t, cols], want[t])
+            assert_close_ref(f"whole prefill bf16 {out}x{inp} m{m} t{t}", whole[t, cols], want[t])

@@ -258,9 +258,8 @@ thq4_status thq4_weight_init(thq4_weight *w, int out, int in, int gs, int sb_dty
 }
 
 size_t thq4_linear_workspace_bytes(const thq4_weight *w, int m) {
-  (void)m;
-  if (!w || w->out <= 0) return 0;
-  return gemv_workspace_bytes(w->out);
+  if (!w || w->out <= 0 || w->in <= 0) return 0;
+  return std::max(gemv_workspace_bytes(w->out), prefill_workspace_bytes(*w, m));
 }
 
 namespace {
@@ -294,7 +293,8 @@ thq4_status thq4_linear(const thq4_weight *w, const void *x, int x_dtype, int m,
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_linear");
   if (s != THQ4_OK) return s;
   if (prefill_supported(m, x_dtype == THQ4_F32)) {
-    const cudaError_t e = prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    const cudaError_t e = prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, workspace, workspace_bytes,
+                                         static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, "thq4_linear (prefill)");
     return THQ4_OK;
   }
@@ -316,7 +316,8 @@ thq4_status thq4_linear_noalloc(const thq4_weight *w, const void *x, int x_dtype
   // the same row-count routing as thq4_linear: the prefill kernel needs no
   // scratch at all
   if (prefill_supported(m, x_dtype == THQ4_F32)) {
-    const cudaError_t e = prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        prefill_launch(*w, nullptr, x, m, y, y_dtype == THQ4_F32, nullptr, 0, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, "thq4_linear_noalloc (prefill)");
     return THQ4_OK;
   }
@@ -413,7 +414,8 @@ thq4_status thq4_gate_up(const thq4_weight *gate, const thq4_weight *up, const v
   s = check_io(x, x_dtype, m, y, y_dtype, "thq4_gate_up");
   if (s != THQ4_OK) return s;
   if (prefill_supported(m, x_dtype == THQ4_F32)) {
-    const cudaError_t e = prefill_launch(*gate, up, x, m, y, y_dtype == THQ4_F32, static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        prefill_launch(*gate, up, x, m, y, y_dtype == THQ4_F32, nullptr, 0, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, "thq4_gate_up (prefill)");
     return THQ4_OK;
   }

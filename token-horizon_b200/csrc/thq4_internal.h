@@ -116,10 +116,15 @@ cudaError_t scalar_launch(const thq4_weight &w, const void *x, bool x_f32, int m
                           cudaStream_t stream);
 
 // ---- prefill GEMM (tcgen05) -------------------------------------------------
-// The tensor-core path serves m > 8 tokens of bf16 x.
+// The tensor-core path serves m > 8 tokens of bf16 x.  With a workspace of at
+// least prefill_workspace_bytes(w0, m) bytes (the decode kernel's region
+// first, untouched, then the split tiles' claim words and f32 parts) the
+// one-weight form splits the k-stages evenly over the CTAs (stream-K);
+// without one (workspace null or smaller) it runs whole tiles.
 bool prefill_supported(int m, bool x_f32);
+size_t prefill_workspace_bytes(const thq4_weight &w0, int m);
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
-                           cudaStream_t stream);
+                           void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
 // bf16 x [rows][k] (k innermost) as a 2-D tensor map with 64 x box_rows
 // boxes and 128-byte swizzle; `map` points to a CUtensorMap.

@@ -36,10 +36,11 @@ def _ptr(t: Optional[torch.Tensor]):
 _WORKSPACES: dict = {}
 
 
-def workspace(desc, device: torch.device) -> torch.Tensor:
-    """A zero-filled workspace big enough for `desc`, cached per device and
-    stream (the kernels return it zeroed after every call)."""
-    need = _lib.lib().thq4_linear_workspace_bytes(ctypes.byref(desc), 1)
+def workspace(desc, device: torch.device, m: int = 1) -> torch.Tensor:
+    """A zero-filled workspace big enough for `desc` at `m` rows, cached per
+    device and stream (the kernels leave its counters zeroed after every
+    call; at m > 8 it also holds the prefill's stream-K parts)."""
+    need = _lib.lib().thq4_linear_workspace_bytes(ctypes.byref(desc), m)
     key = (device.index if device.index is not None else torch.cuda.current_device(),
            torch.cuda.current_stream(device).cuda_stream)
     ws = _WORKSPACES.get(key)
@@ -158,7 +159,7 @@ class QLin:
         xv = x if presum else x.reshape(rows, in_d).contiguous()
         ydt = out_dtype or (torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         y = out if out is not None else torch.empty((rows, self.out), dtype=ydt, device=x.device)
-        ws = workspace(self.packed.desc, x.device)
+        ws = workspace(self.packed.desc, x.device, rows)
         check(_lib.lib().thq4_linear(ctypes.byref(self.packed.desc), _ptr(xv), x_dtype, rows, _ptr(y),
                                      F32 if y.dtype == torch.float32 else BF16, _ptr(ws), ws.numel(), _stream()))
         return y.reshape(dims[:-1] + [self.out])
