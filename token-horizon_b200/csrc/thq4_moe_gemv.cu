@@ -126,6 +126,21 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+// Shared-space accesses by 32-bit address (the ring's base is aligned through
+// an integer, so C++ accesses through it would be generic, 64-bit).
+__device__ __forceinline__ uint4 mg_lds4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 mg_lds2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void mg_sts16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
 __device__ __forceinline__ void mg_consumer_sync() {
   asm volatile("bar.sync 1, %0;\n" ::"r"(kMgConsumers * 32) : "memory");
 }
@@ -134,7 +149,7 @@ __device__ __forceinline__ void mg_consumer_sync() {
 // hold live rows: A from the nibbles, B from the swizzled x box, then
 // y += s * acc + (b - 128 s) * sum(x) per output.
 template <int NS, int NL, bool SF16>
-__device__ __forceinline__ void mg_group(const unsigned char *st, int j, int tile, int lane, float (&y)[NS][4][4]) {
+__device__ __forceinline__ void mg_group(uint32_t st, int j, int tile, int lane, float (&y)[NS][4][4]) {
   using St = MgStage<NS>;
   const int r = lane >> 2, c = lane & 3;
   // A of every stream first (k-step 2p: nibbles 0/4 (rows r) and 2/6 (rows
@@ -144,7 +159,7 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
   float sr[NS], s8[NS], cr[NS], c8[NS];
 #pragma unroll
   for (int si = 0; si < NS; ++si) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(st + St::nib_off + (si * kMgCB + j) * 4096 + tile * 512 + lane * 16);
+    const uint4 w = mg_lds4(st + St::nib_off + (uint32_t)((si * kMgCB + j) * 4096 + tile * 512 + lane * 16));
     av[si][0] = nib_bf16x2(w.x), av[si][1] = nib_bf16x2(w.x >> 8);
     av[si][2] = nib_bf16x2(w.y), av[si][3] = nib_bf16x2(w.y >> 8);
     av[si][4] = nib_bf16x2(w.x >> 4), av[si][5] = nib_bf16x2(w.x >> 12);
@@ -153,15 +168,15 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
     av[si][10] = nib_bf16x2(w.w), av[si][11] = nib_bf16x2(w.w >> 8);
     av[si][12] = nib_bf16x2(w.z >> 4), av[si][13] = nib_bf16x2(w.z >> 12);
     av[si][14] = nib_bf16x2(w.w >> 4), av[si][15] = nib_bf16x2(w.w >> 12);
-    const uint2 q = *reinterpret_cast<const uint2 *>(st + St::sb_off + (si * kMgCB + j) * 512 + tile * 64 + r * 8);
+    const uint2 q = mg_lds2(st + St::sb_off + (uint32_t)((si * kMgCB + j) * 512 + tile * 64 + r * 8));
     sr[si] = sb_to_f32<SF16>(q.x & 0xffffu), s8[si] = sb_to_f32<SF16>(q.y & 0xffffu);
     cr[si] = fmaf(-128.0f, sr[si], sb_to_f32<SF16>(q.x >> 16));
     c8[si] = fmaf(-128.0f, s8[si], sb_to_f32<SF16>(q.y >> 16));
   }
   // B: x rows 8 nb + (lane & 7); k-steps 0/1 from 16-byte chunks 0..3,
   // k-steps 2/3 from chunks 4..7 (swizzled by row & 7)
-  const uint32_t xb = smem_addr(st + St::x_off + j * kXBox);
-  const float *xs = reinterpret_cast<const float *>(st + St::xs_off + j * 128);
+  const uint32_t xb = st + St::x_off + (uint32_t)j * kXBox;
+  const uint32_t xs = st + St::xs_off + (uint32_t)j * 128;
   uint32_t bq[NL][8];
   float2 sx[NL];
 #pragma unroll
@@ -172,7 +187,8 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
     bq[nb][0] = t[0], bq[nb][1] = t[1], bq[nb][2] = t[2], bq[nb][3] = t[3];
     ldsm_x4(t, xb + row * 128 + (((4 + mat) ^ (row & 7)) << 4));
     bq[nb][4] = t[0], bq[nb][5] = t[1], bq[nb][6] = t[2], bq[nb][7] = t[3];
-    sx[nb] = *reinterpret_cast<const float2 *>(xs + nb * 8 + 2 * c);
+    const uint2 sv = mg_lds2(xs + (uint32_t)(nb * 8 + 2 * c) * 4);
+    sx[nb] = make_float2(__uint_as_float(sv.x), __uint_as_float(sv.y));
   }
   // k-step by k-step over every (stream, block) accumulator: NS x NL
   // independent chains in flight
@@ -209,7 +225,7 @@ __device__ __forceinline__ void mg_group(const unsigned char *st, int j, int til
 
 // The groups of a stage holding `cnt` groups.
 template <int NS, int NL, bool SF16>
-__device__ __forceinline__ void mg_stage(const unsigned char *st, int cnt, int tile, int lane, float (&y)[NS][4][4]) {
+__device__ __forceinline__ void mg_stage(uint32_t st, int cnt, int tile, int lane, float (&y)[NS][4][4]) {
   if (cnt == kMgCB) {
 #pragma unroll
     for (int j = 0; j < kMgCB; ++j) mg_group<NS, NL, SF16>(st, j, tile, lane, y);
@@ -304,7 +320,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
         aborted = true;
       }
       if (!aborted) {
-        const unsigned char *st = ring + (size_t)s * St::bytes;
+        const uint32_t st = smem_addr(ring) + (uint32_t)s * St::bytes;
         const int cnt = min(kMgCB, a.ng - cc * kMgCB);
         switch (nlive) {
           case 1: mg_stage<NS, 1, SF16>(st, cnt, tile, lane, y); break;
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
       for (int e = 0; e < 4; ++e) {
         const float v = NS == 2 ? silu_mul(y[0][nb][e], y[NS - 1][nb][e]) : y[0][nb][e];
         const int tok = nb * 8 + 2 * c + (e & 1), row = tile * 16 + r + 8 * (e >> 1);
-        otile[tok * 128 + row] = f32_to_bf16_bits(v);
+        mg_sts16(smem_addr(otile) + (uint32_t)(tok * 128 + row) * 2, f32_to_bf16_bits(v));
       }
     mg_consumer_sync();
     const int tid = threadIdx.x;  // 0 .. 255
@@ -336,17 +352,17 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemv_kernel(const __grid_co
       const int tok = p >> 4, col = (p & 15) * 8;
       if (tok < rows_out && sl * 128 + col < a.n && !aborted)
         *reinterpret_cast<uint4 *>(a.y + ((size_t)gt * kMoeTileRows + tok) * a.n + sl * 128 + col) =
-            *reinterpret_cast<const uint4 *>(otile + tok * 128 + col);
+            mg_lds4(smem_addr(otile) + (uint32_t)(tok * 128 + col) * 2);
     }
     if (a.ysum) {
       // sums of the bf16 values over each token's two 64-row groups: four
       // threads per (token, group), 16 values each, a fixed shuffle tree
       const int qi = tid >> 2, part = tid & 3, tok = qi >> 1, hg = qi & 1;
-      const uint4 *src = reinterpret_cast<const uint4 *>(otile + tok * 128 + hg * 64 + part * 16);
+      const uint32_t src = smem_addr(otile) + (uint32_t)(tok * 128 + hg * 64 + part * 16) * 2;
       float sum = 0.0f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint4 v = src[h];
+        const uint4 v = mg_lds4(src + 16 * h);
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) sum += __uint_as_float(wv[e] << 16) + __uint_as_float(wv[e] & 0xffff0000u);
