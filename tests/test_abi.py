@@ -310,3 +310,30 @@ def test_environment_override_is_parsed_once_and_validated(env, want):
     got = tuple(json.loads(out.strip().splitlines()[-1]))
     assert got[:3] == want[:3] and got[4:] == want[4:]
     assert (got[3] <= 3) if want[3] is None else got[3] == want[3]
+
+
+@pytest.mark.parametrize("out,inp,m,split", [
+    (12288, 4096, 512, True),     # configs[2] M = 512: 192 tiles of 256 tokens fill 1.3 waves -> stream-K
+    (12288, 4096, 1024, False),   # 384 tiles, waves 86% full: whole tiles
+    (12288, 4096, 2048, False),   # 768 tiles, 86%: whole tiles
+    (12288, 4096, 9, False),      # 96 tiles, fewer than the SMs: whole tiles
+    (20000, 1024, 300, True),     # 314 tiles (ragged rows and tokens), 71%
+    (4608, 2048, 1100, True),     # 180 tiles, 61%
+])
+def test_prefill_split_plan_and_workspace(out, inp, m, split):
+    """Host-only: thq4_linear_workspace_bytes(w, m) is the decode kernel's
+    figure unless the prefill splits its k-stages (stream-K), which it does
+    when 256-token tiles outnumber the SMs but fill the waves to less than
+    80%; the split region is 256-aligned after the decode region: one claim
+    word pair and one 128-row x 256-token f32 part per SM (148 here, the
+    library's SM count without a device)."""
+    w = _w(out=out, inp=inp, sbd=thq4.F16)
+    L = thq4.lib()
+    base = L.thq4_linear_workspace_bytes(ctypes.byref(w), 1)
+    got = L.thq4_linear_workspace_bytes(ctypes.byref(w), m)
+    if not split:
+        assert got == base
+        return
+    sms = 148
+    r256 = lambda v: (v + 255) // 256 * 256
+    assert got == r256(base) + r256(sms * 8) + sms * 256 * 128 * 4
