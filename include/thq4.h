@@ -170,9 +170,9 @@ thq4_status thq4_linear_scalar(const thq4_weight *w, const void *x, int x_dtype,
  * 16-row tile.  At m > 8 (bf16 x) the figure can be larger: thq4_linear's
  * prefill then splits the k-stages of its 128-row x 256-token tiles evenly
  * over the SMs (stream-K) and needs, after the decode region, one claim word
- * pair and one f32 part tile (128 KB) per SM.  Given less (or no workspace)
- * the prefill runs whole tiles instead, which is slower when the tiles do
- * not fill whole waves.  The workspace must be 256-byte aligned and
+ * pair and one f32 part tile (128 KB) per SM.  Given less, no workspace or
+ * one that is not 256-byte aligned, the prefill runs whole tiles instead,
+ * which is slower when the tiles do not fill whole waves.  The workspace must be 256-byte aligned and
  * zero-filled before its first use; every call leaves its counters and
  * claim words zeroed (the parts need no clearing), so one allocation serves
  * every later call.  Calls that may overlap on the GPU need separate

@@ -136,3 +136,30 @@ def test_prefill_stream_k_split(out, inp, m, y_f32):
         for t in range(m):
             assert_close_ref(f"split prefill bf16 {out}x{inp} m{m} t{t}", split[t, cols], want[t])
             assert_close_ref(f"whole prefill bf16 {out}x{inp} m{m} t{t}", whole[t, cols], want[t])
+
+
+def test_prefill_split_needs_aligned_workspace():
+    """A workspace large enough for the split but not 256-byte aligned runs
+    whole tiles: the output equals the no-workspace call bit for bit."""
+    import ctypes
+    L = thq4.lib()
+    out, inp, m = 4608, 2048, 1100
+    wq, sb = O.synthetic_weight(out, inp, 5, O.SB_F16)
+    x = dev(O.f32_to_bf16(np.random.default_rng(3).standard_normal((m, inp)).astype(np.float32)))
+    q = thq4.QLin(dev(wq), dev_sb(sb, O.SB_F16), out, inp, 64).tiled()
+    desc = ctypes.byref(q.packed.desc)
+    need = L.thq4_linear_workspace_bytes(desc, m)
+    ws = torch.zeros(need + 256, dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def run(ptr, n):
+        y = torch.empty((m, out), dtype=torch.float32, device="cuda")
+        thq4.check(L.thq4_linear(desc, ctypes.c_void_p(x.data_ptr()), thq4.BF16, m, ctypes.c_void_p(y.data_ptr()),
+                                 thq4.F32, ptr, n, stream))
+        torch.cuda.synchronize()
+        return to_f32(y)
+
+    shifted = run(ctypes.c_void_p(ws.data_ptr() + 16), need)
+    whole = run(None, 0)
+    assert np.array_equal(shifted, whole)
+    assert int(ws.count_nonzero()) == 0, "the misaligned workspace was written"

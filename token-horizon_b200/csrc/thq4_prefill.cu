@@ -894,8 +894,10 @@ cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const v
                            void *workspace, size_t workspace_bytes, cudaStream_t stream) {
   const bool gate_up = w1 != nullptr;
   PfPlan plan = prefill_plan_for(w0, m, gate_up);
-  if (plan.sk && (!workspace || workspace_bytes < prefill_workspace_bytes(w0, m))) {
-    // no room for the parts: whole tiles
+  if (plan.sk && (!workspace || workspace_bytes < prefill_workspace_bytes(w0, m) ||
+                  reinterpret_cast<uintptr_t>(workspace) % 256 != 0)) {
+    // no room for the parts (or not the aligned workspace the split's
+    // claim words and parts assume): whole tiles
     plan.sk = false;
     plan.bt = prefill_plan(m, row_slabs(w0.out), device_sm_count());
     plan.tiles = (long long)((m + plan.bt - 1) / plan.bt) * row_slabs(w0.out);
