@@ -610,7 +610,7 @@ __global__ void __launch_bounds__(PfWarps<DG, EW>::threads, 1)
       // CTA came first) and finishes the tile.
       const bool split = NS == 1 && (kb > 0 || ke < a.ng);
       const int bnd = kb > 0 ? (int)blockIdx.x : (int)blockIdx.x + 1;
-      const float *slot = a.part + (size_t)bnd * (BT * kBN);
+      const float *slot = split ? a.part + (size_t)bnd * (BT * kBN) : nullptr;
       bool first = false;
       if (split) {
         if (et == 0) {
