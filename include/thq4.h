@@ -521,6 +521,14 @@ thq4_status thq4_debug_set_trace(void *buf, size_t bytes);
  * dispatch tables the same way (quant_kernel.rs:5914-5973). */
 thq4_status thq4_debug_gemv_plan(int out, int in, int m, int x_f32, int gate_up, int sms, const int *cluster_fit,
                                  int64_t *plan);
+/* The prefill's launch plan for an out x in weight and m > 8 bf16 tokens
+ * (gate_up: the two-weight form) on a GPU with `sms` SMs.  Fills plan[5] =
+ * {tokens per tile, stream-K split (0/1), tiles, CTAs, bytes of the split's
+ * workspace region after the decode kernel's (0 for whole tiles)}; the split
+ * runs only when the caller's workspace holds that much.  Host only; pins the
+ * prefill's dispatch policy the way thq4_debug_gemv_plan pins the decode
+ * kernel's (the reference pins its own tables, quant_kernel.rs:5914-5973). */
+thq4_status thq4_debug_prefill_plan(int out, int in, int m, int gate_up, int sms, int64_t *plan);
 
 #ifdef __cplusplus
 }

@@ -337,3 +337,36 @@ def test_prefill_split_plan_and_workspace(out, inp, m, split):
     sms = 148
     r256 = lambda v: (v + 255) // 256 * 256
     assert got == r256(base) + r256(sms * 8) + sms * 256 * 128 * 4
+
+
+def _pf_plan(out, inp, m, gate_up=0, sms=148):
+    p = (ctypes.c_int64 * 5)()
+    assert thq4.lib().thq4_debug_prefill_plan(out, inp, m, gate_up, sms, p) == 0, thq4.last_error()
+    return tuple(p)
+
+
+@pytest.mark.parametrize("shape,want", [
+    # configs[2] at M = 512: 256-token tiles fill 1.3 waves -> stream-K over 148 CTAs
+    ((12288, 4096, 512), (256, 1, 192, 148, None)),
+    ((12288, 4096, 1024), (256, 0, 384, 148, 0)),   # waves 86% full: whole 256-token tiles
+    ((12288, 4096, 2048), (256, 0, 768, 148, 0)),
+    ((12288, 4096, 300), (256, 1, 192, 148, None)), # 2 x 96 tiles fill 65% of two waves: split too
+    ((12288, 4096, 40), (192, 0, 96, 96, 0)),       # one token tile: the widest least-cost width
+    ((12288, 4096, 512, 1), (128, 0, 384, 148, 0)), # the gate/up form: 128-token tiles, whole
+])
+def test_prefill_policy_table(shape, want):
+    """Host only: the prefill planner's launch shape for the BASELINE prefill
+    shape and its neighbours on 148 SMs (as test_planner_policy_table pins
+    the decode kernel's)."""
+    got = _pf_plan(*shape)
+    assert got[:4] == want[:4]
+    if want[4] is None:
+        assert got[4] > 148 * 256 * 128 * 4  # the parts, after the decode region
+    else:
+        assert got[4] == want[4]
+
+
+def test_prefill_plan_rejects_decode_rows():
+    assert thq4.lib().thq4_debug_prefill_plan(12288, 4096, 8, 0, 148, (ctypes.c_int64 * 5)()) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert "m > 8" in thq4.last_error()

@@ -946,4 +946,18 @@ thq4_status thq4_debug_gemv_plan(int out, int in, int m, int x_f32, int gate_up,
   return THQ4_OK;
 }
 
+thq4_status thq4_debug_prefill_plan(int out, int in, int m, int gate_up, int sms, int64_t *plan) {
+  if (out < 1 || in < kGroup || in % kGroup || m <= 8 || sms < 1 || sms > 1024 || !plan)
+    return set_error(THQ4_ERR_INVALID_ARGUMENT,
+                     "thq4_debug_prefill_plan: need out >= 1, in a positive multiple of 64, m > 8 (the prefill's "
+                     "rows), 1 <= sms <= 1024, plan non-NULL");
+  const PrefillPlanInfo p = prefill_debug_plan(out, m, gate_up != 0, sms);
+  plan[0] = p.bt;
+  plan[1] = p.split ? 1 : 0;
+  plan[2] = p.tiles;
+  plan[3] = p.grid;
+  plan[4] = (int64_t)p.split_bytes;
+  return THQ4_OK;
+}
+
 }  // extern "C"

@@ -123,6 +123,17 @@ cudaError_t scalar_launch(const thq4_weight &w, const void *x, bool x_f32, int m
 // without one (workspace null or smaller) it runs whole tiles.
 bool prefill_supported(int m, bool x_f32);
 size_t prefill_workspace_bytes(const thq4_weight &w0, int m);
+// The prefill's launch shape for an out-row weight and m tokens on `sms` SMs
+// (host only): token-tile width, stream-K or whole tiles, tiles, CTAs, and
+// the workspace bytes a split call asks for (0 for whole tiles).
+struct PrefillPlanInfo {
+  int bt;
+  bool split;
+  long long tiles;
+  int grid;
+  size_t split_bytes;
+};
+PrefillPlanInfo prefill_debug_plan(int out, int m, bool gate_up, int sms);
 cudaError_t prefill_launch(const thq4_weight &w0, const thq4_weight *w1, const void *x, int m, void *y, bool y_f32,
                            void *workspace, size_t workspace_bytes, cudaStream_t stream);
 

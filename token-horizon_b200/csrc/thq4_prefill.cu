@@ -857,8 +857,8 @@ struct PfPlan {
   long long tiles;
   int grid;
 };
-PfPlan prefill_plan_for(const thq4_weight &w0, int m, bool gate_up) {
-  const int slabs = row_slabs(w0.out), sms = device_sm_count();
+PfPlan prefill_plan_on(int out, int m, bool gate_up, int sms) {
+  const int slabs = row_slabs(out);
   PfPlan p{};
   const int forced = prefill_forced_bt();
   if (gate_up) {
@@ -875,6 +875,9 @@ PfPlan prefill_plan_for(const thq4_weight &w0, int m, bool gate_up) {
   p.grid = (int)std::min<long long>(p.tiles, sms);
   return p;
 }
+PfPlan prefill_plan_for(const thq4_weight &w0, int m, bool gate_up) {
+  return prefill_plan_on(w0.out, m, gate_up, device_sm_count());
+}
 // Workspace layout of a split call: [decode region][claim words][parts].
 size_t round256(size_t v) { return (v + 255) & ~(size_t)255; }
 size_t split_sync_off(const thq4_weight &w0) { return round256(gemv_workspace_bytes(w0.out)); }
@@ -882,6 +885,17 @@ size_t split_part_off(const thq4_weight &w0, int grid) {
   return split_sync_off(w0) + round256((size_t)grid * 2 * sizeof(uint32_t));
 }
 }  // namespace
+
+PrefillPlanInfo prefill_debug_plan(int out, int m, bool gate_up, int sms) {
+  const PfPlan p = prefill_plan_on(out, m, gate_up, sms);
+  PrefillPlanInfo r{p.bt, p.sk, p.tiles, p.grid, 0};
+  if (p.sk) {
+    thq4_weight w{};
+    w.out = out;
+    r.split_bytes = split_part_off(w, p.grid) + (size_t)p.grid * p.bt * kBN * sizeof(float);
+  }
+  return r;
+}
 
 size_t prefill_workspace_bytes(const thq4_weight &w0, int m) {
   if (!prefill_supported(m, false)) return 0;

@@ -179,4 +179,6 @@ extern "C" {
     pub fn thq4_debug_set_trace(buf: *mut c_void, bytes: usize) -> thq4_status;
     pub fn thq4_debug_gemv_plan(out: i32, inp: i32, m: i32, x_f32: i32, gate_up: i32, sms: i32,
                                 cluster_fit: *const i32, plan: *mut i64) -> thq4_status;
+    pub fn thq4_debug_prefill_plan(out: i32, inp: i32, m: i32, gate_up: i32, sms: i32, plan: *mut i64)
+                                   -> thq4_status;
 }

@@ -138,6 +138,7 @@ SIGNATURES = {
     "thq4_debug_set_gemv": (c_int, [c_int, c_int, c_int, c_int]),
     "thq4_debug_set_trace": (c_int, [c_void_p, c_size_t]),
     "thq4_debug_gemv_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "thq4_debug_prefill_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p]),
 }
 
 
